@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""GEMM benchmark for the sm_100a kernels (one JSON line on rank 0).
+
+Workload (default ``bf16_8192``): the BF16 GEMM D = A . B^T with an 8192 x 8192 x 8192 shard per
+GPU, A ~ N(0,1), B ~ N(0,1)/sqrt(K), fp32 accumulate, BF16 output.  With N GPUs
+the M dimension is sharded: rank r owns rows [8192 r, 8192 (r+1)) of A and D, B is replicated,
+and there is no collective on the data path ("scaling": "weak").  ``value`` is the whole-job
+TFLOP/s = total flops / max over ranks of the device time of the timed steps.
+
+Other workloads: ``llm`` (FFN up-projection 16384 x 28672 x 8192 with bias, M split over the N
+GPUs: strong scaling of the BASELINE config 3) and ``smallm`` (M = 128, N = K = 8192: HBM bound).
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier + synchronize on both
+sides, timed with CUDA events on the launching stream, max over ranks.  Inputs are larger than
+the 126 MB L2 (no flush between steps; stated in ``config.l2``).  SM clocks and throttle reasons
+are sampled through NVML during the timed region.
+
+``--impl reference`` times the CPU oracle of the same computation (fp32 matmul on the host
+cores, the reference has no other runnable implementation: its kernel is sm_90a-only) on a
+bounded sample of the workload; under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+if HERE not in sys.path:
+    sys.path.insert(0, HERE)
+
+NOMINAL_DENSE_BF16_TFLOPS = 2250.0
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    # name: (M per GPU or total, N, K, a_scale, b_scale, bias, m_split)
+    "bf16_8192": dict(m=8192, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
+                      m_is_per_gpu=True),
+    "llm": dict(m=16384, n=28672, k=8192, a_scale=1.0, b_scale=0.02, bias=True, m_is_per_gpu=False),
+    "smallm": dict(m=128, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
+                   m_is_per_gpu=True),
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["cpg", "reference"], default="cpg")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_8192")
+    ap.add_argument("--tile-n", type=int, default=256)
+    ap.add_argument("--cluster-m", type=int, default=2)
+    ap.add_argument("--stages", type=int, default=0, help="0 = deepest that fits")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(workload):
+    path = os.path.join(HERE, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    e = d.get(workload)
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+# ------------------------------------------------------------------ clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU on a background thread."""
+
+    REASONS = [
+        (0x4, "sw_power_cap"), (0x8, "hw_slowdown"), (0x20, "sw_thermal_slowdown"),
+        (0x40, "hw_thermal_slowdown"), (0x80, "hw_power_brake_slowdown"),
+        (0x2, "applications_clocks_setting"), (0x10, "sync_boost"),
+    ]
+
+    def __init__(self, cuda_index, period_s=0.01):
+        self.samples = []
+        self.reasons = 0
+        self.period = period_s
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.h = None
+        try:
+            import pynvml
+            self.nv = pynvml
+            pynvml.nvmlInit()
+            self.h = self._handle(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.h = None
+
+    def _handle(self, cuda_index):
+        import torch
+        nv = self.nv
+        try:
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(cuda_index)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.reasons |= int(r)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.h is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if self.h is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        names = [n for bit, n in self.REASONS if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(ngpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != ngpus:
+        raise SystemExit(f"--gpus {ngpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def reduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_matmul_rate(rows, n, k, seconds, max_reps=50, seed=0):
+    """fp32 CPU matmul of a rows x k slab against B^T (the oracle's computation)."""
+    import torch
+    from oracle import gemm_ref
+    cores = gemm_ref.set_threads()
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(rows, k, generator=g).to(torch.bfloat16).float()
+    b = (torch.randn(n, k, generator=g) * k ** -0.5).to(torch.bfloat16).float()
+    torch.matmul(a[: min(rows, 64)], b.t())  # warm the thread pool
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        torch.matmul(a, b.t())
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= max_reps:
+            break
+    return 2.0 * rows * n * k * reps / el / 1e12, cores, reps, el
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU oracle on the host cores, rank 0 only."""
+    import torch
+    from oracle import gemm_ref
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    n, k = w["n"], w["k"]
+    cores = gemm_ref.set_threads()
+    g = torch.Generator().manual_seed(0)
+    b = (torch.randn(n, k, generator=g) * w["b_scale"]).to(torch.bfloat16).float()
+    # Calibrate the per-step sample so the whole run stays within about a minute.
+    probe_rows = 64
+    a = torch.randn(probe_rows, k, generator=g).to(torch.bfloat16).float()
+    torch.matmul(a, b.t())
+    t0 = time.perf_counter()
+    torch.matmul(a, b.t())
+    t_probe = max(time.perf_counter() - t0, 1e-4)
+    per_step_budget = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(max(8, min(w["m"], probe_rows * per_step_budget / t_probe)))
+    rows = max(8, rows // 8 * 8)
+    a = torch.randn(rows, k, generator=g).to(torch.bfloat16).float()
+    for _ in range(args.warmup):
+        torch.matmul(a, b.t())
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        torch.matmul(a, b.t())
+    el = time.perf_counter() - t0
+    flops = 2.0 * rows * n * k * args.steps
+    value = flops / el / 1e12
+    sample = (f"{rows}x{n}x{k} fp32 row slab of the {args.workload} GEMM per step "
+              f"(torch.matmul on {cores} host threads)")
+    line = {
+        "impl": "reference", "metric": metric_name(args.workload), "value": value,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak" if w["m_is_per_gpu"] else "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "m": w["m"], "n": n, "k": k, "rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference kernel is sm_90a CuTe-DSL (wgmma) and cannot run on sm_100; the "
+                "reference arm is the fp32 CPU oracle of D = A @ B.T",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(workload):
+    return {"bf16_8192": "GEMM TFLOPS (BF16 8192^3 per GPU, M-sharded, B replicated)",
+            "llm": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 + bias, M-sharded)",
+            "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)"}[workload]
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_cpg(args, world, rank, local):
+    import torch
+    from cutedsl_pingpong_gemm_b200 import GemmSM90, RasterOrder, compile as cpg_compile
+
+    w = WORKLOADS[args.workload]
+    n, k = w["n"], w["k"]
+    m = w["m"] if w["m_is_per_gpu"] else w["m"] // world
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    # Inputs generated on the device with the workload's distribution (A rows differ per rank,
+    # B is the same replicated weight on every rank).
+    gen_a = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gen_b = torch.Generator(device=dev).manual_seed(7)
+    a = (torch.randn(m, k, generator=gen_a, device=dev) * w["a_scale"]).to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=gen_b, device=dev) * w["b_scale"]).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=gen_b, device=dev)).to(torch.bfloat16) if w["bias"] else None
+    d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+
+    cm = args.cluster_m
+    stages = args.stages or (6 if cm == 2 else 4)
+    if args.tile_n < 256 and not args.stages:
+        stages = 8 if cm == 2 else 6
+    gemm = GemmSM90(tile_shape_mn=(128, args.tile_n), epi_tile_mn=(128, 32),
+                    cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
+                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
+    compiled = cpg_compile(gemm, a, b, d, stream)
+    plan = compiled.plan_for(a, b, d)
+    info = plan.launch_info()
+
+    launches = [0]
+
+    def step():
+        compiled(a, b, d, stream, bias=bias)
+        launches[0] += 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches[0] = 0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sampler.stop()
+    barrier(world)
+    n_launch = launches[0]
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = reduce_max(ms_local, world)
+    status = plan.status()
+    if status != 0:
+        raise SystemExit(f"kernel status {status:#x}")
+
+    flops_per_gpu = 2.0 * m * n * k
+    total_flops = flops_per_gpu * world
+    value = total_flops / (ms * 1e-3) / 1e12
+    achieved = flops_per_gpu / (ms_local * 1e-3) / 1e12  # one kernel launch per step
+    peaks, peak_src = load_peaks()
+
+    # ---------------- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        a_h = a.cpu().pin_memory()
+        b_h = b.cpu().pin_memory()
+        d_h = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        a2 = torch.empty_like(a)
+        b2 = torch.empty_like(b)
+
+        def e2e_step():
+            a2.copy_(a_h, non_blocking=True)
+            b2.copy_(b_h, non_blocking=True)
+            compiled(a2, b2, d, stream, bias=bias)
+            d_h.copy_(d, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = reduce_max(f0.elapsed_time(f1) / args.e2e_steps, world)
+        e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int((a.numel() + b.numel()) * 2 * world),
+               "d2h_bytes_per_step": int(d.numel() * 2 * world), "steps": args.e2e_steps,
+               "ms_per_step": e2e_ms, "gpu_launches": args.e2e_steps * world,
+               "path": "GemmSM90 compiled call (C ABI cpg_gemm_run) with pinned-host A, B in and D out"}
+
+    clocks = sampler.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 512
+        rate, cores, reps, el = cpu_matmul_rate(rows, n, k, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+               "sample": f"{reps} x fp32 torch.matmul of a {rows}x{k} row slab against B^T "
+                         f"({n}x{k}) on the host, {el:.1f} s"}
+
+    if rank == 0:
+        peak = peaks["bf16_tflops"]
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak" if w["m_is_per_gpu"] else "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "pct_nominal_dense_peak": 100.0 * value / (NOMINAL_DENSE_BF16_TFLOPS * world),
+            "config": {"workload": args.workload, "m_per_gpu": m, "n": n, "k": k,
+                       "m_total": m * world, "parallelism": f"m-shard x{world}, B replicated",
+                       "tile": [128, args.tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
+                       "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
+                       "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
+                       "bias": bool(w["bias"])},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "frac_sustained": achieved / peaks.get("bf16_tflops_sustained", peak),
+                         "traffic": load_traffic(args.workload),
+                         "algorithmic_flops_per_launch": flops_per_gpu,
+                         "kernel": "cpg::gemm_bf16_sm100_kernel"},
+            "clocks": clocks,
+            "gpu_launches": n_launch * world,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_cpg(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,590 @@
+// Host side of the C ABI declared in include/cpgemm.h: configuration checks (the reference's
+// constructor asserts), problem checks, kernel selection, tensor-map encoding and launch.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "cpgemm.h"
+#include "gemm_kernel.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CPG_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) return;
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return;
+    ok = true;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D row-major matrix [rows, cols] with row stride `ld` elements, tiled into
+// box_rows x box_cols boxes with 128-byte swizzle.
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* ptr,
+              int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(CPG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(CPG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld",
+                static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols),
+                static_cast<long long>(ld));
+  }
+  return CPG_OK;
+}
+
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const cpg::GemmParams);
+
+struct Variant {
+  int bn;
+  int cta_group;
+  KernelFn fn;
+  int (*smem_bytes)(int, int, int);
+};
+
+template <int BN, int CG>
+int smem_bytes_of(int stages, int epi_stages, int reuse_ab) {
+  return cpg::GemmSmem<BN, CG>::bytes(stages, epi_stages, reuse_ab);
+}
+
+template <int BN, int CG>
+Variant make_variant() {
+  return Variant{BN, CG, &cpg::gemm_bf16_sm100_kernel<BN, CG>, &smem_bytes_of<BN, CG>};
+}
+
+bool find_variant(int bn, int cta_group, Variant* out) {
+  static const Variant table[] = {
+      make_variant<256, 1>(), make_variant<128, 1>(), make_variant<64, 1>(),
+      make_variant<256, 2>(), make_variant<128, 2>(), make_variant<64, 2>(),
+  };
+  for (const Variant& v : table) {
+    if (v.bn == bn && v.cta_group == cta_group) {
+      *out = v;
+      return true;
+    }
+  }
+  return false;
+}
+
+__global__ void fill_rows_kernel(__nv_bfloat16* d, int64_t m, int64_t n, int64_t ldd,
+                                 const __nv_bfloat16* bias) {
+  int64_t total = m * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = i / n, c = i % n;
+    d[r * ldd + c] = bias != nullptr ? bias[c] : __float2bfloat16(0.f);
+  }
+}
+
+int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* out) {
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(v.fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cm * cn == 1) {
+    int per_sm = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, cpg::kNumThreads, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    *out = per_sm * sms;
+    return CPG_OK;
+  }
+  cudaLaunchConfig_t lc = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cm;
+  attr[0].val.clusterDim.y = cn;
+  attr[0].val.clusterDim.z = 1;
+  lc.gridDim = dim3(cm, cn, 1);
+  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, v.fn, &lc);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+  *out = n;
+  return CPG_OK;
+}
+
+}  // namespace
+
+struct cpg_gemm {
+  cpg_gemm_config cfg;
+  cpg_gemm_problem prob;
+  int device;
+  Variant v;
+  int smem_bytes;
+  int grid[3];
+  int cluster[3];
+  int max_active_clusters;
+  cpg::SchedParams sched;
+  int32_t* status_dev;
+  int32_t* trace;
+  int32_t trace_stride;
+  uint64_t timeout_ns;
+  bool maps_valid;
+  const void* map_a_ptr;
+  const void* map_b_ptr;
+  const void* map_d_ptr;
+  CUtensorMap tm_a, tm_b, tm_d;
+};
+
+extern "C" {
+
+int cpg_abi_version(void) { return 1; }
+
+const char* cpg_strerror(int code) {
+  switch (code) {
+    case CPG_OK: return "ok";
+    case CPG_ERR_INVALID_CONFIG: return "invalid GEMM configuration";
+    case CPG_ERR_INVALID_SHAPE: return "invalid problem shape or stride";
+    case CPG_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case CPG_ERR_DTYPE: return "unsupported element type";
+    case CPG_ERR_UNSUPPORTED: return "configuration not implemented on sm_100a";
+    case CPG_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case CPG_ERR_CUDA: return "CUDA call failed";
+    case CPG_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case CPG_ERR_SMEM: return "configuration exceeds shared memory";
+    case CPG_ERR_NULL: return "null pointer argument";
+    default: return "unknown error";
+  }
+}
+
+const char* cpg_last_error_message(void) { return g_last_error.c_str(); }
+
+int cpg_config_validate(const cpg_gemm_config* c) {
+  if (c == nullptr) return fail(CPG_ERR_NULL, "config is NULL");
+  // gemm_base.py:72
+  if (!(c->atom_m >= 1 && c->atom_m <= 3) || !(c->atom_n >= 1 && c->atom_n <= 2))
+    return fail(CPG_ERR_INVALID_CONFIG, "atom_layout_mn must be in {1,2,3} x {1,2}, got (%d, %d)",
+                c->atom_m, c->atom_n);
+  // gemm_base.py:73-74
+  if (!(c->atom_m == 1 || c->tile_m % (c->atom_m * 64) == 0))
+    return fail(CPG_ERR_INVALID_CONFIG, "tile_m %d must be a multiple of atom_m * 64", c->tile_m);
+  if (!(c->atom_n == 1 || c->tile_n % (c->atom_n * 32) == 0))
+    return fail(CPG_ERR_INVALID_CONFIG, "tile_n %d must be a multiple of atom_n * 32", c->tile_n);
+  // gemm_base.py:86-87
+  int wg = c->atom_m * c->atom_n;
+  if (wg < 1 || wg > 3)
+    return fail(CPG_ERR_INVALID_CONFIG, "atom_m * atom_n must be 1, 2 or 3, got %d", wg);
+  // gemm_base.py:113
+  if (c->atom_n > 1 && c->epi_tile_n != c->tile_n)
+    return fail(CPG_ERR_INVALID_CONFIG, "when atom layout n > 1, epi tile n must equal tile n");
+  // gemm_base.py:122
+  if (c->reuse_ab && c->is_persistent)
+    return fail(CPG_ERR_INVALID_CONFIG, "persistent kernel can't reuse AB for epilogue");
+  // tile_scheduler.py:51
+  if (c->cluster_k != 1) return fail(CPG_ERR_INVALID_CONFIG, "cluster_shape_mnk[2] must be 1");
+  if (c->tile_m <= 0 || c->tile_n <= 0 || c->epi_tile_m <= 0 || c->epi_tile_n <= 0 ||
+      c->cluster_m <= 0 || c->cluster_n <= 0 || c->ab_stage <= 0 || c->epi_stage <= 0 ||
+      c->group_size <= 0 || c->gemm_n_prologue < 0)
+    return fail(CPG_ERR_INVALID_CONFIG, "tile, cluster, stage and group sizes must be positive");
+  if (c->raster_order != CPG_RASTER_ALONG_M && c->raster_order != CPG_RASTER_ALONG_N)
+    return fail(CPG_ERR_INVALID_CONFIG, "raster_order must be 0 (AlongM) or 1 (AlongN)");
+  return CPG_OK;
+}
+
+int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
+                    cpg_gemm** out) {
+  if (cfg == nullptr || prob == nullptr || out == nullptr)
+    return fail(CPG_ERR_NULL, "cfg, prob and out must be non-NULL");
+  *out = nullptr;
+  int rc = cpg_config_validate(cfg);
+  if (rc != CPG_OK) return rc;
+
+  // What this sm_100a build implements.
+  if (cfg->tile_m != 128)
+    return fail(CPG_ERR_UNSUPPORTED, "tile_m must be 128 (one TMEM lane per row), got %d",
+                cfg->tile_m);
+  if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256)
+    return fail(CPG_ERR_UNSUPPORTED, "tile_n must be 64, 128 or 256, got %d", cfg->tile_n);
+  if (cfg->cluster_m > 2 || cfg->cluster_n > 2)
+    return fail(CPG_ERR_UNSUPPORTED, "cluster_shape_mnk must be within (2, 2, 1)");
+  if (cfg->tile_m % cfg->epi_tile_m != 0 || cfg->tile_n % cfg->epi_tile_n != 0)
+    return fail(CPG_ERR_UNSUPPORTED, "epi_tile_mn must divide tile_shape_mn");
+  if (cfg->ab_stage > cpg::kMaxStages)
+    return fail(CPG_ERR_SMEM, "ab_stage %d exceeds %d", cfg->ab_stage, cpg::kMaxStages);
+  if (cfg->epi_stage > cpg::kMaxEpiStages)
+    return fail(CPG_ERR_UNSUPPORTED, "epi_stage %d exceeds %d", cfg->epi_stage,
+                cpg::kMaxEpiStages);
+  if (cfg->gemm_n_prologue >= cfg->ab_stage)
+    return fail(CPG_ERR_INVALID_CONFIG, "gemm_n_prologue must be below ab_stage");
+
+  // Problem checks.
+  if (prob->dtype_ab != CPG_DTYPE_BF16 || prob->dtype_d != CPG_DTYPE_BF16)
+    return fail(CPG_ERR_DTYPE, "A, B and D must be BF16 (gemm_base.py:514)");
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (prob->m < 0 || prob->n < 0 || prob->k < 0 || prob->m > lim || prob->n > lim || prob->k > lim)
+    return fail(CPG_ERR_INVALID_SHAPE, "M, N, K must be in [0, 2^31)");
+  if (prob->lda < prob->k || prob->ldb < prob->k || prob->ldd < prob->n)
+    return fail(CPG_ERR_INVALID_SHAPE, "row strides must be at least the row length");
+  if (prob->lda % 8 != 0 || prob->ldb % 8 != 0 || prob->ldd % 8 != 0)
+    return fail(CPG_ERR_ALIGNMENT, "row strides must be multiples of 8 elements (16 bytes)");
+
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(CPG_ERR_NO_DEVICE, "cannot select device %d", device);
+  cudaDeviceProp prop;
+  cudaError_t e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(CPG_ERR_NO_DEVICE, "device %d is sm_%d%d; this build targets sm_100a", device,
+                prop.major, prop.minor);
+
+  Variant v;
+  const int cta_group = cfg->cluster_m == 2 ? 2 : 1;
+  if (!find_variant(cfg->tile_n, cta_group, &v))
+    return fail(CPG_ERR_UNSUPPORTED, "no kernel for tile_n %d, cta_group %d", cfg->tile_n,
+                cta_group);
+  const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
+  if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
+    return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
+                cfg->ab_stage, smem, static_cast<int>(prop.sharedMemPerBlockOptin));
+  int mac = 0;
+  rc = query_max_active_clusters(v, smem, cfg->cluster_m, cfg->cluster_n, &mac);
+  if (rc != CPG_OK) return rc;
+  if (mac <= 0) return fail(CPG_ERR_NO_DEVICE, "kernel cannot be resident (occupancy 0)");
+
+  cpg_gemm* g = new cpg_gemm();
+  std::memset(static_cast<void*>(g), 0, sizeof(*g));
+  g->cfg = *cfg;
+  g->prob = *prob;
+  g->device = device;
+  g->v = v;
+  g->smem_bytes = smem;
+  g->max_active_clusters = mac;
+  g->timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
+  const char* env = std::getenv("CPG_WAIT_TIMEOUT_MS");
+  if (env != nullptr && std::atoi(env) > 0) g->timeout_ns = uint64_t(std::atoi(env)) * 1000000ull;
+
+  const int64_t ntm = prob->m > 0 ? (prob->m + 127) / 128 : 1;
+  const int64_t ntn = prob->n > 0 ? (prob->n + cfg->tile_n - 1) / cfg->tile_n : 1;
+  g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn), 1,
+                                      cfg->raster_order, cfg->group_size, cfg->cluster_m,
+                                      cfg->cluster_n, cfg->is_persistent);
+  int32_t grid[3];
+  cpg::sched_grid_shape(g->sched, mac, grid);
+  for (int i = 0; i < 3; ++i) g->grid[i] = grid[i];
+  g->cluster[0] = cfg->cluster_m;
+  g->cluster[1] = cfg->cluster_n;
+  g->cluster[2] = 1;
+
+  e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
+  if (e != cudaSuccess) {
+    delete g;
+    return cuda_fail(e, "cudaMalloc(status word)");
+  }
+  e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
+  if (e != cudaSuccess) {
+    cudaFree(g->status_dev);
+    delete g;
+    return cuda_fail(e, "cudaMemset(status word)");
+  }
+  *out = g;
+  return CPG_OK;
+}
+
+int cpg_gemm_destroy(cpg_gemm* g) {
+  if (g == nullptr) return CPG_OK;
+  if (g->status_dev != nullptr) {
+    DeviceGuard guard(g->device);
+    cudaFree(g->status_dev);
+  }
+  delete g;
+  return CPG_OK;
+}
+
+int cpg_gemm_launch_info(const cpg_gemm* g, int32_t grid[3], int32_t cluster[3], int32_t* threads,
+                         int32_t* smem_bytes, int32_t* max_active_clusters) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  for (int i = 0; i < 3; ++i) {
+    if (grid) grid[i] = g->grid[i];
+    if (cluster) cluster[i] = g->cluster[i];
+  }
+  if (threads) *threads = cpg::kNumThreads;
+  if (smem_bytes) *smem_bytes = g->smem_bytes;
+  if (max_active_clusters) *max_active_clusters = g->max_active_clusters;
+  return CPG_OK;
+}
+
+int cpg_gemm_sched_params(const cpg_gemm* g, cpg_sched_params* out) {
+  if (g == nullptr || out == nullptr) return fail(CPG_ERR_NULL, "plan and out must be non-NULL");
+  static_assert(sizeof(cpg_sched_params) == sizeof(cpg::SchedParams), "layout mismatch");
+  std::memcpy(out, &g->sched, sizeof(*out));
+  return CPG_OK;
+}
+
+int cpg_gemm_set_trace(cpg_gemm* g, int32_t* device_buf, int32_t tiles_per_cta) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  if (device_buf != nullptr && tiles_per_cta <= 0)
+    return fail(CPG_ERR_INVALID_SHAPE, "tiles_per_cta must be positive");
+  g->trace = device_buf;
+  g->trace_stride = device_buf != nullptr ? tiles_per_cta : 0;
+  return CPG_OK;
+}
+
+int cpg_gemm_set_timeout_ms(cpg_gemm* g, int32_t timeout_ms) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  if (timeout_ms <= 0) return fail(CPG_ERR_INVALID_SHAPE, "timeout must be positive");
+  g->timeout_ns = uint64_t(timeout_ms) * 1000000ull;
+  return CPG_OK;
+}
+
+int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
+  if (g == nullptr || status == nullptr) return fail(CPG_ERR_NULL, "plan and status non-NULL");
+  DeviceGuard guard(g->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int32_t s = 0;
+  e = cudaMemcpy(&s, g->status_dev, sizeof(s), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  *status = s;
+  if (s != 0) {
+    cudaMemset(g->status_dev, 0, sizeof(int32_t));
+    return fail(CPG_ERR_DEVICE_TIMEOUT, "kernel wait timed out at site %d", s & 0xFF);
+  }
+  return CPG_OK;
+}
+
+int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                 void* stream) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  const cpg_gemm_problem& pr = g->prob;
+  if (pr.m == 0 || pr.n == 0) return CPG_OK;
+  if (d == nullptr) return fail(CPG_ERR_NULL, "D is NULL");
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != g->device)
+    return fail(CPG_ERR_NO_DEVICE, "current device %d differs from the plan's device %d", cur,
+                g->device);
+  const void* bias = epi != nullptr ? epi->bias : nullptr;
+  const float alpha = epi != nullptr ? epi->alpha : 1.0f;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if ((reinterpret_cast<uintptr_t>(d) & 15u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "D must be 16-byte aligned");
+  if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "bias must be 2-byte aligned");
+
+  if (pr.k == 0) {
+    // D = bias (or 0): nothing to contract.
+    int blocks = static_cast<int>((pr.m * pr.n + 255) / 256);
+    if (blocks > 4096) blocks = 4096;
+    fill_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<__nv_bfloat16*>(d), pr.m, pr.n, pr.ldd,
+                                             static_cast<const __nv_bfloat16*>(bias));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CPG_OK : cuda_fail(e, "fill kernel launch");
+  }
+  if (a == nullptr || b == nullptr) return fail(CPG_ERR_NULL, "A and B must be non-NULL");
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) != 0 || (reinterpret_cast<uintptr_t>(b) & 15u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+
+  if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
+    int rc = encode_2d(&g->tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, pr.m, pr.k, pr.lda,
+                       cpg::kBM, cpg::kBK);
+    if (rc != CPG_OK) return rc;
+    rc = encode_2d(&g->tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, pr.n, pr.k, pr.ldb,
+                   g->v.bn / g->v.cta_group, cpg::kBK);
+    if (rc != CPG_OK) return rc;
+    rc = encode_2d(&g->tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, pr.m, pr.n, pr.ldd, 32,
+                   cpg::kEpiCols);
+    if (rc != CPG_OK) return rc;
+    g->map_a_ptr = a;
+    g->map_b_ptr = b;
+    g->map_d_ptr = d;
+    g->maps_valid = true;
+  }
+
+  cpg::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.sched = g->sched;
+  p.m = static_cast<int32_t>(pr.m);
+  p.n = static_cast<int32_t>(pr.n);
+  p.k = static_cast<int32_t>(pr.k);
+  p.k_iters = static_cast<int32_t>((pr.k + cpg::kBK - 1) / cpg::kBK);
+  p.ab_stages = g->cfg.ab_stage;
+  p.epi_stages = g->cfg.epi_stage;
+  p.reuse_ab = g->cfg.reuse_ab;
+  p.alpha = alpha;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.tile_trace = g->trace;
+  p.trace_stride = g->trace_stride;
+  p.status = g->status_dev;
+  p.timeout_ns = g->timeout_ns;
+
+  cudaLaunchConfig_t lc = {};
+  cudaLaunchAttribute attr[1];
+  lc.gridDim = dim3(g->grid[0], g->grid[1], g->grid[2]);
+  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.dynamicSmemBytes = g->smem_bytes;
+  lc.stream = st;
+  lc.numAttrs = 0;
+  if (g->cluster[0] * g->cluster[1] > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = g->cluster[0];
+    attr[0].val.clusterDim.y = g->cluster[1];
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p};
+  cudaError_t e = cudaLaunchKernelExC(&lc, reinterpret_cast<const void*>(g->v.fn), args);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM kernel launch");
+  return CPG_OK;
+}
+
+int cpg_fast_divmod_create(int32_t divisor, cpg_fast_divmod* out) {
+  if (out == nullptr) return fail(CPG_ERR_NULL, "out is NULL");
+  if (divisor < 1) return fail(CPG_ERR_INVALID_SHAPE, "divisor must be >= 1, got %d", divisor);
+  cpg::FastDivmod f = cpg::fast_divmod_create(divisor);
+  out->divisor = f.divisor;
+  out->multiplier = f.multiplier;
+  out->shift_right = f.shift_right;
+  return CPG_OK;
+}
+
+int cpg_fast_divmod_divmod(const cpg_fast_divmod* f, int32_t x, int32_t* q, int32_t* r) {
+  if (f == nullptr || q == nullptr || r == nullptr) return fail(CPG_ERR_NULL, "NULL argument");
+  cpg::FastDivmod ff{f->divisor, f->multiplier, f->shift_right};
+  cpg::fast_divmod(ff, x, *q, *r);
+  return CPG_OK;
+}
+
+int cpg_fast_divmod_device(const cpg_fast_divmod* f, const int32_t* x, int32_t* q, int32_t* r,
+                           int64_t n, void* stream) {
+  if (f == nullptr || (n > 0 && (x == nullptr || q == nullptr || r == nullptr)))
+    return fail(CPG_ERR_NULL, "NULL argument");
+  if (n <= 0) return CPG_OK;
+  cpg::FastDivmod ff{f->divisor, f->multiplier, f->shift_right};
+  const int threads = 256;
+  const int64_t blocks = (n + threads - 1) / threads;
+  cpg::fast_divmod_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(ff, x, q, r, n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "fast_divmod_kernel launch");
+}
+
+int cpg_sched_params_create(int32_t ntiles_m, int32_t ntiles_n, int32_t ntiles_l,
+                            int32_t raster_order, int32_t group_size, int32_t cluster_m,
+                            int32_t cluster_n, int32_t cluster_k, int32_t is_persistent,
+                            cpg_sched_params* out) {
+  if (out == nullptr) return fail(CPG_ERR_NULL, "out is NULL");
+  if (cluster_k != 1) return fail(CPG_ERR_INVALID_CONFIG, "cluster_shape_mnk[2] must be 1");
+  if (ntiles_m < 1 || ntiles_n < 1 || ntiles_l < 1 || group_size < 1 || cluster_m < 1 ||
+      cluster_n < 1)
+    return fail(CPG_ERR_INVALID_SHAPE, "tile counts, group size and cluster dims must be >= 1");
+  if (raster_order != CPG_RASTER_ALONG_M && raster_order != CPG_RASTER_ALONG_N)
+    return fail(CPG_ERR_INVALID_CONFIG, "raster_order must be 0 or 1");
+  cpg::SchedParams p = cpg::sched_params_create(ntiles_m, ntiles_n, ntiles_l, raster_order,
+                                                group_size, cluster_m, cluster_n, is_persistent);
+  std::memcpy(out, &p, sizeof(*out));
+  return CPG_OK;
+}
+
+int cpg_sched_grid_shape(const cpg_sched_params* p, int32_t max_active_clusters, int32_t grid[3]) {
+  if (p == nullptr || grid == nullptr) return fail(CPG_ERR_NULL, "NULL argument");
+  cpg::SchedParams sp;
+  std::memcpy(&sp, p, sizeof(sp));
+  cpg::sched_grid_shape(sp, max_active_clusters, grid);
+  return CPG_OK;
+}
+
+int cpg_sched_cluster_map(const cpg_sched_params* p, int32_t* out, int64_t n) {
+  if (p == nullptr || (n > 0 && out == nullptr)) return fail(CPG_ERR_NULL, "NULL argument");
+  cpg::SchedParams sp;
+  std::memcpy(&sp, p, sizeof(sp));
+  for (int64_t i = 0; i < n; ++i) {
+    int32_t cm, cn;
+    cpg::sched_map_cluster(sp, static_cast<int32_t>(i), cm, cn);
+    out[2 * i] = cm;
+    out[2 * i + 1] = cn;
+  }
+  return CPG_OK;
+}
+
+int cpg_sched_cluster_map_device(const cpg_sched_params* p, int32_t* device_out, int64_t n,
+                                 void* stream) {
+  if (p == nullptr || (n > 0 && device_out == nullptr)) return fail(CPG_ERR_NULL, "NULL argument");
+  if (n <= 0) return CPG_OK;
+  cpg::SchedParams sp;
+  std::memcpy(&sp, p, sizeof(sp));
+  const int threads = 256;
+  const int64_t blocks = (n + threads - 1) / threads;
+  cpg::sched_cluster_map_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                                  reinterpret_cast<cudaStream_t>(stream)>>>(sp, device_out, n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "sched_cluster_map_kernel launch");
+}
+
+int cpg_max_active_clusters(int32_t cluster_size, int32_t* out) {
+  if (out == nullptr) return fail(CPG_ERR_NULL, "out is NULL");
+  if (cluster_size < 1 || cluster_size > 4)
+    return fail(CPG_ERR_UNSUPPORTED, "cluster size must be 1..4, got %d", cluster_size);
+  Variant v;
+  const int cg = (cluster_size % 2 == 0) ? 2 : 1;
+  find_variant(256, cg, &v);
+  const int smem = v.smem_bytes(4, 2, 0);
+  int cm = cluster_size >= 2 ? 2 : 1;
+  int cn = cluster_size == 4 ? 2 : (cluster_size == 3 ? 3 : 1);
+  if (cluster_size == 3) cm = 1;
+  int n = 0;
+  int rc = query_max_active_clusters(v, smem, cm, cn, &n);
+  if (rc != CPG_OK) return rc;
+  *out = n;
+  return CPG_OK;
+}
+
+}  // extern "C"

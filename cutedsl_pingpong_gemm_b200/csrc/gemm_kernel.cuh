@@ -1,0 +1,475 @@
+// Warp-specialised persistent BF16 GEMM for sm_100a:  D[M,N] = alpha * A[M,K] . B[N,K]^T (+ bias[N])
+//
+// Role of each warp (192 threads per CTA):
+//   warp 0     TMA producer: one lane streams A/B k-blocks into an `ab_stages`-deep ring of
+//              128B-swizzled shared-memory stages (full/empty mbarrier pairs).  This replaces the
+//              reference's producer warp (gemm_base.py:204-229, produce_mainloop :365-388).
+//   warp 1     MMA issuer: allocates TMEM, one lane issues tcgen05.mma (kind::f16, fp32
+//              accumulate) into one of two TMEM accumulators and commits stage releases and
+//              "accumulator full" signals.  Replaces the consumer warpgroups' wgmma mainloop
+//              (consume_mainloop, gemm_base.py:390-428).
+//   warps 2-5  epilogue: tcgen05.ld the accumulator (each warp owns a 32-lane TMEM quadrant),
+//              scale / add bias, round to BF16, write 128B-swizzled staging buffers and TMA-store
+//              them (epilogue, gemm_base.py:270-363).  Two TMEM accumulators let the epilogue of
+//              tile i overlap the mainloop of tile i+1.
+//
+// CTA pairs (CtaGroup == 2, cluster (2,1)): both CTAs load their own 128 rows of A and their own
+// half of the B tile; the even CTA issues tcgen05.mma.cta_group::2 (M = 256) that reads both
+// CTAs' shared memory, and one tcgen05.commit with a two-CTA mask signals the same barrier in both
+// CTAs.  No TMA load uses cluster multicast.
+//
+// Tile order: every role walks the same sequence from the shared scheduler header, identical to
+// the reference's SimpleTileScheduler (tile_scheduler.py:94-183).
+//
+// Every mbarrier wait is bounded (WaitCtx): on a timeout the kernel records an error code in the
+// status word, the other roles stop at their next wait, in-flight TMA loads and MMAs are drained
+// (again bounded), TMEM is freed and the kernel returns.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+#include "tile_scheduler.h"
+
+namespace cpg {
+
+constexpr int kBM = 128;             // rows of A / D per CTA
+constexpr int kBK = 64;              // BF16 elements per 128-byte swizzled row (one k-block)
+constexpr int kUmmaK = 16;           // K per tcgen05.mma kind::f16
+constexpr int kNumThreads = 192;     // 6 warps
+constexpr int kEpiWarps = 4;
+constexpr int kEpiFirstWarp = 2;
+constexpr int kEpiCols = 64;         // columns per epilogue chunk (one 128-byte swizzled row)
+constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 64 BF16 = 4 KiB
+constexpr int kMaxStages = 12;
+constexpr int kMaxEpiStages = 4;
+constexpr int kMinSmemForOneCtaPerSm = 116 * 1024;
+
+// Wait-site identifiers recorded in the status word on a timeout.
+enum WaitSite : int32_t {
+  kSiteProducerEmpty = 1,
+  kSiteMmaFull = 2,
+  kSiteMmaTmemEmpty = 3,
+  kSiteEpiTmemFull = 4,
+  kSiteDrainLoads = 5,
+  kSiteDrainMma = 6,
+};
+
+struct GemmParams {
+  SchedParams sched;
+  int32_t m, n, k;
+  int32_t k_iters;        // ceil(K / 64)
+  int32_t ab_stages;
+  int32_t epi_stages;
+  int32_t reuse_ab;       // epilogue staging aliases the A/B stages (single-tile CTAs only)
+  float alpha;
+  const __nv_bfloat16* bias;  // optional per-column bias, length N
+  int32_t* tile_trace;    // optional: (pid_m, pid_n) per CTA per tile, trace_stride tiles per CTA
+  int32_t trace_stride;
+  int32_t* status;        // device status word (0 = ok)
+  uint64_t timeout_ns;
+};
+
+template <int BN, int CtaGroup>
+struct GemmSmem {
+  static constexpr int kAStageBytes = kBM * kBK * 2;                       // 16 KiB
+  static constexpr int kBStageBytes = (BN / CtaGroup) * kBK * 2;           // per CTA
+  static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+  static constexpr int kTmemCols = 2 * BN;                                 // two accumulators
+  static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(kTmemCols >= 32 && kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0,
+                "TMEM allocation must be a power of two in [32, 512]");
+
+  // Byte offsets from the 1024-aligned base.
+  static __host__ __device__ int epi_offset(int stages, int reuse_ab) {
+    return reuse_ab ? 0 : stages * kStageBytes;
+  }
+  static __host__ __device__ int barrier_offset(int stages, int epi_stages, int reuse_ab) {
+    int end_stages = stages * kStageBytes;
+    int end_epi = epi_offset(stages, reuse_ab) + kEpiWarps * epi_stages * kEpiBufBytes;
+    return end_stages > end_epi ? end_stages : end_epi;
+  }
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], drain[1]; then tmem slot and abort flag.
+  static __host__ __device__ int bytes(int stages, int epi_stages, int reuse_ab) {
+    int b = barrier_offset(stages, epi_stages, reuse_ab) + (2 * stages + 5) * 8 + 16;
+    b += 1024;  // alignment slack for the dynamic shared memory base
+    return b < kMinSmemForOneCtaPerSm ? kMinSmemForOneCtaPerSm : b;
+  }
+};
+
+// Linear persistent / non-persistent work iterator (tile_scheduler.py:94-107, :159-183).
+struct WorkIter {
+  int32_t cid, stride, total, executed, persistent;
+  __device__ __forceinline__ bool valid() const {
+    return persistent ? (cid < total) : (executed == 0);
+  }
+  __device__ __forceinline__ void advance() {
+    if (persistent) cid += stride;
+    ++executed;
+  }
+};
+
+__device__ __forceinline__ WorkIter make_work_iter(const SchedParams& sp) {
+  WorkIter it;
+  if (sp.is_persistent) {
+    it.cid = static_cast<int32_t>(blockIdx.z);
+    it.stride = static_cast<int32_t>(gridDim.z);
+  } else {
+    it.cid = static_cast<int32_t>(ptx::clusterid_x() + ptx::clusterid_y() * ptx::nclusterid_x());
+    it.stride = 0;
+  }
+  it.total = sched_total_clusters(sp);
+  it.executed = 0;
+  it.persistent = sp.is_persistent;
+  return it;
+}
+
+__device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t cid,
+                                                 int32_t& pid_m, int32_t& pid_n) {
+  int32_t cm, cn;
+  sched_map_cluster(sp, cid, cm, cn);
+  pid_m = cm * sp.cluster_m + static_cast<int32_t>(ptx::cluster_ctaid_x());
+  pid_n = cn * sp.cluster_n + static_cast<int32_t>(ptx::cluster_ctaid_y());
+}
+
+__device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
+  // Allow (epi_stages - 1) stores in flight before reusing the oldest staging buffer.
+  switch (epi_stages) {
+    case 1: ptx::bulk_wait_group_read<0>(); break;
+    case 2: ptx::bulk_wait_group_read<1>(); break;
+    case 3: ptx::bulk_wait_group_read<2>(); break;
+    default: ptx::bulk_wait_group_read<3>(); break;
+  }
+}
+
+template <int BN, int CtaGroup>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tm_a,
+                           const __grid_constant__ CUtensorMap tm_b,
+                           const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using L = GemmSmem<BN, CtaGroup>;
+  constexpr int kBNc = BN / CtaGroup;  // B rows loaded by this CTA
+  constexpr uint32_t kIdesc = ptx::make_idesc_bf16_f32(kBM * CtaGroup, BN);
+  constexpr uint32_t kTxBytes = static_cast<uint32_t>(L::kStageBytes * CtaGroup);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+
+  const int stages = p.ab_stages;
+  const uint32_t epi_base = base + L::epi_offset(stages, p.reuse_ab);
+  const uint32_t bar_base = base + L::barrier_offset(stages, p.epi_stages, p.reuse_ab);
+  const uint32_t full_bar = bar_base;                       // [stages]
+  const uint32_t empty_bar = bar_base + 8u * stages;        // [stages]
+  const uint32_t tfull_bar = bar_base + 16u * stages;       // [2]
+  const uint32_t tempty_bar = tfull_bar + 16u;              // [2]
+  const uint32_t drain_bar = tempty_bar + 16u;              // [1]
+  uint8_t* slot_ptr = base_ptr + (drain_bar + 8u - base);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(slot_ptr);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(slot_ptr + 4);
+
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = ptx::lane_id();
+  const uint32_t rank = (CtaGroup == 2) ? ptx::cluster_ctarank() : 0u;
+  const bool leader = (CtaGroup == 1) || ((rank & 1u) == 0u);
+  const uint32_t leader_rank = rank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);  // both CTAs of the pair
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      ptx::mbar_init(full_bar + 8u * s, 1);
+      ptx::mbar_init(empty_bar + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(tfull_bar + 8u * b, 1);
+      ptx::mbar_init(tempty_bar + 8u * b, kEpiWarps * CtaGroup);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbarrier_init_cluster();
+    ptx::fence_proxy_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_a);
+    ptx::prefetch_tensormap(&tm_b);
+    ptx::prefetch_tensormap(&tm_d);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<CtaGroup>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)), L::kTmemCols);
+    ptx::tmem_relinquish<CtaGroup>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CtaGroup == 2) ptx::cluster_sync();  // peer barriers initialised before use
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  ptx::WaitCtx ctx{abort_flag, p.status, p.timeout_ns};
+  const SchedParams& sp = p.sched;
+  const int k_iters = p.k_iters;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = ptx::policy_evict_normal();
+      const uint64_t pol_b = ptx::policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t fills = 0;
+      bool ok = true;
+      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+        int32_t pid_m, pid_n;
+        work_tile_coords(sp, it.cid, pid_m, pid_n);
+        const int32_t a_row = pid_m * kBM;
+        const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBNc;
+        for (int kb = 0; kb < k_iters; ++kb) {
+          if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kAStageBytes;
+          const uint32_t fb = full_bar + 8u * stage;
+          if constexpr (CtaGroup == 1) {
+            ptx::mbar_arrive_expect_tx(fb, kTxBytes);
+            ptx::tma_load_2d(&tm_a, sa, fb, kb * kBK, a_row, pol_a);
+            ptx::tma_load_2d(&tm_b, sb, fb, kb * kBK, b_row, pol_b);
+          } else {
+            if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
+            const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
+            ptx::tma_load_2d_pair(&tm_a, sa, fb_leader, kb * kBK, a_row, pol_a);
+            ptx::tma_load_2d_pair(&tm_b, sb, fb_leader, kb * kBK, b_row, pol_b);
+          }
+          ++fills;
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: wait (bounded) until every issued fill has landed so no TMA write into this CTA's
+      // shared memory is outstanding when the CTA exits.  Immediate on the normal path.
+      if (leader) {
+        for (int s = 0; s < stages; ++s) {
+          if (fills > static_cast<uint32_t>(s)) {
+            const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
+            ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
+            volatile int32_t no_abort = 0;
+            dctx.abort_flag = &no_abort;
+            ptx::mbar_wait(full_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
+          }
+        }
+      } else {
+        // The peer's loads complete on the leader's barriers; the leader drains them, and the
+        // final cluster barrier keeps this CTA resident until then.  Waiting for the stage to be
+        // released covers loads whose consumer never ran.
+        for (int s = 0; s < stages; ++s) {
+          if (fills > static_cast<uint32_t>(s)) {
+            const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
+            ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
+            volatile int32_t no_abort = 0;
+            dctx.abort_flag = &no_abort;
+            if (*abort_flag == 0)
+              ptx::mbar_wait(empty_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+        if (!ptx::mbar_wait(tempty_bar + 8u * acc, acc_phase ^ 1u, ctx, kSiteMmaTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_iters; ++kb) {
+          if (!ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kAStageBytes;
+          const uint64_t da = ptx::make_sw128_kmajor_desc(sa);
+          const uint64_t db = ptx::make_sw128_kmajor_desc(sb);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // Advance the start address by k * 32 bytes inside the 128-byte swizzled row.
+            ptx::umma_f16_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
+                                       db + static_cast<uint64_t>(2 * k), kIdesc,
+                                       (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          const uint32_t eb = empty_bar + 8u * stage;
+          if constexpr (CtaGroup == 1) {
+            ptx::umma_commit<1>(eb);
+          } else {
+            ptx::umma_commit_pair(eb, pair_mask);
+          }
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t tb = tfull_bar + 8u * acc;
+        if constexpr (CtaGroup == 1) {
+          ptx::umma_commit<1>(tb);
+        } else {
+          ptx::umma_commit_pair(tb, pair_mask);
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: all MMAs issued by this thread complete before TMEM is freed.
+      ptx::umma_commit<CtaGroup>(drain_bar);
+      ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
+      volatile int32_t no_abort = 0;
+      dctx.abort_flag = &no_abort;
+      ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const uint32_t ew = warp - kEpiFirstWarp;  // 0..3
+    const uint32_t quad = warp & 3u;           // TMEM lane quadrant this warp may access
+    const uint32_t row_in_tile = quad * 32u;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int epi_idx = 0;
+    const float alpha = p.alpha;
+    const bool has_bias = p.bias != nullptr;
+    const uint32_t tempty_target =
+        (CtaGroup == 1) ? (tempty_bar) : ptx::mapa_shared(tempty_bar, leader_rank);
+    for (WorkIter it = make_work_iter(sp); it.valid(); it.advance()) {
+      int32_t pid_m, pid_n;
+      work_tile_coords(sp, it.cid, pid_m, pid_n);
+      bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && it.executed < p.trace_stride) {
+        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) *
+                                             (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
+        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + it.executed);
+        t[0] = pid_m;
+        t[1] = pid_n;
+      }
+      __syncwarp();
+      const uint32_t t_row = tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(acc * BN);
+      const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
+#pragma unroll 1
+      for (int c = 0; c < BN / kEpiCols; ++c) {
+        uint32_t v0[32], v1[32];
+        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kEpiCols), v0);
+        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kEpiCols + 32), v1);
+        ptx::tmem_ld_wait();
+        if (c == BN / kEpiCols - 1) {
+          // Accumulator fully read into registers: hand the TMEM buffer back to the MMA warp.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CtaGroup == 1) {
+              ptx::mbar_arrive(tempty_target);
+            } else {
+              ptx::mbar_arrive_cluster(tempty_target);
+            }
+          }
+        }
+        const int32_t col0 = pid_n * BN + c * kEpiCols;
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0 = __uint_as_float(v0[2 * i]) * alpha;
+          float x1 = __uint_as_float(v0[2 * i + 1]) * alpha;
+          float y0 = __uint_as_float(v1[2 * i]) * alpha;
+          float y1 = __uint_as_float(v1[2 * i + 1]) * alpha;
+          if (has_bias) {
+            const int32_t n0 = col0 + 2 * i;
+            const int32_t n1 = col0 + 32 + 2 * i;
+            x0 += (n0 < p.n) ? __bfloat162float(p.bias[n0]) : 0.f;
+            x1 += (n0 + 1 < p.n) ? __bfloat162float(p.bias[n0 + 1]) : 0.f;
+            y0 += (n1 < p.n) ? __bfloat162float(p.bias[n1]) : 0.f;
+            y1 += (n1 + 1 < p.n) ? __bfloat162float(p.bias[n1 + 1]) : 0.f;
+          }
+          packed[i] = ptx::pack_bf16x2(x0, x1);
+          packed[16 + i] = ptx::pack_bf16x2(y0, y1);
+        }
+        const int buf = epi_idx % p.epi_stages;
+        const uint32_t sbuf =
+            epi_base + static_cast<uint32_t>((ew * p.epi_stages + buf) * kEpiBufBytes);
+        if (lane == 0) epi_wait_buffer(p.epi_stages);
+        __syncwarp();
+        const uint32_t row_addr = sbuf + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(j) ^ (lane & 7u);
+          ptx::st_shared_v4(row_addr + (chunk << 4), packed[4 * j], packed[4 * j + 1],
+                            packed[4 * j + 2], packed[4 * j + 3]);
+        }
+        ptx::fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
+          if (g_row < p.m && col0 < p.n) ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+          ptx::bulk_commit_group();
+        }
+        __syncwarp();
+        ++epi_idx;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------------ teardown
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CtaGroup == 2) ptx::cluster_sync();  // peer done with our barriers and TMEM
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<CtaGroup>(tmem_base, L::kTmemCols);
+  }
+#endif
+}
+
+// Small kernels that run the shared device code for host-side verification.
+__global__ void sched_cluster_map_kernel(const SchedParams sp, int32_t* out, int64_t n) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    int32_t cm, cn;
+    sched_map_cluster(sp, static_cast<int32_t>(i), cm, cn);
+    out[2 * i] = cm;
+    out[2 * i + 1] = cn;
+  }
+}
+
+__global__ void fast_divmod_kernel(const FastDivmod f, const int32_t* x, int32_t* q, int32_t* r,
+                                   int64_t n) {
+  int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    int32_t qq, rr;
+    fast_divmod(f, x[i], qq, rr);
+    q[i] = qq;
+    r[i] = rr;
+  }
+}
+
+}  // namespace cpg

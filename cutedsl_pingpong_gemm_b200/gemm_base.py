@@ -1,0 +1,282 @@
+"""The GEMM operator with the interface of the reference's ``gemm_base.GemmSM90``.
+
+Drop-in surface (adelmuursepp/cutedsl_pingpong_gemm, gemm_base.py):
+
+* ``GemmSM90(tile_shape_mn, epi_tile_mn, cluster_shape_mnk, atom_layout_mn, ab_stage=2,
+  epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=True, is_persistent=False,
+  gemm_n_prologue=0)`` -- same arguments, defaults and constructor asserts (gemm_base.py:50-122).
+* ``compile(gemm, a, b, c, stream, options=None)`` -- stands in for ``cute.compile(gemm, a, b, c,
+  stream, options=...)`` (gemm_base.py:608) and returns a callable ``compiled(a, b, c, stream)``
+  (gemm_base.py:609) that writes ``c = a @ b.T`` in place, stream-ordered, without syncing.
+* ``gemm(a, b, c, stream)`` compiles on first use and runs.
+
+``a`` is [M, K], ``b`` is [N, K] and ``c`` is [M, N], all BF16 CUDA tensors with unit stride in
+the last dimension (the reference's harness layout, gemm_base.py:587-590).  Underneath, every call
+goes through the C ABI of ``libcpgemm.so`` into hand-written sm_100a kernels (tcgen05 MMA into
+TMEM, TMA loads/stores, persistent grouped tile scheduler); there is no other execution path.
+
+Argument meaning on sm_100a:
+
+* ``tile_shape_mn``: the CTA tile, (128, N) with N in {64, 128, 256}.
+* ``cluster_shape_mnk``: (1,1,1) runs one CTA per tile; (2,1,1) runs CTA pairs that issue
+  ``tcgen05.mma.cta_group::2`` on a 256-row tile (each CTA loads its own A rows and half of B);
+  (1,2,1) and (2,2,1) group independent CTAs/pairs along N.  Clusters only change the tile order
+  otherwise; no TMA load is multicast.
+* ``ab_stage``: depth of the shared-memory A/B ring; ``epi_stage``: TMA-store staging buffers per
+  epilogue warp; ``reuse_ab``: the epilogue stages through the A/B ring (single-tile CTAs only).
+* ``atom_layout_mn``, ``epi_tile_mn`` and ``gemm_n_prologue`` are validated exactly as in the
+  reference; the tcgen05 kernel issues its MMAs from one thread into TMEM, so they do not change
+  the launch.
+"""
+import ctypes
+import math
+from typing import Optional, Tuple
+
+from . import _lib
+from .tile_scheduler import RasterOrder, SimpleTileScheduler, get_max_active_clusters
+
+THREADS_PER_WG = 128
+THREADS_PER_CTA_SM100 = 192  # TMA warp + MMA warp + 4 epilogue warps
+
+
+def _stream_handle(stream, device) -> int:
+    """cudaStream_t value for None / torch stream / cuda-python CUstream / int."""
+    import torch
+    if stream is None:
+        return torch.cuda.current_stream(device).cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    if isinstance(stream, int):
+        return stream
+    get_ptr = getattr(stream, "getPtr", None)
+    if get_ptr is not None:
+        return int(get_ptr())
+    return int(stream)
+
+
+class CompiledGemm:
+    """Result of ``compile``: ``compiled(a, b, c, stream)`` launches the sm_100a kernel.
+
+    Plans (validated problem + launch shape) are cached per (M, N, K, strides, device), so a
+    compiled GEMM accepts any shape its configuration supports, like the reference's kernel
+    compiled on symbolic shapes.
+    """
+
+    def __init__(self, gemm: "GemmSM90"):
+        self.gemm = gemm
+        self._plans = {}
+
+    def _plan(self, a, b, c):
+        import torch
+        gemm = self.gemm
+        assert a.dtype == b.dtype == c.dtype == torch.bfloat16, \
+            "A, B and D must be BF16 (gemm_base.py:514)"
+        if a.dim() != 2 or b.dim() != 2 or c.dim() != 2:
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE, "A, B and D must be 2-D")
+        m, k = a.shape
+        n, kb = b.shape
+        if kb != k or tuple(c.shape) != (m, n):
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                f"shapes A{tuple(a.shape)} B{tuple(b.shape)} D{tuple(c.shape)} "
+                                f"do not form D = A @ B.T")
+        for name, t in (("A", a), ("B", b), ("D", c)):
+            if t.numel() > 0 and t.stride(1) != 1:
+                raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
+                                    f"{name} must have unit stride in its last dimension")
+            if t.numel() > 0 and not t.is_cuda:
+                raise _lib.CpgError(_lib.CPG_ERR_NO_DEVICE, f"{name} must be a CUDA tensor")
+        def row_stride(t, rows, cols):
+            # A single-row tensor's row stride is never used; give the padded row length.
+            return t.stride(0) if rows > 1 else max(8, (cols + 7) // 8 * 8)
+
+        lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
+        dev = c.device.index if c.is_cuda else torch.cuda.current_device()
+        key = (m, n, k, lda, ldb, ldd, dev)
+        plan = self._plans.get(key)
+        if plan is None:
+            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev)
+            self._plans[key] = plan
+        return plan
+
+    def plan_for(self, a, b, c) -> "_Plan":
+        return self._plan(a, b, c)
+
+    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0):
+        plan = self._plan(a, b, c)
+        plan.run(a, b, c, stream, bias=bias, alpha=alpha)
+        return None
+
+
+class _Plan:
+    """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
+
+    def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device):
+        self.lib = _lib.load()
+        self.m, self.n, self.k = m, n, k
+        self.device = device
+        cfg = gemm._config_c()
+        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, _lib.CPG_DTYPE_BF16, _lib.CPG_DTYPE_BF16)
+        h = ctypes.c_void_p()
+        _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
+                                            ctypes.byref(h)), "compile")
+        self.handle = h
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                self.lib.cpg_gemm_destroy(h)
+            except Exception:
+                pass
+            self.handle = None
+
+    def launch_info(self):
+        grid = (ctypes.c_int32 * 3)()
+        cluster = (ctypes.c_int32 * 3)()
+        threads, smem, mac = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(self.lib.cpg_gemm_launch_info(self.handle, grid, cluster, ctypes.byref(threads),
+                                                 ctypes.byref(smem), ctypes.byref(mac)))
+        return {"grid": tuple(grid), "cluster": tuple(cluster), "threads": threads.value,
+                "smem_bytes": smem.value, "max_active_clusters": mac.value}
+
+    def sched_params(self) -> SimpleTileScheduler.Params:
+        c = _lib.SchedParamsC()
+        _lib.check(self.lib.cpg_gemm_sched_params(self.handle, ctypes.byref(c)))
+        return SimpleTileScheduler.Params.from_c(c)
+
+    def set_trace(self, buf, tiles_per_cta: int) -> None:
+        ptr = None if buf is None else buf.data_ptr()
+        _lib.check(self.lib.cpg_gemm_set_trace(self.handle, ptr, int(tiles_per_cta)), "set_trace")
+
+    def set_timeout_ms(self, ms: int) -> None:
+        _lib.check(self.lib.cpg_gemm_set_timeout_ms(self.handle, int(ms)), "set_timeout_ms")
+
+    def status(self) -> int:
+        s = ctypes.c_int32()
+        rc = self.lib.cpg_gemm_status(self.handle, ctypes.byref(s))
+        if rc not in (_lib.CPG_OK, _lib.CPG_ERR_DEVICE_TIMEOUT):
+            _lib.check(rc, "status")
+        return s.value
+
+    def run(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0) -> None:
+        import torch
+        if bias is not None:
+            if not (bias.dtype == torch.bfloat16 and bias.is_cuda and bias.numel() == self.n
+                    and (bias.dim() == 1 or bias.is_contiguous())):
+                raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                    "bias must be a contiguous BF16 CUDA tensor of length N")
+            if bias.stride(-1) != 1:
+                raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED, "bias must be contiguous")
+        epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr())
+        st = _stream_handle(stream, c.device)
+        rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
+                                   b.data_ptr() if b.numel() else None, c.data_ptr(),
+                                   ctypes.byref(epi), st)
+        _lib.check(rc, "gemm")
+
+
+class GemmSM90:
+    """gemm_base.py:49-566: constructor surface and asserts of the reference, sm_100a kernels."""
+
+    def __init__(
+        self,
+        tile_shape_mn: Tuple[int, int],
+        epi_tile_mn: Tuple[int, int],
+        cluster_shape_mnk: Tuple[int, int, int],
+        atom_layout_mn: Tuple[int, int],
+        ab_stage: int = 2,
+        epi_stage: int = 2,
+        raster_order: RasterOrder = RasterOrder.AlongN,
+        reuse_ab: bool = True,
+        is_persistent: bool = False,
+        gemm_n_prologue: int = 0,
+    ):
+        import torch
+        self.acc_dtype = torch.float32
+        self.raster_order = raster_order
+        self.scheduler_group_size = 8
+        self.cluster_shape_mnk = tuple(cluster_shape_mnk)
+        self.cta_tile_shape_mnk = (*tile_shape_mn, 64)  # K tile: one 128-byte swizzled BF16 row
+        tile_M, tile_N = self.cta_tile_shape_mnk[0], self.cta_tile_shape_mnk[1]
+
+        # Atom layout (gemm_base.py:72-75)
+        assert atom_layout_mn[0] in [1, 2, 3] and atom_layout_mn[1] in [1, 2]
+        assert atom_layout_mn[0] == 1 or tile_M % (atom_layout_mn[0] * 64) == 0
+        assert atom_layout_mn[1] == 1 or tile_N % (atom_layout_mn[1] * 32) == 0
+        self.atom_layout_mnk = (*atom_layout_mn, 1)
+
+        # Multicast fan-out the reference derives (gemm_base.py:77-82); kept for introspection.
+        # The sm_100a kernels never multicast a TMA load.
+        self.mcast_ctas_a = self.cluster_shape_mnk[1]
+        self.mcast_ctas_b = self.cluster_shape_mnk[0]
+        self.is_a_mcast = False
+        self.is_b_mcast = False
+
+        self.occupancy = 1
+        self.mma_warpgroups = math.prod(self.atom_layout_mnk)
+        assert self.mma_warpgroups in [1, 2, 3]
+        self.threads_per_cta = THREADS_PER_CTA_SM100
+
+        self.ab_stage = ab_stage
+        self.epi_stage = epi_stage
+        self.dtype = torch.bfloat16
+        self.buffer_align_bytes = 1024
+
+        self.epi_tile_mn = tuple(epi_tile_mn)
+        self.reuse_ab = reuse_ab
+        assert not (self.atom_layout_mnk[1] > 1) or self.epi_tile_mn[1] == self.cta_tile_shape_mnk[1], \
+            'When atom layout n > 1, we need epi tile n = cta tile n'
+
+        self.is_persistent = is_persistent
+        self._max_active_clusters = None
+        self.gemm_n_prologue = gemm_n_prologue
+
+        assert not (self.reuse_ab and self.is_persistent), "Persistent kernel can't reuse AB for epilogue"
+        self._compiled: Optional[CompiledGemm] = None
+
+    @property
+    def max_active_clusters(self) -> int:
+        """gemm_base.py:117, queried lazily (it needs the GPU)."""
+        if self._max_active_clusters is None:
+            self._max_active_clusters = get_max_active_clusters(math.prod(self.cluster_shape_mnk))
+        return self._max_active_clusters
+
+    def _config_c(self) -> "_lib.GemmConfigC":
+        cm, cn, ck = self.cluster_shape_mnk
+        return _lib.GemmConfigC(
+            self.cta_tile_shape_mnk[0], self.cta_tile_shape_mnk[1],
+            self.epi_tile_mn[0], self.epi_tile_mn[1],
+            cm, cn, ck,
+            self.atom_layout_mnk[0], self.atom_layout_mnk[1],
+            self.ab_stage, self.epi_stage, int(self.raster_order),
+            int(bool(self.reuse_ab)), int(bool(self.is_persistent)), int(self.gemm_n_prologue),
+            int(self.scheduler_group_size))
+
+    def validate(self) -> None:
+        """Run the C ABI's copy of the constructor checks (no GPU needed)."""
+        lib = _lib.load()
+        cfg = self._config_c()
+        _lib.check(lib.cpg_config_validate(ctypes.byref(cfg)), "GemmSM90")
+
+    def compile(self, a, b, c, stream=None) -> CompiledGemm:
+        compiled = CompiledGemm(self)
+        compiled.plan_for(a, b, c)
+        self._compiled = compiled
+        return compiled
+
+    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0):
+        if self._compiled is None:
+            self._compiled = CompiledGemm(self)
+        self._compiled(a, b, c, stream, bias=bias, alpha=alpha)
+
+
+# The B200 name of the same operator.
+GemmSM100 = GemmSM90
+
+
+def compile(gemm: GemmSM90, a, b, c, stream=None, options: Optional[str] = None) -> CompiledGemm:
+    """Stand-in for ``cute.compile(gemm, a, b, c, stream, options=...)`` (gemm_base.py:608).
+
+    ``options`` is accepted for call-site compatibility and ignored (there is no JIT).
+    """
+    return gemm.compile(a, b, c, stream)

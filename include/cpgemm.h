@@ -1,0 +1,179 @@
+/*
+ * cpgemm.h -- C ABI of the B200 (sm_100a) GEMM that replaces the reference's CuTe-DSL GemmSM90.
+ *
+ * Reference surface (adelmuursepp/cutedsl_pingpong_gemm) and the entry point that replaces it:
+ *
+ *   GemmSM90.__init__(tile_shape_mn, epi_tile_mn, cluster_shape_mnk, atom_layout_mn, ab_stage,
+ *                     epi_stage, raster_order, reuse_ab, is_persistent, gemm_n_prologue)
+ *       gemm_base.py:50-122                      -> cpg_config_validate
+ *   cute.compile(gemm, a, b, c, stream)          gemm_base.py:608 (traces GemmSM90.__call__,
+ *       gemm_base.py:124-160: layouts, TMA atoms, scheduler params, grid)
+ *                                                -> cpg_gemm_create
+ *   compiled_gemm(a, b, c, stream)               gemm_base.py:609 (kernel launch :151-160)
+ *                                                -> cpg_gemm_run
+ *   FastDivmod.create / div / divmod             fast_math.py:56-81
+ *                                                -> cpg_fast_divmod_create / cpg_fast_divmod_div
+ *   SimpleTileScheduler.Params.create            tile_scheduler.py:50-78
+ *                                                -> cpg_sched_params_create
+ *   SimpleTileScheduler.get_grid_shape           tile_scheduler.py:110-123 -> cpg_sched_grid_shape
+ *   SimpleTileScheduler._map_cta_coords          tile_scheduler.py:125-146
+ *                                                -> cpg_sched_cluster_map (host),
+ *                                                   cpg_sched_cluster_map_device (device)
+ *   get_max_active_clusters(cluster_size)        tile_scheduler.py:20-22 -> cpg_max_active_clusters
+ *
+ * Conventions: every function returns CPG_OK (0) or a negative CPG_ERR_* code; no exception or
+ * abort crosses this boundary.  cpg_strerror() names a code and cpg_last_error_message() gives
+ * the detail of the calling thread's last failure.  The caller owns A, B, D (device memory);
+ * cpg_gemm_run is stream-ordered and asynchronous, writes D in place and returns without
+ * synchronising, like the reference's compiled kernel call.  Matrices are row-major with
+ * explicit row strides in elements: A [M,K] (K contiguous), B [N,K] (K contiguous), D [M,N]
+ * (N contiguous), i.e. D = A . B^T as in gemm_base.py:587-590.
+ */
+#ifndef CPGEMM_H_
+#define CPGEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CPG_OK 0
+#define CPG_ERR_INVALID_CONFIG (-1)  /* a constructor assert of gemm_base.py:72-74, :87, :113, :122 */
+#define CPG_ERR_INVALID_SHAPE (-2)   /* negative/oversized extents, strides below the extent */
+#define CPG_ERR_ALIGNMENT (-3)       /* TMA needs 16-byte aligned bases and row strides */
+#define CPG_ERR_DTYPE (-4)           /* element types other than the supported ones */
+#define CPG_ERR_UNSUPPORTED (-5)     /* a valid reference config this build does not implement */
+#define CPG_ERR_NO_DEVICE (-6)       /* no sm_100 device, or the device cannot run the kernel */
+#define CPG_ERR_CUDA (-7)            /* a CUDA runtime/driver call failed */
+#define CPG_ERR_DEVICE_TIMEOUT (-8)  /* a kernel wait ran past its deadline (see status) */
+#define CPG_ERR_SMEM (-9)            /* the requested stages do not fit in shared memory */
+#define CPG_ERR_NULL (-10)           /* a required pointer argument is NULL */
+
+/* Element types. */
+#define CPG_DTYPE_BF16 0
+#define CPG_DTYPE_E4M3 1
+#define CPG_DTYPE_F32 2
+
+/* Raster order of the tile scheduler (tile_scheduler.py:24-27). */
+#define CPG_RASTER_ALONG_M 0
+#define CPG_RASTER_ALONG_N 1
+
+typedef struct cpg_fast_divmod {
+  int32_t divisor;
+  uint32_t multiplier;
+  uint32_t shift_right;
+} cpg_fast_divmod;
+
+/* SimpleTileScheduler.Params (tile_scheduler.py:38-48). */
+typedef struct cpg_sched_params {
+  int32_t ncluster_m, ncluster_n, ncluster_l;
+  int32_t raster_order;
+  cpg_fast_divmod dm_clusters_per_problem;
+  int32_t num_groups_regular;
+  cpg_fast_divmod dm_group_size;
+  cpg_fast_divmod dm_group_size_tail;
+  cpg_fast_divmod dm_num_clusters_in_group;
+  int32_t cluster_m, cluster_n;
+  int32_t is_persistent;
+} cpg_sched_params;
+
+/* GemmSM90 constructor arguments (gemm_base.py:50-62) plus the scheduler group size, which the
+ * reference fixes at 8 (gemm_base.py:65). */
+typedef struct cpg_gemm_config {
+  int32_t tile_m, tile_n;
+  int32_t epi_tile_m, epi_tile_n;
+  int32_t cluster_m, cluster_n, cluster_k;
+  int32_t atom_m, atom_n;
+  int32_t ab_stage, epi_stage;
+  int32_t raster_order;
+  int32_t reuse_ab, is_persistent, gemm_n_prologue;
+  int32_t group_size;
+} cpg_gemm_config;
+
+/* Problem description fixed at create time (the reference fixes dtypes and layouts at compile
+ * time and takes M, N, K symbolically; here they are fixed per plan). */
+typedef struct cpg_gemm_problem {
+  int64_t m, n, k;
+  int64_t lda, ldb, ldd; /* row strides in elements */
+  int32_t dtype_ab;      /* CPG_DTYPE_BF16 */
+  int32_t dtype_d;       /* CPG_DTYPE_BF16 */
+} cpg_gemm_problem;
+
+/* Per-call epilogue options.  alpha scales the fp32 accumulator; bias (optional, BF16, length N)
+ * is added per column before rounding to BF16.  The reference has neither (D = A . B^T,
+ * gemm_base.py:133); alpha = 1 and bias = NULL give exactly that. */
+typedef struct cpg_epilogue {
+  float alpha;
+  const void* bias;
+} cpg_epilogue;
+
+typedef struct cpg_gemm cpg_gemm; /* opaque compiled GEMM */
+
+/* Reference constructor asserts (gemm_base.py:72-74, :87, :113, :122; tile_scheduler.py:51). */
+int cpg_config_validate(const cpg_gemm_config* cfg);
+
+/* Validate config + problem for this device, pick the kernel, compute scheduler params and the
+ * launch grid (replaces cute.compile of GemmSM90.__call__, gemm_base.py:124-160, :608). */
+int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
+                    cpg_gemm** out);
+
+/* Launch D = alpha * A . B^T (+ bias) on `stream` (a cudaStream_t, NULL = legacy default
+ * stream).  Replaces compiled_gemm(a, b, c, stream) (gemm_base.py:609).  epi may be NULL. */
+int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                 void* stream);
+
+int cpg_gemm_destroy(cpg_gemm* g);
+
+/* Launch shape chosen at create time: grid and cluster dims, threads per CTA, dynamic shared
+ * memory bytes and the max active clusters the occupancy query returned. */
+int cpg_gemm_launch_info(const cpg_gemm* g, int32_t grid[3], int32_t cluster[3],
+                         int32_t* threads, int32_t* smem_bytes, int32_t* max_active_clusters);
+
+/* Scheduler parameters of this plan. */
+int cpg_gemm_sched_params(const cpg_gemm* g, cpg_sched_params* out);
+
+/* Optional device tile trace: when set, the kernel writes (pid_m, pid_n) of the k-th tile of
+ * CTA c (c = x + gx * (y + gy * z)) to buf[2 * (c * tiles_per_cta + k)].  NULL disables it. */
+int cpg_gemm_set_trace(cpg_gemm* g, int32_t* device_buf, int32_t tiles_per_cta);
+
+/* Per-wait deadline of the kernel in milliseconds (default 10000). */
+int cpg_gemm_set_timeout_ms(cpg_gemm* g, int32_t timeout_ms);
+
+/* Read and clear the plan's device status word (synchronises the device).  *status receives 0 or
+ * 0x100 | wait-site; the return value is CPG_ERR_DEVICE_TIMEOUT when it was nonzero. */
+int cpg_gemm_status(cpg_gemm* g, int32_t* status);
+
+/* FastDivmod (fast_math.py:56-81), host side. */
+int cpg_fast_divmod_create(int32_t divisor, cpg_fast_divmod* out);
+int cpg_fast_divmod_divmod(const cpg_fast_divmod* f, int32_t x, int32_t* q, int32_t* r);
+
+/* FastDivmod on the device, the kernels' own code: q[i], r[i] = divmod(x[i]) for n device values. */
+int cpg_fast_divmod_device(const cpg_fast_divmod* f, const int32_t* x, int32_t* q, int32_t* r,
+                           int64_t n, void* stream);
+
+/* Scheduler (tile_scheduler.py:50-146), host side. */
+int cpg_sched_params_create(int32_t ntiles_m, int32_t ntiles_n, int32_t ntiles_l,
+                            int32_t raster_order, int32_t group_size, int32_t cluster_m,
+                            int32_t cluster_n, int32_t cluster_k, int32_t is_persistent,
+                            cpg_sched_params* out);
+int cpg_sched_grid_shape(const cpg_sched_params* p, int32_t max_active_clusters, int32_t grid[3]);
+/* out[2*i], out[2*i+1] = cluster (m, n) of linear cluster id i, for i < n. */
+int cpg_sched_cluster_map(const cpg_sched_params* p, int32_t* out, int64_t n);
+int cpg_sched_cluster_map_device(const cpg_sched_params* p, int32_t* device_out, int64_t n,
+                                 void* stream);
+
+/* Clusters of `cluster_size` CTAs of the default GEMM kernel that fit on the current device at
+ * once (tile_scheduler.py:20-22). */
+int cpg_max_active_clusters(int32_t cluster_size, int32_t* out);
+
+const char* cpg_strerror(int code);
+const char* cpg_last_error_message(void);
+/* ABI version, bumped on any incompatible change of this header. */
+int cpg_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CPGEMM_H_ */

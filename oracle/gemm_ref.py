@@ -1,0 +1,112 @@
+"""fp32 CPU reference for D = A @ B.T and the tolerance checks -- TEST ORACLE ONLY.
+
+Spec followed: the reference harness computes ``ref = a @ b.t()`` on BF16 inputs and compares the
+kernel's BF16 ``c`` with it (gemm_base.py:587-590, :611).  The reference kernel accumulates in fp32
+(``acc_dtype = Float32``, gemm_base.py:63) and converts to BF16 in the epilogue (:336-338).  Here the
+product is evaluated in fp32 (or fp64 for checksums) on the CPU from the same BF16-rounded inputs.
+
+Tolerances (project spec, stated in the tests that use them):
+
+* relative Frobenius error ``||D - R||_F / ||R||_F <= 1e-2`` for BF16 outputs;
+* element-wise ``|D - R| <= 2^-8 |R| + K * 2^-23 * (|A| @ |B|.T)``: BF16 output rounding (half an
+  ulp is at most 2^-8 relative) plus the worst-case fp32 summation error of a K-term dot product
+  for both the kernel and this reference (each at most (K-1) * 2^-24 * sum|a||b|).
+"""
+import os
+
+import torch
+
+BF16_REL = 2.0 ** -8
+ACC_SLACK_PER_K = 2.0 ** -23
+FROB_TOL_BF16 = 1e-2
+FROB_TOL_FP8 = 3e-2
+
+
+def set_threads():
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+def make_inputs(m, n, k, seed=0, a_scale=1.0, b_scale=1.0, with_bias=False, bias_scale=1.0):
+    """Seeded BF16 inputs: torch.Generator().manual_seed(seed) on the CPU, N(0,1) times a scale."""
+    g = torch.Generator().manual_seed(seed)
+    a = (torch.randn(m, k, generator=g) * a_scale).to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=g) * b_scale).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * bias_scale).to(torch.bfloat16) if with_bias else None
+    return a, b, bias
+
+
+def reference(a, b, bias=None, alpha=1.0, rows=None):
+    """fp32 R = alpha * A @ B.T (+ bias) on the CPU; ``rows`` restricts to a subset of rows."""
+    a32 = a.float() if rows is None else a[rows].float()
+    r = torch.matmul(a32, b.float().t())
+    if alpha != 1.0:
+        r = r * alpha
+    if bias is not None:
+        r = r + bias.float()
+    return r
+
+
+def abs_product(a, b, rows=None):
+    a32 = a.float().abs() if rows is None else a[rows].float().abs()
+    return torch.matmul(a32, b.float().abs().t())
+
+
+def elementwise_bound(r, s, k, alpha=1.0, bias=None):
+    tol = BF16_REL * r.abs() + abs(alpha) * k * ACC_SLACK_PER_K * s
+    if bias is not None:
+        tol = tol + 2.0 ** -24 * bias.float().abs()
+    return tol
+
+
+def rel_frobenius(d, r):
+    d64 = d.double()
+    r64 = r.double()
+    den = torch.linalg.vector_norm(r64)
+    num = torch.linalg.vector_norm(d64 - r64)
+    return float(num / den) if float(den) > 0 else float(num)
+
+
+def check(d, a, b, bias=None, alpha=1.0, rows=None, frob_tol=FROB_TOL_BF16):
+    """Compare GPU output ``d`` (CPU tensor, full or the selected rows) with the fp32 oracle.
+
+    Returns a dict with the error figures; ``ok`` is True when both bounds hold.
+    """
+    k = a.shape[1]
+    r = reference(a, b, bias, alpha, rows)
+    s = abs_product(a, b, rows)
+    dd = d.float() if rows is None or d.shape[0] == r.shape[0] else d[rows].float()
+    if dd.shape != r.shape:
+        raise ValueError(f"shape mismatch {tuple(dd.shape)} vs {tuple(r.shape)}")
+    tol = elementwise_bound(r, s, k, alpha, bias)
+    err = (dd - r).abs()
+    viol = err > tol
+    frob = rel_frobenius(dd, r)
+    n_bad = int(viol.sum())
+    worst = float((err / tol.clamp_min(1e-30)).max()) if err.numel() else 0.0
+    return {"ok": n_bad == 0 and frob <= frob_tol, "n_bad": n_bad, "frob": frob,
+            "worst_ratio": worst, "max_abs_err": float(err.max()) if err.numel() else 0.0}
+
+
+def column_checksum(a, b, bias=None, alpha=1.0):
+    """fp64 sum over rows of R: (1^T A) B^T (+ M * bias).  Cost O(MK + NK)."""
+    colsum_a = a.double().sum(0)
+    r = alpha * torch.matmul(b.double(), colsum_a)
+    if bias is not None:
+        r = r + a.shape[0] * bias.double()
+    return r
+
+
+def row_checksum(a, b, bias=None, alpha=1.0):
+    """fp64 sum over columns of R: A (B^T 1) (+ sum(bias))."""
+    rowsum_b = b.double().sum(0)
+    r = alpha * torch.matmul(a.double(), rowsum_b)
+    if bias is not None:
+        r = r + bias.double().sum()
+    return r
+
+
+def checksum_bound(d_abs_sum, abs_sum_product, k, count):
+    """Bound for a checksum of ``count`` BF16 outputs: rounding of each output plus accumulation."""
+    return BF16_REL * d_abs_sum + k * ACC_SLACK_PER_K * abs_sum_product + 1e-6 * count

@@ -1,0 +1,109 @@
+"""C ABI library checks that need no GPU: it loads, exports every symbol of include/cpgemm.h,
+and its host-side scheduler / FastDivmod code (the same headers the kernels compile) matches the
+golden vectors taken from the reference."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from cutedsl_pingpong_gemm_b200 import _lib
+from cutedsl_pingpong_gemm_b200.fast_math import FastDivmod
+from cutedsl_pingpong_gemm_b200.tile_scheduler import (RasterOrder, SimpleTileScheduler,
+                                                        SimpleTileSchedulerArguments)
+
+
+def declared_functions():
+    with open(os.path.join(ROOT, "include", "cpgemm.h")) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cpg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+    # The ctypes binding covers exactly the declared functions.
+    assert sorted(_lib.SIGNATURES) == names
+
+
+def test_abi_version_and_strerror(lib):
+    assert lib.cpg_abi_version() == _lib.ABI_VERSION
+    for code in range(-10, 1):
+        assert lib.cpg_strerror(code)
+    assert lib.cpg_strerror(-999) == b"unknown error"
+
+
+def test_fastdivmod_host_matches_reference(lib, golden_fdm):
+    for case in golden_fdm:
+        f = FastDivmod.create(case["divisor"])
+        assert (f.multiplier, f.shift_right) == (case["multiplier"], case["shift_right"])
+        for x, q, r in list(zip(case["dividends"], case["quotients"], case["remainders"]))[:12]:
+            assert f.divmod(x) == (q, r)
+
+
+def test_fastdivmod_rejects_bad_divisor(lib):
+    with pytest.raises(_lib.CpgError) as e:
+        FastDivmod.create(0)
+    assert e.value.code == _lib.CPG_ERR_INVALID_SHAPE
+
+
+def _params(cfg, persistent=True):
+    args = SimpleTileSchedulerArguments((cfg["ntiles_m"], cfg["ntiles_n"], 1),
+                                        RasterOrder(cfg["raster_order"]), cfg["group_size_arg"],
+                                        (cfg["cluster_m"], cfg["cluster_n"], 1), persistent)
+    return SimpleTileScheduler.to_underlying_arguments(args)
+
+
+def test_host_scheduler_matches_reference(lib, golden_maps):
+    index, maps = golden_maps
+    for cfg in index["configs"]:
+        p = _params(cfg)
+        g = cfg["params"]
+        assert p.num_groups_regular == g["num_groups_regular"]
+        assert p.dm_group_size.divisor == g["group_size"]
+        assert p.dm_group_size_tail.divisor == g["group_size_tail_divisor"]
+        assert p.dm_num_clusters_in_group.divisor == g["num_clusters_in_group"]
+        assert list(p.ncluster_mnl) == g["ncluster_mnl"]
+        ours = SimpleTileScheduler.cluster_map(p)
+        assert np.array_equal(ours, maps[cfg["key"]]), cfg["key"]
+        for mac, grid in cfg["grid_persistent"].items():
+            assert list(SimpleTileScheduler.get_grid_shape(p, int(mac))) == grid
+        pn = _params(cfg, persistent=False)
+        assert list(SimpleTileScheduler.get_grid_shape(pn, 1)) == cfg["grid_nonpersistent"]
+
+
+def test_host_schedule_matches_oracle_schedule(lib):
+    from oracle import tile_scheduler_ref as ts
+    for persistent in (True, False):
+        for cluster in ((1, 1, 1), (2, 1, 1), (2, 2, 1)):
+            args = SimpleTileSchedulerArguments((9, 17, 1), RasterOrder.AlongN, 8, cluster, persistent)
+            p = SimpleTileScheduler.to_underlying_arguments(args)
+            grid = SimpleTileScheduler.get_grid_shape(p, 5)
+            ours = SimpleTileScheduler.schedule(p, grid)
+            po = ts.params_create((9, 17, 1), ts.ALONG_N, 8, cluster, persistent)
+            assert ours == ts.schedule(po, ts.get_grid_shape(po, 5))
+
+
+def test_sched_params_reject_cluster_k(lib):
+    args = SimpleTileSchedulerArguments((4, 4, 1), RasterOrder.AlongN, 8, (1, 1, 2), True)
+    with pytest.raises(_lib.CpgError) as e:
+        SimpleTileScheduler.to_underlying_arguments(args)
+    assert e.value.code == _lib.CPG_ERR_INVALID_CONFIG
+
+
+def test_gemm_create_without_device_fails_cleanly(lib):
+    """On a machine without a GPU the plan call returns an error code instead of crashing."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    cfg = _lib.GemmConfigC(128, 256, 128, 32, 1, 1, 1, 2, 1, 4, 2, 1, 0, 1, 0, 8)
+    prob = _lib.GemmProblemC(256, 256, 256, 256, 256, 256, 0, 0)
+    h = ctypes.c_void_p()
+    rc = lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), 0, ctypes.byref(h))
+    assert rc in (_lib.CPG_ERR_NO_DEVICE, _lib.CPG_ERR_CUDA)
+    assert not h.value

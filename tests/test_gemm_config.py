@@ -1,0 +1,84 @@
+"""Constructor surface of GemmSM90: same arguments, defaults and asserts as gemm_base.py:50-122,
+and the C ABI's copy of the same checks (cpg_config_validate)."""
+import inspect
+
+import pytest
+
+from cutedsl_pingpong_gemm_b200 import GemmSM90, GemmSM100, RasterOrder, _lib
+
+
+def test_signature_matches_reference():
+    sig = inspect.signature(GemmSM90.__init__)
+    names = list(sig.parameters)[1:]
+    assert names == ["tile_shape_mn", "epi_tile_mn", "cluster_shape_mnk", "atom_layout_mn",
+                     "ab_stage", "epi_stage", "raster_order", "reuse_ab", "is_persistent",
+                     "gemm_n_prologue"]
+    d = {k: v.default for k, v in sig.parameters.items()}
+    assert d["ab_stage"] == 2 and d["epi_stage"] == 2
+    assert d["raster_order"] == RasterOrder.AlongN
+    assert d["reuse_ab"] is True and d["is_persistent"] is False and d["gemm_n_prologue"] == 0
+    assert GemmSM100 is GemmSM90
+
+
+def test_harness_config_attributes():
+    # The reference harness configuration (gemm_base.py:598-604).
+    g = GemmSM90(tile_shape_mn=(128, 256), epi_tile_mn=(128, 32), cluster_shape_mnk=(2, 1, 1),
+                 atom_layout_mn=(2, 1), ab_stage=3, reuse_ab=False, is_persistent=True)
+    assert g.cta_tile_shape_mnk == (128, 256, 64)
+    assert g.atom_layout_mnk == (2, 1, 1)
+    assert g.mma_warpgroups == 2
+    assert g.scheduler_group_size == 8
+    assert g.mcast_ctas_a == 1 and g.mcast_ctas_b == 2
+    assert not g.is_a_mcast and not g.is_b_mcast  # no TMA multicast on sm_100a
+    g.validate()
+
+
+BAD = [
+    # (kwargs, message fragment) -- each is an assert of gemm_base.py
+    (dict(atom_layout_mn=(4, 1)), None),                                   # :72
+    (dict(atom_layout_mn=(1, 3)), None),                                   # :72
+    (dict(tile_shape_mn=(192, 256), atom_layout_mn=(2, 1)), None),         # :73 (192 % 128)
+    (dict(tile_shape_mn=(128, 96), atom_layout_mn=(1, 2)), None),          # :74 (96 % 64)
+    (dict(atom_layout_mn=(2, 2)), None),                                   # :87 (4 warpgroups)
+    (dict(atom_layout_mn=(1, 2), epi_tile_mn=(128, 32)), "epi tile n"),    # :113
+    (dict(reuse_ab=True, is_persistent=True), "reuse AB"),                 # :122
+]
+
+
+@pytest.mark.parametrize("kwargs,msg", BAD)
+def test_reference_asserts(kwargs, msg):
+    base = dict(tile_shape_mn=(128, 256), epi_tile_mn=(128, 32), cluster_shape_mnk=(1, 1, 1),
+                atom_layout_mn=(1, 1), reuse_ab=False, is_persistent=False)
+    base.update(kwargs)
+    with pytest.raises(AssertionError) as e:
+        GemmSM90(**base)
+    if msg:
+        assert msg in str(e.value)
+
+
+@pytest.mark.parametrize("kwargs", [k for k, _ in BAD])
+def test_capi_validate_matches_python_asserts(lib, kwargs):
+    base = dict(tile_m=128, tile_n=256, epi_tile_m=128, epi_tile_n=32, cluster_m=1, cluster_n=1,
+                cluster_k=1, atom_m=1, atom_n=1, ab_stage=4, epi_stage=2, raster_order=1,
+                reuse_ab=0, is_persistent=0, gemm_n_prologue=0, group_size=8)
+    if "atom_layout_mn" in kwargs:
+        base["atom_m"], base["atom_n"] = kwargs["atom_layout_mn"]
+    if "tile_shape_mn" in kwargs:
+        base["tile_m"], base["tile_n"] = kwargs["tile_shape_mn"]
+    if "epi_tile_mn" in kwargs:
+        base["epi_tile_m"], base["epi_tile_n"] = kwargs["epi_tile_mn"]
+    if "reuse_ab" in kwargs:
+        base["reuse_ab"] = int(kwargs["reuse_ab"])
+    if "is_persistent" in kwargs:
+        base["is_persistent"] = int(kwargs["is_persistent"])
+    import ctypes
+    cfg = _lib.GemmConfigC(**base)
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_ERR_INVALID_CONFIG
+
+
+def test_capi_validate_accepts_harness_config(lib):
+    import ctypes
+    cfg = _lib.GemmConfigC(128, 256, 128, 32, 2, 1, 1, 2, 1, 3, 2, 1, 0, 1, 0, 8)
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_OK
+    cfg.cluster_k = 2  # tile_scheduler.py:51
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_ERR_INVALID_CONFIG
