@@ -26,7 +26,7 @@ CPG_DTYPE_BF16 = 0
 CPG_DTYPE_E4M3 = 1
 CPG_DTYPE_F32 = 2
 
-ABI_VERSION = 1
+ABI_VERSION = 3
 
 
 class CpgError(RuntimeError):
@@ -79,7 +79,8 @@ class GemmProblemC(ctypes.Structure):
 
 
 class EpilogueC(ctypes.Structure):
-    _fields_ = [("alpha", ctypes.c_float), ("bias", ctypes.c_void_p)]
+    _fields_ = [("alpha", ctypes.c_float), ("bias", ctypes.c_void_p),
+                ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p)]
 
 
 _P = ctypes.POINTER
@@ -107,6 +108,9 @@ SIGNATURES = {
     "cpg_sched_cluster_map": (ctypes.c_int, [_P(SchedParamsC), _P(_i32), _i64]),
     "cpg_sched_cluster_map_device": (ctypes.c_int, [_P(SchedParamsC), _vp, _i64, _vp]),
     "cpg_max_active_clusters": (ctypes.c_int, [_i32, _P(_i32)]),
+    "cpg_quantize_e4m3": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i32, _i32,
+                                         _vp]),
+    "cpg_cast_f32_bf16": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "cpg_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "cpg_last_error_message": (ctypes.c_char_p, []),
     "cpg_abi_version": (ctypes.c_int, []),

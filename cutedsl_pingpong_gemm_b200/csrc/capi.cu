@@ -13,6 +13,7 @@
 
 #include "cpgemm.h"
 #include "gemm_kernel.cuh"
+#include "quant_kernels.cuh"
 
 namespace {
 
@@ -90,6 +91,8 @@ using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMa
 struct Variant {
   int bn;
   int cta_group;
+  int dtype_ab;
+  int dtype_d;
   KernelFn fn;
   int (*smem_bytes)(int, int, int);
 };
@@ -99,18 +102,44 @@ int smem_bytes_of(int stages, int epi_stages, int reuse_ab) {
   return cpg::GemmSmem<BN, CG>::bytes(stages, epi_stages, reuse_ab);
 }
 
-template <int BN, int CG>
+template <typename T>
+constexpr int dtype_code();
+template <>
+constexpr int dtype_code<__nv_bfloat16>() { return CPG_DTYPE_BF16; }
+template <>
+constexpr int dtype_code<cpg::e4m3_t>() { return CPG_DTYPE_E4M3; }
+template <>
+constexpr int dtype_code<float>() { return CPG_DTYPE_F32; }
+
+template <int BN, int CG, typename AB, typename OutT>
 Variant make_variant() {
-  return Variant{BN, CG, &cpg::gemm_bf16_sm100_kernel<BN, CG>, &smem_bytes_of<BN, CG>};
+  return Variant{BN, CG, dtype_code<AB>(), dtype_code<OutT>(),
+                 &cpg::gemm_sm100_kernel<BN, CG, AB, OutT>, &smem_bytes_of<BN, CG>};
 }
 
-bool find_variant(int bn, int cta_group, Variant* out) {
-  static const Variant table[] = {
-      make_variant<256, 1>(), make_variant<128, 1>(), make_variant<64, 1>(),
-      make_variant<256, 2>(), make_variant<128, 2>(), make_variant<64, 2>(),
-  };
-  for (const Variant& v : table) {
-    if (v.bn == bn && v.cta_group == cta_group) {
+template <typename AB, typename OutT>
+void add_variants(Variant* t, int& n) {
+  t[n++] = make_variant<256, 1, AB, OutT>();
+  t[n++] = make_variant<128, 1, AB, OutT>();
+  t[n++] = make_variant<64, 1, AB, OutT>();
+  t[n++] = make_variant<256, 2, AB, OutT>();
+  t[n++] = make_variant<128, 2, AB, OutT>();
+  t[n++] = make_variant<64, 2, AB, OutT>();
+}
+
+bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, Variant* out) {
+  static Variant table[24];
+  static int count = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    add_variants<__nv_bfloat16, __nv_bfloat16>(table, count);
+    add_variants<__nv_bfloat16, float>(table, count);
+    add_variants<cpg::e4m3_t, __nv_bfloat16>(table, count);
+    add_variants<cpg::e4m3_t, float>(table, count);
+  });
+  for (int i = 0; i < count; ++i) {
+    const Variant& v = table[i];
+    if (v.bn == bn && v.cta_group == cta_group && v.dtype_ab == dtype_ab && v.dtype_d == dtype_d) {
       *out = v;
       return true;
     }
@@ -118,13 +147,25 @@ bool find_variant(int bn, int cta_group, Variant* out) {
   return false;
 }
 
-__global__ void fill_rows_kernel(__nv_bfloat16* d, int64_t m, int64_t n, int64_t ldd,
+int elem_bytes(int dtype) { return dtype == CPG_DTYPE_E4M3 ? 1 : (dtype == CPG_DTYPE_F32 ? 4 : 2); }
+
+CUtensorMapDataType tma_dtype(int dtype) {
+  switch (dtype) {
+    case CPG_DTYPE_E4M3: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    case CPG_DTYPE_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    default: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  }
+}
+
+template <typename OutT>
+__global__ void fill_rows_kernel(OutT* d, int64_t m, int64_t n, int64_t ldd,
                                  const __nv_bfloat16* bias) {
   int64_t total = m * n;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int64_t r = i / n, c = i % n;
-    d[r * ldd + c] = bias != nullptr ? bias[c] : __float2bfloat16(0.f);
+    float v = bias != nullptr ? __bfloat162float(bias[c]) : 0.f;
+    d[r * ldd + c] = static_cast<OutT>(v);
   }
 }
 
@@ -186,7 +227,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 1; }
+int cpg_abi_version(void) { return 3; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -266,15 +307,20 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return fail(CPG_ERR_INVALID_CONFIG, "gemm_n_prologue must be below ab_stage");
 
   // Problem checks.
-  if (prob->dtype_ab != CPG_DTYPE_BF16 || prob->dtype_d != CPG_DTYPE_BF16)
-    return fail(CPG_ERR_DTYPE, "A, B and D must be BF16 (gemm_base.py:514)");
+  if (prob->dtype_ab != CPG_DTYPE_BF16 && prob->dtype_ab != CPG_DTYPE_E4M3)
+    return fail(CPG_ERR_DTYPE, "A and B must be BF16 or FP8 E4M3");
+  if (prob->dtype_d != CPG_DTYPE_BF16 && prob->dtype_d != CPG_DTYPE_F32)
+    return fail(CPG_ERR_DTYPE, "D must be BF16 or FP32");
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (prob->m < 0 || prob->n < 0 || prob->k < 0 || prob->m > lim || prob->n > lim || prob->k > lim)
     return fail(CPG_ERR_INVALID_SHAPE, "M, N, K must be in [0, 2^31)");
   if (prob->lda < prob->k || prob->ldb < prob->k || prob->ldd < prob->n)
     return fail(CPG_ERR_INVALID_SHAPE, "row strides must be at least the row length");
-  if (prob->lda % 8 != 0 || prob->ldb % 8 != 0 || prob->ldd % 8 != 0)
-    return fail(CPG_ERR_ALIGNMENT, "row strides must be multiples of 8 elements (16 bytes)");
+  {
+    const int eab = elem_bytes(prob->dtype_ab), ed = elem_bytes(prob->dtype_d);
+    if ((prob->lda * eab) % 16 != 0 || (prob->ldb * eab) % 16 != 0 || (prob->ldd * ed) % 16 != 0)
+      return fail(CPG_ERR_ALIGNMENT, "row strides must be multiples of 16 bytes");
+  }
 
   DeviceGuard guard(device);
   if (!guard.ok) return fail(CPG_ERR_NO_DEVICE, "cannot select device %d", device);
@@ -287,9 +333,9 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
 
   Variant v;
   const int cta_group = cfg->cluster_m == 2 ? 2 : 1;
-  if (!find_variant(cfg->tile_n, cta_group, &v))
-    return fail(CPG_ERR_UNSUPPORTED, "no kernel for tile_n %d, cta_group %d", cfg->tile_n,
-                cta_group);
+  if (!find_variant(cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d, &v))
+    return fail(CPG_ERR_UNSUPPORTED, "no kernel for tile_n %d, cta_group %d, dtypes %d/%d",
+                cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -423,8 +469,14 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     // D = bias (or 0): nothing to contract.
     int blocks = static_cast<int>((pr.m * pr.n + 255) / 256);
     if (blocks > 4096) blocks = 4096;
-    fill_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<__nv_bfloat16*>(d), pr.m, pr.n, pr.ldd,
-                                             static_cast<const __nv_bfloat16*>(bias));
+    if (pr.dtype_d == CPG_DTYPE_F32) {
+      fill_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<float*>(d), pr.m, pr.n, pr.ldd,
+                                                      static_cast<const __nv_bfloat16*>(bias));
+    } else {
+      fill_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+          static_cast<__nv_bfloat16*>(d), pr.m, pr.n, pr.ldd,
+          static_cast<const __nv_bfloat16*>(bias));
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CPG_OK : cuda_fail(e, "fill kernel launch");
   }
@@ -432,15 +484,16 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   if ((reinterpret_cast<uintptr_t>(a) & 15u) != 0 || (reinterpret_cast<uintptr_t>(b) & 15u) != 0)
     return fail(CPG_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
 
+  const int eab = elem_bytes(pr.dtype_ab), ed = elem_bytes(pr.dtype_d);
+  const int bk = cpg::kRowBytes / eab;         // k-block: one 128-byte row of A / B
+  const int store_cols = cpg::kRowBytes / ed;  // epilogue box: one 128-byte row of D
   if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
-    int rc = encode_2d(&g->tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, pr.m, pr.k, pr.lda,
-                       cpg::kBM, cpg::kBK);
+    int rc = encode_2d(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM, bk);
     if (rc != CPG_OK) return rc;
-    rc = encode_2d(&g->tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, pr.n, pr.k, pr.ldb,
-                   g->v.bn / g->v.cta_group, cpg::kBK);
+    rc = encode_2d(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
+                   g->v.bn / g->v.cta_group, bk);
     if (rc != CPG_OK) return rc;
-    rc = encode_2d(&g->tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, pr.m, pr.n, pr.ldd, 32,
-                   cpg::kEpiCols);
+    rc = encode_2d(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols);
     if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
@@ -454,11 +507,13 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.m = static_cast<int32_t>(pr.m);
   p.n = static_cast<int32_t>(pr.n);
   p.k = static_cast<int32_t>(pr.k);
-  p.k_iters = static_cast<int32_t>((pr.k + cpg::kBK - 1) / cpg::kBK);
+  p.k_iters = static_cast<int32_t>((pr.k + bk - 1) / bk);
   p.ab_stages = g->cfg.ab_stage;
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
   p.alpha = alpha;
+  p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
+  p.scale_b = epi != nullptr ? epi->scale_b : nullptr;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.tile_trace = g->trace;
   p.trace_stride = g->trace_stride;
@@ -575,7 +630,7 @@ int cpg_max_active_clusters(int32_t cluster_size, int32_t* out) {
     return fail(CPG_ERR_UNSUPPORTED, "cluster size must be 1..4, got %d", cluster_size);
   Variant v;
   const int cg = (cluster_size % 2 == 0) ? 2 : 1;
-  find_variant(256, cg, &v);
+  find_variant(256, cg, CPG_DTYPE_BF16, CPG_DTYPE_BF16, &v);
   const int smem = v.smem_bytes(4, 2, 0);
   int cm = cluster_size >= 2 ? 2 : 1;
   int cn = cluster_size == 4 ? 2 : (cluster_size == 3 ? 3 : 1);
@@ -585,6 +640,76 @@ int cpg_max_active_clusters(int32_t cluster_size, int32_t* out) {
   if (rc != CPG_OK) return rc;
   *out = n;
   return CPG_OK;
+}
+
+int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols, int64_t ldx,
+                      void* q, int64_t ldq, float* scales, int32_t block_rows, int32_t block_cols,
+                      void* stream) {
+  if (rows < 0 || cols < 0 || ldx < cols || ldq < cols)
+    return fail(CPG_ERR_INVALID_SHAPE, "bad quantisation extents");
+  if (dtype_x != CPG_DTYPE_BF16 && dtype_x != CPG_DTYPE_F32)
+    return fail(CPG_ERR_DTYPE, "x must be BF16 or FP32");
+  if (scales == nullptr) return fail(CPG_ERR_NULL, "scales is NULL");
+  const bool per_tensor = block_rows == 0 && block_cols == 0;
+  const bool row_block = block_rows == 1 && block_cols == 128;
+  const bool tile_block = block_rows == 128 && block_cols == 128;
+  if (!per_tensor && !row_block && !tile_block)
+    return fail(CPG_ERR_UNSUPPORTED, "blocks must be (0,0) per tensor, (1,128) or (128,128)");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (per_tensor) {
+    cudaError_t e = cudaMemsetAsync(scales, 0, sizeof(float), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scale)");
+  }
+  if (rows == 0 || cols == 0) {
+    if (per_tensor) cpg::finalize_scale_kernel<<<1, 1, 0, st>>>(reinterpret_cast<unsigned*>(scales));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CPG_OK : cuda_fail(e, "quantize launch");
+  }
+  if (x == nullptr || q == nullptr) return fail(CPG_ERR_NULL, "x and q must be non-NULL");
+  uint8_t* qq = static_cast<uint8_t*>(q);
+  const int threads = 256;
+  const unsigned row_blocks = static_cast<unsigned>(rows < 65535 ? rows : 65535);
+  auto launch = [&](auto tag) {
+    using T = decltype(tag);
+    const T* xx = static_cast<const T*>(x);
+    if (per_tensor) {
+      unsigned* amax = reinterpret_cast<unsigned*>(scales);
+      cpg::amax_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, amax);
+      cpg::quant_per_tensor_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, qq,
+                                                                       ldq, amax);
+      cpg::finalize_scale_kernel<<<1, 1, 0, st>>>(amax);
+    } else if (row_block) {
+      const int64_t warps = rows * ((cols + 127) / 128);
+      const int64_t blocks = (warps * 32 + threads - 1) / threads;
+      cpg::quant_row_block_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+          xx, rows, cols, ldx, qq, ldq, scales);
+    } else {
+      const int64_t blocks = ((rows + 127) / 128) * ((cols + 127) / 128);
+      cpg::quant_tile_block_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+          xx, rows, cols, ldx, qq, ldq, scales);
+    }
+  };
+  if (dtype_x == CPG_DTYPE_BF16) {
+    launch(__nv_bfloat16{});
+  } else {
+    launch(float{});
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "quantize launch");
+}
+
+int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, void* y,
+                      int64_t ldy, const void* bias, void* stream) {
+  if (rows < 0 || cols < 0 || ldx < cols || ldy < cols)
+    return fail(CPG_ERR_INVALID_SHAPE, "bad cast extents");
+  if (rows == 0 || cols == 0) return CPG_OK;
+  if (x == nullptr || y == nullptr) return fail(CPG_ERR_NULL, "x and y must be non-NULL");
+  const unsigned blocks = static_cast<unsigned>(rows < 65535 ? rows : 65535);
+  cpg::cast_f32_bf16_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, rows, cols, ldx, static_cast<__nv_bfloat16*>(y), ldy,
+      static_cast<const __nv_bfloat16*>(bias));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "cast launch");
 }
 
 }  // extern "C"

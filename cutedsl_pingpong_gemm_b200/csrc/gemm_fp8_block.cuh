@@ -1,0 +1,301 @@
+// Block-scaled FP8 E4M3 GEMM for sm_100a:
+//   D[m, n] = alpha * sum_kb sa[kb][m] * sb[n / 128][kb] * (A[m, kb-block] . B[n, kb-block]^T)
+// with 1 x 128 scales for A (one per row and 128-element k-block, stored k-block-major) and
+// 128 x 128 scales for B (one per 128 x 128 block), fp32 scales (amax / 448), BF16 output.
+//
+// The tensor-core block-scaled MMA kinds take power-of-two (UE8M0 / UE4M3) scales on 16/32-wide
+// k-blocks, which cannot represent fp32 scales, so the scaling is applied to fp32 partial sums:
+//   warp 0     TMA producer (shared with the plain kernel), one 128-element k-block per stage.
+//   warp 1     MMA issuer: each k-block's 4 tcgen05.mma kind::f8f6f4 write a fresh partial
+//              product P_kb into one of 4 TMEM partial buffers (128 lanes x 128 fp32 columns),
+//              committed to that buffer's `part_full` barrier.
+//   warps 2-5  promotion + epilogue: each thread owns one row of the tile and keeps its 128
+//              running fp32 sums in registers; per k-block it loads P_kb from TMEM, adds
+//              sa * sb * P_kb, frees the partial buffer, and after the last k-block rounds to
+//              BF16 and TMA-stores the row chunks.
+// Tiles are 128 x 128 per CTA (256 x 128 per CTA pair); tile order, pairs, bounded waits and
+// drains are as in gemm_sm100_kernel.
+#pragma once
+#include "gemm_kernel.cuh"
+
+namespace cpg {
+
+constexpr int kBlockBN = 128;
+constexpr int kNumParts = 4;
+
+template <int CtaGroup>
+struct BlockSmem {
+  static constexpr int kAStageBytes = kBM * kRowBytes;
+  static constexpr int kBStageBytes = (kBlockBN / CtaGroup) * kRowBytes;
+  static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+  static constexpr int kTmemCols = kNumParts * kBlockBN;  // 512
+  static __host__ __device__ int epi_offset(int stages) { return stages * kStageBytes; }
+  static __host__ __device__ int barrier_offset(int stages, int epi_stages) {
+    return epi_offset(stages) + kEpiWarps * epi_stages * kEpiBufBytes;
+  }
+  // full[S], empty[S], part_full[4], part_empty[4], drain[1]; then tmem slot and abort flag.
+  static __host__ __device__ int bytes(int stages, int epi_stages, int /*reuse_ab*/) {
+    int b = barrier_offset(stages, epi_stages) + (2 * stages + 2 * kNumParts + 1) * 8 + 16 + 1024;
+    return b < kMinSmemForOneCtaPerSm ? kMinSmemForOneCtaPerSm : b;
+  }
+};
+
+struct BlockScales {
+  const float* sa;  // [ceil(K/128), M]
+  const float* sb;  // [ceil(N/128), ceil(K/128)]
+};
+
+template <int CtaGroup>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_fp8_block_kernel(const __grid_constant__ CUtensorMap tm_a,
+                          const __grid_constant__ CUtensorMap tm_b,
+                          const __grid_constant__ CUtensorMap tm_d, const GemmParams p,
+                          const BlockScales scales) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using L = BlockSmem<CtaGroup>;
+  constexpr int kBK = OperandTraits<e4m3_t>::kBK;        // 128
+  constexpr int kUmmaK = OperandTraits<e4m3_t>::kUmmaK;  // 32
+  constexpr uint32_t kIdesc = ptx::make_idesc_e4m3_f32(kBM * CtaGroup, kBlockBN);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+
+  const int stages = p.ab_stages;
+  const uint32_t epi_base = base + L::epi_offset(stages);
+  const uint32_t bar_base = base + L::barrier_offset(stages, p.epi_stages);
+  const uint32_t full_bar = bar_base;
+  const uint32_t empty_bar = bar_base + 8u * stages;
+  const uint32_t pfull_bar = bar_base + 16u * stages;       // [kNumParts]
+  const uint32_t pempty_bar = pfull_bar + 8u * kNumParts;   // [kNumParts]
+  const uint32_t drain_bar = pempty_bar + 8u * kNumParts;
+  uint8_t* slot_ptr = base_ptr + (drain_bar + 8u - base);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(slot_ptr);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(slot_ptr + 4);
+
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = ptx::lane_id();
+  const uint32_t rank = (CtaGroup == 2) ? ptx::cluster_ctarank() : 0u;
+  const bool leader = (CtaGroup == 1) || ((rank & 1u) == 0u);
+  const uint32_t leader_rank = rank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      ptx::mbar_init(full_bar + 8u * s, 1);
+      ptx::mbar_init(empty_bar + 8u * s, 1);
+    }
+    for (int b = 0; b < kNumParts; ++b) {
+      ptx::mbar_init(pfull_bar + 8u * b, 1);
+      ptx::mbar_init(pempty_bar + 8u * b, kEpiWarps * CtaGroup);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbarrier_init_cluster();
+    ptx::fence_proxy_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_a);
+    ptx::prefetch_tensormap(&tm_b);
+    ptx::prefetch_tensormap(&tm_d);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<CtaGroup>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)), L::kTmemCols);
+    ptx::tmem_relinquish<CtaGroup>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CtaGroup == 2) ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  ptx::WaitCtx ctx{abort_flag, p.status, p.timeout_ns};
+  const SchedParams& sp = p.sched;
+  const int k_iters = p.k_iters;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      producer_loop<kBlockBN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
+          &tm_a, &tm_b, sp, k_iters, stages, base, full_bar, empty_bar, rank, leader, ctx);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int part = 0;
+      uint32_t part_phase = 0;
+      bool ok = true;
+      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+        for (int kb = 0; kb < k_iters; ++kb) {
+          if (!ptx::mbar_wait(pempty_bar + 8u * part, part_phase ^ 1u, ctx, kSiteMmaTmemEmpty) ||
+              !ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(part * kBlockBN);
+          const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
+          const uint64_t da = ptx::make_sw128_kmajor_desc(sa);
+          const uint64_t db = ptx::make_sw128_kmajor_desc(sa + L::kAStageBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
+                                      db + static_cast<uint64_t>(2 * k), kIdesc, k > 0 ? 1u : 0u);
+          }
+          const uint32_t eb = empty_bar + 8u * stage;
+          const uint32_t pb = pfull_bar + 8u * part;
+          if constexpr (CtaGroup == 1) {
+            ptx::umma_commit<1>(eb);
+            ptx::umma_commit<1>(pb);
+          } else {
+            ptx::umma_commit_pair(eb, pair_mask);
+            ptx::umma_commit_pair(pb, pair_mask);
+          }
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (++part == kNumParts) {
+            part = 0;
+            part_phase ^= 1u;
+          }
+        }
+      }
+      ptx::umma_commit<CtaGroup>(drain_bar);
+      ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
+      volatile int32_t no_abort = 0;
+      dctx.abort_flag = &no_abort;
+      ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- promotion + epilogue
+    const uint32_t ew = warp - kEpiFirstWarp;
+    const uint32_t quad = warp & 3u;
+    const uint32_t row_in_tile = quad * 32u;
+    const int64_t nkb_total = k_iters;
+    int part = 0;
+    uint32_t part_phase = 0;
+    int epi_idx = 0;
+    bool ok = true;
+    for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+      int32_t pid_m, pid_n;
+      work_tile_coords(sp, it.cid, pid_m, pid_n);
+      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && it.executed < p.trace_stride) {
+        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) *
+                                             (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
+        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + it.executed);
+        t[0] = pid_m;
+        t[1] = pid_n;
+      }
+      __syncwarp();
+      const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
+      const int32_t my_row = g_row + static_cast<int32_t>(lane);
+      const bool row_ok = my_row < p.m;
+      const float* sb_row = scales.sb + static_cast<int64_t>(pid_n) * nkb_total;
+      float acc[kBlockBN];
+#pragma unroll
+      for (int j = 0; j < kBlockBN; ++j) acc[j] = 0.f;
+      float sa_next = row_ok ? scales.sa[my_row] : 0.f;
+      float sb_next = sb_row[0];
+      for (int kb = 0; kb < k_iters; ++kb) {
+        const float s = sa_next * sb_next;
+        if (kb + 1 < k_iters) {  // prefetch the next k-block's scales behind the wait
+          sa_next = row_ok ? scales.sa[static_cast<int64_t>(kb + 1) * p.m + my_row] : 0.f;
+          sb_next = sb_row[kb + 1];
+        }
+        bool got = ptx::mbar_wait(pfull_bar + 8u * part, part_phase, ctx, kSiteEpiTmemFull);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t t_row =
+            tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(part * kBlockBN);
+#pragma unroll
+        for (int h = 0; h < kBlockBN / 64; ++h) {
+          uint32_t v0[32], v1[32];
+          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h), v0);
+          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h + 32), v1);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            acc[64 * h + j] = fmaf(s, __uint_as_float(v0[j]), acc[64 * h + j]);
+            acc[64 * h + 32 + j] = fmaf(s, __uint_as_float(v1[j]), acc[64 * h + 32 + j]);
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
+          if constexpr (CtaGroup == 1) {
+            ptx::mbar_arrive(pb);
+          } else {
+            ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
+          }
+        }
+        if (++part == kNumParts) {
+          part = 0;
+          part_phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      // Round the row to BF16 and store it in two 64-column chunks.
+#pragma unroll
+      for (int c = 0; c < kBlockBN / 64; ++c) {
+        const int32_t col0 = pid_n * kBlockBN + 64 * c;
+        // Lane l holds bias[col0 + l] and bias[col0 + 32 + l]; shuffles broadcast them.
+        const bool has_bias = p.bias != nullptr;
+        const int32_t nb = col0 + static_cast<int32_t>(lane);
+        const float b0 = (has_bias && nb < p.n) ? __bfloat162float(p.bias[nb]) : 0.f;
+        const float b1 = (has_bias && nb + 32 < p.n) ? __bfloat162float(p.bias[nb + 32]) : 0.f;
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j0 = 2 * i, j1 = 2 * i + 1;
+          const float x0 = acc[64 * c + j0] * p.alpha +
+                           __shfl_sync(0xffffffffu, j0 < 32 ? b0 : b1, j0 & 31);
+          const float x1 = acc[64 * c + j1] * p.alpha +
+                           __shfl_sync(0xffffffffu, j1 < 32 ? b0 : b1, j1 & 31);
+          packed[i] = ptx::pack_bf16x2(x0, x1);
+        }
+        const int buf = epi_idx % p.epi_stages;
+        const uint32_t sbuf =
+            epi_base + static_cast<uint32_t>((ew * p.epi_stages + buf) * kEpiBufBytes);
+        if (lane == 0) epi_wait_buffer(p.epi_stages);
+        __syncwarp();
+        const uint32_t row_addr = sbuf + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(j) ^ (lane & 7u);
+          ptx::st_shared_v4(row_addr + (chunk << 4), packed[4 * j], packed[4 * j + 1],
+                            packed[4 * j + 2], packed[4 * j + 3]);
+        }
+        ptx::fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (g_row < p.m && col0 < p.n) ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+          ptx::bulk_commit_group();
+        }
+        __syncwarp();
+        ++epi_idx;
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CtaGroup == 2) ptx::cluster_sync();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<CtaGroup>(tmem_base, L::kTmemCols);
+  }
+#endif
+}
+
+}  // namespace cpg

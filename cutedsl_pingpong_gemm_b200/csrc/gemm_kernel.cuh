@@ -35,13 +35,44 @@
 namespace cpg {
 
 constexpr int kBM = 128;             // rows of A / D per CTA
-constexpr int kBK = 64;              // BF16 elements per 128-byte swizzled row (one k-block)
-constexpr int kUmmaK = 16;           // K per tcgen05.mma kind::f16
+constexpr int kRowBytes = 128;       // one 128-byte swizzled row of a k-block
 constexpr int kNumThreads = 192;     // 6 warps
 constexpr int kEpiWarps = 4;
 constexpr int kEpiFirstWarp = 2;
-constexpr int kEpiCols = 64;         // columns per epilogue chunk (one 128-byte swizzled row)
-constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 64 BF16 = 4 KiB
+constexpr int kEpiBufBytes = 32 * kRowBytes;  // 32 rows x 128 bytes = 4 KiB per staging buffer
+
+// FP8 E4M3 storage type (one byte per element).
+struct e4m3_t {
+  uint8_t bits;
+};
+
+// Operand element type -> k-block width and UMMA instruction kind.
+template <typename T>
+struct OperandTraits;
+template <>
+struct OperandTraits<__nv_bfloat16> {
+  static constexpr int kBK = 64;     // elements per 128-byte row
+  static constexpr int kUmmaK = 16;  // K per tcgen05.mma kind::f16
+  static constexpr bool kFp8 = false;
+};
+template <>
+struct OperandTraits<e4m3_t> {
+  static constexpr int kBK = 128;
+  static constexpr int kUmmaK = 32;  // K per tcgen05.mma kind::f8f6f4
+  static constexpr bool kFp8 = true;
+};
+
+// Output element type -> columns per 128-byte staging row.
+template <typename T>
+struct OutputTraits;
+template <>
+struct OutputTraits<__nv_bfloat16> {
+  static constexpr int kStoreCols = 64;
+};
+template <>
+struct OutputTraits<float> {
+  static constexpr int kStoreCols = 32;
+};
 constexpr int kMaxStages = 12;
 constexpr int kMaxEpiStages = 4;
 constexpr int kMinSmemForOneCtaPerSm = 116 * 1024;
@@ -64,6 +95,8 @@ struct GemmParams {
   int32_t epi_stages;
   int32_t reuse_ab;       // epilogue staging aliases the A/B stages (single-tile CTAs only)
   float alpha;
+  const float* scale_a;   // optional device scalar (FP8 per-tensor scale of A); D *= *scale_a
+  const float* scale_b;   // optional device scalar (FP8 per-tensor scale of B)
   const __nv_bfloat16* bias;  // optional per-column bias, length N
   int32_t* tile_trace;    // optional: (pid_m, pid_n) per CTA per tile, trace_stride tiles per CTA
   int32_t trace_stride;
@@ -73,8 +106,8 @@ struct GemmParams {
 
 template <int BN, int CtaGroup>
 struct GemmSmem {
-  static constexpr int kAStageBytes = kBM * kBK * 2;                       // 16 KiB
-  static constexpr int kBStageBytes = (BN / CtaGroup) * kBK * 2;           // per CTA
+  static constexpr int kAStageBytes = kBM * kRowBytes;                     // 16 KiB
+  static constexpr int kBStageBytes = (BN / CtaGroup) * kRowBytes;         // per CTA
   static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
   static constexpr int kTmemCols = 2 * BN;                                 // two accumulators
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
@@ -143,17 +176,96 @@ __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
   }
 }
 
-template <int BN, int CtaGroup>
+// TMA producer (one lane): streams the k-blocks of A (128 rows) and B (BN / CtaGroup rows) of
+// every tile of this CTA into the shared-memory stage ring, then drains its in-flight loads.
+template <int BN, int CtaGroup, int kBK, int kStageBytes, int kAStageBytes>
+__device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUtensorMap* tm_b,
+                                              const SchedParams& sp, int k_iters, int stages,
+                                              uint32_t base, uint32_t full_bar, uint32_t empty_bar,
+                                              uint32_t rank, bool leader,
+                                              const ptx::WaitCtx& ctx) {
+  constexpr int kBNc = BN / CtaGroup;
+  constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
+  const uint32_t leader_rank = rank & ~1u;
+  volatile int32_t* abort_flag = ctx.abort_flag;
+  const uint64_t pol_a = ptx::policy_evict_normal();
+  const uint64_t pol_b = ptx::policy_evict_normal();
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t fills = 0;
+  bool ok = true;
+  for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+    int32_t pid_m, pid_n;
+    work_tile_coords(sp, it.cid, pid_m, pid_n);
+    const int32_t a_row = pid_m * kBM;
+    const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBNc;
+    for (int kb = 0; kb < k_iters; ++kb) {
+      if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
+        ok = false;
+        break;
+      }
+      const uint32_t sa = base + static_cast<uint32_t>(stage * kStageBytes);
+      const uint32_t sb = sa + kAStageBytes;
+      const uint32_t fb = full_bar + 8u * stage;
+      if constexpr (CtaGroup == 1) {
+        ptx::mbar_arrive_expect_tx(fb, kTxBytes);
+        ptx::tma_load_2d(tm_a, sa, fb, kb * kBK, a_row, pol_a);
+        ptx::tma_load_2d(tm_b, sb, fb, kb * kBK, b_row, pol_b);
+      } else {
+        if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
+        const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
+        ptx::tma_load_2d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, pol_a);
+        ptx::tma_load_2d_pair(tm_b, sb, fb_leader, kb * kBK, b_row, pol_b);
+      }
+      ++fills;
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+  // Drain: wait (bounded) until every issued fill has landed so no TMA write into this CTA's
+  // shared memory is outstanding when the CTA exits.  Immediate on the normal path.
+  if (leader) {
+    for (int s = 0; s < stages; ++s) {
+      if (fills > static_cast<uint32_t>(s)) {
+        const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
+        ptx::WaitCtx dctx{abort_flag, ctx.status, ctx.timeout_ns};
+        volatile int32_t no_abort = 0;
+        dctx.abort_flag = &no_abort;
+        ptx::mbar_wait(full_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
+      }
+    }
+  } else {
+    // The peer's loads complete on the leader's barriers; the leader drains them, and the
+    // final cluster barrier keeps this CTA resident until then.  Waiting for the stage to be
+    // released covers loads whose consumer never ran.
+    for (int s = 0; s < stages; ++s) {
+      if (fills > static_cast<uint32_t>(s)) {
+        const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
+        ptx::WaitCtx dctx{abort_flag, ctx.status, ctx.timeout_ns};
+        volatile int32_t no_abort = 0;
+        dctx.abort_flag = &no_abort;
+        if (*abort_flag == 0)
+          ptx::mbar_wait(empty_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
+      }
+    }
+  }
+}
+
+template <int BN, int CtaGroup, typename AB, typename OutT>
 __global__ void __launch_bounds__(kNumThreads, 1)
-    gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tm_a,
-                           const __grid_constant__ CUtensorMap tm_b,
-                           const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_b,
+                      const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using L = GemmSmem<BN, CtaGroup>;
-  constexpr int kBNc = BN / CtaGroup;  // B rows loaded by this CTA
-  constexpr uint32_t kIdesc = ptx::make_idesc_bf16_f32(kBM * CtaGroup, BN);
-  constexpr uint32_t kTxBytes = static_cast<uint32_t>(L::kStageBytes * CtaGroup);
-
+  using OT = OperandTraits<AB>;
+  constexpr int kBK = OT::kBK;
+  constexpr int kUmmaK = OT::kUmmaK;
+  constexpr int kStoreCols = OutputTraits<OutT>::kStoreCols;
+  constexpr uint32_t kIdesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kBM * CtaGroup, BN)
+                                       : ptx::make_idesc_bf16_f32(kBM * CtaGroup, BN);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -214,69 +326,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = ptx::policy_evict_normal();
-      const uint64_t pol_b = ptx::policy_evict_normal();
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t fills = 0;
-      bool ok = true;
-      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
-        int32_t pid_m, pid_n;
-        work_tile_coords(sp, it.cid, pid_m, pid_n);
-        const int32_t a_row = pid_m * kBM;
-        const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBNc;
-        for (int kb = 0; kb < k_iters; ++kb) {
-          if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
-            ok = false;
-            break;
-          }
-          const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
-          const uint32_t sb = sa + L::kAStageBytes;
-          const uint32_t fb = full_bar + 8u * stage;
-          if constexpr (CtaGroup == 1) {
-            ptx::mbar_arrive_expect_tx(fb, kTxBytes);
-            ptx::tma_load_2d(&tm_a, sa, fb, kb * kBK, a_row, pol_a);
-            ptx::tma_load_2d(&tm_b, sb, fb, kb * kBK, b_row, pol_b);
-          } else {
-            if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
-            const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
-            ptx::tma_load_2d_pair(&tm_a, sa, fb_leader, kb * kBK, a_row, pol_a);
-            ptx::tma_load_2d_pair(&tm_b, sb, fb_leader, kb * kBK, b_row, pol_b);
-          }
-          ++fills;
-          if (++stage == stages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-      // Drain: wait (bounded) until every issued fill has landed so no TMA write into this CTA's
-      // shared memory is outstanding when the CTA exits.  Immediate on the normal path.
-      if (leader) {
-        for (int s = 0; s < stages; ++s) {
-          if (fills > static_cast<uint32_t>(s)) {
-            const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
-            ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
-            volatile int32_t no_abort = 0;
-            dctx.abort_flag = &no_abort;
-            ptx::mbar_wait(full_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
-          }
-        }
-      } else {
-        // The peer's loads complete on the leader's barriers; the leader drains them, and the
-        // final cluster barrier keeps this CTA resident until then.  Waiting for the stage to be
-        // released covers loads whose consumer never ran.
-        for (int s = 0; s < stages; ++s) {
-          if (fills > static_cast<uint32_t>(s)) {
-            const uint32_t round = (fills - 1u - static_cast<uint32_t>(s)) / stages;
-            ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
-            volatile int32_t no_abort = 0;
-            dctx.abort_flag = &no_abort;
-            if (*abort_flag == 0)
-              ptx::mbar_wait(empty_bar + 8u * s, round & 1u, dctx, kSiteDrainLoads);
-          }
-        }
-      }
+      producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
+          &tm_a, &tm_b, sp, k_iters, stages, base, full_bar, empty_bar, rank, leader, ctx);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -306,10 +357,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint64_t db = ptx::make_sw128_kmajor_desc(sb);
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            // Advance the start address by k * 32 bytes inside the 128-byte swizzled row.
-            ptx::umma_f16_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
-                                       db + static_cast<uint64_t>(2 * k), kIdesc,
-                                       (kb > 0 || k > 0) ? 1u : 0u);
+            // Advance the start address by kUmmaK elements = 32 bytes inside the swizzled row.
+            if constexpr (OT::kFp8) {
+              ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
+                                        db + static_cast<uint64_t>(2 * k), kIdesc,
+                                        (kb > 0 || k > 0) ? 1u : 0u);
+            } else {
+              ptx::umma_f16_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
+                                         db + static_cast<uint64_t>(2 * k), kIdesc,
+                                         (kb > 0 || k > 0) ? 1u : 0u);
+            }
           }
           const uint32_t eb = empty_bar + 8u * stage;
           if constexpr (CtaGroup == 1) {
@@ -350,10 +407,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int epi_idx = 0;
-    const float alpha = p.alpha;
+    float alpha = p.alpha;
+    if (p.scale_a != nullptr) alpha *= *p.scale_a;
+    if (p.scale_b != nullptr) alpha *= *p.scale_b;
     const bool has_bias = p.bias != nullptr;
-    const uint32_t tempty_target =
-        (CtaGroup == 1) ? (tempty_bar) : ptx::mapa_shared(tempty_bar, leader_rank);
     for (WorkIter it = make_work_iter(sp); it.valid(); it.advance()) {
       int32_t pid_m, pid_n;
       work_tile_coords(sp, it.cid, pid_m, pid_n);
@@ -372,41 +429,50 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const uint32_t t_row = tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(acc * BN);
       const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
 #pragma unroll 1
-      for (int c = 0; c < BN / kEpiCols; ++c) {
-        uint32_t v0[32], v1[32];
-        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kEpiCols), v0);
-        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kEpiCols + 32), v1);
+      for (int c = 0; c < BN / kStoreCols; ++c) {
+        // kStoreCols accumulator columns of this thread's row (one 128-byte output row).
+        uint32_t v[kStoreCols];
+#pragma unroll
+        for (int h = 0; h < kStoreCols / 32; ++h) {
+          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kStoreCols + 32 * h),
+                                  *reinterpret_cast<uint32_t(*)[32]>(&v[32 * h]));
+        }
         ptx::tmem_ld_wait();
-        if (c == BN / kEpiCols - 1) {
+        if (c == BN / kStoreCols - 1) {
           // Accumulator fully read into registers: hand the TMEM buffer back to the MMA warp.
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
+            const uint32_t tb = tempty_bar + 8u * static_cast<uint32_t>(acc);
             if constexpr (CtaGroup == 1) {
-              ptx::mbar_arrive(tempty_target);
+              ptx::mbar_arrive(tb);
             } else {
-              ptx::mbar_arrive_cluster(tempty_target);
+              ptx::mbar_arrive_cluster(ptx::mapa_shared(tb, leader_rank));
             }
           }
         }
-        const int32_t col0 = pid_n * BN + c * kEpiCols;
-        uint32_t packed[32];
+        const int32_t col0 = pid_n * BN + c * kStoreCols;
+        float x[kStoreCols];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0 = __uint_as_float(v0[2 * i]) * alpha;
-          float x1 = __uint_as_float(v0[2 * i + 1]) * alpha;
-          float y0 = __uint_as_float(v1[2 * i]) * alpha;
-          float y1 = __uint_as_float(v1[2 * i + 1]) * alpha;
-          if (has_bias) {
-            const int32_t n0 = col0 + 2 * i;
-            const int32_t n1 = col0 + 32 + 2 * i;
-            x0 += (n0 < p.n) ? __bfloat162float(p.bias[n0]) : 0.f;
-            x1 += (n0 + 1 < p.n) ? __bfloat162float(p.bias[n0 + 1]) : 0.f;
-            y0 += (n1 < p.n) ? __bfloat162float(p.bias[n1]) : 0.f;
-            y1 += (n1 + 1 < p.n) ? __bfloat162float(p.bias[n1 + 1]) : 0.f;
+        for (int j = 0; j < kStoreCols; ++j) x[j] = __uint_as_float(v[j]) * alpha;
+        if (has_bias) {
+          // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
+          // they are broadcast across the warp with shuffles.
+#pragma unroll
+          for (int h = 0; h < kStoreCols / 32; ++h) {
+            const int32_t n = col0 + 32 * h + static_cast<int32_t>(lane);
+            const float bl = (n < p.n) ? __bfloat162float(p.bias[n]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[32 * h + j] += __shfl_sync(0xffffffffu, bl, j);
           }
-          packed[i] = ptx::pack_bf16x2(x0, x1);
-          packed[16 + i] = ptx::pack_bf16x2(y0, y1);
+        }
+        uint32_t packed[32];  // 128 bytes of this thread's output row
+        if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) packed[i] = ptx::pack_bf16x2(x[2 * i], x[2 * i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) packed[i] = __float_as_uint(x[i]);
         }
         const int buf = epi_idx % p.epi_stages;
         const uint32_t sbuf =

@@ -11,7 +11,9 @@ Drop-in surface (adelmuursepp/cutedsl_pingpong_gemm, gemm_base.py):
 * ``gemm(a, b, c, stream)`` compiles on first use and runs.
 
 ``a`` is [M, K], ``b`` is [N, K] and ``c`` is [M, N], all BF16 CUDA tensors with unit stride in
-the last dimension (the reference's harness layout, gemm_base.py:587-590).  Underneath, every call
+the last dimension (the reference's harness layout, gemm_base.py:587-590).  Beyond the reference,
+``a``/``b`` may be FP8 E4M3 (``torch.float8_e4m3fn``, with per-tensor ``scale_a``/``scale_b``
+device scalars) and ``c`` may be FP32 (split-K partials); ``bias`` adds a BF16 per-column vector.  Underneath, every call
 goes through the C ABI of ``libcpgemm.so`` into hand-written sm_100a kernels (tcgen05 MMA into
 TMEM, TMA loads/stores, persistent grouped tile scheduler); there is no other execution path.
 
@@ -29,6 +31,7 @@ Argument meaning on sm_100a:
   the launch.
 """
 import ctypes
+import functools
 import math
 from typing import Optional, Tuple
 
@@ -37,6 +40,15 @@ from .tile_scheduler import RasterOrder, SimpleTileScheduler, get_max_active_clu
 
 THREADS_PER_WG = 128
 THREADS_PER_CTA_SM100 = 192  # TMA warp + MMA warp + 4 epilogue warps
+
+
+@functools.lru_cache(maxsize=None)
+def _dtype_tables():
+    """(A/B dtype -> CPG code, D dtype -> CPG code)."""
+    import torch
+    ab = {torch.bfloat16: _lib.CPG_DTYPE_BF16, torch.float8_e4m3fn: _lib.CPG_DTYPE_E4M3}
+    d = {torch.bfloat16: _lib.CPG_DTYPE_BF16, torch.float32: _lib.CPG_DTYPE_F32}
+    return ab, d
 
 
 def _stream_handle(stream, device) -> int:
@@ -69,8 +81,10 @@ class CompiledGemm:
     def _plan(self, a, b, c):
         import torch
         gemm = self.gemm
-        assert a.dtype == b.dtype == c.dtype == torch.bfloat16, \
-            "A, B and D must be BF16 (gemm_base.py:514)"
+        ab_codes, d_codes = _dtype_tables()
+        # gemm_base.py:514 requires BF16 everywhere; sm_100a adds FP8 E4M3 operands and FP32 D.
+        assert a.dtype == b.dtype and a.dtype in ab_codes and c.dtype in d_codes, \
+            "A, B and D must be BF16 (gemm_base.py:514), or FP8 E4M3 A/B, or FP32 D"
         if a.dim() != 2 or b.dim() != 2 or c.dim() != 2:
             raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE, "A, B and D must be 2-D")
         m, k = a.shape
@@ -86,36 +100,39 @@ class CompiledGemm:
             if t.numel() > 0 and not t.is_cuda:
                 raise _lib.CpgError(_lib.CPG_ERR_NO_DEVICE, f"{name} must be a CUDA tensor")
         def row_stride(t, rows, cols):
-            # A single-row tensor's row stride is never used; give the padded row length.
-            return t.stride(0) if rows > 1 else max(8, (cols + 7) // 8 * 8)
+            # A single-row tensor's row stride is never used; give the row length padded to 16 B.
+            per16 = 16 // t.element_size()
+            return t.stride(0) if rows > 1 else max(per16, -(-cols // per16) * per16)
 
         lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()
-        key = (m, n, k, lda, ldb, ldd, dev)
+        dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
+        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d)
         plan = self._plans.get(key)
         if plan is None:
-            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev)
+            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d)
             self._plans[key] = plan
         return plan
 
     def plan_for(self, a, b, c) -> "_Plan":
         return self._plan(a, b, c)
 
-    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0):
+    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
+                 scale_b=None):
         plan = self._plan(a, b, c)
-        plan.run(a, b, c, stream, bias=bias, alpha=alpha)
+        plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
         return None
 
 
 class _Plan:
     """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
 
-    def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device):
+    def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
         self.device = device
         cfg = gemm._config_c()
-        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, _lib.CPG_DTYPE_BF16, _lib.CPG_DTYPE_BF16)
+        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d)
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -158,7 +175,8 @@ class _Plan:
             _lib.check(rc, "status")
         return s.value
 
-    def run(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0) -> None:
+    def run(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
+            scale_b=None) -> None:
         import torch
         if bias is not None:
             if not (bias.dtype == torch.bfloat16 and bias.is_cuda and bias.numel() == self.n
@@ -167,7 +185,13 @@ class _Plan:
                                     "bias must be a contiguous BF16 CUDA tensor of length N")
             if bias.stride(-1) != 1:
                 raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED, "bias must be contiguous")
-        epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr())
+        scales = []
+        for name, sc in (("scale_a", scale_a), ("scale_b", scale_b)):
+            if sc is not None and not (sc.is_cuda and sc.dtype == torch.float32 and sc.numel() == 1):
+                raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                    f"{name} must be a one-element float32 CUDA tensor")
+            scales.append(None if sc is None else sc.data_ptr())
+        epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales)
         st = _stream_handle(stream, c.device)
         rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
                                    b.data_ptr() if b.numel() else None, c.data_ptr(),
@@ -264,10 +288,11 @@ class GemmSM90:
         self._compiled = compiled
         return compiled
 
-    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0):
+    def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
+                 scale_b=None):
         if self._compiled is None:
             self._compiled = CompiledGemm(self)
-        self._compiled(a, b, c, stream, bias=bias, alpha=alpha)
+        self._compiled(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
 
 
 # The B200 name of the same operator.

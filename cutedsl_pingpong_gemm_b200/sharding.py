@@ -1,0 +1,112 @@
+"""Multi-GPU GEMM on one node: one process per GPU, torch.distributed for the plumbing.
+
+Two decompositions of D = A . B^T (the reference has none; it is a single-GPU kernel):
+
+* ``MShardedGemm`` -- rows of A and D are split across ranks in whole 128-row tiles, B (the
+  weight) is replicated, and every rank runs the sm_100a GEMM on its rows.  There is no
+  collective on the data path, so the ranks scale independently.
+* ``SplitKGemm`` -- for tall-K shapes (M, N small, K large) each rank multiplies its K range into
+  an fp32 partial [M, N] with the same kernel (fp32 epilogue), the partials are summed with one
+  NCCL reduce-scatter over NVLink (rank r receives rows ``row_range(M, world, r)``), and a cast
+  kernel rounds the reduced rows to BF16.
+
+The range arithmetic is plain Python so that the decomposition can be exercised on CPU ranks
+(gloo) with any per-rank compute function; the GPU compute always goes through the C ABI.
+"""
+from typing import Callable, List, Optional, Tuple
+
+TILE_M = 128
+K_ALIGN = 64
+
+
+def row_range(m: int, world: int, rank: int, align: int = TILE_M) -> Tuple[int, int]:
+    """Rows [start, stop) of rank ``rank`` when ``m`` rows are split over ``world`` ranks.
+
+    Whole ``align``-row tiles are dealt out as evenly as possible (earlier ranks take the extra
+    tile); the last rank also takes the ragged remainder.  Ranges are disjoint and cover [0, m).
+    """
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} of world {world}")
+    tiles = -(-m // align) if m > 0 else 0
+    base, extra = divmod(tiles, world)
+    start_tile = rank * base + min(rank, extra)
+    ntiles = base + (1 if rank < extra else 0)
+    start = min(start_tile * align, m)
+    stop = min((start_tile + ntiles) * align, m)
+    return start, stop
+
+
+def k_ranges(k: int, parts: int, align: int = K_ALIGN) -> List[Tuple[int, int]]:
+    """Split [0, k) into ``parts`` contiguous ranges whose starts are multiples of ``align``."""
+    return [row_range(k, parts, p, align) for p in range(parts)]
+
+
+def reduce_scatter_rows(partial, world: int, group=None):
+    """Sum ``partial`` [M, N] over ranks; return this rank's rows (``row_range`` split, padded
+    so every rank holds the same number of rows for the collective).
+
+    NCCL: one ``reduce_scatter_tensor``.  Other backends (gloo on CPU, used by the tests): an
+    all-reduce followed by a slice, which has the same result.
+    """
+    import torch
+    import torch.distributed as dist
+    m, n = partial.shape
+    rank = dist.get_rank(group)
+    per = max(row_range(m, world, r)[1] - row_range(m, world, r)[0] for r in range(world))
+    if dist.get_backend(group) == "nccl":
+        padded = partial.new_zeros((per * world, n))
+        for r in range(world):
+            s, e = row_range(m, world, r)
+            padded[r * per: r * per + (e - s)] = partial[s:e]
+        out = partial.new_empty((per, n))
+        dist.reduce_scatter_tensor(out, padded, op=dist.ReduceOp.SUM, group=group)
+        s, e = row_range(m, world, rank)
+        return out[: e - s]
+    full = partial.clone()
+    dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group)
+    s, e = row_range(m, world, rank)
+    return full[s:e].contiguous()
+
+
+class MShardedGemm:
+    """M-sharded GEMM: this rank computes D[rows] = A[rows] . B^T (+ bias) with its own GPU."""
+
+    def __init__(self, gemm, world: int, rank: int):
+        self.gemm = gemm
+        self.world = world
+        self.rank = rank
+
+    def rows(self, m: int) -> Tuple[int, int]:
+        return row_range(m, self.world, self.rank)
+
+    def __call__(self, a_shard, b, d_shard, stream=None, *, bias=None, alpha: float = 1.0):
+        """``a_shard``/``d_shard`` are this rank's rows (see ``rows``); B is the full weight."""
+        self.gemm(a_shard, b, d_shard, stream, bias=bias, alpha=alpha)
+
+
+class SplitKGemm:
+    """Split-K across ranks with an NCCL reduce-scatter of fp32 partials.
+
+    ``partial_fn(a_k, b_k) -> fp32 [M, N]`` computes one rank's partial product; on GPUs it is
+    the sm_100a GEMM with an fp32 epilogue (``gemm_base.GemmSM90.partial``).
+    """
+
+    def __init__(self, world: int, rank: int, partial_fn: Callable, cast_fn: Optional[Callable] = None,
+                 group=None):
+        self.world = world
+        self.rank = rank
+        self.partial_fn = partial_fn
+        self.cast_fn = cast_fn
+        self.group = group
+
+    def k_range(self, k: int) -> Tuple[int, int]:
+        return k_ranges(k, self.world)[self.rank]
+
+    def __call__(self, a_k, b_k, m: int, n: int):
+        """``a_k`` [M, k_r] and ``b_k`` [N, k_r] hold this rank's K range.  Returns this rank's
+        rows of D (``row_range(m, world, rank)``), cast by ``cast_fn`` when given."""
+        partial = self.partial_fn(a_k, b_k)
+        if tuple(partial.shape) != (m, n):
+            raise ValueError(f"partial has shape {tuple(partial.shape)}, expected {(m, n)}")
+        rows = reduce_scatter_rows(partial, self.world, self.group)
+        return self.cast_fn(rows) if self.cast_fn is not None else rows

@@ -96,16 +96,20 @@ typedef struct cpg_gemm_config {
 typedef struct cpg_gemm_problem {
   int64_t m, n, k;
   int64_t lda, ldb, ldd; /* row strides in elements */
-  int32_t dtype_ab;      /* CPG_DTYPE_BF16 */
-  int32_t dtype_d;       /* CPG_DTYPE_BF16 */
+  int32_t dtype_ab;      /* CPG_DTYPE_BF16 or CPG_DTYPE_E4M3 (A and B share one type) */
+  int32_t dtype_d;       /* CPG_DTYPE_BF16, or CPG_DTYPE_F32 for split-K partials */
 } cpg_gemm_problem;
 
-/* Per-call epilogue options.  alpha scales the fp32 accumulator; bias (optional, BF16, length N)
- * is added per column before rounding to BF16.  The reference has neither (D = A . B^T,
- * gemm_base.py:133); alpha = 1 and bias = NULL give exactly that. */
+/* Per-call epilogue options: D = alpha * s_a * s_b * (A . B^T) + bias, rounded to D's type.
+ * alpha scales the fp32 accumulator; scale_a / scale_b (optional device pointers to one fp32
+ * value each) are the per-tensor dequantisation scales of FP8 operands; bias (optional device
+ * pointer, BF16, length N) is added per column.  The reference has none of these (D = A . B^T,
+ * gemm_base.py:133); alpha = 1 and NULL pointers give exactly that. */
 typedef struct cpg_epilogue {
   float alpha;
   const void* bias;
+  const float* scale_a;
+  const float* scale_b;
 } cpg_epilogue;
 
 typedef struct cpg_gemm cpg_gemm; /* opaque compiled GEMM */
@@ -166,6 +170,21 @@ int cpg_sched_cluster_map_device(const cpg_sched_params* p, int32_t* device_out,
 /* Clusters of `cluster_size` CTAs of the default GEMM kernel that fit on the current device at
  * once (tile_scheduler.py:20-22). */
 int cpg_max_active_clusters(int32_t cluster_size, int32_t* out);
+
+/* FP8 E4M3 quantisation of x [rows, cols] (BF16 or FP32, row stride ldx) into q (row stride ldq)
+ * with s = amax(|x|) / 448 per block and q = e4m3(x / s) (round to nearest even, saturating).
+ * (block_rows, block_cols) = (0, 0): one scale per tensor, scales[0];
+ *                            (1, 128): per row and 128 columns, scales[kb * rows + r];
+ *                            (128, 128): scales[rb * ceil(cols / 128) + kb].
+ * Produces the FP8 operands of the GEMM on the GPU (the reference has no FP8 path). */
+int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols, int64_t ldx,
+                      void* q, int64_t ldq, float* scales, int32_t block_rows, int32_t block_cols,
+                      void* stream);
+
+/* y = bf16(x + bias) for x FP32 [rows, cols]: the last step of split-K after the reduction.
+ * bias is optional (BF16, length cols). */
+int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, void* y,
+                      int64_t ldy, const void* bias, void* stream);
 
 const char* cpg_strerror(int code);
 const char* cpg_last_error_message(void);

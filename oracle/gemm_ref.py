@@ -110,3 +110,73 @@ def row_checksum(a, b, bias=None, alpha=1.0):
 def checksum_bound(d_abs_sum, abs_sum_product, k, count):
     """Bound for a checksum of ``count`` BF16 outputs: rounding of each output plus accumulation."""
     return BF16_REL * d_abs_sum + k * ACC_SLACK_PER_K * abs_sum_product + 1e-6 * count
+
+
+E4M3_MAX = 448.0
+
+
+def quantize_e4m3_per_tensor(x):
+    """Per-tensor FP8 E4M3 quantisation of the project spec: s = amax(|x|) / 448, q = e4m3(x / s).
+
+    Returns (q as torch.float8_e4m3fn, s as a 0-d float32 tensor).  The dequantised operand is
+    q.float() * s; the GEMM oracle for FP8 is the fp32 product of dequantised operands.
+    """
+    xf = x.float()
+    amax = xf.abs().max().clamp_min(1e-12)
+    s = (amax / E4M3_MAX).to(torch.float32)
+    q = (xf / s).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+    return q, s
+
+
+def dequantize(q, s):
+    return q.float() * s
+
+
+def make_fp8_inputs(m, n, k, seed=0):
+    """BASELINE config 4 inputs: A, B ~ N(0,1), quantised per tensor."""
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g)
+    b = torch.randn(n, k, generator=g)
+    qa, sa = quantize_e4m3_per_tensor(a)
+    qb, sb = quantize_e4m3_per_tensor(b)
+    return qa, sa, qb, sb
+
+
+def check_fp8(d, qa, sa, qb, sb, rows=None, frob_tol=FROB_TOL_FP8):
+    """FP8 GEMM check against the fp32 product of the dequantised operands."""
+    a = dequantize(qa, sa)
+    b = dequantize(qb, sb)
+    return check(d, a, b, rows=rows, frob_tol=frob_tol)
+
+
+def quantize_e4m3_blocks(x, block):
+    """Block FP8 quantisation (oracle): block (1,128) -> scales [ceil(K/128), M] (one per row and
+    128 columns), block (128,128) -> scales [ceil(M/128), ceil(K/128)].  Same s = amax/448 rule."""
+    xf = x.float()
+    m, k = xf.shape
+    nkb = -(-k // 128)
+    pad_k = nkb * 128 - k
+    if block == (1, 128):
+        xp = torch.nn.functional.pad(xf, (0, pad_k)).reshape(m, nkb, 128)
+        amax = xp.abs().amax(dim=2).clamp_min(1e-12)          # [m, nkb]
+        s = (amax / E4M3_MAX).to(torch.float32)
+        q = (xp / s.unsqueeze(2)).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+        return q.reshape(m, nkb * 128)[:, :k].contiguous(), s.t().contiguous()
+    if block == (128, 128):
+        nmb = -(-m // 128)
+        xp = torch.nn.functional.pad(xf, (0, pad_k, 0, nmb * 128 - m)).reshape(nmb, 128, nkb, 128)
+        amax = xp.abs().amax(dim=(1, 3)).clamp_min(1e-12)    # [nmb, nkb]
+        s = (amax / E4M3_MAX).to(torch.float32)
+        q = (xp / s[:, None, :, None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+        return q.reshape(nmb * 128, nkb * 128)[:m, :k].contiguous(), s
+    raise ValueError(block)
+
+
+def dequantize_blocks(q, s, block):
+    qf = q.float()
+    m, k = qf.shape
+    if block == (1, 128):
+        scale = s.t().repeat_interleave(128, dim=1)[:, :k]
+    else:
+        scale = s.repeat_interleave(128, dim=0).repeat_interleave(128, dim=1)[:m, :k]
+    return qf * scale

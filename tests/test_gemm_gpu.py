@@ -277,3 +277,37 @@ def test_full_8192_cubed(cluster):
 def test_full_llm_ffn_up_with_bias():
     """BASELINE config 3 (one GPU, one M shard of 2048 rows): N=28672, K=8192, bias."""
     _full_size_check(2048, 28672, 8192, make_gemm(256, (2, 1, 1), stages=6), 1.0, 0.02, bias=True)
+
+
+# ---------------------------------------------------------------- FP8 E4M3 (per-tensor scales)
+@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("shape", [(256, 512, 512), (300, 264, 1000 + 8), (1024, 1024, 1024)])
+def test_fp8_per_tensor(shape, cluster, tile_n):
+    """BASELINE config 4 (per-tensor variant) at parity-test sizes; tolerance rel-Frobenius 3e-2
+    and the element-wise bound, against the fp32 product of the dequantised E4M3 operands."""
+    m, n, k = shape
+    qa, sa, qb, sb = gemm_ref.make_fp8_inputs(m, n, k, seed=m + n + k)
+    d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    gemm = make_gemm(tile_n, cluster)
+    gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.reshape(1).cuda(), scale_b=sb.reshape(1).cuda())
+    torch.cuda.synchronize()
+    res = gemm_ref.check_fp8(d.cpu(), qa, sa, qb, sb)
+    assert res["ok"], res
+    assert res["frob"] < 1e-2
+
+
+# ---------------------------------------------------------------- FP32 output (split-K partials)
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("tile_n", [64, 256])
+def test_fp32_output(cluster, tile_n):
+    m, n, k = 384, 520, 768
+    a, b, _ = gemm_ref.make_inputs(m, n, k, seed=11)
+    d = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    gemm = make_gemm(tile_n, cluster)
+    gemm(a.cuda(), b.cuda(), d)
+    torch.cuda.synchronize()
+    r = gemm_ref.reference(a, b)
+    s = gemm_ref.abs_product(a, b)
+    # fp32 output: no output rounding term, only the accumulation bound.
+    assert bool(((d.cpu() - r).abs() <= k * gemm_ref.ACC_SLACK_PER_K * s + 1e-6).all())
