@@ -35,13 +35,21 @@ if HERE not in sys.path:
 NOMINAL_DENSE_BF16_TFLOPS = 2250.0
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+NOMINAL_DENSE_FP8_TFLOPS = 4500.0
+
 WORKLOADS = {
-    # name: (M per GPU or total, N, K, a_scale, b_scale, bias, m_split)
+    # m is per GPU when m_is_per_gpu (weak scaling), else the total split over the GPUs.
     "bf16_8192": dict(m=8192, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
-                      m_is_per_gpu=True),
-    "llm": dict(m=16384, n=28672, k=8192, a_scale=1.0, b_scale=0.02, bias=True, m_is_per_gpu=False),
+                      m_is_per_gpu=True, fp8=None),
+    "llm": dict(m=16384, n=28672, k=8192, a_scale=1.0, b_scale=0.02, bias=True,
+                m_is_per_gpu=False, fp8=None),
     "smallm": dict(m=128, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
-                   m_is_per_gpu=True),
+                   m_is_per_gpu=True, fp8=None),
+    # FP8 E4M3, A and B ~ N(0,1) quantised on the GPU (s = amax / 448) before timing.
+    "fp8": dict(m=16384, n=8192, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
+                m_is_per_gpu=True, fp8="tensor"),
+    "fp8_block": dict(m=16384, n=8192, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
+                      m_is_per_gpu=True, fp8="block"),
 }
 
 
@@ -267,7 +275,10 @@ def run_reference(args, world, rank):
 def metric_name(workload):
     return {"bf16_8192": "GEMM TFLOPS (BF16 8192^3 per GPU, M-sharded, B replicated)",
             "llm": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 + bias, M-sharded)",
-            "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)"}[workload]
+            "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)",
+            "fp8": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, per-tensor scales)",
+            "fp8_block": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, 1x128 / 128x128 block scales)",
+            }[workload]
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -289,22 +300,36 @@ def run_cpg(args, world, rank, local):
     b = (torch.randn(n, k, generator=gen_b, device=dev) * w["b_scale"]).to(torch.bfloat16)
     bias = (torch.randn(n, generator=gen_b, device=dev)).to(torch.bfloat16) if w["bias"] else None
     d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    scale_a = scale_b = None
+    tile_n = args.tile_n
+    if w["fp8"] is not None:
+        from cutedsl_pingpong_gemm_b200.quant import quantize_e4m3
+        if w["fp8"] == "tensor":
+            a, scale_a = quantize_e4m3(a)
+            b, scale_b = quantize_e4m3(b)
+        else:
+            a, scale_a = quantize_e4m3(a, (1, 128))
+            b, scale_b = quantize_e4m3(b, (128, 128))
+            tile_n = 128
+        torch.cuda.synchronize()
 
     cm = args.cluster_m
     stages = args.stages or (6 if cm == 2 else 4)
-    if args.tile_n < 256 and not args.stages:
+    if tile_n < 256 and not args.stages:
         stages = 8 if cm == 2 else 6
-    gemm = GemmSM90(tile_shape_mn=(128, args.tile_n), epi_tile_mn=(128, 32),
+    gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
     compiled = cpg_compile(gemm, a, b, d, stream)
-    plan = compiled.plan_for(a, b, d)
+    compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
+    torch.cuda.synchronize()
+    plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0)
     info = plan.launch_info()
 
     launches = [0]
 
     def step():
-        compiled(a, b, d, stream, bias=bias)
+        compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
         launches[0] += 1
 
     for _ in range(args.warmup):
@@ -350,7 +375,7 @@ def run_cpg(args, world, rank, local):
         def e2e_step():
             a2.copy_(a_h, non_blocking=True)
             b2.copy_(b_h, non_blocking=True)
-            compiled(a2, b2, d, stream, bias=bias)
+            compiled(a2, b2, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
             d_h.copy_(d, non_blocking=True)
 
         for _ in range(2):
@@ -368,7 +393,7 @@ def run_cpg(args, world, rank, local):
         barrier(world)
         e2e_ms = reduce_max(f0.elapsed_time(f1) / args.e2e_steps, world)
         e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": int((a.numel() + b.numel()) * 2 * world),
+               "h2d_bytes_per_step": int((a.numel() + b.numel()) * a.element_size() * world),
                "d2h_bytes_per_step": int(d.numel() * 2 * world), "steps": args.e2e_steps,
                "ms_per_step": e2e_ms, "gpu_launches": args.e2e_steps * world,
                "path": "GemmSM90 compiled call (C ABI cpg_gemm_run) with pinned-host A, B in and D out"}
@@ -384,21 +409,30 @@ def run_cpg(args, world, rank, local):
 
     if rank == 0:
         peak = peaks["bf16_tflops"]
+        nominal = NOMINAL_DENSE_BF16_TFLOPS
+        peak_note = f"{peak_src} bf16_tflops (cuBLAS burst)"
+        if w["fp8"] is not None:
+            # No measured FP8 tensor peak exists on this pool; the dense nominal is the bound.
+            nominal = NOMINAL_DENSE_FP8_TFLOPS
+            peak = NOMINAL_DENSE_FP8_TFLOPS
+            peak_note = "nominal dense FP8 (no measured FP8 peak available)"
         line = {
             "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak" if w["m_is_per_gpu"] else "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "pct_nominal_dense_peak": 100.0 * value / (NOMINAL_DENSE_BF16_TFLOPS * world),
+            "vs_baseline": None, "dtype": "e4m3" if w["fp8"] else "bf16", "data": "synthetic",
+            "pct_nominal_dense_peak": 100.0 * value / (nominal * world),
             "config": {"workload": args.workload, "m_per_gpu": m, "n": n, "k": k,
                        "m_total": m * world, "parallelism": f"m-shard x{world}, B replicated",
-                       "tile": [128, args.tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
+                       "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
+                       "fp8_scales": w["fp8"],
                        "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
                        "bias": bool(w["bias"])},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_source": f"{peak_src} bf16_tflops (burst)",
-                         "frac_sustained": achieved / peaks.get("bf16_tflops_sustained", peak),
+                         "frac": achieved / peak, "peak_source": peak_note,
+                         "frac_sustained": (achieved / peaks.get("bf16_tflops_sustained", peak)
+                                            if w["fp8"] is None else None),
                          "traffic": load_traffic(args.workload),
                          "algorithmic_flops_per_launch": flops_per_gpu,
                          "kernel": "cpg::gemm_bf16_sm100_kernel"},

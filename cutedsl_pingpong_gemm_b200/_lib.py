@@ -26,7 +26,12 @@ CPG_DTYPE_BF16 = 0
 CPG_DTYPE_E4M3 = 1
 CPG_DTYPE_F32 = 2
 
-ABI_VERSION = 3
+CPG_SCALE_TENSOR = 0
+CPG_SCALE_BLOCK = 1
+
+CPG_INJECT_SKIP_LOADS = 1
+
+ABI_VERSION = 5
 
 
 class CpgError(RuntimeError):
@@ -75,6 +80,7 @@ class GemmProblemC(ctypes.Structure):
         ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
         ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldd", ctypes.c_int64),
         ("dtype_ab", ctypes.c_int32), ("dtype_d", ctypes.c_int32),
+        ("scale_mode", ctypes.c_int32),
     ]
 
 
@@ -98,6 +104,7 @@ SIGNATURES = {
     "cpg_gemm_sched_params": (ctypes.c_int, [_vp, _P(SchedParamsC)]),
     "cpg_gemm_set_trace": (ctypes.c_int, [_vp, _vp, _i32]),
     "cpg_gemm_set_timeout_ms": (ctypes.c_int, [_vp, _i32]),
+    "cpg_gemm_set_fault_injection": (ctypes.c_int, [_vp, _i32]),
     "cpg_gemm_status": (ctypes.c_int, [_vp, _P(_i32)]),
     "cpg_fast_divmod_create": (ctypes.c_int, [_i32, _P(FastDivmodC)]),
     "cpg_fast_divmod_divmod": (ctypes.c_int, [_P(FastDivmodC), _i32, _P(_i32), _P(_i32)]),

@@ -12,6 +12,7 @@
 #include <string>
 
 #include "cpgemm.h"
+#include "gemm_fp8_block.cuh"
 #include "gemm_kernel.cuh"
 #include "quant_kernels.cuh"
 
@@ -93,7 +94,8 @@ struct Variant {
   int cta_group;
   int dtype_ab;
   int dtype_d;
-  KernelFn fn;
+  int scale_mode;  // CPG_SCALE_TENSOR (plain kernel) or CPG_SCALE_BLOCK
+  const void* fn;
   int (*smem_bytes)(int, int, int);
 };
 
@@ -113,8 +115,23 @@ constexpr int dtype_code<float>() { return CPG_DTYPE_F32; }
 
 template <int BN, int CG, typename AB, typename OutT>
 Variant make_variant() {
-  return Variant{BN, CG, dtype_code<AB>(), dtype_code<OutT>(),
-                 &cpg::gemm_sm100_kernel<BN, CG, AB, OutT>, &smem_bytes_of<BN, CG>};
+  KernelFn fn = &cpg::gemm_sm100_kernel<BN, CG, AB, OutT>;
+  return Variant{BN, CG, dtype_code<AB>(), dtype_code<OutT>(), CPG_SCALE_TENSOR,
+                 reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>};
+}
+
+template <int CG>
+int block_smem_bytes_of(int stages, int epi_stages, int reuse_ab) {
+  return cpg::BlockSmem<CG>::bytes(stages, epi_stages, reuse_ab);
+}
+
+template <int CG>
+Variant make_block_variant() {
+  using BlockFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                           const cpg::GemmParams, const cpg::BlockScales);
+  BlockFn fn = &cpg::gemm_fp8_block_kernel<CG>;
+  return Variant{cpg::kBlockBN, CG, CPG_DTYPE_E4M3, CPG_DTYPE_BF16, CPG_SCALE_BLOCK,
+                 reinterpret_cast<const void*>(fn), &block_smem_bytes_of<CG>};
 }
 
 template <typename AB, typename OutT>
@@ -127,8 +144,9 @@ void add_variants(Variant* t, int& n) {
   t[n++] = make_variant<64, 2, AB, OutT>();
 }
 
-bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, Variant* out) {
-  static Variant table[24];
+bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, int scale_mode,
+                  Variant* out) {
+  static Variant table[26];
   static int count = 0;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -136,10 +154,14 @@ bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, Variant* out
     add_variants<__nv_bfloat16, float>(table, count);
     add_variants<cpg::e4m3_t, __nv_bfloat16>(table, count);
     add_variants<cpg::e4m3_t, float>(table, count);
+    table[count++] = make_block_variant<1>();
+    table[count++] = make_block_variant<2>();
   });
+  if (scale_mode != CPG_SCALE_BLOCK) scale_mode = CPG_SCALE_TENSOR;
   for (int i = 0; i < count; ++i) {
     const Variant& v = table[i];
-    if (v.bn == bn && v.cta_group == cta_group && v.dtype_ab == dtype_ab && v.dtype_d == dtype_d) {
+    if (v.bn == bn && v.cta_group == cta_group && v.dtype_ab == dtype_ab && v.dtype_d == dtype_d &&
+        v.scale_mode == scale_mode) {
       *out = v;
       return true;
     }
@@ -170,8 +192,7 @@ __global__ void fill_rows_kernel(OutT* d, int64_t m, int64_t n, int64_t ldd,
 }
 
 int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* out) {
-  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(v.fn),
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   int dev = 0;
   cudaGetDevice(&dev);
@@ -218,6 +239,7 @@ struct cpg_gemm {
   int32_t* trace;
   int32_t trace_stride;
   uint64_t timeout_ns;
+  int32_t fault_inject;
   bool maps_valid;
   const void* map_a_ptr;
   const void* map_b_ptr;
@@ -227,7 +249,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 3; }
+int cpg_abi_version(void) { return 5; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -333,9 +355,17 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
 
   Variant v;
   const int cta_group = cfg->cluster_m == 2 ? 2 : 1;
-  if (!find_variant(cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d, &v))
+  if (prob->scale_mode != CPG_SCALE_TENSOR && prob->scale_mode != CPG_SCALE_BLOCK)
+    return fail(CPG_ERR_INVALID_CONFIG, "scale_mode must be 0 (none / per tensor) or 1 (block)");
+  if (prob->scale_mode == CPG_SCALE_BLOCK &&
+      (prob->dtype_ab != CPG_DTYPE_E4M3 || prob->dtype_d != CPG_DTYPE_BF16 || cfg->tile_n != 128))
+    return fail(CPG_ERR_UNSUPPORTED,
+                "block scales need E4M3 operands, BF16 output and tile_n 128");
+  if (!find_variant(cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d, prob->scale_mode, &v))
     return fail(CPG_ERR_UNSUPPORTED, "no kernel for tile_n %d, cta_group %d, dtypes %d/%d",
                 cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);
+  if (v.scale_mode == CPG_SCALE_BLOCK && cfg->reuse_ab)
+    return fail(CPG_ERR_UNSUPPORTED, "reuse_ab is not implemented for block-scaled FP8");
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -430,6 +460,14 @@ int cpg_gemm_set_timeout_ms(cpg_gemm* g, int32_t timeout_ms) {
   return CPG_OK;
 }
 
+int cpg_gemm_set_fault_injection(cpg_gemm* g, int32_t flags) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  if ((flags & ~CPG_INJECT_SKIP_LOADS) != 0)
+    return fail(CPG_ERR_INVALID_CONFIG, "unknown fault-injection flags %d", flags);
+  g->fault_inject = flags;
+  return CPG_OK;
+}
+
 int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
   if (g == nullptr || status == nullptr) return fail(CPG_ERR_NULL, "plan and status non-NULL");
   DeviceGuard guard(g->device);
@@ -512,13 +550,23 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
   p.alpha = alpha;
-  p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
-  p.scale_b = epi != nullptr ? epi->scale_b : nullptr;
+  const bool block = g->v.scale_mode == CPG_SCALE_BLOCK;
+  cpg::BlockScales bs{nullptr, nullptr};
+  if (block) {
+    if (epi == nullptr || epi->scale_a == nullptr || epi->scale_b == nullptr)
+      return fail(CPG_ERR_NULL, "block-scaled FP8 needs scale_a and scale_b");
+    bs.sa = epi->scale_a;
+    bs.sb = epi->scale_b;
+  } else {
+    p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
+    p.scale_b = epi != nullptr ? epi->scale_b : nullptr;
+  }
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.tile_trace = g->trace;
   p.trace_stride = g->trace_stride;
   p.status = g->status_dev;
   p.timeout_ns = g->timeout_ns;
+  p.fault_inject = g->fault_inject;
 
   cudaLaunchConfig_t lc = {};
   cudaLaunchAttribute attr[1];
@@ -535,8 +583,8 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p};
-  cudaError_t e = cudaLaunchKernelExC(&lc, reinterpret_cast<const void*>(g->v.fn), args);
+  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p, &bs};
+  cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM kernel launch");
   return CPG_OK;
 }
@@ -630,7 +678,7 @@ int cpg_max_active_clusters(int32_t cluster_size, int32_t* out) {
     return fail(CPG_ERR_UNSUPPORTED, "cluster size must be 1..4, got %d", cluster_size);
   Variant v;
   const int cg = (cluster_size % 2 == 0) ? 2 : 1;
-  find_variant(256, cg, CPG_DTYPE_BF16, CPG_DTYPE_BF16, &v);
+  find_variant(256, cg, CPG_DTYPE_BF16, CPG_DTYPE_BF16, CPG_SCALE_TENSOR, &v);
   const int smem = v.smem_bytes(4, 2, 0);
   int cm = cluster_size >= 2 ? 2 : 1;
   int cn = cluster_size == 4 ? 2 : (cluster_size == 3 ? 3 : 1);

@@ -102,7 +102,12 @@ struct GemmParams {
   int32_t trace_stride;
   int32_t* status;        // device status word (0 = ok)
   uint64_t timeout_ns;
+  int32_t fault_inject;   // test hook: kInjectSkipLoads makes the producer issue no loads
 };
+
+// Host-selected fault injection for testing the bounded waits: with kInjectSkipLoads the
+// producer issues nothing, so the MMA warp's first `full` wait must run out its deadline.
+constexpr int32_t kInjectSkipLoads = 1;
 
 template <int BN, int CtaGroup>
 struct GemmSmem {
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, stages, base, full_bar, empty_bar, rank, leader, ctx);
     }

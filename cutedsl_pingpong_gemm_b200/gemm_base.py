@@ -78,7 +78,7 @@ class CompiledGemm:
         self.gemm = gemm
         self._plans = {}
 
-    def _plan(self, a, b, c):
+    def _plan(self, a, b, c, scale_mode: int = 0):
         import torch
         gemm = self.gemm
         ab_codes, d_codes = _dtype_tables()
@@ -107,19 +107,22 @@ class CompiledGemm:
         lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()
         dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
-        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d)
+        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode)
         plan = self._plans.get(key)
         if plan is None:
-            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d)
+            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode)
             self._plans[key] = plan
         return plan
 
-    def plan_for(self, a, b, c) -> "_Plan":
-        return self._plan(a, b, c)
+    def plan_for(self, a, b, c, scale_mode: int = 0) -> "_Plan":
+        return self._plan(a, b, c, scale_mode)
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
                  scale_b=None):
-        plan = self._plan(a, b, c)
+        # More than one scale per operand selects the block-scaled FP8 kernel (A: 1 x 128,
+        # B: 128 x 128 blocks, layouts of cpgemm.h); one value each is a per-tensor scale.
+        block = scale_a is not None and scale_a.numel() > 1
+        plan = self._plan(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR)
         plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
         return None
 
@@ -127,12 +130,14 @@ class CompiledGemm:
 class _Plan:
     """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
 
-    def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d):
+    def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d,
+                 scale_mode=0):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
         self.device = device
+        self.scale_mode = scale_mode
         cfg = gemm._config_c()
-        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d)
+        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode)
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -168,6 +173,11 @@ class _Plan:
     def set_timeout_ms(self, ms: int) -> None:
         _lib.check(self.lib.cpg_gemm_set_timeout_ms(self.handle, int(ms)), "set_timeout_ms")
 
+    def set_fault_injection(self, flags: int) -> None:
+        """Test hook (see cpg_gemm_set_fault_injection): 1 = producer issues no loads."""
+        _lib.check(self.lib.cpg_gemm_set_fault_injection(self.handle, int(flags)),
+                   "set_fault_injection")
+
     def status(self) -> int:
         s = ctypes.c_int32()
         rc = self.lib.cpg_gemm_status(self.handle, ctypes.byref(s))
@@ -186,10 +196,17 @@ class _Plan:
             if bias.stride(-1) != 1:
                 raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED, "bias must be contiguous")
         scales = []
+        if self.scale_mode == _lib.CPG_SCALE_BLOCK:
+            nkb, nnb = -(-self.k // 128), -(-self.n // 128)
+            want = {"scale_a": (nkb, self.m), "scale_b": (nnb, nkb)}
+        else:
+            want = {"scale_a": (1,), "scale_b": (1,)}
         for name, sc in (("scale_a", scale_a), ("scale_b", scale_b)):
-            if sc is not None and not (sc.is_cuda and sc.dtype == torch.float32 and sc.numel() == 1):
+            if sc is not None and not (sc.is_cuda and sc.dtype == torch.float32 and sc.is_contiguous()
+                                       and sc.numel() == math.prod(want[name])):
                 raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
-                                    f"{name} must be a one-element float32 CUDA tensor")
+                                    f"{name} must be a contiguous float32 CUDA tensor of shape "
+                                    f"{want[name]}")
             scales.append(None if sc is None else sc.data_ptr())
         epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales)
         st = _stream_handle(stream, c.device)

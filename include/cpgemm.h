@@ -55,6 +55,13 @@ extern "C" {
 #define CPG_DTYPE_E4M3 1
 #define CPG_DTYPE_F32 2
 
+/* FP8 scale modes.  TENSOR: optional per-tensor scales (cpg_epilogue.scale_a / scale_b point to
+ * one fp32 each).  BLOCK: scale_a points to A's 1 x 128 scales laid out [ceil(K/128)][M] and
+ * scale_b to B's 128 x 128 scales laid out [ceil(N/128)][ceil(K/128)] (both fp32); requires
+ * tile_n = 128 and BF16 output. */
+#define CPG_SCALE_TENSOR 0
+#define CPG_SCALE_BLOCK 1
+
 /* Raster order of the tile scheduler (tile_scheduler.py:24-27). */
 #define CPG_RASTER_ALONG_M 0
 #define CPG_RASTER_ALONG_N 1
@@ -98,6 +105,7 @@ typedef struct cpg_gemm_problem {
   int64_t lda, ldb, ldd; /* row strides in elements */
   int32_t dtype_ab;      /* CPG_DTYPE_BF16 or CPG_DTYPE_E4M3 (A and B share one type) */
   int32_t dtype_d;       /* CPG_DTYPE_BF16, or CPG_DTYPE_F32 for split-K partials */
+  int32_t scale_mode;    /* CPG_SCALE_TENSOR, or CPG_SCALE_BLOCK for block-scaled E4M3 */
 } cpg_gemm_problem;
 
 /* Per-call epilogue options: D = alpha * s_a * s_b * (A . B^T) + bias, rounded to D's type.
@@ -143,6 +151,13 @@ int cpg_gemm_set_trace(cpg_gemm* g, int32_t* device_buf, int32_t tiles_per_cta);
 
 /* Per-wait deadline of the kernel in milliseconds (default 10000). */
 int cpg_gemm_set_timeout_ms(cpg_gemm* g, int32_t timeout_ms);
+
+/* Test hook for the kernel's bounded waits.  CPG_INJECT_SKIP_LOADS makes the next launches'
+ * producer issue no loads, so the MMA warp's first wait runs out its deadline: the kernel then
+ * records the wait site in the status word, stops every role, frees TMEM and returns (no GPU
+ * fault, the context stays usable).  0 restores normal operation. */
+#define CPG_INJECT_SKIP_LOADS 1
+int cpg_gemm_set_fault_injection(cpg_gemm* g, int32_t flags);
 
 /* Read and clear the plan's device status word (synchronises the device).  *status receives 0 or
  * 0x100 | wait-site; the return value is CPG_ERR_DEVICE_TIMEOUT when it was nonzero. */

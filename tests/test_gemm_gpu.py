@@ -311,3 +311,52 @@ def test_fp32_output(cluster, tile_n):
     s = gemm_ref.abs_product(a, b)
     # fp32 output: no output rounding term, only the accumulation bound.
     assert bool(((d.cpu() - r).abs() <= k * gemm_ref.ACC_SLACK_PER_K * s + 1e-6).all())
+
+
+# ---------------------------------------------------------------- FP8 E4M3 (block scales)
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("shape", [(128, 128, 128), (256, 384, 1024), (300, 264, 1000 + 8),
+                                   (1024, 1024, 2048)])
+def test_fp8_block_scaled(shape, cluster):
+    """BASELINE config 4 (block variant): A scaled per 1x128, B per 128x128, against the fp32
+    product of the block-dequantised operands."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, generator=g) * torch.rand(m, 1, generator=g) * 4
+    b = torch.randn(n, k, generator=g) * torch.rand(n, 1, generator=g) * 4
+    qa, sa = gemm_ref.quantize_e4m3_blocks(a, (1, 128))
+    qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
+    d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    gemm = make_gemm(128, cluster)
+    gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda())
+    torch.cuda.synchronize()
+    da = gemm_ref.dequantize_blocks(qa, sa, (1, 128))
+    db = gemm_ref.dequantize_blocks(qb, sb, (128, 128))
+    res = gemm_ref.check(d.cpu(), da, db, frob_tol=gemm_ref.FROB_TOL_FP8)
+    assert res["ok"], res
+    assert res["frob"] < 1e-2
+
+
+def test_fp8_block_scaled_many_tiles_per_cta():
+    """Persistent CTAs with several tiles each (partial-buffer phases wrap many times)."""
+    m, n, k = 2048, 2048, 512
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(m, k, generator=g)
+    b = torch.randn(n, k, generator=g)
+    qa, sa = gemm_ref.quantize_e4m3_blocks(a, (1, 128))
+    qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
+    d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    gemm = make_gemm(128, (2, 1, 1), stages=6)
+    gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda())
+    torch.cuda.synchronize()
+    rows = torch.arange(0, m, 7)
+    res = gemm_ref.check(d.cpu()[rows], gemm_ref.dequantize_blocks(qa, sa, (1, 128)),
+                         gemm_ref.dequantize_blocks(qb, sb, (128, 128)), rows=rows,
+                         frob_tol=gemm_ref.FROB_TOL_FP8)
+    assert res["ok"], res
+
+
+def test_many_tiles_per_cta_bf16():
+    """Persistent CTAs with many tiles (both TMEM accumulators reused many times)."""
+    for cluster in ((1, 1, 1), (2, 1, 1)):
+        run_and_check(2048, 4096, 256, make_gemm(128, cluster, stages=6))
