@@ -31,7 +31,7 @@ CPG_SCALE_BLOCK = 1
 
 CPG_INJECT_SKIP_LOADS = 1
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class CpgError(RuntimeError):
@@ -80,7 +80,7 @@ class GemmProblemC(ctypes.Structure):
         ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
         ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldd", ctypes.c_int64),
         ("dtype_ab", ctypes.c_int32), ("dtype_d", ctypes.c_int32),
-        ("scale_mode", ctypes.c_int32),
+        ("scale_mode", ctypes.c_int32), ("split_k", ctypes.c_int32),
     ]
 
 

@@ -240,6 +240,9 @@ struct cpg_gemm {
   int32_t trace_stride;
   uint64_t timeout_ns;
   int32_t fault_inject;
+  int32_t k_iters;
+  int32_t k_iters_per_split;
+  int32_t splits;
   bool maps_valid;
   const void* map_a_ptr;
   const void* map_b_ptr;
@@ -249,7 +252,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 5; }
+int cpg_abi_version(void) { return 6; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -366,6 +369,9 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                 cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);
   if (v.scale_mode == CPG_SCALE_BLOCK && cfg->reuse_ab)
     return fail(CPG_ERR_UNSUPPORTED, "reuse_ab is not implemented for block-scaled FP8");
+  if (prob->split_k < 0) return fail(CPG_ERR_INVALID_SHAPE, "split_k must be >= 0");
+  if (prob->split_k > 1 && (prob->dtype_d != CPG_DTYPE_F32 || v.scale_mode != CPG_SCALE_TENSOR))
+    return fail(CPG_ERR_UNSUPPORTED, "split_k > 1 accumulates into an FP32 D (no block scales)");
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -389,7 +395,16 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
 
   const int64_t ntm = prob->m > 0 ? (prob->m + 127) / 128 : 1;
   const int64_t ntn = prob->n > 0 ? (prob->n + cfg->tile_n - 1) / cfg->tile_n : 1;
-  g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn), 1,
+  // Split-K: the L index of the scheduler selects a K range of k_iters_per_split k-blocks;
+  // every split is non-empty.
+  const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
+  g->k_iters = static_cast<int32_t>((prob->k + bk - 1) / bk);
+  int32_t splits = prob->split_k > 1 ? prob->split_k : 1;
+  if (splits > g->k_iters && g->k_iters > 0) splits = g->k_iters;
+  g->k_iters_per_split = g->k_iters > 0 ? (g->k_iters + splits - 1) / splits : 0;
+  g->splits = g->k_iters_per_split > 0
+                  ? (g->k_iters + g->k_iters_per_split - 1) / g->k_iters_per_split : 1;
+  g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn), g->splits,
                                       cfg->raster_order, cfg->group_size, cfg->cluster_m,
                                       cfg->cluster_n, cfg->is_persistent);
   int32_t grid[3];
@@ -545,7 +560,9 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.m = static_cast<int32_t>(pr.m);
   p.n = static_cast<int32_t>(pr.n);
   p.k = static_cast<int32_t>(pr.k);
-  p.k_iters = static_cast<int32_t>((pr.k + bk - 1) / bk);
+  p.k_iters = g->k_iters;
+  p.k_iters_per_split = g->k_iters_per_split;
+  p.reduce_add = g->splits > 1 ? 1 : 0;
   p.ab_stages = g->cfg.ab_stage;
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
@@ -568,6 +585,11 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.timeout_ns = g->timeout_ns;
   p.fault_inject = g->fault_inject;
 
+  if (g->splits > 1) {
+    // The splits add their partial sums into D.
+    cudaError_t e = cudaMemset2DAsync(d, pr.ldd * ed, 0, pr.n * ed, pr.m, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(D)");
+  }
   cudaLaunchConfig_t lc = {};
   cudaLaunchAttribute attr[1];
   lc.gridDim = dim3(g->grid[0], g->grid[1], g->grid[2]);

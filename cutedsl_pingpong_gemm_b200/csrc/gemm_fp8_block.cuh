@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 0) {
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<kBlockBN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
-          &tm_a, &tm_b, sp, k_iters, stages, base, full_bar, empty_bar, rank, leader, ctx);
+          &tm_a, &tm_b, sp, k_iters, k_iters, stages, base, full_bar, empty_bar, rank, leader,
+          ctx);
     }
     __syncwarp();
   } else if (warp == 1) {

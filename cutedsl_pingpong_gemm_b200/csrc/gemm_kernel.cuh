@@ -90,7 +90,9 @@ enum WaitSite : int32_t {
 struct GemmParams {
   SchedParams sched;
   int32_t m, n, k;
-  int32_t k_iters;        // ceil(K / 64)
+  int32_t k_iters;        // k-blocks of the whole K: ceil(K / BK)
+  int32_t k_iters_per_split;  // k-blocks per L index (split-K); == k_iters without splitting
+  int32_t reduce_add;     // epilogue adds into D (fp32 split-K partial sums) instead of storing
   int32_t ab_stages;
   int32_t epi_stages;
   int32_t reuse_ab;       // epilogue staging aliases the A/B stages (single-tile CTAs only)
@@ -154,7 +156,11 @@ __device__ __forceinline__ WorkIter make_work_iter(const SchedParams& sp) {
     it.cid = static_cast<int32_t>(blockIdx.z);
     it.stride = static_cast<int32_t>(gridDim.z);
   } else {
-    it.cid = static_cast<int32_t>(ptx::clusterid_x() + ptx::clusterid_y() * ptx::nclusterid_x());
+    // tile_scheduler.py:100-102 (clusterid.x + clusterid.y * nclusterid.x), extended by the
+    // grid's z (the L index) so that L > 1 launches cover every (tile, L) pair once.
+    it.cid = static_cast<int32_t>(ptx::clusterid_x() +
+                                  ptx::nclusterid_x() * (ptx::clusterid_y() +
+                                                         ptx::nclusterid_y() * ptx::clusterid_z()));
     it.stride = 0;
   }
   it.total = sched_total_clusters(sp);
@@ -163,12 +169,30 @@ __device__ __forceinline__ WorkIter make_work_iter(const SchedParams& sp) {
   return it;
 }
 
+// Linear cluster id -> (pid_m, pid_n, l).  The id is first split into the L index and the id
+// within one problem with the reference's dm_clusters_per_problem (tile_scheduler.py:70, which
+// the reference computes but never applies); for L = 1 this is the identity and the map is the
+// reference's _map_cta_coords (tile_scheduler.py:125-146).
 __device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t cid,
-                                                 int32_t& pid_m, int32_t& pid_n) {
-  int32_t cm, cn;
-  sched_map_cluster(sp, cid, cm, cn);
+                                                 int32_t& pid_m, int32_t& pid_n, int32_t& l) {
+  int32_t cid_in_problem, cm, cn;
+  fast_divmod(sp.dm_clusters_per_problem, cid, l, cid_in_problem);
+  sched_map_cluster(sp, cid_in_problem, cm, cn);
   pid_m = cm * sp.cluster_m + static_cast<int32_t>(ptx::cluster_ctaid_x());
   pid_n = cn * sp.cluster_n + static_cast<int32_t>(ptx::cluster_ctaid_y());
+}
+
+__device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t cid,
+                                                 int32_t& pid_m, int32_t& pid_n) {
+  int32_t l;
+  work_tile_coords(sp, cid, pid_m, pid_n, l);
+}
+
+// k-block range [kb0, kb1) of L index l.
+__device__ __forceinline__ void split_k_range(const GemmParams& p, int32_t l, int& kb0, int& kb1) {
+  kb0 = l * p.k_iters_per_split;
+  kb1 = kb0 + p.k_iters_per_split;
+  if (kb1 > p.k_iters) kb1 = p.k_iters;
 }
 
 __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
@@ -185,7 +209,8 @@ __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
 // every tile of this CTA into the shared-memory stage ring, then drains its in-flight loads.
 template <int BN, int CtaGroup, int kBK, int kStageBytes, int kAStageBytes>
 __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUtensorMap* tm_b,
-                                              const SchedParams& sp, int k_iters, int stages,
+                                              const SchedParams& sp, int k_iters,
+                                              int k_iters_per_split, int stages,
                                               uint32_t base, uint32_t full_bar, uint32_t empty_bar,
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx) {
@@ -200,11 +225,13 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t fills = 0;
   bool ok = true;
   for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
-    int32_t pid_m, pid_n;
-    work_tile_coords(sp, it.cid, pid_m, pid_n);
+    int32_t pid_m, pid_n, l;
+    work_tile_coords(sp, it.cid, pid_m, pid_n, l);
     const int32_t a_row = pid_m * kBM;
     const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBNc;
-    for (int kb = 0; kb < k_iters; ++kb) {
+    const int kb0 = l * k_iters_per_split;
+    const int kb1 = kb0 + k_iters_per_split < k_iters ? kb0 + k_iters_per_split : k_iters;
+    for (int kb = kb0; kb < kb1; ++kb) {
       if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
         ok = false;
         break;
@@ -332,7 +359,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
-          &tm_a, &tm_b, sp, k_iters, stages, base, full_bar, empty_bar, rank, leader, ctx);
+          &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
+          leader, ctx);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -344,13 +372,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+        int32_t pid_m, pid_n, l;
+        work_tile_coords(sp, it.cid, pid_m, pid_n, l);
+        int kb0, kb1;
+        split_k_range(p, l, kb0, kb1);
         if (!ptx::mbar_wait(tempty_bar + 8u * acc, acc_phase ^ 1u, ctx, kSiteMmaTmemEmpty)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < k_iters; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
             ok = false;
             break;
@@ -366,11 +398,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if constexpr (OT::kFp8) {
               ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
                                         db + static_cast<uint64_t>(2 * k), kIdesc,
-                                        (kb > 0 || k > 0) ? 1u : 0u);
+                                        (kb > kb0 || k > 0) ? 1u : 0u);
             } else {
               ptx::umma_f16_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
                                          db + static_cast<uint64_t>(2 * k), kIdesc,
-                                         (kb > 0 || k > 0) ? 1u : 0u);
+                                         (kb > kb0 || k > 0) ? 1u : 0u);
             }
           }
           const uint32_t eb = empty_bar + 8u * stage;
@@ -417,8 +449,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (p.scale_b != nullptr) alpha *= *p.scale_b;
     const bool has_bias = p.bias != nullptr;
     for (WorkIter it = make_work_iter(sp); it.valid(); it.advance()) {
-      int32_t pid_m, pid_n;
-      work_tile_coords(sp, it.cid, pid_m, pid_n);
+      int32_t pid_m, pid_n, l;
+      work_tile_coords(sp, it.cid, pid_m, pid_n, l);
+      const bool add_bias = has_bias && l == 0;  // split-K: the bias enters the sum once
       bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -460,7 +493,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         float x[kStoreCols];
 #pragma unroll
         for (int j = 0; j < kStoreCols; ++j) x[j] = __uint_as_float(v[j]) * alpha;
-        if (has_bias) {
+        if (add_bias) {
           // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
           // they are broadcast across the warp with shuffles.
 #pragma unroll
@@ -495,7 +528,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         __syncwarp();
         if (lane == 0) {
           // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
-          if (g_row < p.m && col0 < p.n) ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+          if (g_row < p.m && col0 < p.n) {
+            if (p.reduce_add) {
+              ptx::tma_reduce_add_2d(&tm_d, sbuf, col0, g_row);
+            } else {
+              ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+            }
+          }
           ptx::bulk_commit_group();
         }
         __syncwarp();

@@ -183,6 +183,27 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src,
                : "memory");
 }
 
+// Element-wise add of a shared-memory box into global memory (fp32 split-K accumulation in L2).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t src, int32_t x,
+                                                  int32_t y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t clusterid_z() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.z;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t nclusterid_y() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.y;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -78,7 +78,7 @@ class CompiledGemm:
         self.gemm = gemm
         self._plans = {}
 
-    def _plan(self, a, b, c, scale_mode: int = 0):
+    def _plan(self, a, b, c, scale_mode: int = 0, split_k: int = 1):
         import torch
         gemm = self.gemm
         ab_codes, d_codes = _dtype_tables()
@@ -107,22 +107,23 @@ class CompiledGemm:
         lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()
         dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
-        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode)
+        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k)
         plan = self._plans.get(key)
         if plan is None:
-            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode)
+            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k)
             self._plans[key] = plan
         return plan
 
-    def plan_for(self, a, b, c, scale_mode: int = 0) -> "_Plan":
-        return self._plan(a, b, c, scale_mode)
+    def plan_for(self, a, b, c, scale_mode: int = 0, split_k: int = 1) -> "_Plan":
+        return self._plan(a, b, c, scale_mode, split_k)
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-                 scale_b=None):
+                 scale_b=None, split_k: int = 1):
         # More than one scale per operand selects the block-scaled FP8 kernel (A: 1 x 128,
         # B: 128 x 128 blocks, layouts of cpgemm.h); one value each is a per-tensor scale.
         block = scale_a is not None and scale_a.numel() > 1
-        plan = self._plan(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR)
+        plan = self._plan(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR,
+                          int(split_k))
         plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
         return None
 
@@ -131,13 +132,13 @@ class _Plan:
     """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
 
     def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d,
-                 scale_mode=0):
+                 scale_mode=0, split_k=1):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
         self.device = device
         self.scale_mode = scale_mode
         cfg = gemm._config_c()
-        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode)
+        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode, split_k)
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -306,10 +307,11 @@ class GemmSM90:
         return compiled
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-                 scale_b=None):
+                 scale_b=None, split_k: int = 1):
         if self._compiled is None:
             self._compiled = CompiledGemm(self)
-        self._compiled(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
+        self._compiled(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b,
+                       split_k=split_k)
 
 
 # The B200 name of the same operator.

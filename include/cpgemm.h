@@ -106,6 +106,9 @@ typedef struct cpg_gemm_problem {
   int32_t dtype_ab;      /* CPG_DTYPE_BF16 or CPG_DTYPE_E4M3 (A and B share one type) */
   int32_t dtype_d;       /* CPG_DTYPE_BF16, or CPG_DTYPE_F32 for split-K partials */
   int32_t scale_mode;    /* CPG_SCALE_TENSOR, or CPG_SCALE_BLOCK for block-scaled E4M3 */
+  int32_t split_k;       /* 0 or 1: none; S > 1: K is cut into S ranges scheduled as the L
+                            dimension, and the ranges add their FP32 partial sums into D
+                            (dtype_d must be CPG_DTYPE_F32; D is cleared by cpg_gemm_run) */
 } cpg_gemm_problem;
 
 /* Per-call epilogue options: D = alpha * s_a * s_b * (A . B^T) + bias, rounded to D's type.

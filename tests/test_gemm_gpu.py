@@ -360,3 +360,34 @@ def test_many_tiles_per_cta_bf16():
     """Persistent CTAs with many tiles (both TMEM accumulators reused many times)."""
     for cluster in ((1, 1, 1), (2, 1, 1)):
         run_and_check(2048, 4096, 256, make_gemm(128, cluster, stages=6))
+
+
+# ---------------------------------------------------------------- split-K inside one GPU (L dim)
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("split_k,persistent", [(2, True), (3, True), (7, True), (4, False)])
+def test_split_k_fp32(split_k, persistent, cluster):
+    """K cut into split_k ranges scheduled as the L dimension, partial sums added into FP32 D."""
+    m, n, k = 256, 640, 64 * 21 + 8
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=split_k, with_bias=True)
+    d = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    gemm = make_gemm(128, cluster, persistent=persistent)
+    gemm(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=split_k)
+    torch.cuda.synchronize()
+    r = gemm_ref.reference(a, b, bias)
+    s = gemm_ref.abs_product(a, b)
+    bound = k * gemm_ref.ACC_SLACK_PER_K * s + 2.0 ** -23 * bias.float().abs() + 1e-6
+    assert bool(((d.cpu() - r).abs() <= bound).all())
+
+
+def test_split_k_small_m_then_cast():
+    """Decode-like M: split-K partial sums in FP32, then the BF16 cast kernel (with bias)."""
+    from cutedsl_pingpong_gemm_b200.quant import cast_f32_bf16
+    m, n, k = 64, 8192, 8192
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=9, b_scale=k ** -0.5, with_bias=True)
+    d32 = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    gemm = make_gemm(64, (1, 1, 1), stages=8)
+    gemm(a.cuda(), b.cuda(), d32, None, split_k=4)
+    out = cast_f32_bf16(d32, bias.cuda())
+    torch.cuda.synchronize()
+    res = gemm_ref.check(out.cpu(), a, b, bias=bias)
+    assert res["ok"], res
