@@ -50,6 +50,10 @@ WORKLOADS = {
                 m_is_per_gpu=True, fp8="tensor"),
     "fp8_block": dict(m=16384, n=8192, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
                       m_is_per_gpu=True, fp8="block"),
+    # Tall K: M = N = 2048, K = 131072 split over the GPUs (and inside each GPU); fp32 partials
+    # reduced with one NCCL reduce-scatter, then cast to BF16 (strong scaling).
+    "tallk": dict(m=2048, n=2048, k=131072, a_scale=1.0, b_scale=131072 ** -0.5, bias=False,
+                  m_is_per_gpu=False, fp8=None, split="k"),
 }
 
 
@@ -278,7 +282,87 @@ def metric_name(workload):
             "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)",
             "fp8": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, per-tensor scales)",
             "fp8_block": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, 1x128 / 128x128 block scales)",
+            "tallk": "GEMM TFLOPS (BF16 2048x2048x131072 split-K over GPUs, NCCL reduce-scatter)",
             }[workload]
+
+
+# ------------------------------------------------------------------ GPU arm: tall-K split-K
+def run_tallk(args, world, rank, local):
+    """Split-K over GPUs: rank r multiplies its K range (and splits it again inside the GPU)
+    into fp32 partials, one NCCL reduce-scatter sums them, the cast kernel writes BF16 rows."""
+    import torch
+    from cutedsl_pingpong_gemm_b200 import GemmSM90, RasterOrder
+    from cutedsl_pingpong_gemm_b200.sharding import SplitKGemm, k_ranges, row_range
+
+    w = WORKLOADS[args.workload]
+    m, n, k = w["m"], w["n"], w["k"]
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    ks, ke = k_ranges(k, world)[rank]
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    a_k = (torch.randn(m, ke - ks, generator=gen, device=dev) * w["a_scale"]).to(torch.bfloat16)
+    b_k = (torch.randn(n, ke - ks, generator=gen, device=dev) * w["b_scale"]).to(torch.bfloat16)
+    tile_n = args.tile_n
+    cm = args.cluster_m
+    stages = args.stages or (6 if cm == 2 else 4)
+    gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
+                    cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
+                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
+    tiles = -(-m // 128) * -(-n // tile_n)
+    kblocks = -(-(ke - ks) // 64)
+    local_split = max(1, min(kblocks // 8, round(4 * 148 / tiles)))
+    sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=local_split)
+
+    launches = [0]
+
+    def step():
+        out = sk(a_k, b_k, m, n)
+        launches[0] += 2  # GEMM + cast (the memset and NCCL kernels are not ours)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches[0] = 0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sampler.stop()
+    barrier(world)
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = reduce_max(ms_local, world)
+    total_flops = 2.0 * m * n * k
+    value = total_flops / (ms * 1e-3) / 1e12
+    peaks, peak_src = load_peaks()
+    if rank == 0:
+        s0, s1 = row_range(m, world, rank)
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "m": m, "n": n, "k": k,
+                       "parallelism": f"split-K x{world} (NCCL reduce-scatter) x{local_split} in-GPU",
+                       "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
+                       "rows_per_rank": s1 - s0, "l2": "inputs 512 MiB per rank at 1 GPU; no flush"},
+            "roofline": {"bound": "tensor", "achieved": total_flops / world / (ms_local * 1e-3) / 1e12,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": total_flops / world / (ms_local * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                         "peak_source": f"{peak_src} bf16_tflops", "traffic": None,
+                         "note": "achieved covers GEMM + reduce-scatter + cast per step"},
+            "clocks": sampler.summary(), "gpu_launches": launches[0] * world, "e2e": None,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    del out
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -453,7 +537,10 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
-        run_cpg(args, world, rank, local)
+        if WORKLOADS[args.workload].get("split") == "k":
+            run_tallk(args, world, rank, local)
+        else:
+            run_cpg(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -100,9 +100,11 @@ class CompiledGemm:
             if t.numel() > 0 and not t.is_cuda:
                 raise _lib.CpgError(_lib.CPG_ERR_NO_DEVICE, f"{name} must be a CUDA tensor")
         def row_stride(t, rows, cols):
-            # A single-row tensor's row stride is never used; give the row length padded to 16 B.
+            # A single-row or empty tensor's row stride is never used; give the padded row length.
             per16 = 16 // t.element_size()
-            return t.stride(0) if rows > 1 else max(per16, -(-cols // per16) * per16)
+            if rows > 1 and cols > 0:
+                return t.stride(0)
+            return max(per16, -(-cols // per16) * per16)
 
         lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()

@@ -54,6 +54,10 @@ def reduce_scatter_rows(partial, world: int, group=None):
     rank = dist.get_rank(group)
     per = max(row_range(m, world, r)[1] - row_range(m, world, r)[0] for r in range(world))
     if dist.get_backend(group) == "nccl":
+        if per * world == m:  # equal shards: reduce-scatter straight from the partial
+            out = partial.new_empty((per, n))
+            dist.reduce_scatter_tensor(out, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
+            return out
         padded = partial.new_zeros((per * world, n))
         for r in range(world):
             s, e = row_range(m, world, r)
@@ -87,9 +91,30 @@ class MShardedGemm:
 class SplitKGemm:
     """Split-K across ranks with an NCCL reduce-scatter of fp32 partials.
 
-    ``partial_fn(a_k, b_k) -> fp32 [M, N]`` computes one rank's partial product; on GPUs it is
-    the sm_100a GEMM with an fp32 epilogue (``gemm_base.GemmSM90.partial``).
+    ``partial_fn(a_k, b_k) -> fp32 [M, N]`` computes one rank's partial product and ``cast_fn``
+    turns the reduced fp32 rows into the output; ``SplitKGemm.on_gpu`` builds both from the
+    sm_100a kernels (FP32-epilogue GEMM, ``cpg_cast_f32_bf16``).
     """
+
+    @staticmethod
+    def on_gpu(gemm, world: int, rank: int, group=None, bias=None, local_split_k: int = 1):
+        """GPU instance: partials by ``gemm`` (a GemmSM90) into FP32, cast to BF16 (+ bias).
+
+        ``local_split_k`` additionally splits each rank's K range inside the GPU (the kernel's
+        L dimension) when the per-rank problem has too few tiles to fill the SMs.
+        """
+        import torch
+        from .quant import cast_f32_bf16
+
+        def partial(a_k, b_k):
+            out = torch.empty(a_k.shape[0], b_k.shape[0], dtype=torch.float32, device=a_k.device)
+            gemm(a_k, b_k, out, None, split_k=local_split_k)
+            return out
+
+        def cast(rows):
+            return cast_f32_bf16(rows, bias)
+
+        return SplitKGemm(world, rank, partial, cast, group)
 
     def __init__(self, world: int, rank: int, partial_fn: Callable, cast_fn: Optional[Callable] = None,
                  group=None):
@@ -108,5 +133,5 @@ class SplitKGemm:
         partial = self.partial_fn(a_k, b_k)
         if tuple(partial.shape) != (m, n):
             raise ValueError(f"partial has shape {tuple(partial.shape)}, expected {(m, n)}")
-        rows = reduce_scatter_rows(partial, self.world, self.group)
+        rows = partial if self.world == 1 else reduce_scatter_rows(partial, self.world, self.group)
         return self.cast_fn(rows) if self.cast_fn is not None else rows

@@ -158,7 +158,7 @@ def test_non_persistent(persistent, reuse_ab, cluster):
     run_and_check(640, 1536, 320, gemm)
 
 
-@pytest.mark.parametrize("stages,epi_stage", [(1, 1), (2, 2), (3, 1), (6, 4)])
+@pytest.mark.parametrize("stages,epi_stage", [(1, 1), (2, 2), (3, 1), (4, 4), (5, 2)])
 def test_pipeline_depths(stages, epi_stage):
     gemm = make_gemm(128, (1, 1, 1), stages=stages, epi_stage=epi_stage)
     run_and_check(512, 512, 1024, gemm)
