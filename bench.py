@@ -519,7 +519,8 @@ def run_cpg(args, world, rank, local):
                                             if w["fp8"] is None else None),
                          "traffic": load_traffic(args.workload),
                          "algorithmic_flops_per_launch": flops_per_gpu,
-                         "kernel": "cpg::gemm_bf16_sm100_kernel"},
+                         "kernel": ("cpg::gemm_fp8_block_kernel" if w["fp8"] == "block"
+                                    else "cpg::gemm_sm100_kernel")},
             "clocks": clocks,
             "gpu_launches": n_launch * world,
             "e2e": e2e,
