@@ -118,6 +118,8 @@ SIGNATURES = {
     "cpg_quantize_e4m3": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i32, _i32,
                                          _vp]),
     "cpg_cast_f32_bf16": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "cpg_gemm_splitk_static": (ctypes.c_int, [_P(GemmConfigC), _P(GemmProblemC), _vp, _vp, _vp,
+                                              _P(EpilogueC), _vp]),
     "cpg_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "cpg_last_error_message": (ctypes.c_char_p, []),
     "cpg_abi_version": (ctypes.c_int, []),

@@ -783,3 +783,186 @@ int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, v
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Split-K GEMM with BF16 output that allocates no device memory (cpg_gemm_splitk_static).
+//
+// The split-K path needs an FP32 buffer of M x N partial sums between the GEMM (whose K ranges
+// add into it with TMA reduce-add) and the cast to BF16.  Callers that cannot allocate device
+// memory (for example an embedding runtime whose device memory is carved up in advance, or
+// code that must not call cudaMalloc while other work is being captured into a CUDA graph)
+// get that buffer from this file-scope array instead.  Every GPU that loads the library holds
+// the array until the process exits.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB: M * N <= 4,194,304 fp32
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) float g_splitk_scratch[kStaticScratchBytes / sizeof(float)];
+
+std::mutex g_static_mu;
+void* g_static_scratch_addr[kStaticMaxDevices];  // device address of the array, per device
+
+// Device address of g_splitk_scratch on the current device.  The array's name in host code is
+// only a stand-in; the address must come from cudaGetSymbolAddress with the device current,
+// once per device (the first call on a device also loads the module there).
+int static_scratch_address(int dev, float** out) {
+  if (dev < 0 || dev >= kStaticMaxDevices) return fail(CPG_ERR_NO_DEVICE, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_splitk_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static split-K scratch)");
+    g_static_scratch_addr[dev] = ptr;
+  }
+  *out = static_cast<float*>(g_static_scratch_addr[dev]);
+  return CPG_OK;
+}
+
+}  // namespace
+
+extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob,
+                                      const void* a, const void* b, void* d,
+                                      const cpg_epilogue* epi, void* stream) {
+  if (cfg == nullptr || prob == nullptr) return fail(CPG_ERR_NULL, "cfg and prob must be non-NULL");
+  int rc = cpg_config_validate(cfg);
+  if (rc != CPG_OK) return rc;
+  if (cfg->tile_m != 128 || (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256) ||
+      cfg->cluster_m > 2 || cfg->cluster_n > 2 || cfg->ab_stage > cpg::kMaxStages ||
+      cfg->epi_stage > cpg::kMaxEpiStages || cfg->gemm_n_prologue >= cfg->ab_stage)
+    return fail(CPG_ERR_UNSUPPORTED, "tile (128, 64/128/256), cluster within (2, 2, 1) only");
+  if (prob->dtype_ab != CPG_DTYPE_BF16 && prob->dtype_ab != CPG_DTYPE_E4M3)
+    return fail(CPG_ERR_DTYPE, "A and B must be BF16 or FP8 E4M3");
+  if (prob->dtype_d != CPG_DTYPE_BF16) return fail(CPG_ERR_DTYPE, "D must be BF16");
+  if (prob->scale_mode != CPG_SCALE_TENSOR)
+    return fail(CPG_ERR_UNSUPPORTED, "block-scaled FP8 is not available on this entry point");
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (prob->m < 0 || prob->n < 0 || prob->k < 0 || prob->m > lim || prob->n > lim ||
+      prob->k > lim || prob->lda < prob->k || prob->ldb < prob->k || prob->ldd < prob->n ||
+      prob->split_k < 0)
+    return fail(CPG_ERR_INVALID_SHAPE, "bad extents or strides");
+  const int eab = elem_bytes(prob->dtype_ab);
+  if ((prob->lda * eab) % 16 != 0 || (prob->ldb * eab) % 16 != 0 || (prob->ldd * 2) % 16 != 0)
+    return fail(CPG_ERR_ALIGNMENT, "row strides must be multiples of 16 bytes");
+  const int64_t ldw = (prob->n + 3) / 4 * 4;  // FP32 [M, N] rows padded to 16 bytes
+  const int64_t need = prob->m * ldw * static_cast<int64_t>(sizeof(float));
+  if (need > static_cast<int64_t>(kStaticScratchBytes))
+    return fail(CPG_ERR_INVALID_SHAPE,
+                "M x N = %lld x %lld needs %lld bytes of FP32 scratch; the static scratch holds "
+                "%lld bytes (M * round_up(N, 4) <= %lld)",
+                static_cast<long long>(prob->m), static_cast<long long>(prob->n),
+                static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes),
+                static_cast<long long>(kStaticScratchBytes / sizeof(float)));
+  if (prob->m == 0 || prob->n == 0) return CPG_OK;
+  if (d == nullptr) return fail(CPG_ERR_NULL, "D is NULL");
+  if ((reinterpret_cast<uintptr_t>(d) & 15u) != 0) return fail(CPG_ERR_ALIGNMENT, "D alignment");
+  const void* bias = epi != nullptr ? epi->bias : nullptr;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned cast_blocks = static_cast<unsigned>(prob->m < 65535 ? prob->m : 65535);
+
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if (major != 10) return fail(CPG_ERR_NO_DEVICE, "device %d is not sm_100", dev);
+  float* ws = nullptr;
+  rc = static_scratch_address(dev, &ws);
+  if (rc != CPG_OK) return rc;
+
+  if (prob->k == 0) {  // D = bias (or 0): nothing to contract
+    fill_rows_kernel<__nv_bfloat16><<<cast_blocks, 256, 0, st>>>(
+        static_cast<__nv_bfloat16*>(d), prob->m, prob->n, prob->ldd,
+        static_cast<const __nv_bfloat16*>(bias));
+    e = cudaGetLastError();
+    return e == cudaSuccess ? CPG_OK : cuda_fail(e, "fill kernel launch");
+  }
+  if (a == nullptr || b == nullptr) return fail(CPG_ERR_NULL, "A and B must be non-NULL");
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) != 0 || (reinterpret_cast<uintptr_t>(b) & 15u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+
+  // Kernel, shared memory and grid (the same choices cpg_gemm_create makes, kept on the stack).
+  Variant v;
+  const int cta_group = cfg->cluster_m == 2 ? 2 : 1;
+  if (!find_variant(cfg->tile_n, cta_group, prob->dtype_ab, CPG_DTYPE_F32, CPG_SCALE_TENSOR, &v))
+    return fail(CPG_ERR_UNSUPPORTED, "no kernel for this configuration");
+  const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
+  int optin = 0;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem)");
+  if (smem > optin) return fail(CPG_ERR_SMEM, "%d stages need %d bytes", cfg->ab_stage, smem);
+  int mac = 0;
+  rc = query_max_active_clusters(v, smem, cfg->cluster_m, cfg->cluster_n, &mac);
+  if (rc != CPG_OK) return rc;
+  if (mac <= 0) return fail(CPG_ERR_NO_DEVICE, "kernel cannot be resident");
+  const int bk = cpg::kRowBytes / eab;
+  const int32_t k_iters = static_cast<int32_t>((prob->k + bk - 1) / bk);
+  int32_t splits = prob->split_k > 1 ? prob->split_k : 1;
+  if (splits > k_iters) splits = k_iters;
+  const int32_t kps = (k_iters + splits - 1) / splits;
+  splits = (k_iters + kps - 1) / kps;
+  const int32_t ntm = static_cast<int32_t>((prob->m + 127) / 128);
+  const int32_t ntn = static_cast<int32_t>((prob->n + cfg->tile_n - 1) / cfg->tile_n);
+
+  cpg::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.sched = cpg::sched_params_create(ntm, ntn, splits, cfg->raster_order, cfg->group_size,
+                                     cfg->cluster_m, cfg->cluster_n, cfg->is_persistent);
+  int32_t grid[3];
+  cpg::sched_grid_shape(p.sched, mac, grid);
+  p.m = static_cast<int32_t>(prob->m);
+  p.n = static_cast<int32_t>(prob->n);
+  p.k = static_cast<int32_t>(prob->k);
+  p.k_iters = k_iters;
+  p.k_iters_per_split = kps;
+  p.reduce_add = splits > 1 ? 1 : 0;
+  p.ab_stages = cfg->ab_stage;
+  p.epi_stages = cfg->epi_stage;
+  p.reuse_ab = cfg->reuse_ab;
+  p.alpha = epi != nullptr ? epi->alpha : 1.0f;
+  p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
+  p.scale_b = epi != nullptr ? epi->scale_b : nullptr;
+  p.bias = nullptr;      // added once, by the cast
+  p.status = nullptr;    // no status word: a wait past its deadline just stops the kernel
+  p.timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
+
+  CUtensorMap tm_a, tm_b, tm_w;
+  rc = encode_2d(&tm_a, tma_dtype(prob->dtype_ab), eab, a, prob->m, prob->k, prob->lda, cpg::kBM, bk);
+  if (rc != CPG_OK) return rc;
+  rc = encode_2d(&tm_b, tma_dtype(prob->dtype_ab), eab, b, prob->n, prob->k, prob->ldb,
+                 v.bn / v.cta_group, bk);
+  if (rc != CPG_OK) return rc;
+  rc = encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, prob->m, prob->n, ldw, 32,
+                 cpg::kRowBytes / 4);
+  if (rc != CPG_OK) return rc;
+
+  // The array keeps the previous call's sums: clear the region the K ranges add into.
+  if (splits > 1) {
+    e = cudaMemsetAsync(ws, 0, static_cast<size_t>(need), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static scratch)");
+  }
+  cudaLaunchConfig_t lc = {};
+  cudaLaunchAttribute attr[1];
+  lc.gridDim = dim3(grid[0], grid[1], grid[2]);
+  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  if (cfg->cluster_m * cfg->cluster_n > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cfg->cluster_m;
+    attr[0].val.clusterDim.y = cfg->cluster_n;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  cpg::BlockScales unused{nullptr, nullptr};
+  void* args[] = {&tm_a, &tm_b, &tm_w, &p, &unused};
+  e = cudaLaunchKernelExC(&lc, v.fn, args);
+  if (e != cudaSuccess) return cuda_fail(e, "split-K GEMM launch");
+  cpg::cast_f32_bf16_kernel<<<cast_blocks, 256, 0, st>>>(
+      ws, prob->m, prob->n, ldw, static_cast<__nv_bfloat16*>(d), prob->ldd,
+      static_cast<const __nv_bfloat16*>(bias));
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "cast kernel launch");
+}

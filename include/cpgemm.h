@@ -204,6 +204,32 @@ int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols
 int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, void* y,
                       int64_t ldy, const void* bias, void* stream);
 
+/* Split-K GEMM with BF16 output that allocates no device memory.  No counterpart in the
+ * reference: its kernel never needs scratch memory.
+ *
+ * Some callers cannot call cudaMalloc -- an embedding runtime whose device memory is carved up in
+ * advance, or code that must not allocate while other work is being captured into a CUDA graph.
+ * The split-K path (cpg_gemm_run with split_k > 1 into an FP32 D, then cpg_cast_f32_bf16) needs
+ * an FP32 buffer of M x N partial sums; this entry point keeps that buffer in a 16 MiB array
+ * compiled into the library (a file-scope __device__ array that every GPU loading the library
+ * holds until the process exits) and writes BF16 D = alpha * s_a * s_b * A . B^T + bias.
+ *   - cfg and prob as for cpg_gemm_create, with prob->dtype_d = CPG_DTYPE_BF16, scale_mode
+ *     CPG_SCALE_TENSOR and split_k the number of K ranges (0 or 1: none).
+ *   - The caller still passes A, B and D (device memory) and the stream; epi may be NULL.
+ *   - Limit: M * round_up(N, 4) * 4 bytes <= 16 MiB (M * N <= 4,194,304); larger problems are
+ *     rejected with CPG_ERR_INVALID_SHAPE and a message naming the sizes.
+ *   - It calls no cudaMalloc / cudaFree.  The first call on a device looks up the array's
+ *     device address (cudaGetSymbolAddress, which also loads the module there); make that first
+ *     call before any stream capture.
+ *   - Every call uses the same array and it keeps the last call's contents; the call clears the
+ *     part it accumulates into.  Calls that overlap on the GPU (different streams, or different
+ *     host threads) race on the array and must be serialised by the caller.
+ *   - There is no status word: a kernel wait that runs past its deadline stops the kernel
+ *     without a report (use the plan-based API when that must be observed). */
+int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob,
+                           const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                           void* stream);
+
 const char* cpg_strerror(int code);
 const char* cpg_last_error_message(void);
 /* ABI version, bumped on any incompatible change of this header. */
