@@ -64,7 +64,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["cpg", "reference"], default="cpg")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_8192")
-    ap.add_argument("--tile-n", type=int, default=256)
+    ap.add_argument("--tile-n", type=int, default=0, help="0 = 512 for BF16/FP8 (pairs), 128 for block FP8")
     ap.add_argument("--cluster-m", type=int, default=2)
     ap.add_argument("--stages", type=int, default=0, help="0 = deepest that fits")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -302,7 +302,7 @@ def run_tallk(args, world, rank, local):
     gen = torch.Generator(device=dev).manual_seed(2000 + rank)
     a_k = (torch.randn(m, ke - ks, generator=gen, device=dev) * w["a_scale"]).to(torch.bfloat16)
     b_k = (torch.randn(n, ke - ks, generator=gen, device=dev) * w["b_scale"]).to(torch.bfloat16)
-    tile_n = args.tile_n
+    tile_n = args.tile_n or 256
     cm = args.cluster_m
     stages = args.stages or (6 if cm == 2 else 4)
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
@@ -385,7 +385,7 @@ def run_cpg(args, world, rank, local):
     bias = (torch.randn(n, generator=gen_b, device=dev)).to(torch.bfloat16) if w["bias"] else None
     d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     scale_a = scale_b = None
-    tile_n = args.tile_n
+    tile_n = args.tile_n or (512 if args.cluster_m == 2 else 256)
     if w["fp8"] is not None:
         from cutedsl_pingpong_gemm_b200.quant import quantize_e4m3
         if w["fp8"] == "tensor":
@@ -398,9 +398,8 @@ def run_cpg(args, world, rank, local):
         torch.cuda.synchronize()
 
     cm = args.cluster_m
-    stages = args.stages or (6 if cm == 2 else 4)
-    if tile_n < 256 and not args.stages:
-        stages = 8 if cm == 2 else 6
+    stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
+                                                                                   8 if cm == 2 else 6)
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)

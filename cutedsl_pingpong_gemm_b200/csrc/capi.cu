@@ -136,6 +136,8 @@ Variant make_block_variant() {
 
 template <typename AB, typename OutT>
 void add_variants(Variant* t, int& n) {
+  t[n++] = make_variant<512, 1, AB, OutT>();
+  t[n++] = make_variant<512, 2, AB, OutT>();
   t[n++] = make_variant<256, 1, AB, OutT>();
   t[n++] = make_variant<128, 1, AB, OutT>();
   t[n++] = make_variant<64, 1, AB, OutT>();
@@ -146,7 +148,7 @@ void add_variants(Variant* t, int& n) {
 
 bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, int scale_mode,
                   Variant* out) {
-  static Variant table[26];
+  static Variant table[34];
   static int count = 0;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -240,6 +242,7 @@ struct cpg_gemm {
   int32_t trace_stride;
   uint64_t timeout_ns;
   int32_t fault_inject;
+  int32_t l2_policy_a, l2_policy_b;
   int32_t k_iters;
   int32_t k_iters_per_split;
   int32_t splits;
@@ -317,8 +320,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   if (cfg->tile_m != 128)
     return fail(CPG_ERR_UNSUPPORTED, "tile_m must be 128 (one TMEM lane per row), got %d",
                 cfg->tile_m);
-  if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256)
-    return fail(CPG_ERR_UNSUPPORTED, "tile_n must be 64, 128 or 256, got %d", cfg->tile_n);
+  if (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256 && cfg->tile_n != 512)
+    return fail(CPG_ERR_UNSUPPORTED, "tile_n must be 64, 128, 256 or 512, got %d", cfg->tile_n);
   if (cfg->cluster_m > 2 || cfg->cluster_n > 2)
     return fail(CPG_ERR_UNSUPPORTED, "cluster_shape_mnk must be within (2, 2, 1)");
   if (cfg->tile_m % cfg->epi_tile_m != 0 || cfg->tile_n % cfg->epi_tile_n != 0)
@@ -392,6 +395,17 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   g->timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
   const char* env = std::getenv("CPG_WAIT_TIMEOUT_MS");
   if (env != nullptr && std::atoi(env) > 0) g->timeout_ns = uint64_t(std::atoi(env)) * 1000000ull;
+  // L2 eviction priority of the A / B tile loads (0 normal, 1 evict-first, 2 evict-last).  The
+  // grouped raster walks the slow dimension inside a group of `group_size` cluster columns
+  // (AlongN) or rows (AlongM): the operand of the group's columns / rows is re-read by every
+  // tile of the group and is kept (evict-last), the other one streams (evict-first).  Measured
+  // on 8192^3 BF16: +2-3% over the default priority.  CPG_L2_POLICY_A / _B override.
+  g->l2_policy_a = cfg->raster_order == CPG_RASTER_ALONG_N ? 1 : 2;
+  g->l2_policy_b = cfg->raster_order == CPG_RASTER_ALONG_N ? 2 : 1;
+  const char* pa = std::getenv("CPG_L2_POLICY_A");
+  const char* pb = std::getenv("CPG_L2_POLICY_B");
+  if (pa != nullptr) g->l2_policy_a = std::atoi(pa);
+  if (pb != nullptr) g->l2_policy_b = std::atoi(pb);
 
   const int64_t ntm = prob->m > 0 ? (prob->m + 127) / 128 : 1;
   const int64_t ntn = prob->n > 0 ? (prob->n + cfg->tile_n - 1) / cfg->tile_n : 1;
@@ -543,8 +557,9 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
     int rc = encode_2d(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM, bk);
     if (rc != CPG_OK) return rc;
+    // One B box per MMA: min(tile_n, 256) / cta_group rows.
     rc = encode_2d(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
-                   g->v.bn / g->v.cta_group, bk);
+                   (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk);
     if (rc != CPG_OK) return rc;
     rc = encode_2d(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols);
     if (rc != CPG_OK) return rc;
@@ -584,6 +599,8 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.status = g->status_dev;
   p.timeout_ns = g->timeout_ns;
   p.fault_inject = g->fault_inject;
+  p.l2_policy_a = g->l2_policy_a;
+  p.l2_policy_b = g->l2_policy_b;
 
   if (g->splits > 1) {
     // The splits add their partial sums into D.
@@ -827,10 +844,11 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   if (cfg == nullptr || prob == nullptr) return fail(CPG_ERR_NULL, "cfg and prob must be non-NULL");
   int rc = cpg_config_validate(cfg);
   if (rc != CPG_OK) return rc;
-  if (cfg->tile_m != 128 || (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256) ||
+  if (cfg->tile_m != 128 ||
+      (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256 && cfg->tile_n != 512) ||
       cfg->cluster_m > 2 || cfg->cluster_n > 2 || cfg->ab_stage > cpg::kMaxStages ||
       cfg->epi_stage > cpg::kMaxEpiStages || cfg->gemm_n_prologue >= cfg->ab_stage)
-    return fail(CPG_ERR_UNSUPPORTED, "tile (128, 64/128/256), cluster within (2, 2, 1) only");
+    return fail(CPG_ERR_UNSUPPORTED, "tile (128, 64/128/256/512), cluster within (2, 2, 1) only");
   if (prob->dtype_ab != CPG_DTYPE_BF16 && prob->dtype_ab != CPG_DTYPE_E4M3)
     return fail(CPG_ERR_DTYPE, "A and B must be BF16 or FP8 E4M3");
   if (prob->dtype_d != CPG_DTYPE_BF16) return fail(CPG_ERR_DTYPE, "D must be BF16");
@@ -931,7 +949,7 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   rc = encode_2d(&tm_a, tma_dtype(prob->dtype_ab), eab, a, prob->m, prob->k, prob->lda, cpg::kBM, bk);
   if (rc != CPG_OK) return rc;
   rc = encode_2d(&tm_b, tma_dtype(prob->dtype_ab), eab, b, prob->n, prob->k, prob->ldb,
-                 v.bn / v.cta_group, bk);
+                 (v.bn > 256 ? 256 : v.bn) / v.cta_group, bk);
   if (rc != CPG_OK) return rc;
   rc = encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, prob->m, prob->n, ldw, 32,
                  cpg::kRowBytes / 4);

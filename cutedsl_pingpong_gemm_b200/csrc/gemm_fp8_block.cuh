@@ -199,48 +199,61 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       float acc[kBlockBN];
 #pragma unroll
       for (int j = 0; j < kBlockBN; ++j) acc[j] = 0.f;
-      float sa_next = row_ok ? scales.sa[my_row] : 0.f;
-      float sb_next = sb_row[0];
-      for (int kb = 0; kb < k_iters; ++kb) {
-        const float s = sa_next * sb_next;
-        if (kb + 1 < k_iters) {  // prefetch the next k-block's scales behind the wait
-          sa_next = row_ok ? scales.sa[static_cast<int64_t>(kb + 1) * p.m + my_row] : 0.f;
-          sb_next = sb_row[kb + 1];
-        }
-        bool got = ptx::mbar_wait(pfull_bar + 8u * part, part_phase, ctx, kSiteEpiTmemFull);
-        got = __all_sync(0xffffffffu, got);
-        if (!got) {
-          ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
-        const uint32_t t_row =
-            tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(part * kBlockBN);
+      // Scales are fetched kScalePrefetch k-blocks ahead into a register ring (the loop below
+      // is unrolled by the ring length so the ring stays in registers): every k-block's scales
+      // sit in a different cache line, and fetching them just in time stalls on memory latency.
+      constexpr int kScalePrefetch = 4;
+      float ring_a[kScalePrefetch], ring_b[kScalePrefetch];
 #pragma unroll
-        for (int h = 0; h < kBlockBN / 64; ++h) {
-          uint32_t v0[32], v1[32];
-          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h), v0);
-          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h + 32), v1);
-          ptx::tmem_ld_wait();
+      for (int j = 0; j < kScalePrefetch; ++j) {
+        ring_a[j] = (j < k_iters && row_ok) ? scales.sa[static_cast<int64_t>(j) * p.m + my_row] : 0.f;
+        ring_b[j] = j < k_iters ? sb_row[j] : 0.f;
+      }
+      for (int kb0 = 0; ok && kb0 < k_iters; kb0 += kScalePrefetch) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            acc[64 * h + j] = fmaf(s, __uint_as_float(v0[j]), acc[64 * h + j]);
-            acc[64 * h + 32 + j] = fmaf(s, __uint_as_float(v1[j]), acc[64 * h + 32 + j]);
+        for (int j = 0; j < kScalePrefetch; ++j) {
+          const int kb = kb0 + j;
+          if (!ok || kb >= k_iters) continue;
+          const float s = ring_a[j] * ring_b[j];
+          const int kn = kb + kScalePrefetch;
+          ring_a[j] = (kn < k_iters && row_ok) ? scales.sa[static_cast<int64_t>(kn) * p.m + my_row]
+                                               : 0.f;
+          ring_b[j] = kn < k_iters ? sb_row[kn] : 0.f;
+          bool got = ptx::mbar_wait(pfull_bar + 8u * part, part_phase, ctx, kSiteEpiTmemFull);
+          got = __all_sync(0xffffffffu, got);
+          if (!got) {
+            ok = false;
+            continue;
           }
-        }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
-          if constexpr (CtaGroup == 1) {
-            ptx::mbar_arrive(pb);
-          } else {
-            ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
+          ptx::tc_fence_after();
+          const uint32_t t_row =
+              tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(part * kBlockBN);
+#pragma unroll
+          for (int h = 0; h < kBlockBN / 64; ++h) {
+            uint32_t v0[32], v1[32];
+            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h), v0);
+            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h + 32), v1);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              acc[64 * h + i] = fmaf(s, __uint_as_float(v0[i]), acc[64 * h + i]);
+              acc[64 * h + 32 + i] = fmaf(s, __uint_as_float(v1[i]), acc[64 * h + 32 + i]);
+            }
           }
-        }
-        if (++part == kNumParts) {
-          part = 0;
-          part_phase ^= 1u;
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
+            if constexpr (CtaGroup == 1) {
+              ptx::mbar_arrive(pb);
+            } else {
+              ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
+            }
+          }
+          if (++part == kNumParts) {
+            part = 0;
+            part_phase ^= 1u;
+          }
         }
       }
       if (!ok) break;

@@ -105,6 +105,8 @@ struct GemmParams {
   int32_t* status;        // device status word (0 = ok)
   uint64_t timeout_ns;
   int32_t fault_inject;   // test hook: kInjectSkipLoads makes the producer issue no loads
+  int32_t l2_policy_a;    // L2 eviction priority of A / B tile loads: 0 normal, 1 first, 2 last
+  int32_t l2_policy_b;
 };
 
 // Host-selected fault injection for testing the bounded waits: with kInjectSkipLoads the
@@ -116,7 +118,14 @@ struct GemmSmem {
   static constexpr int kAStageBytes = kBM * kRowBytes;                     // 16 KiB
   static constexpr int kBStageBytes = (BN / CtaGroup) * kRowBytes;         // per CTA
   static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
-  static constexpr int kTmemCols = 2 * BN;                                 // two accumulators
+  // tcgen05.mma takes N <= 256: a 512-wide tile issues two MMAs per k-step and keeps a single
+  // accumulator (512 TMEM columns); narrower tiles keep two accumulators so that the epilogue of
+  // one tile overlaps the mainloop of the next.
+  static constexpr int kMmaN = BN > 256 ? 256 : BN;                        // N of one MMA
+  static constexpr int kNumMma = BN / kMmaN;                               // MMAs per k-step
+  static constexpr int kBRowsPerMma = kMmaN / CtaGroup;                    // B rows per CTA
+  static constexpr int kAccStages = 2 * BN <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccStages * BN;
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kTmemCols >= 32 && kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0,
                 "TMEM allocation must be a power of two in [32, 512]");
@@ -205,6 +214,12 @@ __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
   }
 }
 
+// L2 eviction priority for a TMA load: 0 normal, 1 evict-first, 2 evict-last.
+__device__ __forceinline__ uint64_t l2_policy(int32_t which) {
+  return which == 1 ? ptx::policy_evict_first()
+                    : (which == 2 ? ptx::policy_evict_last() : ptx::policy_evict_normal());
+}
+
 // TMA producer (one lane): streams the k-blocks of A (128 rows) and B (BN / CtaGroup rows) of
 // every tile of this CTA into the shared-memory stage ring, then drains its in-flight loads.
 template <int BN, int CtaGroup, int kBK, int kStageBytes, int kAStageBytes>
@@ -213,13 +228,16 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               int k_iters_per_split, int stages,
                                               uint32_t base, uint32_t full_bar, uint32_t empty_bar,
                                               uint32_t rank, bool leader,
-                                              const ptx::WaitCtx& ctx) {
-  constexpr int kBNc = BN / CtaGroup;
+                                              const ptx::WaitCtx& ctx, int32_t l2_a = 0,
+                                              int32_t l2_b = 0) {
+  constexpr int kMmaN = BN > 256 ? 256 : BN;
+  constexpr int kNumMma = BN / kMmaN;
+  constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
   const uint32_t leader_rank = rank & ~1u;
   volatile int32_t* abort_flag = ctx.abort_flag;
-  const uint64_t pol_a = ptx::policy_evict_normal();
-  const uint64_t pol_b = ptx::policy_evict_normal();
+  const uint64_t pol_a = l2_policy(l2_a);
+  const uint64_t pol_b = l2_policy(l2_b);
   int stage = 0;
   uint32_t phase = 0;
   uint32_t fills = 0;
@@ -228,7 +246,9 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
     int32_t pid_m, pid_n, l;
     work_tile_coords(sp, it.cid, pid_m, pid_n, l);
     const int32_t a_row = pid_m * kBM;
-    const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBNc;
+    // B rows of MMA j: [pid_n * BN + j * kMmaN, +kMmaN), of which this CTA of a pair loads its
+    // half (kBRowsPerMma rows at offset rank * kBRowsPerMma) into smem slot j.
+    const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBRowsPerMma;
     const int kb0 = l * k_iters_per_split;
     const int kb1 = kb0 + k_iters_per_split < k_iters ? kb0 + k_iters_per_split : k_iters;
     for (int kb = kb0; kb < kb1; ++kb) {
@@ -242,12 +262,18 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
       if constexpr (CtaGroup == 1) {
         ptx::mbar_arrive_expect_tx(fb, kTxBytes);
         ptx::tma_load_2d(tm_a, sa, fb, kb * kBK, a_row, pol_a);
-        ptx::tma_load_2d(tm_b, sb, fb, kb * kBK, b_row, pol_b);
+#pragma unroll
+        for (int j = 0; j < kNumMma; ++j)
+          ptx::tma_load_2d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * kMmaN,
+                           pol_b);
       } else {
         if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
         const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
         ptx::tma_load_2d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, pol_a);
-        ptx::tma_load_2d_pair(tm_b, sb, fb_leader, kb * kBK, b_row, pol_b);
+#pragma unroll
+        for (int j = 0; j < kNumMma; ++j)
+          ptx::tma_load_2d_pair(tm_b, sb + j * kBRowsPerMma * 128, fb_leader, kb * kBK,
+                                b_row + j * kMmaN, pol_b);
       }
       ++fills;
       if (++stage == stages) {
@@ -296,8 +322,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   constexpr int kBK = OT::kBK;
   constexpr int kUmmaK = OT::kUmmaK;
   constexpr int kStoreCols = OutputTraits<OutT>::kStoreCols;
-  constexpr uint32_t kIdesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kBM * CtaGroup, BN)
-                                       : ptx::make_idesc_bf16_f32(kBM * CtaGroup, BN);
+  constexpr uint32_t kIdesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kBM * CtaGroup, L::kMmaN)
+                                       : ptx::make_idesc_bf16_f32(kBM * CtaGroup, L::kMmaN);
+  constexpr int kAccStages = L::kAccStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -360,7 +387,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
-          leader, ctx);
+          leader, ctx, p.l2_policy_a, p.l2_policy_b);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -394,15 +421,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint64_t db = ptx::make_sw128_kmajor_desc(sb);
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            // Advance the start address by kUmmaK elements = 32 bytes inside the swizzled row.
-            if constexpr (OT::kFp8) {
-              ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
-                                        db + static_cast<uint64_t>(2 * k), kIdesc,
-                                        (kb > kb0 || k > 0) ? 1u : 0u);
-            } else {
-              ptx::umma_f16_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
-                                         db + static_cast<uint64_t>(2 * k), kIdesc,
-                                         (kb > kb0 || k > 0) ? 1u : 0u);
+            // Advance the start address by kUmmaK elements = 32 bytes inside the swizzled row;
+            // MMA j reads B slot j (kBRowsPerMma rows further) into accumulator columns j * kMmaN.
+#pragma unroll
+            for (int j = 0; j < L::kNumMma; ++j) {
+              const uint64_t dbj = db + static_cast<uint64_t>(2 * k + j * L::kBRowsPerMma * 8);
+              const uint32_t dj = d_tmem + static_cast<uint32_t>(j * L::kMmaN);
+              if constexpr (OT::kFp8) {
+                ptx::umma_f8_ss<CtaGroup>(dj, da + static_cast<uint64_t>(2 * k), dbj, kIdesc,
+                                          (kb > kb0 || k > 0) ? 1u : 0u);
+              } else {
+                ptx::umma_f16_ss<CtaGroup>(dj, da + static_cast<uint64_t>(2 * k), dbj, kIdesc,
+                                           (kb > kb0 || k > 0) ? 1u : 0u);
+              }
             }
           }
           const uint32_t eb = empty_bar + 8u * stage;
@@ -423,7 +454,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         } else {
           ptx::umma_commit_pair(tb, pair_mask);
         }
-        if (++acc == 2) {
+        if (++acc == kAccStages) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -540,7 +571,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         __syncwarp();
         ++epi_idx;
       }
-      if (++acc == 2) {
+      if (++acc == kAccStages) {
         acc = 0;
         acc_phase ^= 1u;
       }

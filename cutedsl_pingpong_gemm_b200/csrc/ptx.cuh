@@ -84,29 +84,46 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
                "r"(bytes)
                : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // Arrive on a barrier that may live in another CTA of the cluster (address from mapa_shared).
+// Default (CTA-scope) semantics: the barriers here order tensor-memory accesses, which the
+// tcgen05 fences around the arrive / wait already cover, so no cluster-scope fence is needed.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// As mbar_try_wait, but the thread may be suspended for up to `suspend_ns` nanoseconds while the
+// phase is incomplete (it resumes as soon as the phase completes), so waiting warps sleep
+// instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity,
+                                                      uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
@@ -130,20 +147,20 @@ __device__ __noinline__ void record_timeout(const WaitCtx& ctx, int32_t site) {
 }
 
 // Wait until the phase with parity `parity` of barrier `bar` completed.  Returns false when the
-// deadline passes (recording `site`) or when another role already aborted.
+// deadline passes (recording `site`) or when another role already aborted.  Between checks of
+// the deadline and the abort flag the thread sleeps in try_wait for at most kWaitSuspendNs.
+constexpr uint32_t kWaitSuspendNs = 1000000;  // 1 ms
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& ctx,
                                           int32_t site) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0u) {
-      if (*ctx.abort_flag) return false;
-      if (globaltimer() - t0 > ctx.timeout_ns) {
-        record_timeout(ctx, site);
-        return false;
-      }
+    if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
+    if (*ctx.abort_flag) return false;
+    if (globaltimer() - t0 > ctx.timeout_ns) {
+      record_timeout(ctx, site);
+      return false;
     }
   }
 }

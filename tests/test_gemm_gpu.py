@@ -391,3 +391,28 @@ def test_split_k_small_m_then_cast():
     torch.cuda.synchronize()
     res = gemm_ref.check(out.cpu(), a, b, bias=bias)
     assert res["ok"], res
+
+
+# ---------------------------------------------------------------- 512-wide tiles (two MMAs per k-step)
+@pytest.mark.parametrize("cluster,stages", [((2, 1, 1), 4), ((1, 1, 1), 2), ((2, 2, 1), 4)])
+@pytest.mark.parametrize("shape", [(256, 512, 128), (640, 1536, 1000), (1000, 1032, 4104),
+                                   (2048, 4096, 512)])
+def test_tile_n_512(shape, cluster, stages):
+    m, n, k = shape
+    run_and_check(m, n, k, make_gemm(512, cluster, stages=stages), seed=m + n)
+
+
+def test_tile_n_512_fp8_and_bias():
+    m, n, k = 1024, 2048, 1024
+    qa, sa, qb, sb = gemm_ref.make_fp8_inputs(m, n, k, seed=3)
+    d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    make_gemm(512, (2, 1, 1))(qa.cuda(), qb.cuda(), d, None, scale_a=sa.reshape(1).cuda(),
+                              scale_b=sb.reshape(1).cuda())
+    torch.cuda.synchronize()
+    assert gemm_ref.check_fp8(d.cpu(), qa, sa, qb, sb)["ok"]
+    run_and_check(384, 1536, 512, make_gemm(512, (2, 1, 1)), bias=True)
+
+
+def test_tile_order_512_matches_reference():
+    got, want = traced_schedule(make_gemm(512, (2, 1, 1)), 128 * 9, 512 * 5 + 64, 128)
+    assert got == want

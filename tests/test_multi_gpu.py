@@ -1,0 +1,93 @@
+"""Multi-GPU paths on real GPUs (NCCL): M-sharding with B replicated, and split-K with an NCCL
+reduce-scatter of fp32 partials followed by the BF16 cast kernel.
+
+Runs one process per visible GPU (at least two, otherwise skipped) with a short process-group
+timeout; each rank checks its rows against the fp32 CPU oracle.  NVLS is switched off
+(NCCL_NVLS_ENABLE=0) as for every multi-rank test on this pool.
+"""
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+WORKER = textwrap.dedent(r'''
+    import datetime, os, sys
+    sys.path.insert(0, sys.argv[1])
+    import torch, torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from cutedsl_pingpong_gemm_b200 import GemmSM90
+    from cutedsl_pingpong_gemm_b200.sharding import MShardedGemm, SplitKGemm, k_ranges, row_range
+    from oracle import gemm_ref
+    ok = True
+    # M-shard: LLM-like shape scaled down, bias, B replicated, no collective on the data path.
+    m, n, k = 1024 + 128 * world, 1536, 1024
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=3, b_scale=0.02, with_bias=True)
+    gemm = GemmSM90((128, 256), (128, 32), (2, 1, 1), (1, 1), ab_stage=6, reuse_ab=False,
+                    is_persistent=True)
+    sh = MShardedGemm(gemm, world, rank)
+    s, e = sh.rows(m)
+    d = torch.empty(e - s, n, dtype=torch.bfloat16, device="cuda")
+    sh(a[s:e].cuda(), b.cuda(), d, bias=bias.cuda())
+    torch.cuda.synchronize()
+    res = gemm_ref.check(d.cpu(), a[s:e], b, bias=bias)
+    ok &= res["ok"]
+    # Split-K over ranks: tall K, fp32 partials, NCCL reduce-scatter, cast to BF16.
+    m2, n2, k2 = 512, 768, 8192
+    a2, b2, _ = gemm_ref.make_inputs(m2, n2, k2, seed=5, b_scale=k2 ** -0.5)
+    ks, ke = k_ranges(k2, world)[rank]
+    sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=2)
+    rows = sk(a2[:, ks:ke].cuda().contiguous(), b2[:, ks:ke].cuda().contiguous(), m2, n2)
+    torch.cuda.synchronize()
+    r0, r1 = row_range(m2, world, rank)
+    res2 = gemm_ref.check(rows.cpu(), a2[r0:r1], b2)
+    ok &= res2["ok"]
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        print("RESULT", int(flag.item()), res, res2, flush=True)
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+''')
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_multi_gpu_mshard_and_splitk(tmp_path):
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(ngpu, 8)
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, str(script), ROOT], env=env,
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            out, _ = p.communicate()
+        outs.append((p.returncode, out))
+    assert all(rc == 0 for rc, _ in outs), outs
+    assert "RESULT 1" in outs[0][1], outs[0][1]
