@@ -43,8 +43,9 @@ WORKLOADS = {
                       m_is_per_gpu=True, fp8=None),
     "llm": dict(m=16384, n=28672, k=8192, a_scale=1.0, b_scale=0.02, bias=True,
                 m_is_per_gpu=False, fp8=None),
+    # Decode-like: HBM bound (B is 128 MiB, A 2 MiB); split-K inside the GPU fills the SMs.
     "smallm": dict(m=128, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
-                   m_is_per_gpu=True, fp8=None),
+                   m_is_per_gpu=True, fp8=None, small_m=True),
     # FP8 E4M3, A and B ~ N(0,1) quantised on the GPU (s = amax / 448) before timing.
     "fp8": dict(m=16384, n=8192, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
                 m_is_per_gpu=True, fp8="tensor"),
@@ -67,6 +68,7 @@ def parse_args():
     ap.add_argument("--tile-n", type=int, default=0, help="0 = 512 for BF16/FP8 (pairs), 128 for block FP8")
     ap.add_argument("--cluster-m", type=int, default=2)
     ap.add_argument("--stages", type=int, default=0, help="0 = deepest that fits")
+    ap.add_argument("--split-k", type=int, default=0, help="small-M only: 0 auto, -1 Stream-K, S splits")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -385,7 +387,9 @@ def run_cpg(args, world, rank, local):
     bias = (torch.randn(n, generator=gen_b, device=dev)).to(torch.bfloat16) if w["bias"] else None
     d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     scale_a = scale_b = None
-    tile_n = args.tile_n or (512 if args.cluster_m == 2 else 256)
+    if w.get("small_m"):
+        args.cluster_m = 1  # one 128-row tile: the pair's second CTA would have no rows
+    tile_n = args.tile_n or (128 if w.get("small_m") else (512 if args.cluster_m == 2 else 256))
     if w["fp8"] is not None:
         from cutedsl_pingpong_gemm_b200.quant import quantize_e4m3
         if w["fp8"] == "tensor":
@@ -404,16 +408,21 @@ def run_cpg(args, world, rank, local):
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
     compiled = cpg_compile(gemm, a, b, d, stream)
-    compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
+    split_k = (args.split_k if args.split_k else compiled.auto_split_k(m, n, k)) if w.get("small_m") else 1
+    compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k)
     torch.cuda.synchronize()
-    plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0)
+    if split_k != 1:
+        plan = compiled.plan_for(a, b, compiled._workspace(d), 0, split_k)
+    else:
+        plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0)
     info = plan.launch_info()
+    kernels_per_step = 2 if split_k != 1 else 1  # split-K / Stream-K add the cast kernel
 
     launches = [0]
 
     def step():
-        compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
-        launches[0] += 1
+        compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k)
+        launches[0] += kernels_per_step
 
     for _ in range(args.warmup):
         step()
@@ -445,6 +454,8 @@ def run_cpg(args, world, rank, local):
     value = total_flops / (ms * 1e-3) / 1e12
     achieved = flops_per_gpu / (ms_local * 1e-3) / 1e12  # one kernel launch per step
     peaks, peak_src = load_peaks()
+    # HBM-bound shapes: the roofline is bytes moved / time against the measured copy bandwidth.
+    min_bytes = (m * k + n * k) * a.element_size() + m * n * d.element_size()
 
     # ---------------- end to end through the public API with host buffers
     e2e = None
@@ -458,7 +469,8 @@ def run_cpg(args, world, rank, local):
         def e2e_step():
             a2.copy_(a_h, non_blocking=True)
             b2.copy_(b_h, non_blocking=True)
-            compiled(a2, b2, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b)
+            compiled(a2, b2, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b,
+                     split_k=split_k)
             d_h.copy_(d, non_blocking=True)
 
         for _ in range(2):
@@ -512,14 +524,22 @@ def run_cpg(args, world, rank, local):
                        "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
                        "bias": bool(w["bias"])},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
+                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": min_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                          "peak_source": f"{peak_src} hbm_gbs", "traffic": load_traffic(args.workload),
+                          "algorithmic_bytes_per_step": min_bytes, "split_k": split_k,
+                          "kernel": ("cpg::gemm_sm100_kernel (Stream-K)" if split_k == -1 else
+                                     "cpg::gemm_sm100_kernel (split-K)") + " + cast_f32_bf16_kernel"}
+                         if w.get("small_m") else
+                         {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": peak_note,
                          "frac_sustained": (achieved / peaks.get("bf16_tflops_sustained", peak)
                                             if w["fp8"] is None else None),
                          "traffic": load_traffic(args.workload),
                          "algorithmic_flops_per_launch": flops_per_gpu,
                          "kernel": ("cpg::gemm_fp8_block_kernel" if w["fp8"] == "block"
-                                    else "cpg::gemm_sm100_kernel")},
+                                    else "cpg::gemm_sm100_kernel")}),
             "clocks": clocks,
             "gpu_launches": n_launch * world,
             "e2e": e2e,

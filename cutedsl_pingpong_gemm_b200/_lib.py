@@ -30,6 +30,7 @@ CPG_SCALE_TENSOR = 0
 CPG_SCALE_BLOCK = 1
 
 CPG_INJECT_SKIP_LOADS = 1
+CPG_SPLIT_K_STREAM = -1
 
 ABI_VERSION = 6
 

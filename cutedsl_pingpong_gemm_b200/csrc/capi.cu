@@ -193,6 +193,17 @@ __global__ void fill_rows_kernel(OutT* d, int64_t m, int64_t n, int64_t ldd,
   }
 }
 
+// Grid of cast_f32_bf16_kernel: x covers a row's columns in quads of 4 (256 threads per block),
+// y covers rows (grid-stride beyond 65535), about 32 k blocks in total.
+dim3 cast_grid(int64_t rows, int64_t cols) {
+  const int64_t bx = (cols + 1023) / 1024;
+  int64_t by = (32768 + bx - 1) / bx;
+  if (by > rows) by = rows;
+  if (by > 65535) by = 65535;
+  if (by < 1) by = 1;
+  return dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by), 1);
+}
+
 int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* out) {
   cudaError_t e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
@@ -246,6 +257,7 @@ struct cpg_gemm {
   int32_t k_iters;
   int32_t k_iters_per_split;
   int32_t splits;
+  int32_t stream_k;
   bool maps_valid;
   const void* map_a_ptr;
   const void* map_b_ptr;
@@ -372,9 +384,13 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                 cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);
   if (v.scale_mode == CPG_SCALE_BLOCK && cfg->reuse_ab)
     return fail(CPG_ERR_UNSUPPORTED, "reuse_ab is not implemented for block-scaled FP8");
-  if (prob->split_k < 0) return fail(CPG_ERR_INVALID_SHAPE, "split_k must be >= 0");
-  if (prob->split_k > 1 && (prob->dtype_d != CPG_DTYPE_F32 || v.scale_mode != CPG_SCALE_TENSOR))
-    return fail(CPG_ERR_UNSUPPORTED, "split_k > 1 accumulates into an FP32 D (no block scales)");
+  if (prob->split_k < CPG_SPLIT_K_STREAM)
+    return fail(CPG_ERR_INVALID_SHAPE, "split_k must be >= 0, or CPG_SPLIT_K_STREAM");
+  if ((prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM) &&
+      (prob->dtype_d != CPG_DTYPE_F32 || v.scale_mode != CPG_SCALE_TENSOR))
+    return fail(CPG_ERR_UNSUPPORTED, "split-K / Stream-K accumulate into an FP32 D (no block scales)");
+  if (prob->split_k == CPG_SPLIT_K_STREAM && !cfg->is_persistent)
+    return fail(CPG_ERR_UNSUPPORTED, "Stream-K needs a persistent kernel");
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -402,6 +418,20 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   // on 8192^3 BF16: +2-3% over the default priority.  CPG_L2_POLICY_A / _B override.
   g->l2_policy_a = cfg->raster_order == CPG_RASTER_ALONG_N ? 1 : 2;
   g->l2_policy_b = cfg->raster_order == CPG_RASTER_ALONG_N ? 2 : 1;
+  {
+    // Shapes with one or two row (column) tiles re-read A (B) for every tile along the other
+    // dimension while the other operand streams once: keep that one.  Decode-like M = 128,
+    // N = K = 8192: 44.1 -> 37.2 us per step.
+    const int64_t row_tiles = (prob->m + 128 * cfg->cluster_m - 1) / (128 * cfg->cluster_m);
+    const int64_t col_tiles = (prob->n + cfg->tile_n - 1) / cfg->tile_n;
+    if (row_tiles <= 2 && col_tiles > 2) {
+      g->l2_policy_a = 2;
+      g->l2_policy_b = 1;
+    } else if (col_tiles <= 2 && row_tiles > 2) {
+      g->l2_policy_a = 1;
+      g->l2_policy_b = 2;
+    }
+  }
   const char* pa = std::getenv("CPG_L2_POLICY_A");
   const char* pb = std::getenv("CPG_L2_POLICY_B");
   if (pa != nullptr) g->l2_policy_a = std::atoi(pa);
@@ -413,6 +443,7 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   // every split is non-empty.
   const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
   g->k_iters = static_cast<int32_t>((prob->k + bk - 1) / bk);
+  g->stream_k = prob->split_k == CPG_SPLIT_K_STREAM ? 1 : 0;
   int32_t splits = prob->split_k > 1 ? prob->split_k : 1;
   if (splits > g->k_iters && g->k_iters > 0) splits = g->k_iters;
   g->k_iters_per_split = g->k_iters > 0 ? (g->k_iters + splits - 1) / splits : 0;
@@ -423,6 +454,11 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                                       cfg->cluster_n, cfg->is_persistent);
   int32_t grid[3];
   cpg::sched_grid_shape(g->sched, mac, grid);
+  if (g->stream_k) {
+    // Every resident cluster takes an equal share of the k-blocks, even with fewer tiles.
+    const int64_t units = int64_t(cpg::sched_total_clusters(g->sched)) * g->k_iters;
+    grid[2] = static_cast<int32_t>(units < mac ? (units > 0 ? units : 1) : mac);
+  }
   for (int i = 0; i < 3; ++i) g->grid[i] = grid[i];
   g->cluster[0] = cfg->cluster_m;
   g->cluster[1] = cfg->cluster_n;
@@ -577,7 +613,8 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.k = static_cast<int32_t>(pr.k);
   p.k_iters = g->k_iters;
   p.k_iters_per_split = g->k_iters_per_split;
-  p.reduce_add = g->splits > 1 ? 1 : 0;
+  p.reduce_add = (g->splits > 1 || g->stream_k) ? 1 : 0;
+  p.stream_k = g->stream_k;
   p.ab_stages = g->cfg.ab_stage;
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
@@ -602,8 +639,8 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.l2_policy_a = g->l2_policy_a;
   p.l2_policy_b = g->l2_policy_b;
 
-  if (g->splits > 1) {
-    // The splits add their partial sums into D.
+  if (g->splits > 1 || g->stream_k) {
+    // The splits / Stream-K segments add their partial sums into D.
     cudaError_t e = cudaMemset2DAsync(d, pr.ldd * ed, 0, pr.n * ed, pr.m, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(D)");
   }
@@ -791,8 +828,8 @@ int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, v
     return fail(CPG_ERR_INVALID_SHAPE, "bad cast extents");
   if (rows == 0 || cols == 0) return CPG_OK;
   if (x == nullptr || y == nullptr) return fail(CPG_ERR_NULL, "x and y must be non-NULL");
-  const unsigned blocks = static_cast<unsigned>(rows < 65535 ? rows : 65535);
-  cpg::cast_f32_bf16_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  const dim3 grid = cast_grid(rows, cols);
+  cpg::cast_f32_bf16_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, rows, cols, ldx, static_cast<__nv_bfloat16*>(y), ldy,
       static_cast<const __nv_bfloat16*>(bias));
   cudaError_t e = cudaGetLastError();
@@ -978,7 +1015,7 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   void* args[] = {&tm_a, &tm_b, &tm_w, &p, &unused};
   e = cudaLaunchKernelExC(&lc, v.fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "split-K GEMM launch");
-  cpg::cast_f32_bf16_kernel<<<cast_blocks, 256, 0, st>>>(
+  cpg::cast_f32_bf16_kernel<<<cast_grid(prob->m, prob->n), 256, 0, st>>>(
       ws, prob->m, prob->n, ldw, static_cast<__nv_bfloat16*>(d), prob->ldd,
       static_cast<const __nv_bfloat16*>(bias));
   e = cudaGetLastError();

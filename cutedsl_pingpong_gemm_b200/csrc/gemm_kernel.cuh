@@ -93,6 +93,7 @@ struct GemmParams {
   int32_t k_iters;        // k-blocks of the whole K: ceil(K / BK)
   int32_t k_iters_per_split;  // k-blocks per L index (split-K); == k_iters without splitting
   int32_t reduce_add;     // epilogue adds into D (fp32 split-K partial sums) instead of storing
+  int32_t stream_k;       // persistent CTAs split the (tile, k-block) space evenly (Stream-K)
   int32_t ab_stages;
   int32_t epi_stages;
   int32_t reuse_ab;       // epilogue staging aliases the A/B stages (single-tile CTAs only)
@@ -197,11 +198,64 @@ __device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t 
   work_tile_coords(sp, cid, pid_m, pid_n, l);
 }
 
-// k-block range [kb0, kb1) of L index l.
-__device__ __forceinline__ void split_k_range(const GemmParams& p, int32_t l, int& kb0, int& kb1) {
-  kb0 = l * p.k_iters_per_split;
-  kb1 = kb0 + p.k_iters_per_split;
-  if (kb1 > p.k_iters) kb1 = p.k_iters;
+// One unit of work of a CTA: k-blocks [kb0, kb1) of the tile at linear cluster id `cid`.
+struct Segment {
+  int32_t cid;
+  int32_t kb0, kb1;
+  int32_t index;  // how many segments this CTA produced before this one
+};
+
+// Walks this CTA's segments.  Tile mode: the scheduler's tiles (and L index: k-blocks
+// [l * kps, (l + 1) * kps) for split-K), one segment per tile.  Stream-K: the linearised
+// (tile, k-block) space of tiles * k_iters k-blocks is cut into gridDim.z equal ranges and
+// cluster z walks range z, one segment per tile it touches; the tiles keep the reference's
+// linear-id -> (m, n) map.
+struct SegmentIter {
+  WorkIter it;
+  int64_t pos, end;
+  int32_t k_iters, kps, stream, index;
+
+  __device__ __forceinline__ bool next(const SchedParams& sp, Segment& s) {
+    if (stream) {
+      if (pos >= end) return false;
+      const int64_t tile = pos / k_iters;
+      const int32_t kb0 = static_cast<int32_t>(pos - tile * k_iters);
+      int64_t kb1 = kb0 + (end - pos);
+      if (kb1 > k_iters) kb1 = k_iters;
+      s.cid = static_cast<int32_t>(tile);
+      s.kb0 = kb0;
+      s.kb1 = static_cast<int32_t>(kb1);
+      pos += kb1 - kb0;
+    } else {
+      if (!it.valid()) return false;
+      int32_t l, cid_in_problem;
+      fast_divmod(sp.dm_clusters_per_problem, it.cid, l, cid_in_problem);
+      s.cid = it.cid;
+      s.kb0 = l * kps;
+      s.kb1 = s.kb0 + kps < k_iters ? s.kb0 + kps : k_iters;
+      it.advance();
+    }
+    s.index = index++;
+    return true;
+  }
+};
+
+__device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, int32_t k_iters,
+                                                         int32_t kps, int32_t stream_k) {
+  SegmentIter si;
+  si.it = make_work_iter(sp);
+  si.k_iters = k_iters;
+  si.kps = kps;
+  si.stream = stream_k;
+  si.index = 0;
+  si.pos = si.end = 0;
+  if (stream_k) {
+    const int64_t total = static_cast<int64_t>(sched_total_clusters(sp)) * k_iters;
+    const int64_t z = blockIdx.z, g = gridDim.z;
+    si.pos = total * z / g;
+    si.end = total * (z + 1) / g;
+  }
+  return si;
 }
 
 __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
@@ -229,7 +283,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               uint32_t base, uint32_t full_bar, uint32_t empty_bar,
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
-                                              int32_t l2_b = 0) {
+                                              int32_t l2_b = 0, int32_t stream_k = 0) {
   constexpr int kMmaN = BN > 256 ? 256 : BN;
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
@@ -242,16 +296,16 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t phase = 0;
   uint32_t fills = 0;
   bool ok = true;
-  for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
-    int32_t pid_m, pid_n, l;
-    work_tile_coords(sp, it.cid, pid_m, pid_n, l);
+  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k);
+  Segment sg;
+  while (ok && si.next(sp, sg)) {
+    int32_t pid_m, pid_n;
+    work_tile_coords(sp, sg.cid, pid_m, pid_n);
     const int32_t a_row = pid_m * kBM;
     // B rows of MMA j: [pid_n * BN + j * kMmaN, +kMmaN), of which this CTA of a pair loads its
     // half (kBRowsPerMma rows at offset rank * kBRowsPerMma) into smem slot j.
     const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBRowsPerMma;
-    const int kb0 = l * k_iters_per_split;
-    const int kb1 = kb0 + k_iters_per_split < k_iters ? kb0 + k_iters_per_split : k_iters;
-    for (int kb = kb0; kb < kb1; ++kb) {
+    for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
       if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
         ok = false;
         break;
@@ -387,7 +441,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
-          leader, ctx, p.l2_policy_a, p.l2_policy_b);
+          leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -398,11 +452,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
-        int32_t pid_m, pid_n, l;
-        work_tile_coords(sp, it.cid, pid_m, pid_n, l);
-        int kb0, kb1;
-        split_k_range(p, l, kb0, kb1);
+      SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k);
+      Segment sg;
+      while (ok && si.next(sp, sg)) {
+        const int kb0 = sg.kb0, kb1 = sg.kb1;
         if (!ptx::mbar_wait(tempty_bar + 8u * acc, acc_phase ^ 1u, ctx, kSiteMmaTmemEmpty)) {
           ok = false;
           break;
@@ -479,18 +532,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (p.scale_a != nullptr) alpha *= *p.scale_a;
     if (p.scale_b != nullptr) alpha *= *p.scale_b;
     const bool has_bias = p.bias != nullptr;
-    for (WorkIter it = make_work_iter(sp); it.valid(); it.advance()) {
-      int32_t pid_m, pid_n, l;
-      work_tile_coords(sp, it.cid, pid_m, pid_n, l);
-      const bool add_bias = has_bias && l == 0;  // split-K: the bias enters the sum once
+    SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k);
+    Segment sg;
+    while (si.next(sp, sg)) {
+      int32_t pid_m, pid_n;
+      work_tile_coords(sp, sg.cid, pid_m, pid_n);
+      // Split-K / Stream-K: only the segment holding a tile's first k-block adds the bias.
+      const bool add_bias = has_bias && sg.kb0 == 0;
       bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       ptx::tc_fence_after();
-      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && it.executed < p.trace_stride) {
+      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && sg.index < p.trace_stride) {
         const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) *
                                              (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
-        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + it.executed);
+        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + sg.index);
         t[0] = pid_m;
         t[1] = pid_n;
       }

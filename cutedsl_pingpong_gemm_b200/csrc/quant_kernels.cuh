@@ -148,15 +148,47 @@ __global__ void quant_tile_block_kernel(const T* __restrict__ x, int64_t rows, i
   }
 }
 
-// y = bf16(x + bias) for split-K results (x fp32 [rows, cols]).
+// y = bf16(x + bias) for split-K results (x fp32 [rows, cols]).  Vector path when cols, ldx and
+// ldy are multiples of 4 and the bases are 16 / 8-byte aligned: each thread converts 4
+// consecutive values (one float4 load, one 8-byte store); blockIdx.x walks a row's column
+// quads and blockIdx.y (grid-stride) the rows, so there is no per-element division.
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
                                      int64_t ldx, __nv_bfloat16* __restrict__ y, int64_t ldy,
                                      const __nv_bfloat16* __restrict__ bias) {
-  CPG_ROW_LOOP({
-    float v = x[r * ldx + c];
-    if (bias != nullptr) v += __bfloat162float(bias[c]);
-    y[r * ldy + c] = __float2bfloat16_rn(v);
-  });
+  const bool vec = (cols % 4 == 0) && (ldx % 4 == 0) && (ldy % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(y) % 8 == 0);
+  if (vec) {
+    const int64_t c4 = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4;
+    if (c4 >= cols) return;
+    float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+    if (bias != nullptr) {
+      b0 = __bfloat162float(bias[c4]);
+      b1 = __bfloat162float(bias[c4 + 1]);
+      b2 = __bfloat162float(bias[c4 + 2]);
+      b3 = __bfloat162float(bias[c4 + 3]);
+    }
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+      const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c4);
+      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x + b0, v.y + b1);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(v.z + b2, v.w + b3);
+      uint2 packed;
+      packed.x = *reinterpret_cast<uint32_t*>(&lo);
+      packed.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(y + r * ldy + c4) = packed;
+    }
+    return;
+  }
+  // Scalar path: same grid and the same 4 columns per thread, element by element.
+  const int64_t c0 = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = c0 + j;
+      if (c >= cols) break;
+      const float b = bias != nullptr ? __bfloat162float(bias[c]) : 0.f;
+      y[r * ldy + c] = __float2bfloat16_rn(x[r * ldx + c] + b);
+    }
+  }
 }
 
 #undef CPG_ROW_LOOP

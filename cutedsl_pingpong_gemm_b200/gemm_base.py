@@ -77,6 +77,7 @@ class CompiledGemm:
     def __init__(self, gemm: "GemmSM90"):
         self.gemm = gemm
         self._plans = {}
+        self._workspaces = {}
 
     def _plan(self, a, b, c, scale_mode: int = 0, split_k: int = 1):
         import torch
@@ -121,13 +122,55 @@ class CompiledGemm:
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
                  scale_b=None, split_k: int = 1):
+        """``split_k`` > 1 cuts K into that many ranges scheduled as the kernel's L dimension;
+        ``split_k=-1`` is Stream-K (every resident cluster takes an equal share of the (tile,
+        k-block) pairs); ``split_k=0`` picks from the tile count (see ``auto_split_k``).  With a
+        BF16 ``c`` the partial sums add into an FP32 workspace that is then rounded into ``c``
+        (plus bias)."""
+        import torch
         # More than one scale per operand selects the block-scaled FP8 kernel (A: 1 x 128,
         # B: 128 x 128 blocks, layouts of cpgemm.h); one value each is a per-tensor scale.
         block = scale_a is not None and scale_a.numel() > 1
-        plan = self._plan(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR,
-                          int(split_k))
+        mode = _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR
+        if split_k == 0:
+            split_k = 1 if block else self.auto_split_k(a.shape[0], b.shape[0], a.shape[1])
+        split_k = int(split_k)
+        if (split_k > 1 or split_k == _lib.CPG_SPLIT_K_STREAM) and c.dtype == torch.bfloat16:
+            ws = self._workspace(c)
+            plan = self._plan(a, b, ws, mode, split_k)
+            plan.run(a, b, ws, stream, bias=None, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
+            from .quant import cast_f32_bf16
+            cast_f32_bf16(ws, bias, out=c, stream=stream)
+            return None
+        plan = self._plan(a, b, c, mode, split_k)
         plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
         return None
+
+    def _workspace(self, c):
+        """FP32 [M, N] buffer for split-K partial sums (kept and reused per shape/device)."""
+        import torch
+        key = (tuple(c.shape), c.device)
+        ws = self._workspaces.get(key)
+        if ws is None:
+            ws = torch.empty(c.shape, dtype=torch.float32, device=c.device)
+            self._workspaces[key] = ws
+        return ws
+
+    def auto_split_k(self, m: int, n: int, k: int) -> int:
+        """When the output tiles alone cannot fill the GPU (decode-like small M): Stream-K for a
+        persistent kernel (-1), else about three waves of K ranges; 1 otherwise."""
+        gemm = self.gemm
+        cm, cn, _ = gemm.cluster_shape_mnk
+        tiles = -(-max(m, 1) // (128 * cm)) * -(-max(n, 1) // gemm.cta_tile_shape_mnk[1])
+        tiles = -(-tiles // cn)
+        slots = gemm.max_active_clusters
+        if tiles >= slots:
+            return 1
+        kblocks = -(-max(k, 1) // 64)
+        if gemm.is_persistent and kblocks >= 8:
+            return _lib.CPG_SPLIT_K_STREAM
+        want = -(-3 * slots // tiles)
+        return max(1, min(want, kblocks // 4))
 
 
 class _Plan:

@@ -42,8 +42,8 @@ def quantize_e4m3(x, block: Optional[Tuple[int, int]] = None):
     return q, scales
 
 
-def cast_f32_bf16(x, bias=None, out=None):
-    """out = bf16(x + bias) for a 2-D FP32 CUDA tensor x."""
+def cast_f32_bf16(x, bias=None, out=None, stream=None):
+    """out = bf16(x + bias) for a 2-D FP32 CUDA tensor x (on ``stream``, default current)."""
     import torch
     if not x.is_cuda or x.dim() != 2 or x.dtype != torch.float32:
         raise _lib.CpgError(_lib.CPG_ERR_DTYPE, "x must be a 2-D FP32 CUDA tensor")
@@ -55,8 +55,10 @@ def cast_f32_bf16(x, bias=None, out=None):
     ldx = x.stride(0) if rows > 1 else cols
     ldy = out.stride(0) if rows > 1 else cols
     lib = _lib.load()
+    from .gemm_base import _stream_handle
+    st = _stream_handle(stream, x.device)
     _lib.check(lib.cpg_cast_f32_bf16(x.data_ptr() if x.numel() else None, rows, cols, ldx,
                                      out.data_ptr() if out.numel() else None, ldy,
-                                     None if bias is None else bias.data_ptr(), _stream(x)),
+                                     None if bias is None else bias.data_ptr(), st),
                "cast_f32_bf16")
     return out

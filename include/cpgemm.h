@@ -108,8 +108,12 @@ typedef struct cpg_gemm_problem {
   int32_t scale_mode;    /* CPG_SCALE_TENSOR, or CPG_SCALE_BLOCK for block-scaled E4M3 */
   int32_t split_k;       /* 0 or 1: none; S > 1: K is cut into S ranges scheduled as the L
                             dimension, and the ranges add their FP32 partial sums into D
-                            (dtype_d must be CPG_DTYPE_F32; D is cleared by cpg_gemm_run) */
+                            (dtype_d must be CPG_DTYPE_F32; D is cleared by cpg_gemm_run);
+                            CPG_SPLIT_K_STREAM: Stream-K, every resident cluster takes an equal
+                            share of all (tile, k-block) pairs and adds into FP32 D */
 } cpg_gemm_problem;
+
+#define CPG_SPLIT_K_STREAM (-1)
 
 /* Per-call epilogue options: D = alpha * s_a * s_b * (A . B^T) + bias, rounded to D's type.
  * alpha scales the fp32 accumulator; scale_a / scale_b (optional device pointers to one fp32

@@ -416,3 +416,54 @@ def test_tile_n_512_fp8_and_bias():
 def test_tile_order_512_matches_reference():
     got, want = traced_schedule(make_gemm(512, (2, 1, 1)), 128 * 9, 512 * 5 + 64, 128)
     assert got == want
+
+
+@pytest.mark.parametrize("m", [16, 64, 128])
+def test_small_m_auto_split_bf16(m):
+    """BASELINE config 5 (decode-like M at N = K = 8192): split-K picked automatically, partial
+    sums in the FP32 workspace, then rounded into the BF16 output with the bias."""
+    n, k = 8192, 8192
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=m, b_scale=k ** -0.5, with_bias=True)
+    gemm = make_gemm(256, (1, 1, 1))
+    d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    compiled = cpg_compile(gemm, a.cuda(), b.cuda(), d)
+    assert compiled.auto_split_k(m, n, k) != 1  # Stream-K (-1) for this persistent kernel
+    compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=0)
+    torch.cuda.synchronize()
+    assert gemm_ref.check(d.cpu(), a, b, bias=bias)["ok"]
+    # The same through explicit K ranges (the kernel's L dimension).
+    compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=7)
+    torch.cuda.synchronize()
+    res = gemm_ref.check(d.cpu(), a, b, bias=bias)
+    assert res["ok"], res
+
+
+# ---------------------------------------------------------------- Stream-K
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("shape", [(128, 8192, 8192), (64, 1024, 4096 + 64), (300, 520, 1000 + 8),
+                                   (1024, 1024, 1024)])
+def test_stream_k_fp32(shape, cluster):
+    """Stream-K: persistent clusters split the (tile, k-block) space evenly; partial tiles add
+    into FP32 D (element-wise accumulation bound only: no BF16 rounding)."""
+    m, n, k = shape
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=k, b_scale=k ** -0.5, with_bias=True)
+    d = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    gemm = make_gemm(256, cluster, stages=4 if cluster[0] == 1 else 6)
+    gemm(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=-1)
+    torch.cuda.synchronize()
+    r = gemm_ref.reference(a, b, bias)
+    s = gemm_ref.abs_product(a, b)
+    bound = k * gemm_ref.ACC_SLACK_PER_K * s + 2.0 ** -22 * bias.float().abs() + 1e-6
+    assert bool(((d.cpu() - r).abs() <= bound).all())
+
+
+def test_stream_k_bf16_through_api():
+    m, n, k = 16, 8192, 8192
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=1, b_scale=k ** -0.5, with_bias=True)
+    d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    compiled = cpg_compile(make_gemm(256, (1, 1, 1)), a.cuda(), b.cuda(), d)
+    assert compiled.auto_split_k(m, n, k) == -1
+    for _ in range(2):  # the workspace is reused: the second call must clear it again
+        compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=0)
+    torch.cuda.synchronize()
+    assert gemm_ref.check(d.cpu(), a, b, bias=bias)["ok"]

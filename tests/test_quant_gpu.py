@@ -52,3 +52,14 @@ def test_cast_with_bias():
     y = cast_f32_bf16(x.cuda(), bias.cuda())
     want = (x + bias.float()).to(torch.bfloat16)
     assert torch.equal(y.cpu(), want)
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (129, 1030), (64, 8192)])
+def test_cast_odd_and_strided_shapes(shape):
+    """Scalar path (columns not a multiple of 4) and strided views."""
+    rows, cols = shape
+    g = torch.Generator().manual_seed(rows * cols)
+    full = torch.randn(rows, cols + 5, generator=g) * 50
+    x = full[:, 1:cols + 1]
+    y = cast_f32_bf16(x.cuda())
+    assert torch.equal(y.cpu(), x.to(torch.bfloat16))
