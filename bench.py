@@ -404,6 +404,8 @@ def run_cpg(args, world, rank, local):
     cm = args.cluster_m
     stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
                                                                                    8 if cm == 2 else 6)
+    if w["fp8"] == "block" and not args.stages:
+        stages = 6  # 8 promotion warps stage 64 KiB of epilogue output
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)

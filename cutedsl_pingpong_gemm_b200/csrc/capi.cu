@@ -97,6 +97,7 @@ struct Variant {
   int scale_mode;  // CPG_SCALE_TENSOR (plain kernel) or CPG_SCALE_BLOCK
   const void* fn;
   int (*smem_bytes)(int, int, int);
+  int threads;
 };
 
 template <int BN, int CG>
@@ -117,7 +118,7 @@ template <int BN, int CG, typename AB, typename OutT>
 Variant make_variant() {
   KernelFn fn = &cpg::gemm_sm100_kernel<BN, CG, AB, OutT>;
   return Variant{BN, CG, dtype_code<AB>(), dtype_code<OutT>(), CPG_SCALE_TENSOR,
-                 reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>};
+                 reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>, cpg::kNumThreads};
 }
 
 template <int CG>
@@ -131,7 +132,7 @@ Variant make_block_variant() {
                            const cpg::GemmParams, const cpg::BlockScales);
   BlockFn fn = &cpg::gemm_fp8_block_kernel<CG>;
   return Variant{cpg::kBlockBN, CG, CPG_DTYPE_E4M3, CPG_DTYPE_BF16, CPG_SCALE_BLOCK,
-                 reinterpret_cast<const void*>(fn), &block_smem_bytes_of<CG>};
+                 reinterpret_cast<const void*>(fn), &block_smem_bytes_of<CG>, cpg::kBlockThreads};
 }
 
 template <typename AB, typename OutT>
@@ -211,7 +212,7 @@ int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* o
   cudaGetDevice(&dev);
   if (cm * cn == 1) {
     int per_sm = 0, sms = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, cpg::kNumThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.threads, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
@@ -225,7 +226,7 @@ int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* o
   attr[0].val.clusterDim.y = cn;
   attr[0].val.clusterDim.z = 1;
   lc.gridDim = dim3(cm, cn, 1);
-  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.blockDim = dim3(v.threads, 1, 1);
   lc.dynamicSmemBytes = smem;
   lc.attrs = attr;
   lc.numAttrs = 1;
@@ -496,7 +497,7 @@ int cpg_gemm_launch_info(const cpg_gemm* g, int32_t grid[3], int32_t cluster[3],
     if (grid) grid[i] = g->grid[i];
     if (cluster) cluster[i] = g->cluster[i];
   }
-  if (threads) *threads = cpg::kNumThreads;
+  if (threads) *threads = g->v.threads;
   if (smem_bytes) *smem_bytes = g->smem_bytes;
   if (max_active_clusters) *max_active_clusters = g->max_active_clusters;
   return CPG_OK;
@@ -647,7 +648,7 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   cudaLaunchConfig_t lc = {};
   cudaLaunchAttribute attr[1];
   lc.gridDim = dim3(g->grid[0], g->grid[1], g->grid[2]);
-  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.blockDim = dim3(g->v.threads, 1, 1);
   lc.dynamicSmemBytes = g->smem_bytes;
   lc.stream = st;
   lc.numAttrs = 0;
@@ -1000,7 +1001,7 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   cudaLaunchConfig_t lc = {};
   cudaLaunchAttribute attr[1];
   lc.gridDim = dim3(grid[0], grid[1], grid[2]);
-  lc.blockDim = dim3(cpg::kNumThreads, 1, 1);
+  lc.blockDim = dim3(v.threads, 1, 1);
   lc.dynamicSmemBytes = smem;
   lc.stream = st;
   if (cfg->cluster_m * cfg->cluster_n > 1) {

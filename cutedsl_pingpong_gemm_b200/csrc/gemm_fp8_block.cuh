@@ -9,10 +9,10 @@
 //   warp 1     MMA issuer: each k-block's 4 tcgen05.mma kind::f8f6f4 write a fresh partial
 //              product P_kb into one of 4 TMEM partial buffers (128 lanes x 128 fp32 columns),
 //              committed to that buffer's `part_full` barrier.
-//   warps 2-5  promotion + epilogue: each thread owns one row of the tile and keeps its 128
-//              running fp32 sums in registers; per k-block it loads P_kb from TMEM, adds
-//              sa * sb * P_kb, frees the partial buffer, and after the last k-block rounds to
-//              BF16 and TMA-stores the row chunks.
+//   warps 2-9  promotion + epilogue: each thread owns 64 columns of one row of the tile and
+//              keeps those running fp32 sums in registers; per k-block it loads its part of P_kb
+//              from TMEM, adds sa * sb * P_kb, frees the partial buffer, and after the last
+//              k-block rounds to BF16 and TMA-stores its 128-byte row chunk.
 // Tiles are 128 x 128 per CTA (256 x 128 per CTA pair); tile order, pairs, bounded waits and
 // drains are as in gemm_sm100_kernel.
 #pragma once
@@ -22,6 +22,13 @@ namespace cpg {
 
 constexpr int kBlockBN = 128;
 constexpr int kNumParts = 4;
+// Eight promotion warps: two per TMEM lane quadrant, each owning 64 of the tile's 128 columns
+// (warp w covers lanes 32 (w mod 4) .. +31 and columns 64 ((w - 2) / 4) .. +63).  Splitting the
+// columns halves the per-warp FMA and TMEM-load work per k-block, which keeps the promotion
+// within the MMA time of a k-block.
+constexpr int kBlockEpiWarps = 8;
+constexpr int kBlockThreads = (kEpiFirstWarp + kBlockEpiWarps) * 32;  // 320
+constexpr int kBlockColsPerWarp = kBlockBN / (kBlockEpiWarps / 4);    // 64
 
 template <int CtaGroup>
 struct BlockSmem {
@@ -31,7 +38,7 @@ struct BlockSmem {
   static constexpr int kTmemCols = kNumParts * kBlockBN;  // 512
   static __host__ __device__ int epi_offset(int stages) { return stages * kStageBytes; }
   static __host__ __device__ int barrier_offset(int stages, int epi_stages) {
-    return epi_offset(stages) + kEpiWarps * epi_stages * kEpiBufBytes;
+    return epi_offset(stages) + kBlockEpiWarps * epi_stages * kEpiBufBytes;
   }
   // full[S], empty[S], part_full[4], part_empty[4], drain[1]; then tmem slot and abort flag.
   static __host__ __device__ int bytes(int stages, int epi_stages, int /*reuse_ab*/) {
@@ -46,7 +53,7 @@ struct BlockScales {
 };
 
 template <int CtaGroup>
-__global__ void __launch_bounds__(kNumThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
     gemm_fp8_block_kernel(const __grid_constant__ CUtensorMap tm_a,
                           const __grid_constant__ CUtensorMap tm_b,
                           const __grid_constant__ CUtensorMap tm_d, const GemmParams p,
@@ -88,7 +95,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     for (int b = 0; b < kNumParts; ++b) {
       ptx::mbar_init(pfull_bar + 8u * b, 1);
-      ptx::mbar_init(pempty_bar + 8u * b, kEpiWarps * CtaGroup);
+      ptx::mbar_init(pempty_bar + 8u * b, kBlockEpiWarps * CtaGroup);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -173,9 +180,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- promotion + epilogue
-    const uint32_t ew = warp - kEpiFirstWarp;
-    const uint32_t quad = warp & 3u;
+    const uint32_t ew = warp - kEpiFirstWarp;  // 0..7
+    const uint32_t quad = warp & 3u;           // TMEM lane quadrant this warp may access
     const uint32_t row_in_tile = quad * 32u;
+    const uint32_t col_off = (ew >> 2) * kBlockColsPerWarp;
     const int64_t nkb_total = k_iters;
     int part = 0;
     uint32_t part_phase = 0;
@@ -196,9 +204,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int32_t my_row = g_row + static_cast<int32_t>(lane);
       const bool row_ok = my_row < p.m;
       const float* sb_row = scales.sb + static_cast<int64_t>(pid_n) * nkb_total;
-      float acc[kBlockBN];
+      float acc[kBlockColsPerWarp];
 #pragma unroll
-      for (int j = 0; j < kBlockBN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < kBlockColsPerWarp; ++j) acc[j] = 0.f;
       // Scales are fetched kScalePrefetch k-blocks ahead into a register ring (the loop below
       // is unrolled by the ring length so the ring stays in registers): every k-block's scales
       // sit in a different cache line, and fetching them just in time stalls on memory latency.
@@ -226,18 +234,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             continue;
           }
           ptx::tc_fence_after();
-          const uint32_t t_row =
-              tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(part * kBlockBN);
-#pragma unroll
-          for (int h = 0; h < kBlockBN / 64; ++h) {
+          const uint32_t t_row = tmem_base + (row_in_tile << 16) +
+                                 static_cast<uint32_t>(part * kBlockBN) + col_off;
+          {
             uint32_t v0[32], v1[32];
-            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h), v0);
-            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(64 * h + 32), v1);
+            ptx::tmem_ld_32x32b_x32(t_row, v0);
+            ptx::tmem_ld_32x32b_x32(t_row + 32u, v1);
             ptx::tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              acc[64 * h + i] = fmaf(s, __uint_as_float(v0[i]), acc[64 * h + i]);
-              acc[64 * h + 32 + i] = fmaf(s, __uint_as_float(v1[i]), acc[64 * h + 32 + i]);
+              acc[i] = fmaf(s, __uint_as_float(v0[i]), acc[i]);
+              acc[32 + i] = fmaf(s, __uint_as_float(v1[i]), acc[32 + i]);
             }
           }
           ptx::tc_fence_before();
@@ -257,10 +264,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
       if (!ok) break;
-      // Round the row to BF16 and store it in two 64-column chunks.
-#pragma unroll
-      for (int c = 0; c < kBlockBN / 64; ++c) {
-        const int32_t col0 = pid_n * kBlockBN + 64 * c;
+      // Round this warp's 64 columns of the row to BF16 and store them (one 128-byte row).
+      {
+        const int32_t col0 = pid_n * kBlockBN + static_cast<int32_t>(col_off);
         // Lane l holds bias[col0 + l] and bias[col0 + 32 + l]; shuffles broadcast them.
         const bool has_bias = p.bias != nullptr;
         const int32_t nb = col0 + static_cast<int32_t>(lane);
@@ -270,10 +276,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int j0 = 2 * i, j1 = 2 * i + 1;
-          const float x0 = acc[64 * c + j0] * p.alpha +
-                           __shfl_sync(0xffffffffu, j0 < 32 ? b0 : b1, j0 & 31);
-          const float x1 = acc[64 * c + j1] * p.alpha +
-                           __shfl_sync(0xffffffffu, j1 < 32 ? b0 : b1, j1 & 31);
+          const float x0 = acc[j0] * p.alpha + __shfl_sync(0xffffffffu, j0 < 32 ? b0 : b1, j0 & 31);
+          const float x1 = acc[j1] * p.alpha + __shfl_sync(0xffffffffu, j1 < 32 ? b0 : b1, j1 & 31);
           packed[i] = ptx::pack_bf16x2(x0, x1);
         }
         const int buf = epi_idx % p.epi_stages;
