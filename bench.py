@@ -65,7 +65,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["cpg", "reference"], default="cpg")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_8192")
-    ap.add_argument("--tile-n", type=int, default=0, help="0 = 512 for BF16/FP8 (pairs), 128 for block FP8")
+    ap.add_argument("--tile-n", type=int, default=0, help="0 = 512 for BF16/FP8 (pairs), 256 for block FP8")
     ap.add_argument("--cluster-m", type=int, default=2)
     ap.add_argument("--stages", type=int, default=0, help="0 = deepest that fits")
     ap.add_argument("--split-k", type=int, default=0, help="small-M only: 0 auto, -1 Stream-K, S splits")
@@ -398,14 +398,15 @@ def run_cpg(args, world, rank, local):
         else:
             a, scale_a = quantize_e4m3(a, (1, 128))
             b, scale_b = quantize_e4m3(b, (128, 128))
-            tile_n = 128
+            tile_n = args.tile_n if args.tile_n in (128, 256) else 256
         torch.cuda.synchronize()
 
     cm = args.cluster_m
     stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
                                                                                    8 if cm == 2 else 6)
     if w["fp8"] == "block" and not args.stages:
-        stages = 6  # 8 promotion warps stage 64 KiB of epilogue output
+        # Largest ring next to 8 promotion warps x 2 epilogue buffers (64 KiB).
+        stages = {(128, 1): 4, (128, 2): 6, (256, 1): 3, (256, 2): 5}[(tile_n, cm)]
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)

@@ -121,18 +121,19 @@ Variant make_variant() {
                  reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>, cpg::kNumThreads};
 }
 
-template <int CG>
+template <int BN, int CG>
 int block_smem_bytes_of(int stages, int epi_stages, int reuse_ab) {
-  return cpg::BlockSmem<CG>::bytes(stages, epi_stages, reuse_ab);
+  return cpg::BlockSmem<BN, CG>::bytes(stages, epi_stages, reuse_ab);
 }
 
-template <int CG>
+template <int BN, int CG>
 Variant make_block_variant() {
   using BlockFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                            const cpg::GemmParams, const cpg::BlockScales);
-  BlockFn fn = &cpg::gemm_fp8_block_kernel<CG>;
-  return Variant{cpg::kBlockBN, CG, CPG_DTYPE_E4M3, CPG_DTYPE_BF16, CPG_SCALE_BLOCK,
-                 reinterpret_cast<const void*>(fn), &block_smem_bytes_of<CG>, cpg::kBlockThreads};
+  BlockFn fn = &cpg::gemm_fp8_block_kernel<BN, CG>;
+  return Variant{BN, CG, CPG_DTYPE_E4M3, CPG_DTYPE_BF16, CPG_SCALE_BLOCK,
+                 reinterpret_cast<const void*>(fn), &block_smem_bytes_of<BN, CG>,
+                 cpg::BlockShape<BN>::kThreads};
 }
 
 template <typename AB, typename OutT>
@@ -149,7 +150,7 @@ void add_variants(Variant* t, int& n) {
 
 bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, int scale_mode,
                   Variant* out) {
-  static Variant table[34];
+  static Variant table[36];
   static int count = 0;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -157,8 +158,10 @@ bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, int scale_mo
     add_variants<__nv_bfloat16, float>(table, count);
     add_variants<cpg::e4m3_t, __nv_bfloat16>(table, count);
     add_variants<cpg::e4m3_t, float>(table, count);
-    table[count++] = make_block_variant<1>();
-    table[count++] = make_block_variant<2>();
+    table[count++] = make_block_variant<128, 1>();
+    table[count++] = make_block_variant<128, 2>();
+    table[count++] = make_block_variant<256, 1>();
+    table[count++] = make_block_variant<256, 2>();
   });
   if (scale_mode != CPG_SCALE_BLOCK) scale_mode = CPG_SCALE_TENSOR;
   for (int i = 0; i < count; ++i) {
@@ -377,9 +380,10 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   if (prob->scale_mode != CPG_SCALE_TENSOR && prob->scale_mode != CPG_SCALE_BLOCK)
     return fail(CPG_ERR_INVALID_CONFIG, "scale_mode must be 0 (none / per tensor) or 1 (block)");
   if (prob->scale_mode == CPG_SCALE_BLOCK &&
-      (prob->dtype_ab != CPG_DTYPE_E4M3 || prob->dtype_d != CPG_DTYPE_BF16 || cfg->tile_n != 128))
+      (prob->dtype_ab != CPG_DTYPE_E4M3 || prob->dtype_d != CPG_DTYPE_BF16 ||
+       (cfg->tile_n != 128 && cfg->tile_n != 256)))
     return fail(CPG_ERR_UNSUPPORTED,
-                "block scales need E4M3 operands, BF16 output and tile_n 128");
+                "block scales need E4M3 operands, BF16 output and tile_n 128 or 256");
   if (!find_variant(cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d, prob->scale_mode, &v))
     return fail(CPG_ERR_UNSUPPORTED, "no kernel for tile_n %d, cta_group %d, dtypes %d/%d",
                 cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);

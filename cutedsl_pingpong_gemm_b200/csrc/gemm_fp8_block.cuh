@@ -7,42 +7,59 @@
 // k-blocks, which cannot represent fp32 scales, so the scaling is applied to fp32 partial sums:
 //   warp 0     TMA producer (shared with the plain kernel), one 128-element k-block per stage.
 //   warp 1     MMA issuer: each k-block's 4 tcgen05.mma kind::f8f6f4 write a fresh partial
-//              product P_kb into one of 4 TMEM partial buffers (128 lanes x 128 fp32 columns),
-//              committed to that buffer's `part_full` barrier.
-//   warps 2-9  promotion + epilogue: each thread owns 64 columns of one row of the tile and
+//              product P_kb into one of 512 / BN TMEM partial buffers (128 lanes x BN fp32
+//              columns), committed to that buffer's `part_full` barrier.
+//   8 warps    promotion + epilogue: each thread owns BN / 2 columns of one row of the tile and
 //              keeps those running fp32 sums in registers; per k-block it loads its part of P_kb
-//              from TMEM, adds sa * sb * P_kb, frees the partial buffer, and after the last
-//              k-block rounds to BF16 and TMA-stores its 128-byte row chunk.
-// Tiles are 128 x 128 per CTA (256 x 128 per CTA pair); tile order, pairs, bounded waits and
-// drains are as in gemm_sm100_kernel.
+//              from TMEM, adds sa * sb * P_kb (packed fp32x2 FMAs), frees the partial buffer, and
+//              after the last k-block rounds to BF16 and TMA-stores its 128-byte row chunks.
+// Tiles are 128 x BN per CTA (256 x BN per CTA pair), BN = 128 or 256.  Per k-block a CTA loads
+// 16 KiB of A and BN / CtaGroup rows of B from L2; the 256-wide tile does 1.5x the flops per
+// loaded byte of the 128-wide one, whose throughput is bounded by that L2 -> SM traffic.  It has
+// two partial buffers instead of four and 128 running sums per thread, which fit only after a
+// register split: 384 threads launch with 168 registers each, then the warpgroup of the producer
+// and MMA warps (two of its warps idle) drops to 40 and the two promotion warpgroups rise to 232
+// (128 * 40 + 256 * 232 = 384 * 168).  Tile order, pairs, bounded waits and drains are as in
+// gemm_sm100_kernel.
 #pragma once
 #include "gemm_kernel.cuh"
 
 namespace cpg {
 
-constexpr int kBlockBN = 128;
-constexpr int kNumParts = 4;
-// Eight promotion warps: two per TMEM lane quadrant, each owning 64 of the tile's 128 columns
-// (warp w covers lanes 32 (w mod 4) .. +31 and columns 64 ((w - 2) / 4) .. +63).  Splitting the
-// columns halves the per-warp FMA and TMEM-load work per k-block, which keeps the promotion
-// within the MMA time of a k-block.
 constexpr int kBlockEpiWarps = 8;
-constexpr int kBlockThreads = (kEpiFirstWarp + kBlockEpiWarps) * 32;  // 320
-constexpr int kBlockColsPerWarp = kBlockBN / (kBlockEpiWarps / 4);    // 64
 
-template <int CtaGroup>
+// Promotion warps: two per TMEM lane quadrant, each owning half of the tile's columns (warp w
+// covers lanes 32 (w mod 4) .. +31 and columns (BN / 2) ((w - first) / 4) .. +BN/2-1), so a
+// warp's columns never straddle a 128-column scale block of B.
+template <int BN>
+struct BlockShape {
+  static_assert(BN == 128 || BN == 256, "block-scaled tiles are 128 or 256 columns wide");
+  static constexpr int kParts = 512 / BN;                         // TMEM partial buffers
+  static constexpr int kColsPerWarp = BN / (kBlockEpiWarps / 4);  // 64 or 128
+  static constexpr bool kSplitRegs = BN == 256;
+  static constexpr int kFirstPromoWarp = kSplitRegs ? 4 : 2;
+  static constexpr int kThreads = (kFirstPromoWarp + kBlockEpiWarps) * 32;  // 320 or 384
+  static constexpr int kLaunchRegs = 168;  // 65536 / 384, rounded down to a multiple of 8
+  static constexpr int kLowRegs = 40;
+  static constexpr int kHighRegs = 232;
+  static_assert(!kSplitRegs || 128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs,
+                "register split must add up to the launch allocation");
+};
+
+template <int BN, int CtaGroup>
 struct BlockSmem {
   static constexpr int kAStageBytes = kBM * kRowBytes;
-  static constexpr int kBStageBytes = (kBlockBN / CtaGroup) * kRowBytes;
+  static constexpr int kBStageBytes = (BN / CtaGroup) * kRowBytes;
   static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
-  static constexpr int kTmemCols = kNumParts * kBlockBN;  // 512
+  static constexpr int kTmemCols = 512;
   static __host__ __device__ int epi_offset(int stages) { return stages * kStageBytes; }
   static __host__ __device__ int barrier_offset(int stages, int epi_stages) {
     return epi_offset(stages) + kBlockEpiWarps * epi_stages * kEpiBufBytes;
   }
-  // full[S], empty[S], part_full[4], part_empty[4], drain[1]; then tmem slot and abort flag.
+  // full[S], empty[S], part_full[P], part_empty[P], drain[1]; then tmem slot and abort flag.
   static __host__ __device__ int bytes(int stages, int epi_stages, int /*reuse_ab*/) {
-    int b = barrier_offset(stages, epi_stages) + (2 * stages + 2 * kNumParts + 1) * 8 + 16 + 1024;
+    int b = barrier_offset(stages, epi_stages) +
+            (2 * stages + 2 * BlockShape<BN>::kParts + 1) * 8 + 16 + 1024;
     return b < kMinSmemForOneCtaPerSm ? kMinSmemForOneCtaPerSm : b;
   }
 };
@@ -52,17 +69,20 @@ struct BlockScales {
   const float* sb;  // [ceil(N/128), ceil(K/128)]
 };
 
-template <int CtaGroup>
-__global__ void __launch_bounds__(kBlockThreads, 1)
+template <int BN, int CtaGroup>
+__global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
     gemm_fp8_block_kernel(const __grid_constant__ CUtensorMap tm_a,
                           const __grid_constant__ CUtensorMap tm_b,
                           const __grid_constant__ CUtensorMap tm_d, const GemmParams p,
                           const BlockScales scales) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using L = BlockSmem<CtaGroup>;
+  using L = BlockSmem<BN, CtaGroup>;
+  using Shape = BlockShape<BN>;
+  constexpr int kParts = Shape::kParts;
+  constexpr int kCols = Shape::kColsPerWarp;
   constexpr int kBK = OperandTraits<e4m3_t>::kBK;        // 128
   constexpr int kUmmaK = OperandTraits<e4m3_t>::kUmmaK;  // 32
-  constexpr uint32_t kIdesc = ptx::make_idesc_e4m3_f32(kBM * CtaGroup, kBlockBN);
+  constexpr uint32_t kIdesc = ptx::make_idesc_e4m3_f32(kBM * CtaGroup, BN);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
@@ -74,9 +94,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const uint32_t bar_base = base + L::barrier_offset(stages, p.epi_stages);
   const uint32_t full_bar = bar_base;
   const uint32_t empty_bar = bar_base + 8u * stages;
-  const uint32_t pfull_bar = bar_base + 16u * stages;       // [kNumParts]
-  const uint32_t pempty_bar = pfull_bar + 8u * kNumParts;   // [kNumParts]
-  const uint32_t drain_bar = pempty_bar + 8u * kNumParts;
+  const uint32_t pfull_bar = bar_base + 16u * stages;   // [kParts]
+  const uint32_t pempty_bar = pfull_bar + 8u * kParts;  // [kParts]
+  const uint32_t drain_bar = pempty_bar + 8u * kParts;
   uint8_t* slot_ptr = base_ptr + (drain_bar + 8u - base);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(slot_ptr);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(slot_ptr + 4);
@@ -93,7 +113,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       ptx::mbar_init(full_bar + 8u * s, 1);
       ptx::mbar_init(empty_bar + 8u * s, 1);
     }
-    for (int b = 0; b < kNumParts; ++b) {
+    for (int b = 0; b < kParts; ++b) {
       ptx::mbar_init(pfull_bar + 8u * b, 1);
       ptx::mbar_init(pempty_bar + 8u * b, kBlockEpiWarps * CtaGroup);
     }
@@ -121,70 +141,77 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const SchedParams& sp = p.sched;
   const int k_iters = p.k_iters;
 
-  if (warp == 0) {
-    if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
-      producer_loop<kBlockBN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
-          &tm_a, &tm_b, sp, k_iters, k_iters, stages, base, full_bar, empty_bar, rank, leader,
-          ctx);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (leader && lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int part = 0;
-      uint32_t part_phase = 0;
-      bool ok = true;
-      for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
-        for (int kb = 0; kb < k_iters; ++kb) {
-          if (!ptx::mbar_wait(pempty_bar + 8u * part, part_phase ^ 1u, ctx, kSiteMmaTmemEmpty) ||
-              !ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(part * kBlockBN);
-          const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
-          const uint64_t da = ptx::make_sw128_kmajor_desc(sa);
-          const uint64_t db = ptx::make_sw128_kmajor_desc(sa + L::kAStageBytes);
-#pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
-                                      db + static_cast<uint64_t>(2 * k), kIdesc, k > 0 ? 1u : 0u);
-          }
-          const uint32_t eb = empty_bar + 8u * stage;
-          const uint32_t pb = pfull_bar + 8u * part;
-          if constexpr (CtaGroup == 1) {
-            ptx::umma_commit<1>(eb);
-            ptx::umma_commit<1>(pb);
-          } else {
-            ptx::umma_commit_pair(eb, pair_mask);
-            ptx::umma_commit_pair(pb, pair_mask);
-          }
-          if (++stage == stages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-          if (++part == kNumParts) {
-            part = 0;
-            part_phase ^= 1u;
+  // Each warpgroup changes its register budget inside its own role branch, so the compiler
+  // allocates the producer / MMA code and the promotion code separately.
+  if (warp < static_cast<uint32_t>(Shape::kFirstPromoWarp)) {
+    if constexpr (Shape::kSplitRegs) ptx::setmaxnreg_dec<Shape::kLowRegs>();
+    if (warp == 0) {
+      if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
+        producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
+            &tm_a, &tm_b, sp, k_iters, k_iters, stages, base, full_bar, empty_bar, rank, leader,
+            ctx, p.l2_policy_a, p.l2_policy_b);
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      if (leader && lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int part = 0;
+        uint32_t part_phase = 0;
+        bool ok = true;
+        for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+          for (int kb = 0; kb < k_iters; ++kb) {
+            if (!ptx::mbar_wait(pempty_bar + 8u * part, part_phase ^ 1u, ctx, kSiteMmaTmemEmpty) ||
+                !ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(part * BN);
+            const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
+            const uint64_t da = ptx::make_sw128_kmajor_desc(sa);
+            const uint64_t db = ptx::make_sw128_kmajor_desc(sa + L::kAStageBytes);
+  #pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
+                                        db + static_cast<uint64_t>(2 * k), kIdesc, k > 0 ? 1u : 0u);
+            }
+            const uint32_t eb = empty_bar + 8u * stage;
+            const uint32_t pb = pfull_bar + 8u * part;
+            if constexpr (CtaGroup == 1) {
+              ptx::umma_commit<1>(eb);
+              ptx::umma_commit<1>(pb);
+            } else {
+              ptx::umma_commit_pair(eb, pair_mask);
+              ptx::umma_commit_pair(pb, pair_mask);
+            }
+            if (++stage == stages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            if (++part == kParts) {
+              part = 0;
+              part_phase ^= 1u;
+            }
           }
         }
+        ptx::umma_commit<CtaGroup>(drain_bar);
+        ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
+        volatile int32_t no_abort = 0;
+        dctx.abort_flag = &no_abort;
+        ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
       }
-      ptx::umma_commit<CtaGroup>(drain_bar);
-      ptx::WaitCtx dctx{abort_flag, p.status, p.timeout_ns};
-      volatile int32_t no_abort = 0;
-      dctx.abort_flag = &no_abort;
-      ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
+    if constexpr (Shape::kSplitRegs) ptx::setmaxnreg_inc<Shape::kHighRegs>();
     // ---------------------------------------------------------------- promotion + epilogue
-    const uint32_t ew = warp - kEpiFirstWarp;  // 0..7
-    const uint32_t quad = warp & 3u;           // TMEM lane quadrant this warp may access
+    const uint32_t ew = warp - Shape::kFirstPromoWarp;  // 0..7
+    const uint32_t quad = warp & 3u;                    // TMEM lane quadrant this warp may access
     const uint32_t row_in_tile = quad * 32u;
-    const uint32_t col_off = (ew >> 2) * kBlockColsPerWarp;
+    const uint32_t col_off = (ew >> 2) * kCols;
     const int64_t nkb_total = k_iters;
+    const int32_t n_blocks = (p.n + 127) / 128;  // rows of sb
     int part = 0;
     uint32_t part_phase = 0;
     int epi_idx = 0;
@@ -203,10 +230,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
       const int32_t my_row = g_row + static_cast<int32_t>(lane);
       const bool row_ok = my_row < p.m;
-      const float* sb_row = scales.sb + static_cast<int64_t>(pid_n) * nkb_total;
-      float acc[kBlockColsPerWarp];
+      const int32_t col0 = pid_n * BN + static_cast<int32_t>(col_off);
+      // This warp's columns lie in one 128-column scale block of B; past the last block of a
+      // ragged N (the right half of a 256-wide edge tile) the scale reads are skipped.
+      const int32_t nblk = col0 >> 7;
+      const bool nblk_ok = nblk < n_blocks;
+      const float* sb_row = scales.sb + static_cast<int64_t>(nblk_ok ? nblk : 0) * nkb_total;
+      float acc[kCols];
 #pragma unroll
-      for (int j = 0; j < kBlockColsPerWarp; ++j) acc[j] = 0.f;
+      for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
       // Scales are fetched kScalePrefetch k-blocks ahead into a register ring (the loop below
       // is unrolled by the ring length so the ring stays in registers): every k-block's scales
       // sit in a different cache line, and fetching them just in time stalls on memory latency.
@@ -215,7 +247,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 #pragma unroll
       for (int j = 0; j < kScalePrefetch; ++j) {
         ring_a[j] = (j < k_iters && row_ok) ? scales.sa[static_cast<int64_t>(j) * p.m + my_row] : 0.f;
-        ring_b[j] = j < k_iters ? sb_row[j] : 0.f;
+        ring_b[j] = (j < k_iters && nblk_ok) ? sb_row[j] : 0.f;
       }
       for (int kb0 = 0; ok && kb0 < k_iters; kb0 += kScalePrefetch) {
 #pragma unroll
@@ -226,7 +258,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           const int kn = kb + kScalePrefetch;
           ring_a[j] = (kn < k_iters && row_ok) ? scales.sa[static_cast<int64_t>(kn) * p.m + my_row]
                                                : 0.f;
-          ring_b[j] = kn < k_iters ? sb_row[kn] : 0.f;
+          ring_b[j] = (kn < k_iters && nblk_ok) ? sb_row[kn] : 0.f;
           bool got = ptx::mbar_wait(pfull_bar + 8u * part, part_phase, ctx, kSiteEpiTmemFull);
           got = __all_sync(0xffffffffu, got);
           if (!got) {
@@ -235,49 +267,60 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           }
           ptx::tc_fence_after();
           const uint32_t t_row = tmem_base + (row_in_tile << 16) +
-                                 static_cast<uint32_t>(part * kBlockBN) + col_off;
-          {
-            uint32_t v0[32], v1[32];
-            ptx::tmem_ld_32x32b_x32(t_row, v0);
-            ptx::tmem_ld_32x32b_x32(t_row + 32u, v1);
-            ptx::tmem_ld_wait();
+                                 static_cast<uint32_t>(part * BN) + col_off;
+          // 64 columns per TMEM round trip; the partial buffer is released as soon as its last
+          // columns are in registers, before their FMAs.
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              acc[i] = fmaf(s, __uint_as_float(v0[i]), acc[i]);
-              acc[32 + i] = fmaf(s, __uint_as_float(v1[i]), acc[32 + i]);
+          for (int c = 0; c < kCols; c += 64) {
+            uint32_t v0[32], v1[32];
+            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), v0);
+            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c) + 32u, v1);
+            ptx::tmem_ld_wait();
+            if (c + 64 == kCols) {
+              ptx::tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
+                if constexpr (CtaGroup == 1) {
+                  ptx::mbar_arrive(pb);
+                } else {
+                  ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              ptx::fma2(acc[c + i], acc[c + i + 1], s, __uint_as_float(v0[i]),
+                        __uint_as_float(v0[i + 1]));
+              ptx::fma2(acc[c + 32 + i], acc[c + 33 + i], s, __uint_as_float(v1[i]),
+                        __uint_as_float(v1[i + 1]));
             }
           }
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
-            if constexpr (CtaGroup == 1) {
-              ptx::mbar_arrive(pb);
-            } else {
-              ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
-            }
-          }
-          if (++part == kNumParts) {
+          if (++part == kParts) {
             part = 0;
             part_phase ^= 1u;
           }
         }
       }
       if (!ok) break;
-      // Round this warp's 64 columns of the row to BF16 and store them (one 128-byte row).
-      {
-        const int32_t col0 = pid_n * kBlockBN + static_cast<int32_t>(col_off);
-        // Lane l holds bias[col0 + l] and bias[col0 + 32 + l]; shuffles broadcast them.
-        const bool has_bias = p.bias != nullptr;
-        const int32_t nb = col0 + static_cast<int32_t>(lane);
+      // Round this warp's columns of the row to BF16 and store them, one 128-byte row chunk
+      // (64 columns) per TMA store.
+      const bool has_bias = p.bias != nullptr;
+#pragma unroll
+      for (int c = 0; c < kCols; c += 64) {
+        const int32_t cc = col0 + c;
+        // Lane l holds bias[cc + l] and bias[cc + 32 + l]; shuffles broadcast them.
+        const int32_t nb = cc + static_cast<int32_t>(lane);
         const float b0 = (has_bias && nb < p.n) ? __bfloat162float(p.bias[nb]) : 0.f;
         const float b1 = (has_bias && nb + 32 < p.n) ? __bfloat162float(p.bias[nb + 32]) : 0.f;
         uint32_t packed[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int j0 = 2 * i, j1 = 2 * i + 1;
-          const float x0 = acc[j0] * p.alpha + __shfl_sync(0xffffffffu, j0 < 32 ? b0 : b1, j0 & 31);
-          const float x1 = acc[j1] * p.alpha + __shfl_sync(0xffffffffu, j1 < 32 ? b0 : b1, j1 & 31);
+          const float x0 =
+              acc[c + j0] * p.alpha + __shfl_sync(0xffffffffu, j0 < 32 ? b0 : b1, j0 & 31);
+          const float x1 =
+              acc[c + j1] * p.alpha + __shfl_sync(0xffffffffu, j1 < 32 ? b0 : b1, j1 & 31);
           packed[i] = ptx::pack_bf16x2(x0, x1);
         }
         const int buf = epi_idx % p.epi_stages;
@@ -295,7 +338,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ptx::fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
-          if (g_row < p.m && col0 < p.n) ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+          if (g_row < p.m && cc < p.n) ptx::tma_store_2d(&tm_d, sbuf, cc, g_row);
           ptx::bulk_commit_group();
         }
         __syncwarp();

@@ -421,6 +421,29 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// (c0, c1) += s * (x0, x1): one packed fp32x2 FMA (round-to-nearest per element, the same result
+// as two fmaf calls), which halves the FMA issue slots on sm_100a.
+__device__ __forceinline__ void fma2(float& c0, float& c1, float s, float x0, float x1) {
+  asm("{\n\t.reg .b64 xa, sa, ca;\n\t"
+      "mov.b64 xa, {%2, %3};\n\t"
+      "mov.b64 sa, {%4, %4};\n\t"
+      "mov.b64 ca, {%0, %1};\n\t"
+      "fma.rn.f32x2 ca, xa, sa, ca;\n\t"
+      "mov.b64 {%0, %1}, ca;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(x0), "f"(x1), "f"(s));
+}
+
+// Per-warpgroup register budget changes (all four warps of a warpgroup execute the same one).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),

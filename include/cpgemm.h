@@ -58,7 +58,7 @@ extern "C" {
 /* FP8 scale modes.  TENSOR: optional per-tensor scales (cpg_epilogue.scale_a / scale_b point to
  * one fp32 each).  BLOCK: scale_a points to A's 1 x 128 scales laid out [ceil(K/128)][M] and
  * scale_b to B's 128 x 128 scales laid out [ceil(N/128)][ceil(K/128)] (both fp32); requires
- * tile_n = 128 and BF16 output. */
+ * tile_n = 128 or 256 and BF16 output. */
 #define CPG_SCALE_TENSOR 0
 #define CPG_SCALE_BLOCK 1
 

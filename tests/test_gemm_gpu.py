@@ -314,30 +314,40 @@ def test_fp32_output(cluster, tile_n):
 
 
 # ---------------------------------------------------------------- FP8 E4M3 (block scales)
+def _block_stages(tile_n, cluster):
+    # Largest ring that fits next to 8 warps x 2 epilogue buffers (227 KiB of shared memory).
+    return {(128, 1): 4, (128, 2): 6, (256, 1): 3, (256, 2): 5}[(tile_n, cluster[0])]
+
+
 @pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
+@pytest.mark.parametrize("tile_n", [128, 256])
 @pytest.mark.parametrize("shape", [(128, 128, 128), (256, 384, 1024), (300, 264, 1000 + 8),
-                                   (1024, 1024, 2048)])
-def test_fp8_block_scaled(shape, cluster):
+                                   (1024, 1024, 2048), (136, 392, 272)])
+def test_fp8_block_scaled(shape, tile_n, cluster):
     """BASELINE config 4 (block variant): A scaled per 1x128, B per 128x128, against the fp32
-    product of the block-dequantised operands."""
+    product of the block-dequantised operands.  N = 264 and 392 leave 256-wide edge tiles whose
+    right half lies past the last scale block of B."""
     m, n, k = shape
     g = torch.Generator().manual_seed(m * 7 + n + k)
     a = torch.randn(m, k, generator=g) * torch.rand(m, 1, generator=g) * 4
     b = torch.randn(n, k, generator=g) * torch.rand(n, 1, generator=g) * 4
     qa, sa = gemm_ref.quantize_e4m3_blocks(a, (1, 128))
     qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
+    bias = (torch.randn(n, generator=g) * 4).to(torch.bfloat16) if n % 2 == 0 else None
     d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-    gemm = make_gemm(128, cluster)
-    gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda())
+    gemm = make_gemm(tile_n, cluster, stages=_block_stages(tile_n, cluster))
+    gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda(),
+         bias=None if bias is None else bias.cuda())
     torch.cuda.synchronize()
     da = gemm_ref.dequantize_blocks(qa, sa, (1, 128))
     db = gemm_ref.dequantize_blocks(qb, sb, (128, 128))
-    res = gemm_ref.check(d.cpu(), da, db, frob_tol=gemm_ref.FROB_TOL_FP8)
+    res = gemm_ref.check(d.cpu(), da, db, bias=bias, frob_tol=gemm_ref.FROB_TOL_FP8)
     assert res["ok"], res
     assert res["frob"] < 1e-2
 
 
-def test_fp8_block_scaled_many_tiles_per_cta():
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_fp8_block_scaled_many_tiles_per_cta(tile_n):
     """Persistent CTAs with several tiles each (partial-buffer phases wrap many times)."""
     m, n, k = 2048, 2048, 512
     g = torch.Generator().manual_seed(5)
@@ -346,7 +356,7 @@ def test_fp8_block_scaled_many_tiles_per_cta():
     qa, sa = gemm_ref.quantize_e4m3_blocks(a, (1, 128))
     qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    gemm = make_gemm(128, (2, 1, 1), stages=6)
+    gemm = make_gemm(tile_n, (2, 1, 1), stages=_block_stages(tile_n, (2, 1, 1)))
     gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda())
     torch.cuda.synchronize()
     rows = torch.arange(0, m, 7)
