@@ -404,13 +404,17 @@ def run_cpg(args, world, rank, local):
     cm = args.cluster_m
     stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
                                                                                    8 if cm == 2 else 6)
+    epi_stage = 2
     if w["fp8"] == "block" and not args.stages:
-        # Largest ring next to 8 promotion warps x 2 epilogue buffers (64 KiB).
-        stages = {(128, 1): 4, (128, 2): 6, (256, 1): 3, (256, 2): 5}[(tile_n, cm)]
+        # Deepest ring that fits 227 KiB next to 8 promotion warps' epilogue staging (4 KiB per
+        # warp and epilogue stage).
+        stages, epi_stage = {(128, 1): (5, 2), (128, 2): (8, 1), (256, 1): (4, 1),
+                             (256, 2): (6, 1)}[(tile_n, cm)]
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
-                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
-    compiled = cpg_compile(gemm, a, b, d, stream)
+                    epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
+                    is_persistent=True)
+    compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b)
     split_k = (args.split_k if args.split_k else compiled.auto_split_k(m, n, k)) if w.get("small_m") else 1
     compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k)
     torch.cuda.synchronize()

@@ -69,6 +69,13 @@ struct BlockScales {
   const float* sb;  // [ceil(N/128), ceil(K/128)]
 };
 
+// acc[j] += s * v[j] for 32 columns (16 packed FMAs).
+__device__ __forceinline__ void promote32(float* acc, float s, const uint32_t (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2)
+    ptx::fma2(acc[i], acc[i + 1], s, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+}
+
 template <int BN, int CtaGroup>
 __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
     gemm_fp8_block_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
             const uint32_t sa = base + static_cast<uint32_t>(stage * L::kStageBytes);
             const uint64_t da = ptx::make_sw128_kmajor_desc(sa);
             const uint64_t db = ptx::make_sw128_kmajor_desc(sa + L::kAStageBytes);
-  #pragma unroll
+#pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
               ptx::umma_f8_ss<CtaGroup>(d_tmem, da + static_cast<uint64_t>(2 * k),
                                         db + static_cast<uint64_t>(2 * k), kIdesc, k > 0 ? 1u : 0u);
@@ -268,33 +275,38 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
           ptx::tc_fence_after();
           const uint32_t t_row = tmem_base + (row_in_tile << 16) +
                                  static_cast<uint32_t>(part * BN) + col_off;
-          // 64 columns per TMEM round trip; the partial buffer is released as soon as its last
-          // columns are in registers, before their FMAs.
-#pragma unroll
-          for (int c = 0; c < kCols; c += 64) {
-            uint32_t v0[32], v1[32];
-            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c), v0);
-            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c) + 32u, v1);
-            ptx::tmem_ld_wait();
-            if (c + 64 == kCols) {
-              ptx::tc_fence_before();
-              __syncwarp();
-              if (lane == 0) {
-                const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
-                if constexpr (CtaGroup == 1) {
-                  ptx::mbar_arrive(pb);
-                } else {
-                  ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
-                }
+          const uint32_t pb = pempty_bar + 8u * static_cast<uint32_t>(part);
+          auto release = [&]() {
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (CtaGroup == 1) {
+                ptx::mbar_arrive(pb);
+              } else {
+                ptx::mbar_arrive_cluster(ptx::mapa_shared(pb, leader_rank));
               }
             }
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              ptx::fma2(acc[c + i], acc[c + i + 1], s, __uint_as_float(v0[i]),
-                        __uint_as_float(v0[i + 1]));
-              ptx::fma2(acc[c + 32 + i], acc[c + 33 + i], s, __uint_as_float(v1[i]),
-                        __uint_as_float(v1[i + 1]));
-            }
+          };
+          // Columns move through 64 registers, 32 per tcgen05.ld; the partial buffer is
+          // released as soon as its last columns are in registers, before their FMAs.
+          uint32_t va[32], vb[32];
+          ptx::tmem_ld_32x32b_x32(t_row, va);
+          ptx::tmem_ld_32x32b_x32(t_row + 32u, vb);
+          ptx::tmem_ld_wait();
+          if constexpr (kCols == 64) {
+            release();
+            promote32(acc, s, va);
+            promote32(acc + 32, s, vb);
+          } else {
+            // The loads of columns 64-127 overlap the FMAs of columns 0-63.
+            promote32(acc, s, va);
+            ptx::tmem_ld_32x32b_x32(t_row + 64u, va);
+            promote32(acc + 32, s, vb);
+            ptx::tmem_ld_32x32b_x32(t_row + 96u, vb);
+            ptx::tmem_ld_wait();
+            release();
+            promote32(acc + 64, s, va);
+            promote32(acc + 96, s, vb);
           }
           if (++part == kParts) {
             part = 0;

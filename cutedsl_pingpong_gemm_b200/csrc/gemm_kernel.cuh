@@ -276,7 +276,9 @@ __device__ __forceinline__ uint64_t l2_policy(int32_t which) {
 
 // TMA producer (one lane): streams the k-blocks of A (128 rows) and B (BN / CtaGroup rows) of
 // every tile of this CTA into the shared-memory stage ring, then drains its in-flight loads.
-template <int BN, int CtaGroup, int kBK, int kStageBytes, int kAStageBytes>
+// B is loaded as BN / kMmaN slots, one per MMA of width kMmaN.
+template <int BN, int CtaGroup, int kBK, int kStageBytes, int kAStageBytes,
+          int kMmaN = (BN > 256 ? 256 : BN)>
 __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUtensorMap* tm_b,
                                               const SchedParams& sp, int k_iters,
                                               int k_iters_per_split, int stages,
@@ -284,7 +286,6 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
                                               int32_t l2_b = 0, int32_t stream_k = 0) {
-  constexpr int kMmaN = BN > 256 ? 256 : BN;
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);

@@ -314,9 +314,11 @@ def test_fp32_output(cluster, tile_n):
 
 
 # ---------------------------------------------------------------- FP8 E4M3 (block scales)
-def _block_stages(tile_n, cluster):
-    # Largest ring that fits next to 8 warps x 2 epilogue buffers (227 KiB of shared memory).
-    return {(128, 1): 4, (128, 2): 6, (256, 1): 3, (256, 2): 5}[(tile_n, cluster[0])]
+def _block_gemm(tile_n, cluster):
+    # Deepest ring that fits 227 KiB next to 8 promotion warps' epilogue staging.
+    stages, epi = {(128, 1): (5, 2), (128, 2): (8, 1), (256, 1): (4, 1),
+                   (256, 2): (6, 1)}[(tile_n, cluster[0])]
+    return make_gemm(tile_n, cluster, stages=stages, epi_stage=epi)
 
 
 @pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1)])
@@ -335,7 +337,7 @@ def test_fp8_block_scaled(shape, tile_n, cluster):
     qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
     bias = (torch.randn(n, generator=g) * 4).to(torch.bfloat16) if n % 2 == 0 else None
     d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-    gemm = make_gemm(tile_n, cluster, stages=_block_stages(tile_n, cluster))
+    gemm = _block_gemm(tile_n, cluster)
     gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda(),
          bias=None if bias is None else bias.cuda())
     torch.cuda.synchronize()
@@ -356,7 +358,7 @@ def test_fp8_block_scaled_many_tiles_per_cta(tile_n):
     qa, sa = gemm_ref.quantize_e4m3_blocks(a, (1, 128))
     qb, sb = gemm_ref.quantize_e4m3_blocks(b, (128, 128))
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    gemm = make_gemm(tile_n, (2, 1, 1), stages=_block_stages(tile_n, (2, 1, 1)))
+    gemm = _block_gemm(tile_n, (2, 1, 1))
     gemm(qa.cuda(), qb.cuda(), d, None, scale_a=sa.cuda(), scale_b=sb.cuda())
     torch.cuda.synchronize()
     rows = torch.arange(0, m, 7)
