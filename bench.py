@@ -105,7 +105,7 @@ class ClockSampler:
         (0x2, "applications_clocks_setting"), (0x10, "sync_boost"),
     ]
 
-    def __init__(self, cuda_index, period_s=0.01):
+    def __init__(self, cuda_index, period_s=0.002):
         self.samples = []
         self.reasons = 0
         self.period = period_s
@@ -328,13 +328,14 @@ def run_tallk(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
-    sampler.start()
     launches[0] = 0
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
         out = step()
+        if i == 0:
+            sampler.start()  # the GPU is busy from here on: no idle-clock samples
     e1.record(stream)
     torch.cuda.synchronize()
     sampler.stop()
@@ -438,13 +439,14 @@ def run_cpg(args, world, rank, local):
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
-    sampler.start()
     launches[0] = 0
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
         step()
+        if i == 0:
+            sampler.start()  # the GPU is busy from here on: no idle-clock samples
     e1.record(stream)
     torch.cuda.synchronize()
     sampler.stop()

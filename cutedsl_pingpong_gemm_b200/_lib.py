@@ -32,7 +32,15 @@ CPG_SCALE_BLOCK = 1
 CPG_INJECT_SKIP_LOADS = 1
 CPG_SPLIT_K_STREAM = -1
 
-ABI_VERSION = 6
+CPG_ACT_NONE = 0
+CPG_ACT_RELU = 1
+CPG_ACT_SILU = 2
+CPG_ACT_GELU = 3
+CPG_ACT_GELU_TANH = 4
+ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
+               "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
+
+ABI_VERSION = 7
 
 
 class CpgError(RuntimeError):
@@ -82,12 +90,15 @@ class GemmProblemC(ctypes.Structure):
         ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldd", ctypes.c_int64),
         ("dtype_ab", ctypes.c_int32), ("dtype_d", ctypes.c_int32),
         ("scale_mode", ctypes.c_int32), ("split_k", ctypes.c_int32),
+        ("gated", ctypes.c_int32),
     ]
 
 
 class EpilogueC(ctypes.Structure):
     _fields_ = [("alpha", ctypes.c_float), ("bias", ctypes.c_void_p),
-                ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p)]
+                ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
+                ("beta", ctypes.c_float), ("activation", ctypes.c_int32),
+                ("source", ctypes.c_void_p), ("ld_source", ctypes.c_int64)]
 
 
 _P = ctypes.POINTER

@@ -271,7 +271,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 6; }
+int cpg_abi_version(void) { return 7; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -396,6 +396,15 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return fail(CPG_ERR_UNSUPPORTED, "split-K / Stream-K accumulate into an FP32 D (no block scales)");
   if (prob->split_k == CPG_SPLIT_K_STREAM && !cfg->is_persistent)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K needs a persistent kernel");
+  if (prob->gated != 0 && prob->gated != 1)
+    return fail(CPG_ERR_INVALID_CONFIG, "gated must be 0 or 1, got %d", prob->gated);
+  if (prob->gated && (cfg->tile_n != 512 || v.scale_mode != CPG_SCALE_TENSOR ||
+                      prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM))
+    return fail(CPG_ERR_UNSUPPORTED,
+                "gated GEMM needs tile_n 512 (256 gate + 256 up columns), no block scales and "
+                "no split-K");
+  if (prob->gated && prob->n > (int64_t(1) << 30))
+    return fail(CPG_ERR_INVALID_SHAPE, "gated GEMM: 2 N must fit in 31 bits");
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -428,7 +437,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     // dimension while the other operand streams once: keep that one.  Decode-like M = 128,
     // N = K = 8192: 44.1 -> 37.2 us per step.
     const int64_t row_tiles = (prob->m + 128 * cfg->cluster_m - 1) / (128 * cfg->cluster_m);
-    const int64_t col_tiles = (prob->n + cfg->tile_n - 1) / cfg->tile_n;
+    const int64_t tile_out = prob->gated ? cfg->tile_n / 2 : cfg->tile_n;
+    const int64_t col_tiles = (prob->n + tile_out - 1) / tile_out;
     if (row_tiles <= 2 && col_tiles > 2) {
       g->l2_policy_a = 2;
       g->l2_policy_b = 1;
@@ -443,7 +453,9 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   if (pb != nullptr) g->l2_policy_b = std::atoi(pb);
 
   const int64_t ntm = prob->m > 0 ? (prob->m + 127) / 128 : 1;
-  const int64_t ntn = prob->n > 0 ? (prob->n + cfg->tile_n - 1) / cfg->tile_n : 1;
+  // A gated tile stores 256 output columns (its 512 accumulator columns are gate and up).
+  const int64_t tile_out_n = prob->gated ? cfg->tile_n / 2 : cfg->tile_n;
+  const int64_t ntn = prob->n > 0 ? (prob->n + tile_out_n - 1) / tile_out_n : 1;
   // Split-K: the L index of the scheduler selects a K range of k_iters_per_split k-blocks;
   // every split is non-empty.
   const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
@@ -572,8 +584,29 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     return fail(CPG_ERR_ALIGNMENT, "D must be 16-byte aligned");
   if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u) != 0)
     return fail(CPG_ERR_ALIGNMENT, "bias must be 2-byte aligned");
+  const int32_t act = epi != nullptr ? epi->activation : CPG_ACT_NONE;
+  const void* src = epi != nullptr ? epi->source : nullptr;
+  if (act < CPG_ACT_NONE || act > CPG_ACT_GELU_TANH)
+    return fail(CPG_ERR_INVALID_CONFIG, "activation %d is not one of CPG_ACT_*", act);
+  if ((act != CPG_ACT_NONE || src != nullptr) && (g->splits > 1 || g->stream_k))
+    return fail(CPG_ERR_UNSUPPORTED,
+                "activations and a C source need the whole K in one pass (no split-K)");
+  if (g->v.scale_mode == CPG_SCALE_BLOCK && (act != CPG_ACT_NONE || src != nullptr))
+    return fail(CPG_ERR_UNSUPPORTED, "the block-scaled FP8 kernel has no activation or C source");
+  if (pr.gated && (bias != nullptr || src != nullptr))
+    return fail(CPG_ERR_UNSUPPORTED, "gated GEMM takes no bias and no C source");
+  if (src != nullptr) {
+    const int es = elem_bytes(pr.dtype_d);
+    if (epi->ld_source < pr.n || (epi->ld_source * es) % 16 != 0)
+      return fail(CPG_ERR_ALIGNMENT, "C row stride %lld must be >= N and a multiple of 16 bytes",
+                  static_cast<long long>(epi->ld_source));
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0)
+      return fail(CPG_ERR_ALIGNMENT, "C must be 16-byte aligned");
+  }
 
   if (pr.k == 0) {
+    if (act != CPG_ACT_NONE || src != nullptr)
+      return fail(CPG_ERR_UNSUPPORTED, "K = 0 with an activation or a C source");
     // D = bias (or 0): nothing to contract.
     int blocks = static_cast<int>((pr.m * pr.n + 255) / 256);
     if (blocks > 4096) blocks = 4096;
@@ -598,8 +631,9 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
     int rc = encode_2d(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM, bk);
     if (rc != CPG_OK) return rc;
-    // One B box per MMA: min(tile_n, 256) / cta_group rows.
-    rc = encode_2d(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
+    // One B box per MMA: min(tile_n, 256) / cta_group rows; a gated B holds 2 N rows.
+    rc = encode_2d(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.gated ? 2 * pr.n : pr.n, pr.k,
+                   pr.ldb,
                    (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk);
     if (rc != CPG_OK) return rc;
     rc = encode_2d(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols);
@@ -643,6 +677,11 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.fault_inject = g->fault_inject;
   p.l2_policy_a = g->l2_policy_a;
   p.l2_policy_b = g->l2_policy_b;
+  p.act = act;
+  p.beta = epi != nullptr ? epi->beta : 0.f;
+  p.src = src;
+  p.ld_src = src != nullptr ? epi->ld_source : 0;
+  p.gated = pr.gated;
 
   if (g->splits > 1 || g->stream_k) {
     // The splits / Stream-K segments add their partial sums into D.
@@ -896,6 +935,9 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   if (prob->dtype_d != CPG_DTYPE_BF16) return fail(CPG_ERR_DTYPE, "D must be BF16");
   if (prob->scale_mode != CPG_SCALE_TENSOR)
     return fail(CPG_ERR_UNSUPPORTED, "block-scaled FP8 is not available on this entry point");
+  if (prob->gated != 0 ||
+      (epi != nullptr && (epi->activation != CPG_ACT_NONE || epi->source != nullptr)))
+    return fail(CPG_ERR_UNSUPPORTED, "gated GEMM, activations and C are not available here");
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (prob->m < 0 || prob->n < 0 || prob->k < 0 || prob->m > lim || prob->n > lim ||
       prob->k > lim || prob->lda < prob->k || prob->ldb < prob->k || prob->ldd < prob->n ||

@@ -108,7 +108,33 @@ struct GemmParams {
   int32_t fault_inject;   // test hook: kInjectSkipLoads makes the producer issue no loads
   int32_t l2_policy_a;    // L2 eviction priority of A / B tile loads: 0 normal, 1 first, 2 last
   int32_t l2_policy_b;
+  // Fused epilogue: D = act(alpha * acc + bias + beta * C); gated (512-wide tiles only):
+  // D[:, n] = act(alpha * acc_gate[:, n]) * alpha * acc_up[:, n] with B = [W_gate; W_up].
+  int32_t act;            // kActNone, kActRelu, kActSilu, kActGelu, kActGeluTanh
+  float beta;
+  const void* src;        // optional C, same type and shape as D
+  int64_t ld_src;         // row stride of C, elements
+  int32_t gated;
 };
+
+enum Activation : int32_t {
+  kActNone = 0,
+  kActRelu = 1,
+  kActSilu = 2,
+  kActGelu = 3,      // 0.5 y (1 + erf(y / sqrt(2)))
+  kActGeluTanh = 4,  // 0.5 y (1 + tanh(sqrt(2 / pi) (y + 0.044715 y^3)))
+};
+
+__device__ __forceinline__ float apply_act(int32_t act, float y) {
+  switch (act) {
+    case kActRelu: return fmaxf(y, 0.f);
+    case kActSilu: return y / (1.f + __expf(-y));
+    case kActGelu: return 0.5f * y * (1.f + erff(y * 0.70710678118654752f));
+    case kActGeluTanh:
+      return 0.5f * y * (1.f + tanhf(0.79788456080286536f * (y + 0.044715f * y * y * y)));
+    default: return y;
+  }
+}
 
 // Host-selected fault injection for testing the bounded waits: with kInjectSkipLoads the
 // producer issues nothing, so the MMA warp's first `full` wait must run out its deadline.
@@ -268,6 +294,59 @@ __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
   }
 }
 
+// This thread's 128-byte chunk of row `row` of the C source from column col0, as raw words;
+// elements outside C read as zero.
+template <typename OutT>
+__device__ __forceinline__ void load_row_chunk(const GemmParams& p, int32_t row, int32_t col0,
+                                               uint4 (&cs)[8]) {
+  constexpr int kCols = 128 / static_cast<int>(sizeof(OutT));
+  constexpr int kPer = 16 / static_cast<int>(sizeof(OutT));  // elements per 16 bytes
+  const OutT* base = static_cast<const OutT*>(p.src) + static_cast<int64_t>(row) * p.ld_src + col0;
+  if (row < p.m && col0 + kCols <= p.n) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cs[q] = ptx::ld_global_nc_v4(base + q * kPer);
+    return;
+  }
+  const bool row_ok = row < p.m;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (sizeof(OutT) == 2) {
+        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(base) + q * 8 + 2 * i;
+        const int32_t c = col0 + q * 8 + 2 * i;
+        const uint32_t lo = (row_ok && c < p.n) ? b16[0] : 0u;
+        const uint32_t hi = (row_ok && c + 1 < p.n) ? b16[1] : 0u;
+        w[i] = lo | (hi << 16);
+      } else {
+        const int32_t c = col0 + q * 4 + i;
+        w[i] = (row_ok && c < p.n) ? reinterpret_cast<const uint32_t*>(base)[q * 4 + i] : 0u;
+      }
+    }
+    cs[q] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// x[j] += beta * C[j] for the 128-byte chunk of raw words from load_row_chunk.
+template <typename OutT>
+__device__ __forceinline__ void add_row_chunk(float beta, const uint4 (&cs)[8],
+                                              float (&x)[128 / sizeof(OutT)]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t w[4] = {cs[q].x, cs[q].y, cs[q].z, cs[q].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (sizeof(OutT) == 2) {
+        x[q * 8 + 2 * i] += beta * __uint_as_float(w[i] << 16);
+        x[q * 8 + 2 * i + 1] += beta * __uint_as_float(w[i] & 0xffff0000u);
+      } else {
+        x[q * 4 + i] += beta * __uint_as_float(w[i]);
+      }
+    }
+  }
+}
+
 // L2 eviction priority for a TMA load: 0 normal, 1 evict-first, 2 evict-last.
 __device__ __forceinline__ uint64_t l2_policy(int32_t which) {
   return which == 1 ? ptx::policy_evict_first()
@@ -285,7 +364,8 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               uint32_t base, uint32_t full_bar, uint32_t empty_bar,
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
-                                              int32_t l2_b = 0, int32_t stream_k = 0) {
+                                              int32_t l2_b = 0, int32_t stream_k = 0,
+                                              int32_t b_slot_rows = 0) {
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
@@ -304,8 +384,12 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
     work_tile_coords(sp, sg.cid, pid_m, pid_n);
     const int32_t a_row = pid_m * kBM;
     // B rows of MMA j: [pid_n * BN + j * kMmaN, +kMmaN), of which this CTA of a pair loads its
-    // half (kBRowsPerMma rows at offset rank * kBRowsPerMma) into smem slot j.
-    const int32_t b_row = pid_n * BN + static_cast<int32_t>(rank & 1u) * kBRowsPerMma;
+    // half (kBRowsPerMma rows at offset rank * kBRowsPerMma) into smem slot j.  Gated tiles
+    // (b_slot_rows = N > 0) take MMA j's rows from the j-th of the stacked [W_gate; W_up]:
+    // [j * N + pid_n * kMmaN, +kMmaN).
+    const int32_t tile_rows = b_slot_rows > 0 ? kMmaN : BN;
+    const int32_t slot_rows = b_slot_rows > 0 ? b_slot_rows : kMmaN;
+    const int32_t b_row = pid_n * tile_rows + static_cast<int32_t>(rank & 1u) * kBRowsPerMma;
     for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
       if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) {
         ok = false;
@@ -319,7 +403,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
         ptx::tma_load_2d(tm_a, sa, fb, kb * kBK, a_row, pol_a);
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
-          ptx::tma_load_2d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * kMmaN,
+          ptx::tma_load_2d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * slot_rows,
                            pol_b);
       } else {
         if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
@@ -328,7 +412,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
           ptx::tma_load_2d_pair(tm_b, sb + j * kBRowsPerMma * 128, fb_leader, kb * kBK,
-                                b_row + j * kMmaN, pol_b);
+                                b_row + j * slot_rows, pol_b);
       }
       ++fills;
       if (++stage == stages) {
@@ -442,7 +526,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
-          leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k);
+          leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -533,6 +617,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (p.scale_a != nullptr) alpha *= *p.scale_a;
     if (p.scale_b != nullptr) alpha *= *p.scale_b;
     const bool has_bias = p.bias != nullptr;
+    const bool has_src = p.src != nullptr;
+    const bool gated = (BN == 512) && p.gated != 0;
+    // Accumulator fully read into registers: hand the TMEM buffer back to the MMA warp.
+    auto release_tmem = [&](int which) {
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t tb = tempty_bar + 8u * static_cast<uint32_t>(which);
+        if constexpr (CtaGroup == 1) {
+          ptx::mbar_arrive(tb);
+        } else {
+          ptx::mbar_arrive_cluster(ptx::mapa_shared(tb, leader_rank));
+        }
+      }
+    };
     SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k);
     Segment sg;
     while (si.next(sp, sg)) {
@@ -554,33 +653,47 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       __syncwarp();
       const uint32_t t_row = tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(acc * BN);
       const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
+      const int32_t my_row = g_row + static_cast<int32_t>(lane);
+      // A gated 512-wide tile holds gate columns [0, 256) and up columns [256, 512) of the same
+      // 256 output columns.
+      const int out_cols = gated ? BN / 2 : BN;
+      const int n_chunks = out_cols / kStoreCols;
 #pragma unroll 1
-      for (int c = 0; c < BN / kStoreCols; ++c) {
-        // kStoreCols accumulator columns of this thread's row (one 128-byte output row).
-        uint32_t v[kStoreCols];
+      for (int c = 0; c < n_chunks; ++c) {
+        const int32_t col0 = pid_n * out_cols + c * kStoreCols;
+        // C (beta * C source): this thread's 128-byte row chunk, fetched before the TMEM loads
+        // so that the two latencies overlap.
+        uint4 cs[8];
+        if (has_src) load_row_chunk<OutT>(p, my_row, col0, cs);
+        float x[kStoreCols];
+        if (!gated) {
+          // kStoreCols accumulator columns of this thread's row (one 128-byte output row).
+          uint32_t v[kStoreCols];
 #pragma unroll
-        for (int h = 0; h < kStoreCols / 32; ++h) {
-          ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kStoreCols + 32 * h),
-                                  *reinterpret_cast<uint32_t(*)[32]>(&v[32 * h]));
-        }
-        ptx::tmem_ld_wait();
-        if (c == BN / kStoreCols - 1) {
-          // Accumulator fully read into registers: hand the TMEM buffer back to the MMA warp.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            const uint32_t tb = tempty_bar + 8u * static_cast<uint32_t>(acc);
-            if constexpr (CtaGroup == 1) {
-              ptx::mbar_arrive(tb);
-            } else {
-              ptx::mbar_arrive_cluster(ptx::mapa_shared(tb, leader_rank));
-            }
+          for (int h = 0; h < kStoreCols / 32; ++h) {
+            ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * kStoreCols + 32 * h),
+                                    *reinterpret_cast<uint32_t(*)[32]>(&v[32 * h]));
+          }
+          ptx::tmem_ld_wait();
+          if (c == n_chunks - 1) release_tmem(acc);
+#pragma unroll
+          for (int j = 0; j < kStoreCols; ++j) x[j] = __uint_as_float(v[j]) * alpha;
+        } else {
+          // 32 gate and 32 up columns per TMEM round trip.
+#pragma unroll
+          for (int h = 0; h < kStoreCols / 32; ++h) {
+            uint32_t vg[32], vu[32];
+            const uint32_t tc = t_row + static_cast<uint32_t>(c * kStoreCols + 32 * h);
+            ptx::tmem_ld_32x32b_x32(tc, vg);
+            ptx::tmem_ld_32x32b_x32(tc + static_cast<uint32_t>(BN / 2), vu);
+            ptx::tmem_ld_wait();
+            if (c == n_chunks - 1 && h == kStoreCols / 32 - 1) release_tmem(acc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              x[32 * h + j] = apply_act(p.act, __uint_as_float(vg[j]) * alpha) *
+                              (__uint_as_float(vu[j]) * alpha);
           }
         }
-        const int32_t col0 = pid_n * BN + c * kStoreCols;
-        float x[kStoreCols];
-#pragma unroll
-        for (int j = 0; j < kStoreCols; ++j) x[j] = __uint_as_float(v[j]) * alpha;
         if (add_bias) {
           // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
           // they are broadcast across the warp with shuffles.
@@ -591,6 +704,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) x[32 * h + j] += __shfl_sync(0xffffffffu, bl, j);
           }
+        }
+        if (has_src) add_row_chunk<OutT>(p.beta, cs, x);
+        if (!gated && p.act != kActNone) {
+#pragma unroll
+          for (int j = 0; j < kStoreCols; ++j) x[j] = apply_act(p.act, x[j]);
         }
         uint32_t packed[32];  // 128 bytes of this thread's output row
         if constexpr (sizeof(OutT) == 2) {

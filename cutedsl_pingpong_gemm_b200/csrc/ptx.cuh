@@ -444,6 +444,15 @@ __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// 16-byte read-only global load (the address must be 16-byte aligned).
+__device__ __forceinline__ uint4 ld_global_nc_v4(const void* ptr) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(ptr));
+  return r;
+}
+
 // 16-byte global store (the address must be 16-byte aligned).
 __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {

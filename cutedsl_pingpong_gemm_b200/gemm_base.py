@@ -79,7 +79,7 @@ class CompiledGemm:
         self._plans = {}
         self._workspaces = {}
 
-    def _plan(self, a, b, c, scale_mode: int = 0, split_k: int = 1):
+    def _plan(self, a, b, c, scale_mode: int = 0, split_k: int = 1, gated: bool = False):
         import torch
         gemm = self.gemm
         ab_codes, d_codes = _dtype_tables()
@@ -90,10 +90,16 @@ class CompiledGemm:
             raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE, "A, B and D must be 2-D")
         m, k = a.shape
         n, kb = b.shape
+        if gated:
+            # B = [W_gate; W_up] (2N rows), D is M x N.
+            n //= 2
+            if b.shape[0] != 2 * n:
+                raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                    f"gated B must have an even number of rows, got {b.shape[0]}")
         if kb != k or tuple(c.shape) != (m, n):
             raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
                                 f"shapes A{tuple(a.shape)} B{tuple(b.shape)} D{tuple(c.shape)} "
-                                f"do not form D = A @ B.T")
+                                f"do not form D = A @ B.T" + (" (gated)" if gated else ""))
         for name, t in (("A", a), ("B", b), ("D", c)):
             if t.numel() > 0 and t.stride(1) != 1:
                 raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
@@ -107,33 +113,49 @@ class CompiledGemm:
                 return t.stride(0)
             return max(per16, -(-cols // per16) * per16)
 
-        lda, ldb, ldd = row_stride(a, m, k), row_stride(b, n, k), row_stride(c, m, n)
+        lda, ldb, ldd = row_stride(a, m, k), row_stride(b, b.shape[0], k), row_stride(c, m, n)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()
         dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
-        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k)
+        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k, bool(gated))
         plan = self._plans.get(key)
         if plan is None:
-            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k)
+            plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k,
+                         gated)
             self._plans[key] = plan
         return plan
 
-    def plan_for(self, a, b, c, scale_mode: int = 0, split_k: int = 1) -> "_Plan":
-        return self._plan(a, b, c, scale_mode, split_k)
+    def plan_for(self, a, b, c, scale_mode: int = 0, split_k: int = 1,
+                 gated: bool = False) -> "_Plan":
+        return self._plan(a, b, c, scale_mode, split_k, gated)
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-                 scale_b=None, split_k: int = 1):
+                 scale_b=None, split_k: int = 1, activation: Optional[str] = None,
+                 source=None, beta: float = 1.0, gated: bool = False):
         """``split_k`` > 1 cuts K into that many ranges scheduled as the kernel's L dimension;
         ``split_k=-1`` is Stream-K (every resident cluster takes an equal share of the (tile,
         k-block) pairs); ``split_k=0`` picks from the tile count (see ``auto_split_k``).  With a
         BF16 ``c`` the partial sums add into an FP32 workspace that is then rounded into ``c``
-        (plus bias)."""
+        (plus bias).
+
+        Fused epilogue (none of it exists in the reference, whose kernel computes D = A . B^T,
+        gemm_base.py:133): ``c = act(alpha * A . B^T + bias + beta * source)`` with
+        ``activation`` one of None, "relu", "silu", "gelu", "gelu_tanh" and ``source`` an
+        optional tensor of c's type and shape (it may be ``c`` itself).  ``gated=True`` (tile_n
+        512): ``b`` is the stacked [W_gate; W_up] of 2 N rows and
+        ``c = act(alpha * A . W_gate^T) * (alpha * A . W_up^T)`` (SwiGLU with "silu").
+        Activations, ``source`` and ``gated`` need the whole K in one pass (split_k 1)."""
         import torch
+        if activation not in _lib.ACTIVATIONS:
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_CONFIG, f"unknown activation {activation!r}")
+        act = _lib.ACTIVATIONS[activation]
+        fused = act != _lib.CPG_ACT_NONE or source is not None or gated
         # More than one scale per operand selects the block-scaled FP8 kernel (A: 1 x 128,
         # B: 128 x 128 blocks, layouts of cpgemm.h); one value each is a per-tensor scale.
         block = scale_a is not None and scale_a.numel() > 1
         mode = _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR
         if split_k == 0:
-            split_k = 1 if block else self.auto_split_k(a.shape[0], b.shape[0], a.shape[1])
+            split_k = 1 if (block or fused) else self.auto_split_k(a.shape[0], b.shape[0],
+                                                                    a.shape[1])
         split_k = int(split_k)
         if (split_k > 1 or split_k == _lib.CPG_SPLIT_K_STREAM) and c.dtype == torch.bfloat16:
             ws = self._workspace(c)
@@ -142,8 +164,9 @@ class CompiledGemm:
             from .quant import cast_f32_bf16
             cast_f32_bf16(ws, bias, out=c, stream=stream)
             return None
-        plan = self._plan(a, b, c, mode, split_k)
-        plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
+        plan = self._plan(a, b, c, mode, split_k, gated)
+        plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b,
+                 activation=act, source=source, beta=beta)
         return None
 
     def _workspace(self, c):
@@ -177,13 +200,14 @@ class _Plan:
     """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
 
     def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d,
-                 scale_mode=0, split_k=1):
+                 scale_mode=0, split_k=1, gated=False):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
         self.device = device
         self.scale_mode = scale_mode
         cfg = gemm._config_c()
-        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode, split_k)
+        prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode, split_k,
+                                 1 if gated else 0)
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -232,7 +256,7 @@ class _Plan:
         return s.value
 
     def run(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-            scale_b=None) -> None:
+            scale_b=None, activation: int = 0, source=None, beta: float = 1.0) -> None:
         import torch
         if bias is not None:
             if not (bias.dtype == torch.bfloat16 and bias.is_cuda and bias.numel() == self.n
@@ -254,7 +278,18 @@ class _Plan:
                                     f"{name} must be a contiguous float32 CUDA tensor of shape "
                                     f"{want[name]}")
             scales.append(None if sc is None else sc.data_ptr())
-        epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales)
+        src_ptr, ld_src = None, 0
+        if source is not None:
+            if not (source.is_cuda and source.dtype == c.dtype and tuple(source.shape) == (self.m, self.n)
+                    and (source.numel() == 0 or source.stride(1) == 1)):
+                raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                    "source must be a CUDA tensor of D's dtype and shape with unit "
+                                    "column stride")
+            per16 = 16 // source.element_size()
+            ld_src = source.stride(0) if self.m > 1 else max(per16, -(-self.n // per16) * per16)
+            src_ptr = source.data_ptr() if source.numel() else None
+        epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales,
+                             float(beta), int(activation), src_ptr, int(ld_src))
         st = _stream_handle(stream, c.device)
         rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
                                    b.data_ptr() if b.numel() else None, c.data_ptr(),
@@ -356,11 +391,13 @@ class GemmSM90:
         return compiled
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-                 scale_b=None, split_k: int = 1):
+                 scale_b=None, split_k: int = 1, activation: Optional[str] = None, source=None,
+                 beta: float = 1.0, gated: bool = False):
         if self._compiled is None:
             self._compiled = CompiledGemm(self)
         self._compiled(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b,
-                       split_k=split_k)
+                       split_k=split_k, activation=activation, source=source, beta=beta,
+                       gated=gated)
 
 
 # The B200 name of the same operator.

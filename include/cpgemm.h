@@ -111,21 +111,40 @@ typedef struct cpg_gemm_problem {
                             (dtype_d must be CPG_DTYPE_F32; D is cleared by cpg_gemm_run);
                             CPG_SPLIT_K_STREAM: Stream-K, every resident cluster takes an equal
                             share of all (tile, k-block) pairs and adds into FP32 D */
+  int32_t gated;         /* 0, or 1: gated FFN (e.g. SwiGLU).  B holds [W_gate; W_up] as 2N rows
+                            of K (ldb its row stride), D is M x N and
+                            D[:, n] = act(alpha s_a s_b A . W_gate[n]) * alpha s_a s_b A . W_up[n];
+                            needs tile_n 512 (each tile: 256 gate + 256 up accumulator columns),
+                            no bias, no C source and no split-K */
 } cpg_gemm_problem;
 
 #define CPG_SPLIT_K_STREAM (-1)
 
-/* Per-call epilogue options: D = alpha * s_a * s_b * (A . B^T) + bias, rounded to D's type.
+/* Per-call epilogue options:
+ *   D = act(alpha * s_a * s_b * (A . B^T) + bias + beta * C), rounded to D's type.
  * alpha scales the fp32 accumulator; scale_a / scale_b (optional device pointers to one fp32
  * value each) are the per-tensor dequantisation scales of FP8 operands; bias (optional device
- * pointer, BF16, length N) is added per column.  The reference has none of these (D = A . B^T,
- * gemm_base.py:133); alpha = 1 and NULL pointers give exactly that. */
+ * pointer, BF16, length N) is added per column; source (optional device pointer to C, same type
+ * and M x N shape as D, row stride ld_source elements, 16-byte aligned rows; it may be D itself)
+ * is added times beta; activation is one of CPG_ACT_*.  The reference has none of these
+ * (D = A . B^T, gemm_base.py:133); alpha = 1, NULL pointers and CPG_ACT_NONE give exactly that.
+ * Activations and C need the whole K in one pass (no split-K / Stream-K). */
 typedef struct cpg_epilogue {
   float alpha;
   const void* bias;
   const float* scale_a;
   const float* scale_b;
+  float beta;
+  int32_t activation;
+  const void* source;
+  int64_t ld_source;
 } cpg_epilogue;
+
+#define CPG_ACT_NONE 0
+#define CPG_ACT_RELU 1
+#define CPG_ACT_SILU 2      /* y / (1 + exp(-y)) */
+#define CPG_ACT_GELU 3      /* 0.5 y (1 + erf(y / sqrt 2)) */
+#define CPG_ACT_GELU_TANH 4 /* 0.5 y (1 + tanh(sqrt(2 / pi) (y + 0.044715 y^3))) */
 
 typedef struct cpg_gemm cpg_gemm; /* opaque compiled GEMM */
 

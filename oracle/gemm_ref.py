@@ -180,3 +180,69 @@ def dequantize_blocks(q, s, block):
     else:
         scale = s.repeat_interleave(128, dim=0).repeat_interleave(128, dim=1)[:m, :k]
     return qf * scale
+
+
+# ---------------------------------------------------------------- fused epilogue (spec of cpgemm.h)
+# D = act(alpha * A @ B.T + bias + beta * C); gated: D = act(alpha * A @ Wg.T) * (alpha * A @ Wu.T).
+# Activation formulas as documented for CPG_ACT_*; the kernel evaluates them with CUDA's expf /
+# erff / tanhf family, which the ACT_REL term below covers.
+ACT_SLOPE = 1.13   # max |act'(y)| over the reals for relu, silu (1.0998), gelu (1.1289), gelu_tanh
+ACT_REL = 2.0 ** -18
+
+
+def activation(name, y):
+    if name in (None, "none"):
+        return y
+    if name == "relu":
+        return y.clamp_min(0.0)
+    if name == "silu":
+        return y * torch.sigmoid(y)
+    if name == "gelu":
+        return 0.5 * y * (1.0 + torch.erf(y * 0.7071067811865476))
+    if name == "gelu_tanh":
+        return 0.5 * y * (1.0 + torch.tanh(0.7978845608028654 * (y + 0.044715 * y * y * y)))
+    raise ValueError(name)
+
+
+def check_epilogue(d, a, b, bias=None, alpha=1.0, beta=1.0, c=None, act=None,
+                   frob_tol=FROB_TOL_BF16, out_rounding=BF16_REL):
+    """Check D = act(alpha A B^T + bias + beta C) (fp32 CPU oracle, C given on the CPU)."""
+    k = a.shape[1]
+    pre = reference(a, b, bias, alpha)
+    tol_pre = abs(alpha) * k * ACC_SLACK_PER_K * abs_product(a, b)
+    if bias is not None:
+        tol_pre = tol_pre + 2.0 ** -24 * bias.float().abs()
+    if c is not None:
+        bc = beta * c.float()
+        pre = pre + bc
+        tol_pre = tol_pre + 2.0 ** -23 * (bc.abs() + pre.abs())
+    r = activation(act, pre)
+    tol = out_rounding * r.abs() + ACT_SLOPE * tol_pre + ACT_REL * pre.abs() + 1e-6
+    return _verdict(d.float(), r, tol, frob_tol)
+
+
+def check_gated(d, a, b_stacked, alpha=1.0, act="silu", frob_tol=FROB_TOL_BF16):
+    """Check D = act(alpha A Wg^T) * (alpha A Wu^T) for B = [Wg; Wu] (2N rows)."""
+    k = a.shape[1]
+    n = b_stacked.shape[0] // 2
+    wg, wu = b_stacked[:n], b_stacked[n:]
+    g = reference(a, wg, None, alpha)
+    u = reference(a, wu, None, alpha)
+    tg = abs(alpha) * k * ACC_SLACK_PER_K * abs_product(a, wg)
+    tu = abs(alpha) * k * ACC_SLACK_PER_K * abs_product(a, wu)
+    ag = activation(act, g)
+    r = ag * u
+    tol = (BF16_REL * r.abs() + ACT_SLOPE * tg * (u.abs() + tu) + ag.abs() * tu
+           + ACT_REL * (g.abs() * u.abs() + r.abs()) + 1e-6)
+    return _verdict(d.float(), r, tol, frob_tol)
+
+
+def _verdict(dd, r, tol, frob_tol):
+    if dd.shape != r.shape:
+        raise ValueError(f"shape mismatch {tuple(dd.shape)} vs {tuple(r.shape)}")
+    err = (dd - r).abs()
+    n_bad = int((err > tol).sum())
+    frob = rel_frobenius(dd, r)
+    worst = float((err / tol.clamp_min(1e-30)).max()) if err.numel() else 0.0
+    return {"ok": n_bad == 0 and frob <= frob_tol, "n_bad": n_bad, "frob": frob,
+            "worst_ratio": worst, "max_abs_err": float(err.max()) if err.numel() else 0.0}

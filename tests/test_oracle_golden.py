@@ -100,3 +100,16 @@ def test_schedule_covers_every_tile_once():
             assert len(tiles) == len(set(tiles))
             ncm, ncn = p.ncluster_mnl[:2]
             assert len(tiles) == ncm * cluster[0] * ncn * cluster[1]
+
+
+def test_oracle_activations_match_torch():
+    """The fused-epilogue oracle's activation formulas equal torch's published ones."""
+    import torch
+    import torch.nn.functional as F
+    from oracle import gemm_ref
+    y = torch.linspace(-30, 30, 100001, dtype=torch.float64)
+    assert torch.allclose(gemm_ref.activation("silu", y), F.silu(y), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(gemm_ref.activation("gelu", y), F.gelu(y), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(gemm_ref.activation("gelu_tanh", y), F.gelu(y, approximate="tanh"),
+                          rtol=1e-12, atol=1e-12)
+    assert torch.equal(gemm_ref.activation("relu", y), F.relu(y))
