@@ -43,6 +43,10 @@ WORKLOADS = {
                       m_is_per_gpu=True, fp8=None),
     "llm": dict(m=16384, n=28672, k=8192, a_scale=1.0, b_scale=0.02, bias=True,
                 m_is_per_gpu=False, fp8=None),
+    # The same FFN up-projection as a fused SwiGLU: B = [W_gate; W_up] (2 x 14336 rows), D =
+    # silu(A W_gate^T) * A W_up^T (14336 columns); the same flops as "llm".
+    "llm_swiglu": dict(m=16384, n=14336, k=8192, a_scale=1.0, b_scale=0.02, bias=False,
+                       m_is_per_gpu=False, fp8=None, gated=True, act="silu"),
     # Decode-like: HBM bound (B is 128 MiB, A 2 MiB); split-K inside the GPU fills the SMs.
     "smallm": dict(m=128, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
                    m_is_per_gpu=True, fp8=None, small_m=True),
@@ -73,6 +77,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--activation", default=None,
+                    choices=["relu", "silu", "gelu", "gelu_tanh"],
+                    help="fused epilogue activation for the GEMM workloads")
     return ap.parse_args()
 
 
@@ -240,25 +247,34 @@ def run_reference(args, world, rank):
     n, k = w["n"], w["k"]
     cores = gemm_ref.set_threads()
     g = torch.Generator().manual_seed(0)
-    b = (torch.randn(n, k, generator=g) * w["b_scale"]).to(torch.bfloat16).float()
+    gated = bool(w.get("gated"))
+    b_rows = 2 * n if gated else n
+    b = (torch.randn(b_rows, k, generator=g) * w["b_scale"]).to(torch.bfloat16).float()
+
+    def cpu_step(a):
+        r = torch.matmul(a, b.t())
+        if gated:  # the fused epilogue of the gated form, on the host
+            r = gemm_ref.activation(w.get("act"), r[:, :n]) * r[:, n:]
+        return r
+
     # Calibrate the per-step sample so the whole run stays within about a minute.
     probe_rows = 64
     a = torch.randn(probe_rows, k, generator=g).to(torch.bfloat16).float()
-    torch.matmul(a, b.t())
+    cpu_step(a)
     t0 = time.perf_counter()
-    torch.matmul(a, b.t())
+    cpu_step(a)
     t_probe = max(time.perf_counter() - t0, 1e-4)
     per_step_budget = 60.0 / max(1, args.steps + args.warmup)
     rows = int(max(8, min(w["m"], probe_rows * per_step_budget / t_probe)))
     rows = max(8, rows // 8 * 8)
     a = torch.randn(rows, k, generator=g).to(torch.bfloat16).float()
     for _ in range(args.warmup):
-        torch.matmul(a, b.t())
+        cpu_step(a)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        torch.matmul(a, b.t())
+        cpu_step(a)
     el = time.perf_counter() - t0
-    flops = 2.0 * rows * n * k * args.steps
+    flops = 2.0 * rows * b_rows * k * args.steps
     value = flops / el / 1e12
     sample = (f"{rows}x{n}x{k} fp32 row slab of the {args.workload} GEMM per step "
               f"(torch.matmul on {cores} host threads)")
@@ -281,6 +297,8 @@ def run_reference(args, world, rank):
 def metric_name(workload):
     return {"bf16_8192": "GEMM TFLOPS (BF16 8192^3 per GPU, M-sharded, B replicated)",
             "llm": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 + bias, M-sharded)",
+            "llm_swiglu": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 as fused SwiGLU, "
+                          "D 16384x14336, M-sharded)",
             "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)",
             "fp8": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, per-tensor scales)",
             "fp8_block": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, 1x128 / 128x128 block scales)",
@@ -383,14 +401,18 @@ def run_cpg(args, world, rank, local):
     # B is the same replicated weight on every rank).
     gen_a = torch.Generator(device=dev).manual_seed(1000 + rank)
     gen_b = torch.Generator(device=dev).manual_seed(7)
+    gated = bool(w.get("gated"))
+    act = w.get("act") or args.activation
+    b_rows = 2 * n if gated else n
     a = (torch.randn(m, k, generator=gen_a, device=dev) * w["a_scale"]).to(torch.bfloat16)
-    b = (torch.randn(n, k, generator=gen_b, device=dev) * w["b_scale"]).to(torch.bfloat16)
+    b = (torch.randn(b_rows, k, generator=gen_b, device=dev) * w["b_scale"]).to(torch.bfloat16)
     bias = (torch.randn(n, generator=gen_b, device=dev)).to(torch.bfloat16) if w["bias"] else None
     d = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     scale_a = scale_b = None
     if w.get("small_m"):
         args.cluster_m = 1  # one 128-row tile: the pair's second CTA would have no rows
-    tile_n = args.tile_n or (128 if w.get("small_m") else (512 if args.cluster_m == 2 else 256))
+    tile_n = args.tile_n or (128 if w.get("small_m") else
+                             (512 if args.cluster_m == 2 or gated else 256))
     if w["fp8"] is not None:
         from cutedsl_pingpong_gemm_b200.quant import quantize_e4m3
         if w["fp8"] == "tensor":
@@ -415,21 +437,23 @@ def run_cpg(args, world, rank, local):
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
                     is_persistent=True)
-    compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b)
+    compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
     split_k = (args.split_k if args.split_k else compiled.auto_split_k(m, n, k)) if w.get("small_m") else 1
-    compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k)
+    compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k,
+             activation=act, gated=gated)
     torch.cuda.synchronize()
     if split_k != 1:
         plan = compiled.plan_for(a, b, compiled._workspace(d), 0, split_k)
     else:
-        plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0)
+        plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0, gated=gated)
     info = plan.launch_info()
     kernels_per_step = 2 if split_k != 1 else 1  # split-K / Stream-K add the cast kernel
 
     launches = [0]
 
     def step():
-        compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k)
+        compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k,
+                 activation=act, gated=gated)
         launches[0] += kernels_per_step
 
     for _ in range(args.warmup):
@@ -458,13 +482,13 @@ def run_cpg(args, world, rank, local):
     if status != 0:
         raise SystemExit(f"kernel status {status:#x}")
 
-    flops_per_gpu = 2.0 * m * n * k
+    flops_per_gpu = 2.0 * m * b_rows * k  # a gated step computes gate and up: 2 N columns
     total_flops = flops_per_gpu * world
     value = total_flops / (ms * 1e-3) / 1e12
     achieved = flops_per_gpu / (ms_local * 1e-3) / 1e12  # one kernel launch per step
     peaks, peak_src = load_peaks()
     # HBM-bound shapes: the roofline is bytes moved / time against the measured copy bandwidth.
-    min_bytes = (m * k + n * k) * a.element_size() + m * n * d.element_size()
+    min_bytes = (m * k + b_rows * k) * a.element_size() + m * n * d.element_size()
 
     # ---------------- end to end through the public API with host buffers
     e2e = None
@@ -479,7 +503,7 @@ def run_cpg(args, world, rank, local):
             a2.copy_(a_h, non_blocking=True)
             b2.copy_(b_h, non_blocking=True)
             compiled(a2, b2, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b,
-                     split_k=split_k)
+                     split_k=split_k, activation=act, gated=gated)
             d_h.copy_(d, non_blocking=True)
 
         for _ in range(2):
@@ -532,7 +556,7 @@ def run_cpg(args, world, rank, local):
                        "fp8_scales": w["fp8"],
                        "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
-                       "bias": bool(w["bias"])},
+                       "bias": bool(w["bias"]), "activation": act, "gated": gated},
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": min_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"],

@@ -125,14 +125,39 @@ enum Activation : int32_t {
   kActGeluTanh = 4,  // 0.5 y (1 + tanh(sqrt(2 / pi) (y + 0.044715 y^3)))
 };
 
-__device__ __forceinline__ float apply_act(int32_t act, float y) {
+__device__ __forceinline__ float act_relu(float y) { return fmaxf(y, 0.f); }
+// y / (1 + e^-y); the fast divide returns 0 once e^-y passes 2^126, the limit of silu there.
+__device__ __forceinline__ float act_silu(float y) { return __fdividef(y, 1.f + __expf(-y)); }
+__device__ __forceinline__ float act_gelu(float y) {
+  return 0.5f * y * (1.f + erff(y * 0.70710678118654752f));
+}
+__device__ __forceinline__ float act_gelu_tanh(float y) {
+  return 0.5f * y * (1.f + tanhf(0.79788456080286536f * (y + 0.044715f * y * y * y)));
+}
+
+// x[j] = act(x[j]).  The switch sits outside the unrolled loops, so each activation's code is
+// one contiguous block (a switch per element would interleave all four bodies N times).
+template <int N>
+__device__ __forceinline__ void act_inplace(int32_t act, float (&x)[N]) {
   switch (act) {
-    case kActRelu: return fmaxf(y, 0.f);
-    case kActSilu: return y / (1.f + __expf(-y));
-    case kActGelu: return 0.5f * y * (1.f + erff(y * 0.70710678118654752f));
+    case kActRelu:
+#pragma unroll
+      for (int j = 0; j < N; ++j) x[j] = act_relu(x[j]);
+      break;
+    case kActSilu:
+#pragma unroll
+      for (int j = 0; j < N; ++j) x[j] = act_silu(x[j]);
+      break;
+    case kActGelu:
+#pragma unroll
+      for (int j = 0; j < N; ++j) x[j] = act_gelu(x[j]);
+      break;
     case kActGeluTanh:
-      return 0.5f * y * (1.f + tanhf(0.79788456080286536f * (y + 0.044715f * y * y * y)));
-    default: return y;
+#pragma unroll
+      for (int j = 0; j < N; ++j) x[j] = act_gelu_tanh(x[j]);
+      break;
+    default:
+      break;
   }
 }
 
@@ -688,10 +713,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ptx::tmem_ld_32x32b_x32(tc + static_cast<uint32_t>(BN / 2), vu);
             ptx::tmem_ld_wait();
             if (c == n_chunks - 1 && h == kStoreCols / 32 - 1) release_tmem(acc);
+            float gv[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              x[32 * h + j] = apply_act(p.act, __uint_as_float(vg[j]) * alpha) *
-                              (__uint_as_float(vu[j]) * alpha);
+            for (int j = 0; j < 32; ++j) gv[j] = __uint_as_float(vg[j]) * alpha;
+            act_inplace(p.act, gv);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[32 * h + j] = gv[j] * (__uint_as_float(vu[j]) * alpha);
           }
         }
         if (add_bias) {
@@ -706,10 +733,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
         if (has_src) add_row_chunk<OutT>(p.beta, cs, x);
-        if (!gated && p.act != kActNone) {
-#pragma unroll
-          for (int j = 0; j < kStoreCols; ++j) x[j] = apply_act(p.act, x[j]);
-        }
+        if (!gated) act_inplace(p.act, x);
         uint32_t packed[32];  // 128 bytes of this thread's output row
         if constexpr (sizeof(OutT) == 2) {
 #pragma unroll

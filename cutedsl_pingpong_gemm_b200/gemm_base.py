@@ -380,13 +380,15 @@ class GemmSM90:
         cfg = self._config_c()
         _lib.check(lib.cpg_config_validate(ctypes.byref(cfg)), "GemmSM90")
 
-    def compile(self, a, b, c, stream=None, *, scale_a=None, scale_b=None) -> CompiledGemm:
+    def compile(self, a, b, c, stream=None, *, scale_a=None, scale_b=None,
+                gated: bool = False) -> CompiledGemm:
         """Validate and plan for the example tensors.  Block scales (``scale_a`` with more than
-        one element, as in ``__call__``) plan the block-scaled FP8 kernel instead of the plain one.
-        """
+        one element, as in ``__call__``) plan the block-scaled FP8 kernel instead of the plain one;
+        ``gated`` plans the gated FFN form (B = [W_gate; W_up])."""
         compiled = CompiledGemm(self)
         block = scale_a is not None and scale_a.numel() > 1
-        compiled.plan_for(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR)
+        compiled.plan_for(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR,
+                          gated=gated)
         self._compiled = compiled
         return compiled
 
@@ -405,10 +407,10 @@ GemmSM100 = GemmSM90
 
 
 def compile(gemm: GemmSM90, a, b, c, stream=None, options: Optional[str] = None, *,
-            scale_a=None, scale_b=None) -> CompiledGemm:
+            scale_a=None, scale_b=None, gated: bool = False) -> CompiledGemm:
     """Stand-in for ``cute.compile(gemm, a, b, c, stream, options=...)`` (gemm_base.py:608).
 
     ``options`` is accepted for call-site compatibility and ignored (there is no JIT).  FP8
     callers may pass their scales so that the plan matches the kernel the call will use.
     """
-    return gemm.compile(a, b, c, stream, scale_a=scale_a, scale_b=scale_b)
+    return gemm.compile(a, b, c, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
