@@ -40,7 +40,7 @@ CPG_ACT_GELU_TANH = 4
 ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
                "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 class CpgError(RuntimeError):
@@ -91,6 +91,9 @@ class GemmProblemC(ctypes.Structure):
         ("dtype_ab", ctypes.c_int32), ("dtype_d", ctypes.c_int32),
         ("scale_mode", ctypes.c_int32), ("split_k", ctypes.c_int32),
         ("gated", ctypes.c_int32),
+        ("l", ctypes.c_int64),
+        ("batch_stride_a", ctypes.c_int64), ("batch_stride_b", ctypes.c_int64),
+        ("batch_stride_d", ctypes.c_int64),
     ]
 
 
@@ -98,7 +101,8 @@ class EpilogueC(ctypes.Structure):
     _fields_ = [("alpha", ctypes.c_float), ("bias", ctypes.c_void_p),
                 ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
                 ("beta", ctypes.c_float), ("activation", ctypes.c_int32),
-                ("source", ctypes.c_void_p), ("ld_source", ctypes.c_int64)]
+                ("source", ctypes.c_void_p), ("ld_source", ctypes.c_int64),
+                ("batch_stride_source", ctypes.c_int64)]
 
 
 _P = ctypes.POINTER

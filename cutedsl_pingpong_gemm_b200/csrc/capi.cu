@@ -67,21 +67,35 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D row-major matrix [rows, cols] with row stride `ld` elements, tiled into
 // box_rows x box_cols boxes with 128-byte swizzle.
-int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* ptr,
-              int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols) {
+// 3-D tiled tensor map (columns, rows, batches) with a 128-byte swizzled box of box_rows x
+// box_cols x 1.  An unbatched operand has one batch; its batch stride is then any legal value.
+int encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* ptr,
+                 int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols,
+                 int64_t batches = 1, int64_t batch_stride = 0) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(CPG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  if (batches < 1) batches = 1;
+  if (batches == 1) {
+    const int64_t span = (rows > 1 ? rows : 1) * ld;
+    batch_stride = batch_stride > span ? batch_stride : span;
+    batch_stride = (batch_stride * elem_bytes + 15) / 16 * 16 / elem_bytes;
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(batches)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * elem_bytes),
+                           static_cast<cuuint64_t>(batch_stride * elem_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    return fail(CPG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld",
+    return fail(CPG_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld batches=%lld "
+                "batch_stride=%lld",
                 static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols),
-                static_cast<long long>(ld));
+                static_cast<long long>(ld), static_cast<long long>(batches),
+                static_cast<long long>(batch_stride));
   }
   return CPG_OK;
 }
@@ -262,6 +276,7 @@ struct cpg_gemm {
   int32_t k_iters_per_split;
   int32_t splits;
   int32_t stream_k;
+  int64_t batches;
   bool maps_valid;
   const void* map_a_ptr;
   const void* map_b_ptr;
@@ -271,7 +286,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 7; }
+int cpg_abi_version(void) { return 8; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -405,6 +420,21 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                 "no split-K");
   if (prob->gated && prob->n > (int64_t(1) << 30))
     return fail(CPG_ERR_INVALID_SHAPE, "gated GEMM: 2 N must fit in 31 bits");
+  if (prob->l < 0) return fail(CPG_ERR_INVALID_SHAPE, "l (batches) must be >= 0");
+  const int64_t batches = prob->l > 1 ? prob->l : 1;
+  if (batches > 1) {
+    if (v.scale_mode == CPG_SCALE_BLOCK)
+      return fail(CPG_ERR_UNSUPPORTED, "batched block-scaled FP8 is not implemented");
+    const int eab = elem_bytes(prob->dtype_ab), ed = elem_bytes(prob->dtype_d);
+    if (batches > 65535) return fail(CPG_ERR_INVALID_SHAPE, "at most 65535 batches");
+    if ((prob->batch_stride_a * eab) % 16 != 0 || (prob->batch_stride_b * eab) % 16 != 0 ||
+        (prob->batch_stride_d * ed) % 16 != 0 || prob->batch_stride_a < 0 ||
+        prob->batch_stride_b < 0)
+      return fail(CPG_ERR_ALIGNMENT, "batch strides must be multiples of 16 bytes");
+    if (prob->batch_stride_d < prob->m * prob->ldd)
+      return fail(CPG_ERR_INVALID_SHAPE, "batches of D overlap: batch_stride_d %lld < m * ldd",
+                  static_cast<long long>(prob->batch_stride_d));
+  }
   const int smem = v.smem_bytes(cfg->ab_stage, cfg->epi_stage, cfg->reuse_ab);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "%d stages need %d bytes of shared memory, device allows %d",
@@ -466,9 +496,17 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   g->k_iters_per_split = g->k_iters > 0 ? (g->k_iters + splits - 1) / splits : 0;
   g->splits = g->k_iters_per_split > 0
                   ? (g->k_iters + g->k_iters_per_split - 1) / g->k_iters_per_split : 1;
-  g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn), g->splits,
-                                      cfg->raster_order, cfg->group_size, cfg->cluster_m,
-                                      cfg->cluster_n, cfg->is_persistent);
+  g->batches = batches;
+  // The scheduler's L index runs over batches x split-K ranges (batch-major).
+  const int64_t ntl = int64_t(g->splits) * batches;
+  if (ntm * ntn * ntl > (int64_t(1) << 31) - 1) {
+    delete g;
+    return fail(CPG_ERR_INVALID_SHAPE, "more than 2^31 - 1 tiles");
+  }
+  g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn),
+                                      static_cast<int32_t>(ntl), cfg->raster_order,
+                                      cfg->group_size, cfg->cluster_m, cfg->cluster_n,
+                                      cfg->is_persistent);
   int32_t grid[3];
   cpg::sched_grid_shape(g->sched, mac, grid);
   if (g->stream_k) {
@@ -600,6 +638,8 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     if (epi->ld_source < pr.n || (epi->ld_source * es) % 16 != 0)
       return fail(CPG_ERR_ALIGNMENT, "C row stride %lld must be >= N and a multiple of 16 bytes",
                   static_cast<long long>(epi->ld_source));
+    if (g->batches > 1 && (epi->batch_stride_source * es) % 16 != 0)
+      return fail(CPG_ERR_ALIGNMENT, "C batch stride must be a multiple of 16 bytes");
     if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0)
       return fail(CPG_ERR_ALIGNMENT, "C must be 16-byte aligned");
   }
@@ -610,13 +650,19 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     // D = bias (or 0): nothing to contract.
     int blocks = static_cast<int>((pr.m * pr.n + 255) / 256);
     if (blocks > 4096) blocks = 4096;
-    if (pr.dtype_d == CPG_DTYPE_F32) {
-      fill_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<float*>(d), pr.m, pr.n, pr.ldd,
-                                                      static_cast<const __nv_bfloat16*>(bias));
-    } else {
-      fill_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-          static_cast<__nv_bfloat16*>(d), pr.m, pr.n, pr.ldd,
-          static_cast<const __nv_bfloat16*>(bias));
+    if (blocks < 1) blocks = 1;
+    const int ed0 = elem_bytes(pr.dtype_d);
+    for (int64_t bt = 0; bt < g->batches; ++bt) {
+      void* db = static_cast<char*>(d) + bt * pr.batch_stride_d * ed0;
+      if (pr.dtype_d == CPG_DTYPE_F32) {
+        fill_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<float*>(db), pr.m, pr.n,
+                                                        pr.ldd,
+                                                        static_cast<const __nv_bfloat16*>(bias));
+      } else {
+        fill_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+            static_cast<__nv_bfloat16*>(db), pr.m, pr.n, pr.ldd,
+            static_cast<const __nv_bfloat16*>(bias));
+      }
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CPG_OK : cuda_fail(e, "fill kernel launch");
@@ -629,14 +675,16 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   const int bk = cpg::kRowBytes / eab;         // k-block: one 128-byte row of A / B
   const int store_cols = cpg::kRowBytes / ed;  // epilogue box: one 128-byte row of D
   if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
-    int rc = encode_2d(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM, bk);
+    int rc = encode_tiled(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM,
+                          bk, g->batches, pr.batch_stride_a);
     if (rc != CPG_OK) return rc;
     // One B box per MMA: min(tile_n, 256) / cta_group rows; a gated B holds 2 N rows.
-    rc = encode_2d(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.gated ? 2 * pr.n : pr.n, pr.k,
-                   pr.ldb,
-                   (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk);
+    rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.gated ? 2 * pr.n : pr.n, pr.k,
+                      pr.ldb, (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk, g->batches,
+                      pr.batch_stride_b);
     if (rc != CPG_OK) return rc;
-    rc = encode_2d(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols);
+    rc = encode_tiled(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols,
+                      g->batches, pr.batch_stride_d);
     if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
@@ -681,12 +729,17 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.beta = epi != nullptr ? epi->beta : 0.f;
   p.src = src;
   p.ld_src = src != nullptr ? epi->ld_source : 0;
+  p.src_batch_stride = (src != nullptr && g->batches > 1) ? epi->batch_stride_source : 0;
   p.gated = pr.gated;
+  p.num_splits = g->splits;
 
   if (g->splits > 1 || g->stream_k) {
     // The splits / Stream-K segments add their partial sums into D.
-    cudaError_t e = cudaMemset2DAsync(d, pr.ldd * ed, 0, pr.n * ed, pr.m, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(D)");
+    for (int64_t bt = 0; bt < g->batches; ++bt) {
+      cudaError_t e = cudaMemset2DAsync(static_cast<char*>(d) + bt * pr.batch_stride_d * ed,
+                                        pr.ldd * ed, 0, pr.n * ed, pr.m, st);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync(D)");
+    }
   }
   cudaLaunchConfig_t lc = {};
   cudaLaunchAttribute attr[1];
@@ -935,9 +988,10 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   if (prob->dtype_d != CPG_DTYPE_BF16) return fail(CPG_ERR_DTYPE, "D must be BF16");
   if (prob->scale_mode != CPG_SCALE_TENSOR)
     return fail(CPG_ERR_UNSUPPORTED, "block-scaled FP8 is not available on this entry point");
-  if (prob->gated != 0 ||
+  if (prob->gated != 0 || prob->l > 1 ||
       (epi != nullptr && (epi->activation != CPG_ACT_NONE || epi->source != nullptr)))
-    return fail(CPG_ERR_UNSUPPORTED, "gated GEMM, activations and C are not available here");
+    return fail(CPG_ERR_UNSUPPORTED,
+                "gated GEMM, batches, activations and C are not available here");
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (prob->m < 0 || prob->n < 0 || prob->k < 0 || prob->m > lim || prob->n > lim ||
       prob->k > lim || prob->lda < prob->k || prob->ldb < prob->k || prob->ldd < prob->n ||
@@ -1018,6 +1072,7 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   p.k = static_cast<int32_t>(prob->k);
   p.k_iters = k_iters;
   p.k_iters_per_split = kps;
+  p.num_splits = splits;
   p.reduce_add = splits > 1 ? 1 : 0;
   p.ab_stages = cfg->ab_stage;
   p.epi_stages = cfg->epi_stage;
@@ -1030,13 +1085,14 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   p.timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
 
   CUtensorMap tm_a, tm_b, tm_w;
-  rc = encode_2d(&tm_a, tma_dtype(prob->dtype_ab), eab, a, prob->m, prob->k, prob->lda, cpg::kBM, bk);
+  rc = encode_tiled(&tm_a, tma_dtype(prob->dtype_ab), eab, a, prob->m, prob->k, prob->lda,
+                    cpg::kBM, bk);
   if (rc != CPG_OK) return rc;
-  rc = encode_2d(&tm_b, tma_dtype(prob->dtype_ab), eab, b, prob->n, prob->k, prob->ldb,
-                 (v.bn > 256 ? 256 : v.bn) / v.cta_group, bk);
+  rc = encode_tiled(&tm_b, tma_dtype(prob->dtype_ab), eab, b, prob->n, prob->k, prob->ldb,
+                    (v.bn > 256 ? 256 : v.bn) / v.cta_group, bk);
   if (rc != CPG_OK) return rc;
-  rc = encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, prob->m, prob->n, ldw, 32,
-                 cpg::kRowBytes / 4);
+  rc = encode_tiled(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws, prob->m, prob->n, ldw, 32,
+                    cpg::kRowBytes / 4);
   if (rc != CPG_OK) return rc;
 
   // The array keeps the previous call's sums: clear the region the K ranges add into.

@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
         ptx::fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
-          if (g_row < p.m && cc < p.n) ptx::tma_store_2d(&tm_d, sbuf, cc, g_row);
+          if (g_row < p.m && cc < p.n) ptx::tma_store_3d(&tm_d, sbuf, cc, g_row, 0);
           ptx::bulk_commit_group();
         }
         __syncwarp();

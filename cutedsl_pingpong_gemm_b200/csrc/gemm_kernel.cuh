@@ -114,7 +114,10 @@ struct GemmParams {
   float beta;
   const void* src;        // optional C, same type and shape as D
   int64_t ld_src;         // row stride of C, elements
+  int64_t src_batch_stride;  // elements between the batches of C
   int32_t gated;
+  // The scheduler's L index is batch * num_splits + split (split-K ranges of each batch).
+  int32_t num_splits;
 };
 
 enum Activation : int32_t {
@@ -253,18 +256,20 @@ __device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t 
 struct Segment {
   int32_t cid;
   int32_t kb0, kb1;
+  int32_t batch;  // L index of the batched GEMM (0 when unbatched)
   int32_t index;  // how many segments this CTA produced before this one
 };
 
-// Walks this CTA's segments.  Tile mode: the scheduler's tiles (and L index: k-blocks
-// [l * kps, (l + 1) * kps) for split-K), one segment per tile.  Stream-K: the linearised
-// (tile, k-block) space of tiles * k_iters k-blocks is cut into gridDim.z equal ranges and
-// cluster z walks range z, one segment per tile it touches; the tiles keep the reference's
-// linear-id -> (m, n) map.
+// Walks this CTA's segments.  Tile mode: the scheduler's tiles, one segment per tile; the L
+// index l = batch * splits + split selects the batch and, for split-K, the k-blocks
+// [split * kps, (split + 1) * kps).  Stream-K: the linearised (tile, k-block) space of
+// tiles * k_iters k-blocks (tiles of all batches) is cut into gridDim.z equal ranges and cluster
+// z walks range z, one segment per tile it touches; the tiles keep the reference's
+// linear-id -> (m, n, l) map.
 struct SegmentIter {
   WorkIter it;
   int64_t pos, end;
-  int32_t k_iters, kps, stream, index;
+  int32_t k_iters, kps, stream, index, splits;
 
   __device__ __forceinline__ bool next(const SchedParams& sp, Segment& s) {
     if (stream) {
@@ -276,13 +281,18 @@ struct SegmentIter {
       s.cid = static_cast<int32_t>(tile);
       s.kb0 = kb0;
       s.kb1 = static_cast<int32_t>(kb1);
+      int32_t l, cid_in_problem;
+      fast_divmod(sp.dm_clusters_per_problem, s.cid, l, cid_in_problem);
+      s.batch = l;
       pos += kb1 - kb0;
     } else {
       if (!it.valid()) return false;
       int32_t l, cid_in_problem;
       fast_divmod(sp.dm_clusters_per_problem, it.cid, l, cid_in_problem);
+      const int32_t batch = splits > 1 ? l / splits : l;
       s.cid = it.cid;
-      s.kb0 = l * kps;
+      s.batch = batch;
+      s.kb0 = (l - batch * splits) * kps;
       s.kb1 = s.kb0 + kps < k_iters ? s.kb0 + kps : k_iters;
       it.advance();
     }
@@ -292,12 +302,14 @@ struct SegmentIter {
 };
 
 __device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, int32_t k_iters,
-                                                         int32_t kps, int32_t stream_k) {
+                                                         int32_t kps, int32_t stream_k,
+                                                         int32_t splits) {
   SegmentIter si;
   si.it = make_work_iter(sp);
   si.k_iters = k_iters;
   si.kps = kps;
   si.stream = stream_k;
+  si.splits = splits > 1 ? splits : 1;
   si.index = 0;
   si.pos = si.end = 0;
   if (stream_k) {
@@ -322,11 +334,12 @@ __device__ __forceinline__ void epi_wait_buffer(int epi_stages) {
 // This thread's 128-byte chunk of row `row` of the C source from column col0, as raw words;
 // elements outside C read as zero.
 template <typename OutT>
-__device__ __forceinline__ void load_row_chunk(const GemmParams& p, int32_t row, int32_t col0,
-                                               uint4 (&cs)[8]) {
+__device__ __forceinline__ void load_row_chunk(const GemmParams& p, int32_t batch, int32_t row,
+                                               int32_t col0, uint4 (&cs)[8]) {
   constexpr int kCols = 128 / static_cast<int>(sizeof(OutT));
   constexpr int kPer = 16 / static_cast<int>(sizeof(OutT));  // elements per 16 bytes
-  const OutT* base = static_cast<const OutT*>(p.src) + static_cast<int64_t>(row) * p.ld_src + col0;
+  const OutT* base = static_cast<const OutT*>(p.src) + batch * p.src_batch_stride +
+                     static_cast<int64_t>(row) * p.ld_src + col0;
   if (row < p.m && col0 + kCols <= p.n) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) cs[q] = ptx::ld_global_nc_v4(base + q * kPer);
@@ -390,7 +403,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
                                               int32_t l2_b = 0, int32_t stream_k = 0,
-                                              int32_t b_slot_rows = 0) {
+                                              int32_t b_slot_rows = 0, int32_t splits = 1) {
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
@@ -402,7 +415,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t phase = 0;
   uint32_t fills = 0;
   bool ok = true;
-  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k);
+  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits);
   Segment sg;
   while (ok && si.next(sp, sg)) {
     int32_t pid_m, pid_n;
@@ -425,19 +438,19 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
       const uint32_t fb = full_bar + 8u * stage;
       if constexpr (CtaGroup == 1) {
         ptx::mbar_arrive_expect_tx(fb, kTxBytes);
-        ptx::tma_load_2d(tm_a, sa, fb, kb * kBK, a_row, pol_a);
+        ptx::tma_load_3d(tm_a, sa, fb, kb * kBK, a_row, sg.batch, pol_a);
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
-          ptx::tma_load_2d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * slot_rows,
-                           pol_b);
+          ptx::tma_load_3d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * slot_rows,
+                           sg.batch, pol_b);
       } else {
         if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
         const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
-        ptx::tma_load_2d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, pol_a);
+        ptx::tma_load_3d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, sg.batch, pol_a);
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
-          ptx::tma_load_2d_pair(tm_b, sb + j * kBRowsPerMma * 128, fb_leader, kb * kBK,
-                                b_row + j * slot_rows, pol_b);
+          ptx::tma_load_3d_pair(tm_b, sb + j * kBRowsPerMma * 128, fb_leader, kb * kBK,
+                                b_row + j * slot_rows, sg.batch, pol_b);
       }
       ++fills;
       if (++stage == stages) {
@@ -551,7 +564,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
-          leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0);
+          leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0,
+          p.num_splits);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -562,7 +576,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k);
+      SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k,
+                                         p.num_splits);
       Segment sg;
       while (ok && si.next(sp, sg)) {
         const int kb0 = sg.kb0, kb1 = sg.kb1;
@@ -657,7 +672,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
     };
-    SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k);
+    SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k,
+                                       p.num_splits);
     Segment sg;
     while (si.next(sp, sg)) {
       int32_t pid_m, pid_n;
@@ -689,7 +705,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // C (beta * C source): this thread's 128-byte row chunk, fetched before the TMEM loads
         // so that the two latencies overlap.
         uint4 cs[8];
-        if (has_src) load_row_chunk<OutT>(p, my_row, col0, cs);
+        if (has_src) load_row_chunk<OutT>(p, sg.batch, my_row, col0, cs);
         float x[kStoreCols];
         if (!gated) {
           // kStoreCols accumulator columns of this thread's row (one 128-byte output row).
@@ -760,9 +776,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
           if (g_row < p.m && col0 < p.n) {
             if (p.reduce_add) {
-              ptx::tma_reduce_add_2d(&tm_d, sbuf, col0, g_row);
+              ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.batch);
             } else {
-              ptx::tma_store_2d(&tm_d, sbuf, col0, g_row);
+              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.batch);
             }
           }
           ptx::bulk_commit_group();

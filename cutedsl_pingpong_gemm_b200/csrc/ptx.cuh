@@ -170,43 +170,46 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-// 2-D tiled load into this CTA's shared memory, completing `bytes` on barrier `bar` (this CTA).
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* m, uint32_t dst, uint32_t bar,
-                                            int32_t x, int32_t y, uint64_t policy) {
+// Tensor maps are 3-D: (columns, rows, batch); an unbatched operand has one batch (z = 0).
+
+// Tiled load into this CTA's shared memory, completing its bytes on barrier `bar` (this CTA).
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* m, uint32_t dst, uint32_t bar,
+                                            int32_t x, int32_t y, int32_t z, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
 
-// 2-D tiled load for a CTA pair: data lands in this CTA's shared memory, the transaction bytes
+// Tiled load for a CTA pair: data lands in this CTA's shared memory, the transaction bytes
 // complete on `cluster_bar`, which may be the pair leader's barrier (address from mapa_shared).
-__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* m, uint32_t dst,
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* m, uint32_t dst,
                                                  uint32_t cluster_bar, int32_t x, int32_t y,
-                                                 uint64_t policy) {
+                                                 int32_t z, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x,
-                                             int32_t y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(m)),
-               "r"(src), "r"(x), "r"(y)
-               : "memory");
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src, int32_t x,
+                                             int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
+      : "memory");
 }
 
 // Element-wise add of a shared-memory box into global memory (fp32 split-K accumulation in L2).
-__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t src, int32_t x,
-                                                  int32_t y) {
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, uint32_t src, int32_t x,
+                                                  int32_t y, int32_t z) {
   asm volatile(
-      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(m)),
-      "r"(src), "r"(x), "r"(y)
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], "
+      "[%1];" ::"l"(reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 

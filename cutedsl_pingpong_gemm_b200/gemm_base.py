@@ -86,22 +86,30 @@ class CompiledGemm:
         # gemm_base.py:514 requires BF16 everywhere; sm_100a adds FP8 E4M3 operands and FP32 D.
         assert a.dtype == b.dtype and a.dtype in ab_codes and c.dtype in d_codes, \
             "A, B and D must be BF16 (gemm_base.py:514), or FP8 E4M3 A/B, or FP32 D"
-        if a.dim() != 2 or b.dim() != 2 or c.dim() != 2:
-            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE, "A, B and D must be 2-D")
-        m, k = a.shape
-        n, kb = b.shape
+        nd = a.dim()
+        if nd not in (2, 3) or b.dim() != nd or c.dim() != nd:
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                "A, B and D must all be 2-D, or all 3-D [L, rows, cols] (batched)")
+        batches = a.shape[0] if nd == 3 else 1
+        if nd == 3 and (b.shape[0] != batches or c.shape[0] != batches):
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                f"batch counts differ: A{tuple(a.shape)} B{tuple(b.shape)} "
+                                f"D{tuple(c.shape)}")
+        m, k = a.shape[-2:]
+        n, kb = b.shape[-2:]
+        b_rows = n
         if gated:
             # B = [W_gate; W_up] (2N rows), D is M x N.
             n //= 2
-            if b.shape[0] != 2 * n:
+            if b_rows != 2 * n:
                 raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
-                                    f"gated B must have an even number of rows, got {b.shape[0]}")
-        if kb != k or tuple(c.shape) != (m, n):
+                                    f"gated B must have an even number of rows, got {b_rows}")
+        if kb != k or tuple(c.shape[-2:]) != (m, n):
             raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
                                 f"shapes A{tuple(a.shape)} B{tuple(b.shape)} D{tuple(c.shape)} "
                                 f"do not form D = A @ B.T" + (" (gated)" if gated else ""))
         for name, t in (("A", a), ("B", b), ("D", c)):
-            if t.numel() > 0 and t.stride(1) != 1:
+            if t.numel() > 0 and t.stride(-1) != 1:
                 raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
                                     f"{name} must have unit stride in its last dimension")
             if t.numel() > 0 and not t.is_cuda:
@@ -110,17 +118,21 @@ class CompiledGemm:
             # A single-row or empty tensor's row stride is never used; give the padded row length.
             per16 = 16 // t.element_size()
             if rows > 1 and cols > 0:
-                return t.stride(0)
+                return t.stride(-2)
             return max(per16, -(-cols // per16) * per16)
 
-        lda, ldb, ldd = row_stride(a, m, k), row_stride(b, b.shape[0], k), row_stride(c, m, n)
+        lda, ldb, ldd = row_stride(a, m, k), row_stride(b, b_rows, k), row_stride(c, m, n)
+        # The L mode of the reference's (M, K, L) tensors (gemm_base.py:221 fixes it at one).
+        l = batches if batches > 1 else 0
+        bsa, bsb, bsd = (a.stride(0), b.stride(0), c.stride(0)) if l else (0, 0, 0)
         dev = c.device.index if c.is_cuda else torch.cuda.current_device()
         dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
-        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k, bool(gated))
+        key = (m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k, bool(gated), l,
+               bsa, bsb, bsd)
         plan = self._plans.get(key)
         if plan is None:
             plan = _Plan(gemm, m, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, scale_mode, split_k,
-                         gated)
+                         gated, l, bsa, bsb, bsd)
             self._plans[key] = plan
         return plan
 
@@ -153,16 +165,23 @@ class CompiledGemm:
         # B: 128 x 128 blocks, layouts of cpgemm.h); one value each is a per-tensor scale.
         block = scale_a is not None and scale_a.numel() > 1
         mode = _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR
+        if a.dim() == 3 and a.shape[0] == 0:
+            return None  # no batches: nothing to compute
         if split_k == 0:
-            split_k = 1 if (block or fused) else self.auto_split_k(a.shape[0], b.shape[0],
-                                                                    a.shape[1])
+            batches = a.shape[0] if a.dim() == 3 else 1
+            split_k = 1 if (block or fused) else self.auto_split_k(
+                a.shape[-2], b.shape[-2], a.shape[-1], batches)
         split_k = int(split_k)
         if (split_k > 1 or split_k == _lib.CPG_SPLIT_K_STREAM) and c.dtype == torch.bfloat16:
+            if c.dim() == 3 and not c.is_contiguous():
+                raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
+                                    "batched split-K into BF16 needs a contiguous D")
             ws = self._workspace(c)
             plan = self._plan(a, b, ws, mode, split_k)
             plan.run(a, b, ws, stream, bias=None, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
             from .quant import cast_f32_bf16
-            cast_f32_bf16(ws, bias, out=c, stream=stream)
+            n = c.shape[-1]
+            cast_f32_bf16(ws.reshape(-1, n), bias, out=c.reshape(-1, n), stream=stream)
             return None
         plan = self._plan(a, b, c, mode, split_k, gated)
         plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b,
@@ -179,13 +198,13 @@ class CompiledGemm:
             self._workspaces[key] = ws
         return ws
 
-    def auto_split_k(self, m: int, n: int, k: int) -> int:
+    def auto_split_k(self, m: int, n: int, k: int, batches: int = 1) -> int:
         """When the output tiles alone cannot fill the GPU (decode-like small M): Stream-K for a
         persistent kernel (-1), else about three waves of K ranges; 1 otherwise."""
         gemm = self.gemm
         cm, cn, _ = gemm.cluster_shape_mnk
         tiles = -(-max(m, 1) // (128 * cm)) * -(-max(n, 1) // gemm.cta_tile_shape_mnk[1])
-        tiles = -(-tiles // cn)
+        tiles = -(-tiles // cn) * max(batches, 1)
         slots = gemm.max_active_clusters
         if tiles >= slots:
             return 1
@@ -200,14 +219,17 @@ class _Plan:
     """One ``cpg_gemm`` handle: fixed problem, kernel variant and launch grid."""
 
     def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d,
-                 scale_mode=0, split_k=1, gated=False):
+                 scale_mode=0, split_k=1, gated=False, l=0, batch_stride_a=0, batch_stride_b=0,
+                 batch_stride_d=0):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
+        self.l = l
         self.device = device
         self.scale_mode = scale_mode
         cfg = gemm._config_c()
         prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode, split_k,
-                                 1 if gated else 0)
+                                 1 if gated else 0, l, batch_stride_a, batch_stride_b,
+                                 batch_stride_d)
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -278,18 +300,19 @@ class _Plan:
                                     f"{name} must be a contiguous float32 CUDA tensor of shape "
                                     f"{want[name]}")
             scales.append(None if sc is None else sc.data_ptr())
-        src_ptr, ld_src = None, 0
+        src_ptr, ld_src, bs_src = None, 0, 0
         if source is not None:
-            if not (source.is_cuda and source.dtype == c.dtype and tuple(source.shape) == (self.m, self.n)
-                    and (source.numel() == 0 or source.stride(1) == 1)):
+            if not (source.is_cuda and source.dtype == c.dtype and source.shape == c.shape
+                    and (source.numel() == 0 or source.stride(-1) == 1)):
                 raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
                                     "source must be a CUDA tensor of D's dtype and shape with unit "
                                     "column stride")
             per16 = 16 // source.element_size()
-            ld_src = source.stride(0) if self.m > 1 else max(per16, -(-self.n // per16) * per16)
+            ld_src = source.stride(-2) if self.m > 1 else max(per16, -(-self.n // per16) * per16)
+            bs_src = source.stride(0) if source.dim() == 3 else 0
             src_ptr = source.data_ptr() if source.numel() else None
         epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales,
-                             float(beta), int(activation), src_ptr, int(ld_src))
+                             float(beta), int(activation), src_ptr, int(ld_src), int(bs_src))
         st = _stream_handle(stream, c.device)
         rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
                                    b.data_ptr() if b.numel() else None, c.data_ptr(),

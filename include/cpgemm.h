@@ -116,6 +116,12 @@ typedef struct cpg_gemm_problem {
                             D[:, n] = act(alpha s_a s_b A . W_gate[n]) * alpha s_a s_b A . W_up[n];
                             needs tile_n 512 (each tile: 256 gate + 256 up accumulator columns),
                             no bias, no C source and no split-K */
+  int64_t l;             /* batches: the L mode of the reference's (M, K, L) tensors, which its
+                            kernel fixes at one (gemm_base.py:221, tile_scheduler.py:96); 0 or 1:
+                            one batch.  Batch b of A, B and D starts batch_stride_* elements
+                            after batch b - 1 (multiples of 16 bytes; D's batches must not
+                            overlap: batch_stride_d >= m * ldd).  Not with block scales. */
+  int64_t batch_stride_a, batch_stride_b, batch_stride_d;
 } cpg_gemm_problem;
 
 #define CPG_SPLIT_K_STREAM (-1)
@@ -138,6 +144,7 @@ typedef struct cpg_epilogue {
   int32_t activation;
   const void* source;
   int64_t ld_source;
+  int64_t batch_stride_source; /* elements between the batches of C (batched problems) */
 } cpg_epilogue;
 
 #define CPG_ACT_NONE 0
