@@ -107,3 +107,29 @@ def test_gemm_create_without_device_fails_cleanly(lib):
     rc = lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), 0, ctypes.byref(h))
     assert rc in (_lib.CPG_ERR_NO_DEVICE, _lib.CPG_ERR_CUDA)
     assert not h.value
+
+
+def _header_struct_fields(name):
+    """Field names, in order, of `typedef struct name { ... } name;` in include/cpgemm.h."""
+    import re
+    text = open(os.path.join(ROOT, "include", "cpgemm.h")).read()
+    body = text[text.index(f"typedef struct {name} {{"):]
+    body = body[body.index("{") + 1:body.index(f"}} {name};")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        names = decl.split(None, 1)[1] if not decl.startswith("const ") else decl.split(None, 2)[2]
+        for part in names.split(","):
+            fields.append(part.strip().lstrip("*").strip())
+    return fields
+
+
+@pytest.mark.parametrize("c_name,py_struct", [("cpg_gemm_config", "GemmConfigC"),
+                                              ("cpg_gemm_problem", "GemmProblemC"),
+                                              ("cpg_epilogue", "EpilogueC")])
+def test_ctypes_structs_match_header(c_name, py_struct):
+    struct = getattr(_lib, py_struct)
+    assert [f[0] for f in struct._fields_] == _header_struct_fields(c_name)
