@@ -77,6 +77,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--m", type=int, default=0,
+                    help="override the workload's M (per GPU for weak scaling; for smaller "
+                         "profiling cases)")
     ap.add_argument("--activation", default=None,
                     choices=["relu", "silu", "gelu", "gelu_tanh"],
                     help="fused epilogue activation for the GEMM workloads")
@@ -393,7 +396,8 @@ def run_cpg(args, world, rank, local):
 
     w = WORKLOADS[args.workload]
     n, k = w["n"], w["k"]
-    m = w["m"] if w["m_is_per_gpu"] else w["m"] // world
+    m_w = args.m or w["m"]
+    m = m_w if w["m_is_per_gpu"] else m_w // world
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
 
