@@ -80,6 +80,9 @@ def parse_args():
     ap.add_argument("--m", type=int, default=0,
                     help="override the workload's M (per GPU for weak scaling; for smaller "
                          "profiling cases)")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="tallk: column chunks whose reduce-scatter overlaps the next chunk's "
+                         "GEMM (measured slower than 1 on two GPUs: see DESIGN.md)")
     ap.add_argument("--activation", default=None,
                     choices=["relu", "silu", "gelu", "gelu_tanh"],
                     help="fused epilogue activation for the GEMM workloads")
@@ -331,16 +334,15 @@ def run_tallk(args, world, rank, local):
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
-    tiles = -(-m // 128) * -(-n // tile_n)
-    kblocks = -(-(ke - ks) // 64)
-    local_split = max(1, min(kblocks // 8, round(4 * 148 / tiles)))
-    sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=local_split)
+    chunks = max(1, args.chunks)
+    # The in-GPU split of each (chunk's) GEMM is picked from its tile count (auto_split_k).
+    sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=0, chunks=chunks)
 
     launches = [0]
 
     def step():
         out = sk(a_k, b_k, m, n)
-        launches[0] += 2  # GEMM + cast (the memset and NCCL kernels are not ours)
+        launches[0] += 2 * len(sk.column_chunks(n)) if chunks > 1 else 2  # GEMM + cast each
         return out
 
     for _ in range(args.warmup):
@@ -374,7 +376,8 @@ def run_tallk(args, world, rank, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": args.workload, "m": m, "n": n, "k": k,
-                       "parallelism": f"split-K x{world} (NCCL reduce-scatter) x{local_split} in-GPU",
+                       "parallelism": f"split-K x{world} (NCCL reduce-scatter), auto in-GPU split",
+                       "rs_chunks": chunks,
                        "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
                        "rows_per_rank": s1 - s0, "l2": "inputs 512 MiB per rank at 1 GPU; no flush"},
             "roofline": {"bound": "tensor", "achieved": total_flops / world / (ms_local * 1e-3) / 1e12,

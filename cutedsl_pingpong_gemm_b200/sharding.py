@@ -91,17 +91,26 @@ class MShardedGemm:
 class SplitKGemm:
     """Split-K across ranks with an NCCL reduce-scatter of fp32 partials.
 
-    ``partial_fn(a_k, b_k) -> fp32 [M, N]`` computes one rank's partial product and ``cast_fn``
-    turns the reduced fp32 rows into the output; ``SplitKGemm.on_gpu`` builds both from the
+    ``partial_fn(a_k, b_k) -> fp32 [M, N]`` computes one rank's partial product (for the B rows
+    it is given) and ``cast_fn(rows, cs, ce, out)`` turns reduced fp32 rows of columns [cs, ce)
+    into the output (writing ``out`` when given); ``SplitKGemm.on_gpu`` builds both from the
     sm_100a kernels (FP32-epilogue GEMM, ``cpg_cast_f32_bf16``).
+
+    With ``chunks`` > 1 the columns are cut into that many ranges: chunk c's GEMM runs on the
+    caller's stream while the reduce-scatter (and cast) of chunk c - 1 runs on a second stream,
+    so the collective overlaps the compute and only the last chunk's exchange is exposed.
     """
 
+    CHUNK_ALIGN = 256  # column chunks start on tile boundaries
+
     @staticmethod
-    def on_gpu(gemm, world: int, rank: int, group=None, bias=None, local_split_k: int = 1):
+    def on_gpu(gemm, world: int, rank: int, group=None, bias=None, local_split_k: int = 1,
+               chunks: int = 1):
         """GPU instance: partials by ``gemm`` (a GemmSM90) into FP32, cast to BF16 (+ bias).
 
         ``local_split_k`` additionally splits each rank's K range inside the GPU (the kernel's
-        L dimension) when the per-rank problem has too few tiles to fill the SMs.
+        L dimension; 0 picks from the tile count, Stream-K for few tiles) when the per-rank
+        problem has too few tiles to fill the SMs.
         """
         import torch
         from .quant import cast_f32_bf16
@@ -111,27 +120,80 @@ class SplitKGemm:
             gemm(a_k, b_k, out, None, split_k=local_split_k)
             return out
 
-        def cast(rows):
-            return cast_f32_bf16(rows, bias)
+        def cast(rows, cs, ce, out=None):
+            return cast_f32_bf16(rows, None if bias is None else bias[cs:ce], out=out)
 
-        return SplitKGemm(world, rank, partial, cast, group)
+        return SplitKGemm(world, rank, partial, cast, group, chunks=chunks,
+                          out_dtype=torch.bfloat16)
 
     def __init__(self, world: int, rank: int, partial_fn: Callable, cast_fn: Optional[Callable] = None,
-                 group=None):
+                 group=None, chunks: int = 1, out_dtype=None):
         self.world = world
         self.rank = rank
         self.partial_fn = partial_fn
         self.cast_fn = cast_fn
         self.group = group
+        self.chunks = max(1, int(chunks))
+        self.out_dtype = out_dtype  # dtype of cast_fn's output (None: the partials' dtype)
+        self._comm = {}
 
     def k_range(self, k: int) -> Tuple[int, int]:
         return k_ranges(k, self.world)[self.rank]
 
+    def column_chunks(self, n: int) -> List[Tuple[int, int]]:
+        """Non-empty column ranges [cs, ce) of the chunked exchange, in order."""
+        cols = [row_range(n, self.chunks, c, self.CHUNK_ALIGN) for c in range(self.chunks)]
+        return [(cs, ce) for cs, ce in cols if ce > cs]
+
     def __call__(self, a_k, b_k, m: int, n: int):
         """``a_k`` [M, k_r] and ``b_k`` [N, k_r] hold this rank's K range.  Returns this rank's
         rows of D (``row_range(m, world, rank)``), cast by ``cast_fn`` when given."""
+        if self.world > 1 and self.chunks > 1 and n > self.CHUNK_ALIGN:
+            return self._chunked(a_k, b_k, m, n)
         partial = self.partial_fn(a_k, b_k)
         if tuple(partial.shape) != (m, n):
             raise ValueError(f"partial has shape {tuple(partial.shape)}, expected {(m, n)}")
         rows = partial if self.world == 1 else reduce_scatter_rows(partial, self.world, self.group)
-        return self.cast_fn(rows) if self.cast_fn is not None else rows
+        return self.cast_fn(rows, 0, n) if self.cast_fn is not None else rows
+
+    def _chunked(self, a_k, b_k, m: int, n: int):
+        import torch
+        s, e = row_range(m, self.world, self.rank)
+        on_gpu = a_k.is_cuda
+        out = None
+        if on_gpu:
+            compute = torch.cuda.current_stream(a_k.device)
+            comm = self._comm.get(a_k.device)
+            if comm is None:
+                comm = self._comm[a_k.device] = torch.cuda.Stream(a_k.device)
+        for cs, ce in self.column_chunks(n):
+            partial = self.partial_fn(a_k, b_k[cs:ce])
+            if tuple(partial.shape) != (m, ce - cs):
+                raise ValueError(f"partial has shape {tuple(partial.shape)}, "
+                                 f"expected {(m, ce - cs)}")
+            if not on_gpu:
+                rows = reduce_scatter_rows(partial, self.world, self.group)
+                out = self._place(rows, cs, ce, s, e, n, out)
+                continue
+            ready = torch.cuda.Event()
+            ready.record(compute)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ready)
+                partial.record_stream(comm)
+                rows = reduce_scatter_rows(partial, self.world, self.group)
+                out = self._place(rows, cs, ce, s, e, n, out)
+        if on_gpu:
+            compute.wait_stream(comm)
+            out.record_stream(compute)
+        return out
+
+    def _place(self, rows, cs, ce, s, e, n, out):
+        """Write reduced rows of columns [cs, ce) into this rank's [e - s, n] output."""
+        if out is None:
+            dtype = self.out_dtype if self.cast_fn is not None and self.out_dtype else rows.dtype
+            out = rows.new_empty((e - s, n), dtype=dtype)
+        if self.cast_fn is None:
+            out[:, cs:ce] = rows
+        else:
+            self.cast_fn(rows, cs, ce, out[:, cs:ce])
+        return out

@@ -52,10 +52,17 @@ WORKER = textwrap.dedent(r'''
     r0, r1 = row_range(m2, world, rank)
     res2 = gemm_ref.check(rows.cpu(), a2[r0:r1], b2)
     ok &= res2["ok"]
+    # The same with the exchange cut into 3 column chunks (reduce-scatter of chunk c overlaps
+    # the GEMM of chunk c + 1 on a second stream), each chunk choosing its own in-GPU split.
+    skc = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=0, chunks=3)
+    rows_c = skc(a2[:, ks:ke].cuda().contiguous(), b2[:, ks:ke].cuda().contiguous(), m2, n2)
+    torch.cuda.synchronize()
+    res3 = gemm_ref.check(rows_c.cpu(), a2[r0:r1], b2)
+    ok &= res3["ok"]
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
-        print("RESULT", int(flag.item()), res, res2, flush=True)
+        print("RESULT", int(flag.item()), res, res2, res3, flush=True)
     dist.destroy_process_group()
     sys.exit(0 if ok else 1)
 ''')

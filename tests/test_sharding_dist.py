@@ -86,6 +86,30 @@ def _worker(rank, world, port, q):
         s, e = row_range(m, world, rank)
         want = torch.matmul(a.double(), b.double().t())[s:e]
         assert torch.allclose(rows, want, rtol=1e-12, atol=1e-9)
+
+        # Chunked split-K (reduce-scatter per column chunk): same rows, ragged last chunk, and a
+        # cast that writes each chunk's columns of the preallocated output.
+        n2 = 700
+        b2 = torch.randn(n2, k, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16)
+        want2 = torch.matmul(a.double(), b2.double().t())[s:e]
+        sk3 = SplitKGemm(world, rank, partial, chunks=3)
+        assert sk3.column_chunks(n2) == [(0, 256), (256, 512), (512, 700)]
+        rows3 = sk3(a[:, ks:ke], b2[:, ks:ke], m, n2)
+        assert torch.allclose(rows3, want2, rtol=1e-12, atol=1e-9)
+        seen = []
+
+        def cast(r, cs, ce, out=None):
+            seen.append((cs, ce))
+            y = (2 * r).float()
+            if out is None:
+                return y
+            out.copy_(y)
+            return out
+
+        skc = SplitKGemm(world, rank, partial, cast, chunks=3, out_dtype=torch.float32)
+        rc = skc(a[:, ks:ke], b2[:, ks:ke], m, n2)
+        assert rc.dtype == torch.float32 and seen == skc.column_chunks(n2)
+        assert torch.allclose(rc.double(), 2 * want2, rtol=1e-6, atol=1e-4)
         q.put((rank, "ok"))
     except Exception as ex:  # pragma: no cover - reported through the queue
         q.put((rank, repr(ex)))
