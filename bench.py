@@ -82,7 +82,7 @@ def parse_args():
                          "profiling cases)")
     ap.add_argument("--chunks", type=int, default=1,
                     help="tallk: column chunks whose reduce-scatter overlaps the next chunk's "
-                         "GEMM (measured slower than 1 on two GPUs: see DESIGN.md)")
+                         "GEMM (measured slower than 1 on two GPUs)")
     ap.add_argument("--activation", default=None,
                     choices=["relu", "silu", "gelu", "gelu_tanh"],
                     help="fused epilogue activation for the GEMM workloads")
@@ -500,38 +500,66 @@ def run_cpg(args, world, rank, local):
     # ---------------- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        # Every step uploads its A and B from pinned host memory and downloads its D, through
+        # the public API.  Steps are pipelined over two device buffer sets and three streams:
+        # the upload of step i + 1 and the download of step i - 1 overlap the GEMM of step i
+        # (PCIe moves both directions at once), as a serving loop would run them.
         a_h = a.cpu().pin_memory()
         b_h = b.cpu().pin_memory()
-        d_h = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
-        a2 = torch.empty_like(a)
-        b2 = torch.empty_like(b)
+        h2d = torch.cuda.Stream(dev)
+        d2h = torch.cuda.Stream(dev)
+        sets = [(torch.empty_like(a), torch.empty_like(b), torch.empty_like(d),
+                 torch.empty(d.shape, dtype=d.dtype).pin_memory()) for _ in range(2)]
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        gemm_done = [torch.cuda.Event() for _ in range(2)]
+        out_done = [torch.cuda.Event() for _ in range(2)]
+        for j in range(2):
+            gemm_done[j].record(stream)
+            out_done[j].record(stream)
 
-        def e2e_step():
-            a2.copy_(a_h, non_blocking=True)
-            b2.copy_(b_h, non_blocking=True)
-            compiled(a2, b2, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b,
+        def e2e_step(i):
+            j = i % 2
+            a2, b2, d2, dh = sets[j]
+            h2d.wait_event(gemm_done[j])  # the GEMM that last read this buffer set is done
+            with torch.cuda.stream(h2d):
+                a2.copy_(a_h, non_blocking=True)
+                b2.copy_(b_h, non_blocking=True)
+            in_ready[j].record(h2d)
+            stream.wait_event(in_ready[j])
+            stream.wait_event(out_done[j])  # D of the previous use of this set is downloaded
+            compiled(a2, b2, d2, stream, bias=bias, scale_a=scale_a, scale_b=scale_b,
                      split_k=split_k, activation=act, gated=gated)
-            d_h.copy_(d, non_blocking=True)
+            gemm_done[j].record(stream)
+            d2h.wait_event(gemm_done[j])
+            with torch.cuda.stream(d2h):
+                dh.copy_(d2, non_blocking=True)
+            out_done[j].record(d2h)
 
-        for _ in range(2):
-            e2e_step()
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         f0 = torch.cuda.Event(enable_timing=True)
         f1 = torch.cuda.Event(enable_timing=True)
         f0.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
+        h2d.wait_stream(stream)  # no upload starts before the timed region
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        stream.wait_stream(h2d)
+        stream.wait_stream(d2h)
         f1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         e2e_ms = reduce_max(f0.elapsed_time(f1) / args.e2e_steps, world)
         e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": int((a.numel() + b.numel()) * a.element_size() * world),
-               "d2h_bytes_per_step": int(d.numel() * 2 * world), "steps": args.e2e_steps,
-               "ms_per_step": e2e_ms, "gpu_launches": args.e2e_steps * world,
-               "path": "GemmSM90 compiled call (C ABI cpg_gemm_run) with pinned-host A, B in and D out"}
+               "d2h_bytes_per_step": int(d.numel() * d.element_size() * world),
+               "steps": args.e2e_steps, "ms_per_step": e2e_ms,
+               "gpu_launches": args.e2e_steps * world,
+               "path": "GemmSM90 compiled call (C ABI cpg_gemm_run); every step uploads A, B from "
+                       "pinned host memory and downloads D; uploads of step i + 1 and the "
+                       "download of step i - 1 overlap the GEMM of step i (two buffer sets)"}
 
     clocks = sampler.summary()
     cpu = None
