@@ -40,7 +40,7 @@ CPG_ACT_GELU_TANH = 4
 ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
                "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 
 class CpgError(RuntimeError):
@@ -94,6 +94,7 @@ class GemmProblemC(ctypes.Structure):
         ("l", ctypes.c_int64),
         ("batch_stride_a", ctypes.c_int64), ("batch_stride_b", ctypes.c_int64),
         ("batch_stride_d", ctypes.c_int64),
+        ("grouped", ctypes.c_int32),
     ]
 
 
@@ -115,6 +116,7 @@ SIGNATURES = {
     "cpg_config_validate": (ctypes.c_int, [_P(GemmConfigC)]),
     "cpg_gemm_create": (ctypes.c_int, [_P(GemmConfigC), _P(GemmProblemC), ctypes.c_int, _P(_vp)]),
     "cpg_gemm_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _P(EpilogueC), _vp]),
+    "cpg_gemm_run_grouped": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _P(EpilogueC), _vp]),
     "cpg_gemm_destroy": (ctypes.c_int, [_vp]),
     "cpg_gemm_launch_info": (ctypes.c_int, [_vp, _P(_i32), _P(_i32), _P(_i32), _P(_i32), _P(_i32)]),
     "cpg_gemm_sched_params": (ctypes.c_int, [_vp, _P(SchedParamsC)]),

@@ -211,6 +211,49 @@ __global__ void fill_rows_kernel(OutT* d, int64_t m, int64_t n, int64_t ldd,
   }
 }
 
+// Status word value of a grouped launch whose offsets broke the rule (groups made empty).
+constexpr int32_t kStatusBadGroups = 0x200;
+constexpr int kPrefixThreads = 1024;
+
+// Cluster-tile prefix of a grouped GEMM: prefix[g] = sum over h < g of
+// ceil(M_h / rows_per_cluster) * n_clusters with M_h = offsets[h + 1] - offsets[h].  One block:
+// thread t sums its contiguous run of groups, a block-wide scan gives each run's start.
+__global__ void __launch_bounds__(kPrefixThreads)
+    group_tile_prefix_kernel(const int32_t* offsets, int32_t groups, int64_t rows,
+                             int32_t rows_per_cluster, int32_t n_clusters, int32_t* prefix,
+                             int32_t* status) {
+  __shared__ int64_t sums[kPrefixThreads];
+  const int t = threadIdx.x;
+  const int per = (groups + kPrefixThreads - 1) / kPrefixThreads;
+  const int g0 = min(t * per, groups), g1 = min(g0 + per, groups);
+  bool bad = false;
+  auto tiles = [&](int g) -> int64_t {
+    const int32_t s = offsets[g], e = offsets[g + 1];
+    if (s < 0 || e < s || e > rows) {
+      bad = true;
+      return 0;
+    }
+    return static_cast<int64_t>((e - s + rows_per_cluster - 1) / rows_per_cluster) * n_clusters;
+  };
+  int64_t local = 0;
+  for (int g = g0; g < g1; ++g) local += tiles(g);
+  sums[t] = local;
+  __syncthreads();
+  for (int o = 1; o < kPrefixThreads; o <<= 1) {
+    const int64_t v = t >= o ? sums[t - o] : 0;
+    __syncthreads();
+    sums[t] += v;
+    __syncthreads();
+  }
+  int64_t run = t > 0 ? sums[t - 1] : 0;
+  for (int g = g0; g < g1; ++g) {
+    prefix[g] = static_cast<int32_t>(run);
+    run += tiles(g);
+  }
+  if (t == kPrefixThreads - 1) prefix[groups] = static_cast<int32_t>(sums[t]);
+  if (bad && status != nullptr) atomicCAS(status, 0, kStatusBadGroups);
+}
+
 // Grid of cast_f32_bf16_kernel: x covers a row's columns in quads of 4 (256 threads per block),
 // y covers rows (grid-stride beyond 65535), about 32 k blocks in total.
 dim3 cast_grid(int64_t rows, int64_t cols) {
@@ -277,6 +320,9 @@ struct cpg_gemm {
   int32_t splits;
   int32_t stream_k;
   int64_t batches;
+  int64_t groups;            // grouped GEMM: number of groups (0: not grouped)
+  int32_t group_n_clusters;  // cluster columns of every group
+  int32_t* tile_prefix_dev;  // [groups + 1], written by group_tile_prefix_kernel per launch
   bool maps_valid;
   const void* map_a_ptr;
   const void* map_b_ptr;
@@ -286,7 +332,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 8; }
+int cpg_abi_version(void) { return 9; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -421,7 +467,22 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   if (prob->gated && prob->n > (int64_t(1) << 30))
     return fail(CPG_ERR_INVALID_SHAPE, "gated GEMM: 2 N must fit in 31 bits");
   if (prob->l < 0) return fail(CPG_ERR_INVALID_SHAPE, "l (batches) must be >= 0");
-  const int64_t batches = prob->l > 1 ? prob->l : 1;
+  if (prob->grouped != 0 && prob->grouped != 1)
+    return fail(CPG_ERR_INVALID_CONFIG, "grouped must be 0 or 1, got %d", prob->grouped);
+  const int64_t groups = prob->grouped ? prob->l : 0;
+  if (prob->grouped) {
+    if (groups < 1 || groups > (int64_t(1) << 20))
+      return fail(CPG_ERR_INVALID_SHAPE, "a grouped GEMM needs 1 <= l (groups) <= 2^20");
+    if (!cfg->is_persistent)
+      return fail(CPG_ERR_UNSUPPORTED, "a grouped GEMM needs a persistent kernel");
+    if (prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM ||
+        v.scale_mode != CPG_SCALE_TENSOR)
+      return fail(CPG_ERR_UNSUPPORTED, "grouped GEMM: no split-K and no block scales");
+    if (prob->k == 0) return fail(CPG_ERR_UNSUPPORTED, "grouped GEMM: K must be > 0");
+    if ((prob->batch_stride_b * elem_bytes(prob->dtype_ab)) % 16 != 0 || prob->batch_stride_b < 0)
+      return fail(CPG_ERR_ALIGNMENT, "batch_stride_b must be a multiple of 16 bytes");
+  }
+  const int64_t batches = (!prob->grouped && prob->l > 1) ? prob->l : 1;
   if (batches > 1) {
     if (v.scale_mode == CPG_SCALE_BLOCK)
       return fail(CPG_ERR_UNSUPPORTED, "batched block-scaled FP8 is not implemented");
@@ -497,6 +558,7 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   g->splits = g->k_iters_per_split > 0
                   ? (g->k_iters + g->k_iters_per_split - 1) / g->k_iters_per_split : 1;
   g->batches = batches;
+  g->groups = groups;
   // The scheduler's L index runs over batches x split-K ranges (batch-major).
   const int64_t ntl = int64_t(g->splits) * batches;
   if (ntm * ntn * ntl > (int64_t(1) << 31) - 1) {
@@ -514,6 +576,19 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     const int64_t units = int64_t(cpg::sched_total_clusters(g->sched)) * g->k_iters;
     grid[2] = static_cast<int32_t>(units < mac ? (units > 0 ? units : 1) : mac);
   }
+  if (groups > 0) {
+    // Grouped: at most ceil(m / rows per cluster) + groups cluster rows (each group adds at
+    // most one partial row of tiles) times the cluster columns.
+    const int64_t rows_per_cluster = 128 * cfg->cluster_m;
+    const int64_t ncol = (ntn + cfg->cluster_n - 1) / cfg->cluster_n;
+    const int64_t bound = ((prob->m + rows_per_cluster - 1) / rows_per_cluster + groups) * ncol;
+    if (bound > (int64_t(1) << 31) - 1) {
+      delete g;
+      return fail(CPG_ERR_INVALID_SHAPE, "grouped GEMM: more than 2^31 - 1 tiles");
+    }
+    g->group_n_clusters = static_cast<int32_t>(ncol);
+    grid[2] = static_cast<int32_t>(bound < mac ? (bound > 0 ? bound : 1) : mac);
+  }
   for (int i = 0; i < 3; ++i) g->grid[i] = grid[i];
   g->cluster[0] = cfg->cluster_m;
   g->cluster[1] = cfg->cluster_n;
@@ -530,15 +605,24 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     delete g;
     return cuda_fail(e, "cudaMemset(status word)");
   }
+  if (groups > 0) {
+    e = cudaMalloc(&g->tile_prefix_dev, sizeof(int32_t) * (groups + 1));
+    if (e != cudaSuccess) {
+      cudaFree(g->status_dev);
+      delete g;
+      return cuda_fail(e, "cudaMalloc(group tile prefix)");
+    }
+  }
   *out = g;
   return CPG_OK;
 }
 
 int cpg_gemm_destroy(cpg_gemm* g) {
   if (g == nullptr) return CPG_OK;
-  if (g->status_dev != nullptr) {
+  if (g->status_dev != nullptr || g->tile_prefix_dev != nullptr) {
     DeviceGuard guard(g->device);
-    cudaFree(g->status_dev);
+    if (g->status_dev != nullptr) cudaFree(g->status_dev);
+    if (g->tile_prefix_dev != nullptr) cudaFree(g->tile_prefix_dev);
   }
   delete g;
   return CPG_OK;
@@ -599,14 +683,37 @@ int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
   *status = s;
   if (s != 0) {
     cudaMemset(g->status_dev, 0, sizeof(int32_t));
+    if (s == kStatusBadGroups)
+      return fail(CPG_ERR_INVALID_SHAPE, "group offsets not non-decreasing within [0, m]");
     return fail(CPG_ERR_DEVICE_TIMEOUT, "kernel wait timed out at site %d", s & 0xFF);
   }
   return CPG_OK;
 }
 
+static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                    void* stream, const int32_t* group_offsets);
+
 int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
                  void* stream) {
   if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  if (g->groups > 0)
+    return fail(CPG_ERR_INVALID_CONFIG, "grouped plan: launch it with cpg_gemm_run_grouped");
+  return run_impl(g, a, b, d, epi, stream, nullptr);
+}
+
+int cpg_gemm_run_grouped(cpg_gemm* g, const void* a, const void* b, void* d,
+                         const int32_t* group_offsets, const cpg_epilogue* epi, void* stream) {
+  if (g == nullptr) return fail(CPG_ERR_NULL, "plan is NULL");
+  if (g->groups == 0)
+    return fail(CPG_ERR_INVALID_CONFIG, "plan is not grouped (create it with prob->grouped = 1)");
+  if (group_offsets == nullptr) return fail(CPG_ERR_NULL, "group_offsets is NULL");
+  if ((reinterpret_cast<uintptr_t>(group_offsets) & 3u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "group_offsets must be 4-byte aligned");
+  return run_impl(g, a, b, d, epi, stream, group_offsets);
+}
+
+static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                    void* stream, const int32_t* group_offsets) {
   const cpg_gemm_problem& pr = g->prob;
   if (pr.m == 0 || pr.n == 0) return CPG_OK;
   if (d == nullptr) return fail(CPG_ERR_NULL, "D is NULL");
@@ -678,10 +785,11 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
     int rc = encode_tiled(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda, cpg::kBM,
                           bk, g->batches, pr.batch_stride_a);
     if (rc != CPG_OK) return rc;
-    // One B box per MMA: min(tile_n, 256) / cta_group rows; a gated B holds 2 N rows.
+    // One B box per MMA: min(tile_n, 256) / cta_group rows; a gated B holds 2 N rows; a
+    // grouped B has one batch per group.
     rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.gated ? 2 * pr.n : pr.n, pr.k,
-                      pr.ldb, (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk, g->batches,
-                      pr.batch_stride_b);
+                      pr.ldb, (g->v.bn > 256 ? 256 : g->v.bn) / g->v.cta_group, bk,
+                      g->groups > 0 ? g->groups : g->batches, pr.batch_stride_b);
     if (rc != CPG_OK) return rc;
     rc = encode_tiled(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 32, store_cols,
                       g->batches, pr.batch_stride_d);
@@ -732,6 +840,19 @@ int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_e
   p.src_batch_stride = (src != nullptr && g->batches > 1) ? epi->batch_stride_source : 0;
   p.gated = pr.gated;
   p.num_splits = g->splits;
+  p.d = d;
+  p.ldd = pr.ldd;
+  if (g->groups > 0) {
+    p.num_groups = static_cast<int32_t>(g->groups);
+    p.group_offsets = group_offsets;
+    p.tile_prefix = g->tile_prefix_dev;
+    p.group_n_clusters = g->group_n_clusters;
+    group_tile_prefix_kernel<<<1, kPrefixThreads, 0, st>>>(
+        group_offsets, p.num_groups, pr.m, 128 * g->cfg.cluster_m, g->group_n_clusters,
+        g->tile_prefix_dev, g->status_dev);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "group tile prefix launch");
+  }
 
   if (g->splits > 1 || g->stream_k) {
     // The splits / Stream-K segments add their partial sums into D.

@@ -118,7 +118,27 @@ struct GemmParams {
   int32_t gated;
   // The scheduler's L index is batch * num_splits + split (split-K ranges of each batch).
   int32_t num_splits;
+  // Grouped GEMM (ragged groups, MoE-style; GroupInfo): group g owns rows
+  // [group_offsets[g], group_offsets[g + 1]) of A and D and batch g of B.
+  int32_t num_groups;             // 0: not grouped
+  const int32_t* group_offsets;   // [num_groups + 1], device
+  const int32_t* tile_prefix;     // [num_groups + 1]: cluster tiles of the groups before g
+  int32_t group_n_clusters;       // cluster columns of every group
+  void* d;                        // D itself: rows at a group boundary are stored per thread
+  int64_t ldd;
 };
+
+// The grouped mode of the segment iterator (num_groups == 0: the scheduler's tiles).
+struct GroupInfo {
+  int32_t num_groups;
+  const int32_t* offsets;
+  const int32_t* prefix;
+  int32_t n_clusters;
+};
+
+__device__ __forceinline__ GroupInfo group_info(const GemmParams& p) {
+  return GroupInfo{p.num_groups, p.group_offsets, p.tile_prefix, p.group_n_clusters};
+}
 
 enum Activation : int32_t {
   kActNone = 0,
@@ -256,8 +276,12 @@ __device__ __forceinline__ void work_tile_coords(const SchedParams& sp, int32_t 
 struct Segment {
   int32_t cid;
   int32_t kb0, kb1;
-  int32_t batch;  // L index of the batched GEMM (0 when unbatched)
-  int32_t index;  // how many segments this CTA produced before this one
+  int32_t pid_m, pid_n;   // this CTA's tile
+  int32_t batch;          // L index of the batched GEMM / group of a grouped GEMM (else 0)
+  int32_t ab_batch;       // TMA batch coordinate of A and D (a grouped A / D has one batch)
+  int32_t row_base;       // first row of A / D of the tile's problem (group), and its end
+  int32_t row_end;
+  int32_t index;          // how many segments this CTA produced before this one
 };
 
 // Walks this CTA's segments.  Tile mode: the scheduler's tiles, one segment per tile; the L
@@ -270,8 +294,39 @@ struct SegmentIter {
   WorkIter it;
   int64_t pos, end;
   int32_t k_iters, kps, stream, index, splits;
+  GroupInfo gi;
+  int32_t group_total;  // cluster tiles of all groups (grouped mode)
 
   __device__ __forceinline__ bool next(const SchedParams& sp, Segment& s) {
+    if (gi.num_groups > 0) {
+      // Grouped: linear cluster tile -> group (binary search of the tile prefix) -> m-fastest
+      // order inside the group, so the group's row tiles share each column tile of B in L2.
+      if (it.cid >= group_total) return false;
+      const int32_t cid = it.cid;
+      int32_t lo = 0, hi = gi.num_groups;
+      while (hi - lo > 1) {
+        const int32_t mid = (lo + hi) >> 1;
+        if (gi.prefix[mid] <= cid) lo = mid; else hi = mid;
+      }
+      const int32_t local = cid - gi.prefix[lo];
+      const int32_t count = gi.prefix[lo + 1] - gi.prefix[lo];
+      const int32_t m_clusters = count / gi.n_clusters;
+      const int32_t cm = local % m_clusters, cn = local / m_clusters;
+      s.cid = cid;
+      s.kb0 = 0;
+      s.kb1 = k_iters;
+      s.pid_m = cm * sp.cluster_m + static_cast<int32_t>(ptx::cluster_ctaid_x());
+      s.pid_n = cn * sp.cluster_n + static_cast<int32_t>(ptx::cluster_ctaid_y());
+      s.batch = lo;
+      s.ab_batch = 0;
+      s.row_base = gi.offsets[lo];
+      s.row_end = gi.offsets[lo + 1];
+      it.cid += it.stride;
+      s.index = index++;
+      return true;
+    }
+    s.row_base = 0;
+    s.row_end = 0x7fffffff;
     if (stream) {
       if (pos >= end) return false;
       const int64_t tile = pos / k_iters;
@@ -284,6 +339,8 @@ struct SegmentIter {
       int32_t l, cid_in_problem;
       fast_divmod(sp.dm_clusters_per_problem, s.cid, l, cid_in_problem);
       s.batch = l;
+      s.ab_batch = l;
+      work_tile_coords(sp, s.cid, s.pid_m, s.pid_n);
       pos += kb1 - kb0;
     } else {
       if (!it.valid()) return false;
@@ -292,8 +349,10 @@ struct SegmentIter {
       const int32_t batch = splits > 1 ? l / splits : l;
       s.cid = it.cid;
       s.batch = batch;
+      s.ab_batch = batch;
       s.kb0 = (l - batch * splits) * kps;
       s.kb1 = s.kb0 + kps < k_iters ? s.kb0 + kps : k_iters;
+      work_tile_coords(sp, s.cid, s.pid_m, s.pid_n);
       it.advance();
     }
     s.index = index++;
@@ -303,9 +362,13 @@ struct SegmentIter {
 
 __device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, int32_t k_iters,
                                                          int32_t kps, int32_t stream_k,
-                                                         int32_t splits) {
+                                                         int32_t splits,
+                                                         GroupInfo gi = GroupInfo{0, nullptr,
+                                                                                  nullptr, 1}) {
   SegmentIter si;
   si.it = make_work_iter(sp);
+  si.gi = gi;
+  si.group_total = gi.num_groups > 0 ? gi.prefix[gi.num_groups] : 0;
   si.k_iters = k_iters;
   si.kps = kps;
   si.stream = stream_k;
@@ -366,6 +429,34 @@ __device__ __forceinline__ void load_row_chunk(const GemmParams& p, int32_t batc
   }
 }
 
+// Store this thread's 128-byte output chunk (packed BF16 pairs or FP32 words, row order) to
+// row `row` of D from column col0, if row < row_end; columns past N are not written.
+template <typename OutT>
+__device__ __forceinline__ void store_row_chunk(const GemmParams& p, int32_t row, int32_t row_end,
+                                                int32_t col0, const uint32_t (&packed)[32]) {
+  if (row >= row_end) return;
+  constexpr int kCols = 128 / static_cast<int>(sizeof(OutT));
+  uint32_t* base = reinterpret_cast<uint32_t*>(static_cast<OutT*>(p.d) +
+                                               static_cast<int64_t>(row) * p.ldd + col0);
+  if (col0 + kCols <= p.n) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      ptx::st_global_v4(base + 4 * q, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                        packed[4 * q + 3]);
+    return;
+  }
+  if constexpr (sizeof(OutT) == 2) {
+    uint16_t* b16 = reinterpret_cast<uint16_t*>(base);
+#pragma unroll
+    for (int j = 0; j < kCols; ++j)
+      if (col0 + j < p.n) b16[j] = static_cast<uint16_t>(packed[j >> 1] >> (16 * (j & 1)));
+  } else {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j)
+      if (col0 + j < p.n) base[j] = packed[j];
+  }
+}
+
 // x[j] += beta * C[j] for the 128-byte chunk of raw words from load_row_chunk.
 template <typename OutT>
 __device__ __forceinline__ void add_row_chunk(float beta, const uint4 (&cs)[8],
@@ -403,7 +494,8 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               uint32_t rank, bool leader,
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
                                               int32_t l2_b = 0, int32_t stream_k = 0,
-                                              int32_t b_slot_rows = 0, int32_t splits = 1) {
+                                              int32_t b_slot_rows = 0, int32_t splits = 1,
+                                              GroupInfo gi = GroupInfo{0, nullptr, nullptr, 1}) {
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
@@ -415,12 +507,11 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t phase = 0;
   uint32_t fills = 0;
   bool ok = true;
-  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits);
+  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits, gi);
   Segment sg;
   while (ok && si.next(sp, sg)) {
-    int32_t pid_m, pid_n;
-    work_tile_coords(sp, sg.cid, pid_m, pid_n);
-    const int32_t a_row = pid_m * kBM;
+    const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
+    const int32_t a_row = sg.row_base + pid_m * kBM;
     // B rows of MMA j: [pid_n * BN + j * kMmaN, +kMmaN), of which this CTA of a pair loads its
     // half (kBRowsPerMma rows at offset rank * kBRowsPerMma) into smem slot j.  Gated tiles
     // (b_slot_rows = N > 0) take MMA j's rows from the j-th of the stacked [W_gate; W_up]:
@@ -438,7 +529,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
       const uint32_t fb = full_bar + 8u * stage;
       if constexpr (CtaGroup == 1) {
         ptx::mbar_arrive_expect_tx(fb, kTxBytes);
-        ptx::tma_load_3d(tm_a, sa, fb, kb * kBK, a_row, sg.batch, pol_a);
+        ptx::tma_load_3d(tm_a, sa, fb, kb * kBK, a_row, sg.ab_batch, pol_a);
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
           ptx::tma_load_3d(tm_b, sb + j * kBRowsPerMma * 128, fb, kb * kBK, b_row + j * slot_rows,
@@ -446,7 +537,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
       } else {
         if (leader) ptx::mbar_arrive_expect_tx(fb, kTxBytes);
         const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
-        ptx::tma_load_3d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, sg.batch, pol_a);
+        ptx::tma_load_3d_pair(tm_a, sa, fb_leader, kb * kBK, a_row, sg.ab_batch, pol_a);
 #pragma unroll
         for (int j = 0; j < kNumMma; ++j)
           ptx::tma_load_3d_pair(tm_b, sb + j * kBRowsPerMma * 128, fb_leader, kb * kBK,
@@ -565,7 +656,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
           leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0,
-          p.num_splits);
+          p.num_splits, group_info(p));
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -577,7 +668,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k,
-                                         p.num_splits);
+                                         p.num_splits, group_info(p));
       Segment sg;
       while (ok && si.next(sp, sg)) {
         const int kb0 = sg.kb0, kb1 = sg.kb1;
@@ -673,11 +764,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     };
     SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k,
-                                       p.num_splits);
+                                       p.num_splits, group_info(p));
     Segment sg;
     while (si.next(sp, sg)) {
-      int32_t pid_m, pid_n;
-      work_tile_coords(sp, sg.cid, pid_m, pid_n);
+      const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
       // Split-K / Stream-K: only the segment holding a tile's first k-block adds the bias.
       const bool add_bias = has_bias && sg.kb0 == 0;
       bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
@@ -693,8 +783,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       __syncwarp();
       const uint32_t t_row = tmem_base + (row_in_tile << 16) + static_cast<uint32_t>(acc * BN);
-      const int32_t g_row = pid_m * kBM + static_cast<int32_t>(row_in_tile);
+      const int32_t g_row = sg.row_base + pid_m * kBM + static_cast<int32_t>(row_in_tile);
       const int32_t my_row = g_row + static_cast<int32_t>(lane);
+      // Rows of this warp that belong to the tile's problem (a grouped tile may end inside).
+      const int32_t row_end = sg.row_end < p.m ? sg.row_end : p.m;
       // A gated 512-wide tile holds gate columns [0, 256) and up columns [256, 512) of the same
       // 256 output columns.
       const int out_cols = gated ? BN / 2 : BN;
@@ -705,7 +797,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // C (beta * C source): this thread's 128-byte row chunk, fetched before the TMEM loads
         // so that the two latencies overlap.
         uint4 cs[8];
-        if (has_src) load_row_chunk<OutT>(p, sg.batch, my_row, col0, cs);
+        if (has_src) load_row_chunk<OutT>(p, sg.ab_batch, my_row, col0, cs);
         float x[kStoreCols];
         if (!gated) {
           // kStoreCols accumulator columns of this thread's row (one 128-byte output row).
@@ -772,13 +864,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         ptx::fence_proxy_async_shared();
         __syncwarp();
+        // The TMA box covers this warp's 32 rows and is clipped at D's last row; a grouped
+        // tile whose group ends inside the box (before D ends) would write the next group's
+        // rows with it, so there each thread stores its own row if it is in the group.
+        // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
+        const bool box = g_row + 32 <= row_end || (g_row < row_end && row_end == p.m);
+        if (!box && g_row < row_end && col0 < p.n)
+          store_row_chunk<OutT>(p, my_row, row_end, col0, packed);
         if (lane == 0) {
-          // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
-          if (g_row < p.m && col0 < p.n) {
+          if (box && col0 < p.n) {
             if (p.reduce_add) {
-              ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.batch);
+              ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
             } else {
-              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.batch);
+              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
             }
           }
           ptx::bulk_commit_group();

@@ -188,6 +188,69 @@ class CompiledGemm:
                  activation=act, source=source, beta=beta)
         return None
 
+    def grouped(self, a, b, c, group_offsets, stream=None, *, bias=None, alpha: float = 1.0,
+                scale_a=None, scale_b=None, activation: Optional[str] = None, source=None,
+                beta: float = 1.0, gated: bool = False):
+        """Grouped GEMM (ragged groups, e.g. the experts of an MoE layer), on the device alone:
+        for every group g, ``c[r] = epilogue(a[r] @ b[g].T)`` for the rows
+        ``group_offsets[g] <= r < group_offsets[g + 1]``.
+
+        ``a`` [T, K] holds the groups' rows one after the other, ``b`` [G, N, K] (or
+        [G, 2N, K] with ``gated``), ``c`` [T, N]; ``group_offsets`` is an int32 CUDA tensor of
+        G + 1 non-decreasing offsets within [0, T] (read on the device: no host synchronisation);
+        rows outside every group are not written.  Epilogue options as in ``__call__``; no
+        split-K and no block scales.  The reference has no grouped form (its kernel fixes the L
+        mode at one, gemm_base.py:221)."""
+        import torch
+        if activation not in _lib.ACTIVATIONS:
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_CONFIG, f"unknown activation {activation!r}")
+        if a.dim() != 2 or b.dim() != 3 or c.dim() != 2:
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                "grouped: a [T, K], b [G, N, K] and c [T, N]")
+        groups = b.shape[0]
+        if not (group_offsets.is_cuda and group_offsets.dtype == torch.int32
+                and group_offsets.dim() == 1 and group_offsets.numel() == groups + 1
+                and group_offsets.is_contiguous()):
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                "group_offsets must be a contiguous int32 CUDA tensor of G + 1")
+        if groups == 0 or a.shape[0] == 0:
+            return None
+        plan = self._grouped_plan(a, b, c, gated)
+        plan.run(a, b, c, stream, bias=bias, alpha=alpha, scale_a=scale_a, scale_b=scale_b,
+                 activation=_lib.ACTIVATIONS[activation], source=source, beta=beta,
+                 group_offsets=group_offsets)
+        return None
+
+    def _grouped_plan(self, a, b, c, gated):
+        import torch
+        ab_codes, d_codes = _dtype_tables()
+        assert a.dtype == b.dtype and a.dtype in ab_codes and c.dtype in d_codes, \
+            "A, B and D must be BF16 (gemm_base.py:514), or FP8 E4M3 A/B, or FP32 D"
+        t, k = a.shape
+        groups, b_rows, kb = b.shape
+        n = b_rows // 2 if gated else b_rows
+        if kb != k or tuple(c.shape) != (t, n) or (gated and b_rows != 2 * n):
+            raise _lib.CpgError(_lib.CPG_ERR_INVALID_SHAPE,
+                                f"grouped shapes A{tuple(a.shape)} B{tuple(b.shape)} "
+                                f"D{tuple(c.shape)} do not match")
+        for name, x in (("A", a), ("B", b), ("D", c)):
+            if x.numel() > 0 and (x.stride(-1) != 1 or not x.is_cuda):
+                raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
+                                    f"{name} must be a CUDA tensor with unit last stride")
+        per16 = 16 // a.element_size()
+        lda = a.stride(0) if t > 1 else max(per16, -(-k // per16) * per16)
+        ldb = b.stride(1) if b_rows > 1 else max(per16, -(-k // per16) * per16)
+        ldd = c.stride(0) if t > 1 else max(16 // c.element_size(), n)
+        dev = c.device.index
+        dt_ab, dt_d = ab_codes[a.dtype], d_codes[c.dtype]
+        key = ("grouped", t, n, k, groups, lda, ldb, ldd, b.stride(0), dev, dt_ab, dt_d, bool(gated))
+        plan = self._plans.get(key)
+        if plan is None:
+            plan = _Plan(self.gemm, t, n, k, lda, ldb, ldd, dev, dt_ab, dt_d, 0, 1, gated, groups,
+                         0, b.stride(0), 0, grouped=True)
+            self._plans[key] = plan
+        return plan
+
     def _workspace(self, c):
         """FP32 [M, N] buffer for split-K partial sums (kept and reused per shape/device)."""
         import torch
@@ -250,7 +313,7 @@ class _Plan:
 
     def __init__(self, gemm: "GemmSM90", m, n, k, lda, ldb, ldd, device, dtype_ab, dtype_d,
                  scale_mode=0, split_k=1, gated=False, l=0, batch_stride_a=0, batch_stride_b=0,
-                 batch_stride_d=0):
+                 batch_stride_d=0, grouped=False):
         self.lib = _lib.load()
         self.m, self.n, self.k = m, n, k
         self.l = l
@@ -259,7 +322,8 @@ class _Plan:
         cfg = gemm._config_c()
         prob = _lib.GemmProblemC(m, n, k, lda, ldb, ldd, dtype_ab, dtype_d, scale_mode, split_k,
                                  1 if gated else 0, l, batch_stride_a, batch_stride_b,
-                                 batch_stride_d)
+                                 batch_stride_d, 1 if grouped else 0)
+        self.grouped = grouped
         h = ctypes.c_void_p()
         _lib.check(self.lib.cpg_gemm_create(ctypes.byref(cfg), ctypes.byref(prob), int(device),
                                             ctypes.byref(h)), "compile")
@@ -308,7 +372,8 @@ class _Plan:
         return s.value
 
     def run(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
-            scale_b=None, activation: int = 0, source=None, beta: float = 1.0) -> None:
+            scale_b=None, activation: int = 0, source=None, beta: float = 1.0,
+            group_offsets=None) -> None:
         import torch
         if bias is not None:
             if not (bias.dtype == torch.bfloat16 and bias.is_cuda and bias.numel() == self.n
@@ -344,9 +409,14 @@ class _Plan:
         epi = _lib.EpilogueC(float(alpha), None if bias is None else bias.data_ptr(), *scales,
                              float(beta), int(activation), src_ptr, int(ld_src), int(bs_src))
         st = _stream_handle(stream, c.device)
-        rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
-                                   b.data_ptr() if b.numel() else None, c.data_ptr(),
-                                   ctypes.byref(epi), st)
+        if self.grouped:
+            rc = self.lib.cpg_gemm_run_grouped(self.handle, a.data_ptr() if a.numel() else None,
+                                               b.data_ptr() if b.numel() else None, c.data_ptr(),
+                                               group_offsets.data_ptr(), ctypes.byref(epi), st)
+        else:
+            rc = self.lib.cpg_gemm_run(self.handle, a.data_ptr() if a.numel() else None,
+                                       b.data_ptr() if b.numel() else None, c.data_ptr(),
+                                       ctypes.byref(epi), st)
         _lib.check(rc, "gemm")
 
 
@@ -444,6 +514,12 @@ class GemmSM90:
                           gated=gated)
         self._compiled = compiled
         return compiled
+
+    def grouped(self, a, b, c, group_offsets, stream=None, **epilogue):
+        """Grouped GEMM (see ``CompiledGemm.grouped``)."""
+        if self._compiled is None:
+            self._compiled = CompiledGemm(self)
+        return self._compiled.grouped(a, b, c, group_offsets, stream, **epilogue)
 
     def __call__(self, a, b, c, stream=None, *, bias=None, alpha: float = 1.0, scale_a=None,
                  scale_b=None, split_k: int = 1, activation: Optional[str] = None, source=None,

@@ -122,6 +122,12 @@ typedef struct cpg_gemm_problem {
                             after batch b - 1 (multiples of 16 bytes; D's batches must not
                             overlap: batch_stride_d >= m * ldd).  Not with block scales. */
   int64_t batch_stride_a, batch_stride_b, batch_stride_d;
+  int32_t grouped;       /* 0, or 1: grouped GEMM (ragged groups, e.g. the experts of an MoE
+                            layer).  l is the number of groups G; A is [m, k] with the rows of
+                            every group one after the other, B is [G, n, k] (batch_stride_b
+                            between groups), D is [m, n]; the group boundaries are given per
+                            call to cpg_gemm_run_grouped.  Needs a persistent kernel; no split-K,
+                            no block scales, K > 0. */
 } cpg_gemm_problem;
 
 #define CPG_SPLIT_K_STREAM (-1)
@@ -167,6 +173,16 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
  * stream).  Replaces compiled_gemm(a, b, c, stream) (gemm_base.py:609).  epi may be NULL. */
 int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
                  void* stream);
+
+/* Grouped GEMM launch on a plan created with prob->grouped = 1: for every group g,
+ *   D[r] = epilogue(A[r] . B[g]^T) for the rows r in [group_offsets[g], group_offsets[g + 1]),
+ * with group_offsets a device array of G + 1 int32 (non-decreasing, within [0, m]; empty groups
+ * allowed); rows of D outside every group are not written.  A small kernel turns the offsets
+ * into the tile list on the device (no host synchronisation).  Offsets that break the rule make
+ * their groups empty and set status 0x200 (cpg_gemm_status).  No counterpart in the reference,
+ * whose kernel fixes the L mode at one (gemm_base.py:221). */
+int cpg_gemm_run_grouped(cpg_gemm* plan, const void* a, const void* b, void* d,
+                         const int32_t* group_offsets, const cpg_epilogue* epi, void* stream);
 
 int cpg_gemm_destroy(cpg_gemm* g);
 
