@@ -55,6 +55,11 @@ WORKLOADS = {
                 m_is_per_gpu=True, fp8="tensor"),
     "fp8_block": dict(m=16384, n=8192, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
                       m_is_per_gpu=True, fp8="block"),
+    # MoE expert FFN up-projection as one grouped GEMM: 8 experts of [W_gate; W_up]
+    # (2 x 14336 rows, K = 4096), 16384 routed token rows per GPU spread unevenly over the
+    # experts (seeded), fused SwiGLU; experts replicated, tokens per GPU (weak scaling).
+    "moe": dict(m=16384, n=14336, k=4096, a_scale=1.0, b_scale=0.02, bias=False,
+                m_is_per_gpu=True, fp8=None, gated=True, act="silu", groups=8),
     # Tall K: M = N = 2048, K = 131072 split over the GPUs (and inside each GPU); fp32 partials
     # reduced with one NCCL reduce-scatter, then cast to BF16 (strong scaling).
     "tallk": dict(m=2048, n=2048, k=131072, a_scale=1.0, b_scale=131072 ** -0.5, bias=False,
@@ -309,6 +314,8 @@ def metric_name(workload):
             "fp8": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, per-tensor scales)",
             "fp8_block": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, 1x128 / 128x128 block scales)",
             "tallk": "GEMM TFLOPS (BF16 2048x2048x131072 split-K over GPUs, NCCL reduce-scatter)",
+            "moe": "GEMM TFLOPS (BF16 grouped MoE up-projection, 8 experts x [2x14336, 4096], "
+                   "16384 token rows per GPU, fused SwiGLU)",
             }[workload]
 
 
@@ -390,6 +397,97 @@ def run_tallk(args, world, rank, local):
         }
         print(json.dumps(line), flush=True)
     del out
+
+
+# ------------------------------------------------------------------ GPU arm: grouped (MoE)
+def group_sizes(rows, groups, seed=0):
+    """Seeded uneven split of ``rows`` token rows over ``groups`` experts (router-like skew)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    p = torch.softmax(torch.randn(groups, generator=g) * 0.5, 0)
+    sizes = torch.floor(p * rows).long()
+    sizes[0] += rows - int(sizes.sum())
+    return [int(x) for x in sizes]
+
+
+def run_grouped(args, world, rank, local):
+    import torch
+    from cutedsl_pingpong_gemm_b200 import GemmSM90, RasterOrder
+
+    w = WORKLOADS[args.workload]
+    n, k, groups = w["n"], w["k"], w["groups"]
+    t = args.m or w["m"]
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    gated, act = bool(w.get("gated")), w.get("act")
+    b_rows = 2 * n if gated else n
+    gen_a = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gen_b = torch.Generator(device=dev).manual_seed(7)
+    a = (torch.randn(t, k, generator=gen_a, device=dev) * w["a_scale"]).to(torch.bfloat16)
+    b = (torch.randn(groups, b_rows, k, generator=gen_b, device=dev) * w["b_scale"]).to(
+        torch.bfloat16)
+    d = torch.empty(t, n, dtype=torch.bfloat16, device=dev)
+    sizes = group_sizes(t, groups, seed=11 + rank)
+    off = [0]
+    for sz in sizes:
+        off.append(off[-1] + sz)
+    offs = torch.tensor(off, dtype=torch.int32, device=dev)
+    cm = args.cluster_m
+    tile_n = 512 if gated else (args.tile_n or (512 if cm == 2 else 256))
+    stages = args.stages or {(512, 2): 4, (512, 1): 2}.get((tile_n, cm), 6 if cm == 2 else 4)
+    gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
+                    cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
+                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False,
+                    is_persistent=True)
+
+    def step():
+        gemm.grouped(a, b, d, offs, stream, activation=act, gated=gated)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step()
+        if i == 0:
+            sampler.start()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sampler.stop()
+    barrier(world)
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = reduce_max(ms_local, world)
+    flops_per_gpu = 2.0 * t * b_rows * k
+    value = flops_per_gpu * world / (ms * 1e-3) / 1e12
+    achieved = flops_per_gpu / (ms_local * 1e-3) / 1e12
+    peaks, peak_src = load_peaks()
+    if rank == 0:
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "rows_per_gpu": t, "n": n, "k": k,
+                       "groups": groups, "group_rows": sizes, "tile": [128, tile_n],
+                       "cluster": [cm, 1, 1], "ab_stage": stages, "activation": act,
+                       "gated": gated, "parallelism": f"tokens per GPU x{world}, experts replicated",
+                       "l2": "B is 1.9 GB; no flush"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                         "peak_source": f"{peak_src} bf16_tflops (cuBLAS burst)",
+                         "frac_sustained": achieved / peaks.get("bf16_tflops_sustained",
+                                                                peaks["bf16_tflops"]),
+                         "traffic": None, "algorithmic_flops_per_launch": flops_per_gpu,
+                         "kernel": "group_tile_prefix_kernel + cpg::gemm_sm100_kernel (grouped)"},
+            "clocks": sampler.summary(), "gpu_launches": 2 * args.steps * world, "e2e": None,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -627,6 +725,8 @@ def main():
     try:
         if WORKLOADS[args.workload].get("split") == "k":
             run_tallk(args, world, rank, local)
+        elif WORKLOADS[args.workload].get("groups"):
+            run_grouped(args, world, rank, local)
         else:
             run_cpg(args, world, rank, local)
     finally:
