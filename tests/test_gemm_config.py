@@ -82,3 +82,21 @@ def test_capi_validate_accepts_harness_config(lib):
     assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_OK
     cfg.cluster_k = 2  # tile_scheduler.py:51
     assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_ERR_INVALID_CONFIG
+
+
+def test_wave_split_k_choices():
+    """K ranges that fill whole waves of resident clusters (the automatic in-GPU split)."""
+    from cutedsl_pingpong_gemm_b200.gemm_base import wave_split_k
+    # 2048 x 2048 in 256 x 256 pair tiles (64 clusters of 74), K = 65536: 8 ranges fill 512 of
+    # 518 cluster slots; a quarter of the columns (16 clusters) takes 9.
+    assert wave_split_k(64, 1024, 74, min_fill=0.85) == 8
+    assert wave_split_k(16, 1024, 74, min_fill=0.85) == 9
+    # Decode-like M = 128, N = K = 8192 (64 tiles of 148 slots, 128 k-blocks): no split fills a
+    # wave well enough with >= 32 k-blocks per range, so the caller falls back to Stream-K.
+    assert wave_split_k(64, 128, 148) is None
+    for clusters, kblocks, slots in ((64, 1024, 74), (16, 1024, 74), (10, 4096, 148)):
+        s = wave_split_k(clusters, kblocks, slots, min_fill=0.85)
+        units = clusters * s
+        assert kblocks // s >= 32
+        assert units / (-(-units // slots) * slots) >= 0.85
+    assert wave_split_k(4, 40, 148) is None  # too few k-blocks to split
