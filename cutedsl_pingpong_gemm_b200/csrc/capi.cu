@@ -1016,9 +1016,21 @@ int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols
     const T* xx = static_cast<const T*>(x);
     if (per_tensor) {
       unsigned* amax = reinterpret_cast<unsigned*>(scales);
-      cpg::amax_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, amax);
-      cpg::quant_per_tensor_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, qq,
-                                                                       ldq, amax);
+      // Whole 16-byte vectors per row (x rows 16-byte aligned, q rows aligned to a vector's
+      // E4M3 bytes): the vectorised kernels; otherwise the element kernels.
+      constexpr int V = cpg::Vec16<T>::kElems;
+      const bool vec = cols % V == 0 && ldx % V == 0 && ldq % V == 0 &&
+                       (reinterpret_cast<uintptr_t>(xx) & 15u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(qq) & static_cast<uintptr_t>(V - 1)) == 0;
+      if (vec) {
+        cpg::amax_vec_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, amax);
+        cpg::quant_per_tensor_vec_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx,
+                                                                             qq, ldq, amax);
+      } else {
+        cpg::amax_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, amax);
+        cpg::quant_per_tensor_kernel<T><<<row_blocks, threads, 0, st>>>(xx, rows, cols, ldx, qq,
+                                                                         ldq, amax);
+      }
       cpg::finalize_scale_kernel<<<1, 1, 0, st>>>(amax);
     } else if (row_block) {
       const int64_t warps = rows * ((cols + 127) / 128);

@@ -14,11 +14,26 @@ def _bits(q):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(1, 16), (128, 256), (300, 1000), (1024, 4096)])
+@pytest.mark.parametrize("shape", [(1, 16), (128, 256), (300, 1000), (1024, 4096), (7, 1001),
+                                   (3, 6)])
 def test_per_tensor_bit_exact(shape, dtype):
+    """Whole 16-byte vectors per row take the vectorised kernels, the odd widths the element
+    kernels; both must give the oracle's bytes."""
     g = torch.Generator().manual_seed(sum(shape))
     x = (torch.randn(*shape, generator=g) * 3.0).to(dtype)
     q, s = quantize_e4m3(x.cuda())
+    qr, sr = gemm_ref.quantize_e4m3_per_tensor(x)
+    assert s.cpu().item() == sr.item()
+    assert torch.equal(_bits(q.cpu()), _bits(qr))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_per_tensor_unaligned_view(dtype):
+    """A column window whose rows start off a 16-byte boundary: element kernels."""
+    g = torch.Generator().manual_seed(99)
+    big = (torch.randn(64, 1040, generator=g) * 2).to(dtype)
+    x = big[:, 3:1027]
+    q, s = quantize_e4m3(big.cuda()[:, 3:1027])
     qr, sr = gemm_ref.quantize_e4m3_per_tensor(x)
     assert s.cpu().item() == sr.item()
     assert torch.equal(_bits(q.cpu()), _bits(qr))
