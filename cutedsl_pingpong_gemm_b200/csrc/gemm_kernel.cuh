@@ -1,25 +1,30 @@
-// Warp-specialised persistent BF16 GEMM for sm_100a:  D[M,N] = alpha * A[M,K] . B[N,K]^T (+ bias[N])
+// Warp-specialised persistent GEMM for sm_100a (BF16 or FP8 E4M3 operands, BF16 or FP32 D):
+//   D[M,N] = act(alpha * s_a * s_b * A[M,K] . B[N,K]^T + bias[N] + beta * C)
 //
 // Role of each warp (192 threads per CTA):
 //   warp 0     TMA producer: one lane streams A/B k-blocks into an `ab_stages`-deep ring of
 //              128B-swizzled shared-memory stages (full/empty mbarrier pairs).  This replaces the
 //              reference's producer warp (gemm_base.py:204-229, produce_mainloop :365-388).
-//   warp 1     MMA issuer: allocates TMEM, one lane issues tcgen05.mma (kind::f16, fp32
-//              accumulate) into one of two TMEM accumulators and commits stage releases and
-//              "accumulator full" signals.  Replaces the consumer warpgroups' wgmma mainloop
-//              (consume_mainloop, gemm_base.py:390-428).
+//   warp 1     MMA issuer: allocates TMEM, one lane issues tcgen05.mma (kind::f16 or
+//              kind::f8f6f4, fp32 accumulate) into a TMEM accumulator and commits stage releases
+//              and "accumulator full" signals.  Replaces the consumer warpgroups' wgmma mainloop
+//              (consume_mainloop, gemm_base.py:390-428).  Tiles up to 256 wide keep two
+//              accumulators, so the epilogue of tile i overlaps the mainloop of tile i+1; a
+//              512-wide tile (two N = 256 MMAs per k-step) fills TMEM with one.
 //   warps 2-5  epilogue: tcgen05.ld the accumulator (each warp owns a 32-lane TMEM quadrant),
-//              scale / add bias, round to BF16, write 128B-swizzled staging buffers and TMA-store
-//              them (epilogue, gemm_base.py:270-363).  Two TMEM accumulators let the epilogue of
-//              tile i overlap the mainloop of tile i+1.
+//              scale, add bias and beta * C, apply the activation (or the gated product of a
+//              gate / up accumulator pair), round, write 128B-swizzled staging buffers and
+//              TMA-store or TMA-reduce-add them (epilogue, gemm_base.py:270-363).
 //
 // CTA pairs (CtaGroup == 2, cluster (2,1)): both CTAs load their own 128 rows of A and their own
 // half of the B tile; the even CTA issues tcgen05.mma.cta_group::2 (M = 256) that reads both
 // CTAs' shared memory, and one tcgen05.commit with a two-CTA mask signals the same barrier in both
 // CTAs.  No TMA load uses cluster multicast.
 //
-// Tile order: every role walks the same sequence from the shared scheduler header, identical to
-// the reference's SimpleTileScheduler (tile_scheduler.py:94-183).
+// Tile order: every role walks the same sequence of segments (SegmentIter): the tiles of the
+// shared scheduler header, identical to the reference's SimpleTileScheduler
+// (tile_scheduler.py:94-183) with its L index carrying batches and split-K ranges; Stream-K
+// ranges of the (tile, k-block) space; or the tiles of a grouped GEMM's ragged groups.
 //
 // Every mbarrier wait is bounded (WaitCtx): on a timeout the kernel records an error code in the
 // status word, the other roles stop at their next wait, in-flight TMA loads and MMAs are drained
