@@ -546,16 +546,21 @@ def run_cpg(args, world, rank, local):
                     epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
                     is_persistent=True)
     compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
-    split_k = (args.split_k if args.split_k else compiled.auto_split_k(m, n, k)) if w.get("small_m") else 1
+    # The split is picked from the tile count (small M: K ranges or Stream-K; a partial last
+    # wave: data-parallel waves + Stream-K tail); fused epilogues and block scales run whole.
+    fused_epi = gated or act is not None or w["fp8"] == "block"
+    split_k = args.split_k if args.split_k else (1 if fused_epi else compiled.auto_split_k(m, n, k))
     compiled(a, b, d, stream, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k,
              activation=act, gated=gated)
     torch.cuda.synchronize()
-    if split_k != 1:
+    ws_path = split_k > 1 or split_k == -1  # FP32 workspace + cast kernel (BF16 D)
+    if ws_path:
         plan = compiled.plan_for(a, b, compiled._workspace(d), 0, split_k)
     else:
-        plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0, gated=gated)
+        plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0, split_k, gated=gated)
     info = plan.launch_info()
-    kernels_per_step = 2 if split_k != 1 else 1  # split-K / Stream-K add the cast kernel
+    # K ranges and Stream-K into a BF16 D add the cast kernel (the hybrid finishes in the GEMM).
+    kernels_per_step = 2 if ws_path else 1
 
     launches = [0]
 
@@ -713,6 +718,7 @@ def run_cpg(args, world, rank, local):
                        "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
                        "bias": bool(w["bias"]), "activation": act, "gated": gated,
+                       "split_k": split_k,
                        "cuda_graph": use_graph},
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -101,7 +101,7 @@ int encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const v
 }
 
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
-                          const cpg::GemmParams);
+                          const CUtensorMap, const cpg::GemmParams);
 
 struct Variant {
   int bn;
@@ -319,6 +319,14 @@ struct cpg_gemm {
   int32_t k_iters_per_split;
   int32_t splits;
   int32_t stream_k;
+  // Stream-K with in-kernel fixup (BF16 Stream-K, and the data-parallel + Stream-K hybrid):
+  // leading whole tiles, FP32 workspace tiles and k-block counts of the Stream-K tail.
+  int32_t fixup;
+  int32_t dp_tiles;
+  float* ws_dev;
+  int32_t* cnt_dev;
+  int64_t ws_bytes, cnt_bytes;
+  CUtensorMap tm_ws;
   int64_t batches;
   int64_t groups;            // grouped GEMM: number of groups (0: not grouped)
   int32_t group_n_clusters;  // cluster columns of every group
@@ -332,7 +340,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 9; }
+int cpg_abi_version(void) { return 10; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -450,17 +458,21 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                 cfg->tile_n, cta_group, prob->dtype_ab, prob->dtype_d);
   if (v.scale_mode == CPG_SCALE_BLOCK && cfg->reuse_ab)
     return fail(CPG_ERR_UNSUPPORTED, "reuse_ab is not implemented for block-scaled FP8");
-  if (prob->split_k < CPG_SPLIT_K_STREAM)
-    return fail(CPG_ERR_INVALID_SHAPE, "split_k must be >= 0, or CPG_SPLIT_K_STREAM");
-  if ((prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM) &&
+  if (prob->split_k < CPG_SPLIT_K_HYBRID)
+    return fail(CPG_ERR_INVALID_SHAPE,
+                "split_k must be >= 0, CPG_SPLIT_K_STREAM or CPG_SPLIT_K_HYBRID");
+  const bool sk_any = prob->split_k == CPG_SPLIT_K_STREAM || prob->split_k == CPG_SPLIT_K_HYBRID;
+  if (prob->split_k > 1 &&
       (prob->dtype_d != CPG_DTYPE_F32 || v.scale_mode != CPG_SCALE_TENSOR))
-    return fail(CPG_ERR_UNSUPPORTED, "split-K / Stream-K accumulate into an FP32 D (no block scales)");
-  if (prob->split_k == CPG_SPLIT_K_STREAM && !cfg->is_persistent)
+    return fail(CPG_ERR_UNSUPPORTED, "split-K ranges accumulate into an FP32 D (no block scales)");
+  if (sk_any && v.scale_mode != CPG_SCALE_TENSOR)
+    return fail(CPG_ERR_UNSUPPORTED, "Stream-K is not available with block scales");
+  if (sk_any && !cfg->is_persistent)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K needs a persistent kernel");
   if (prob->gated != 0 && prob->gated != 1)
     return fail(CPG_ERR_INVALID_CONFIG, "gated must be 0 or 1, got %d", prob->gated);
   if (prob->gated && (cfg->tile_n != 512 || v.scale_mode != CPG_SCALE_TENSOR ||
-                      prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM))
+                      prob->split_k > 1 || sk_any))
     return fail(CPG_ERR_UNSUPPORTED,
                 "gated GEMM needs tile_n 512 (256 gate + 256 up columns), no block scales and "
                 "no split-K");
@@ -475,8 +487,7 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
       return fail(CPG_ERR_INVALID_SHAPE, "a grouped GEMM needs 1 <= l (groups) <= 2^20");
     if (!cfg->is_persistent)
       return fail(CPG_ERR_UNSUPPORTED, "a grouped GEMM needs a persistent kernel");
-    if (prob->split_k > 1 || prob->split_k == CPG_SPLIT_K_STREAM ||
-        v.scale_mode != CPG_SCALE_TENSOR)
+    if (prob->split_k > 1 || sk_any || v.scale_mode != CPG_SCALE_TENSOR)
       return fail(CPG_ERR_UNSUPPORTED, "grouped GEMM: no split-K and no block scales");
     if (prob->k == 0) return fail(CPG_ERR_UNSUPPORTED, "grouped GEMM: K must be > 0");
     if ((prob->batch_stride_b * elem_bytes(prob->dtype_ab)) % 16 != 0 || prob->batch_stride_b < 0)
@@ -551,7 +562,11 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   // every split is non-empty.
   const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
   g->k_iters = static_cast<int32_t>((prob->k + bk - 1) / bk);
-  g->stream_k = prob->split_k == CPG_SPLIT_K_STREAM ? 1 : 0;
+  g->stream_k = sk_any ? 1 : 0;
+  // FP32 Stream-K adds straight into D (after a memset); BF16 Stream-K and the hybrid finish
+  // their split tiles in the kernel from an FP32 workspace.
+  g->fixup = (prob->split_k == CPG_SPLIT_K_HYBRID ||
+              (prob->split_k == CPG_SPLIT_K_STREAM && prob->dtype_d != CPG_DTYPE_F32)) ? 1 : 0;
   int32_t splits = prob->split_k > 1 ? prob->split_k : 1;
   if (splits > g->k_iters && g->k_iters > 0) splits = g->k_iters;
   g->k_iters_per_split = g->k_iters > 0 ? (g->k_iters + splits - 1) / splits : 0;
@@ -593,6 +608,21 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   g->cluster[0] = cfg->cluster_m;
   g->cluster[1] = cfg->cluster_n;
   g->cluster[2] = 1;
+  int64_t sk_tiles = 0;
+  if (g->fixup) {
+    // Hybrid: all full waves but the last are computed whole; the last full wave and the
+    // partial one go to Stream-K, so every cluster finishes with about the same work and each
+    // split tile has at most two or three contributors.
+    const int64_t total = cpg::sched_total_clusters(g->sched);
+    const int64_t waves_g = grid[2];
+    int64_t dp = 0;
+    if (prob->split_k == CPG_SPLIT_K_HYBRID) {
+      if (total % waves_g == 0) dp = total;
+      else if (total >= 2 * waves_g) dp = (total / waves_g - 1) * waves_g;
+    }
+    g->dp_tiles = static_cast<int32_t>(dp);
+    sk_tiles = total - dp;
+  }
 
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e != cudaSuccess) {
@@ -604,6 +634,30 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     cudaFree(g->status_dev);
     delete g;
     return cuda_fail(e, "cudaMemset(status word)");
+  }
+  if (sk_tiles > 0) {
+    // One FP32 workspace tile (128 rows x the tile's output columns) and four k-block counts
+    // (one per epilogue warp) per CTA of every Stream-K tile, zero between launches.
+    const int64_t ctas = int64_t(cfg->cluster_m) * cfg->cluster_n;
+    const int64_t ws_rows = sk_tiles * ctas * 128;
+    const int64_t ws_cols = cfg->tile_n;
+    g->ws_bytes = ws_rows * ws_cols * 4;
+    g->cnt_bytes = sk_tiles * ctas * 4 * 4;
+    e = cudaMalloc(&g->ws_dev, g->ws_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&g->cnt_dev, g->cnt_bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->ws_dev, 0, g->ws_bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->cnt_dev, 0, g->cnt_bytes);
+    int rc2 = e == cudaSuccess
+                  ? encode_tiled(&g->tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g->ws_dev, ws_rows,
+                                 ws_cols, ws_cols, 32, cpg::kRowBytes / 4)
+                  : cuda_fail(e, "Stream-K workspace");
+    if (rc2 != CPG_OK) {
+      if (g->ws_dev) cudaFree(g->ws_dev);
+      if (g->cnt_dev) cudaFree(g->cnt_dev);
+      cudaFree(g->status_dev);
+      delete g;
+      return rc2;
+    }
   }
   if (groups > 0) {
     e = cudaMalloc(&g->tile_prefix_dev, sizeof(int32_t) * (groups + 1));
@@ -619,10 +673,13 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
 
 int cpg_gemm_destroy(cpg_gemm* g) {
   if (g == nullptr) return CPG_OK;
-  if (g->status_dev != nullptr || g->tile_prefix_dev != nullptr) {
+  if (g->status_dev != nullptr || g->tile_prefix_dev != nullptr || g->ws_dev != nullptr ||
+      g->cnt_dev != nullptr) {
     DeviceGuard guard(g->device);
     if (g->status_dev != nullptr) cudaFree(g->status_dev);
     if (g->tile_prefix_dev != nullptr) cudaFree(g->tile_prefix_dev);
+    if (g->ws_dev != nullptr) cudaFree(g->ws_dev);
+    if (g->cnt_dev != nullptr) cudaFree(g->cnt_dev);
   }
   delete g;
   return CPG_OK;
@@ -683,6 +740,9 @@ int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
   *status = s;
   if (s != 0) {
     cudaMemset(g->status_dev, 0, sizeof(int32_t));
+    // A launch that stopped early may have left Stream-K workspace tiles and counts behind.
+    if (g->ws_dev != nullptr) cudaMemset(g->ws_dev, 0, g->ws_bytes);
+    if (g->cnt_dev != nullptr) cudaMemset(g->cnt_dev, 0, g->cnt_bytes);
     if (s == kStatusBadGroups)
       return fail(CPG_ERR_INVALID_SHAPE, "group offsets not non-decreasing within [0, m]");
     return fail(CPG_ERR_DEVICE_TIMEOUT, "kernel wait timed out at site %d", s & 0xFF);
@@ -808,8 +868,13 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
   p.k = static_cast<int32_t>(pr.k);
   p.k_iters = g->k_iters;
   p.k_iters_per_split = g->k_iters_per_split;
-  p.reduce_add = (g->splits > 1 || g->stream_k) ? 1 : 0;
+  p.reduce_add = (g->splits > 1 || (g->stream_k && !g->fixup)) ? 1 : 0;
   p.stream_k = g->stream_k;
+  p.fixup = g->fixup;
+  p.dp_tiles = g->dp_tiles;
+  p.fixup_count = g->cnt_dev;
+  p.fixup_ws = g->ws_dev;
+  p.ws_cols = g->cfg.tile_n;
   p.ab_stages = g->cfg.ab_stage;
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
@@ -854,7 +919,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     if (e != cudaSuccess) return cuda_fail(e, "group tile prefix launch");
   }
 
-  if (g->splits > 1 || g->stream_k) {
+  if (g->splits > 1 || (g->stream_k && !g->fixup)) {
     // The splits / Stream-K segments add their partial sums into D.
     for (int64_t bt = 0; bt < g->batches; ++bt) {
       cudaError_t e = cudaMemset2DAsync(static_cast<char*>(d) + bt * pr.batch_stride_d * ed,
@@ -877,8 +942,9 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p, &bs};
-  cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, args);
+  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &g->tm_ws, &p};
+  void* block_args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p, &bs};
+  cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, block ? block_args : args);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM kernel launch");
   return CPG_OK;
 }
@@ -1247,8 +1313,9 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  cpg::BlockScales unused{nullptr, nullptr};
-  void* args[] = {&tm_a, &tm_b, &tm_w, &p, &unused};
+  CUtensorMap tm_unused;  // the Stream-K workspace map: no Stream-K here
+  std::memset(&tm_unused, 0, sizeof(tm_unused));
+  void* args[] = {&tm_a, &tm_b, &tm_w, &tm_unused, &p};
   e = cudaLaunchKernelExC(&lc, v.fn, args);
   if (e != cudaSuccess) return cuda_fail(e, "split-K GEMM launch");
   cpg::cast_f32_bf16_kernel<<<cast_grid(prob->m, prob->n), 256, 0, st>>>(

@@ -131,6 +131,17 @@ struct GemmParams {
   int32_t group_n_clusters;       // cluster columns of every group
   void* d;                        // D itself: rows at a group boundary are stored per thread
   int64_t ldd;
+  // Stream-K with in-kernel fixup (stream_k != 0 and fixup != 0): the first dp_tiles cluster
+  // tiles are computed whole (data-parallel waves, persistent stride), the k-blocks of the
+  // others are shared evenly by the clusters.  A segment that covers only part of a tile adds
+  // alpha * acc into that CTA's FP32 workspace tile (tm_ws, rows (cid - dp_tiles) * ctas + rank)
+  // and counts its k-blocks in fixup_count; the segment that completes the count rounds the
+  // tile (+ bias) into D and clears the workspace tile and its count for the next launch.
+  int32_t fixup;
+  int32_t dp_tiles;
+  int32_t* fixup_count;           // [sk tiles * CTAs per cluster], zero between launches
+  float* fixup_ws;                // FP32 workspace the fixup reads (and clears)
+  int32_t ws_cols;                // row length of a workspace tile (the tile's output columns)
 };
 
 // The grouped mode of the segment iterator (num_groups == 0: the scheduler's tiles).
@@ -301,6 +312,7 @@ struct SegmentIter {
   int32_t k_iters, kps, stream, index, splits;
   GroupInfo gi;
   int32_t group_total;  // cluster tiles of all groups (grouped mode)
+  int32_t dp_tiles;     // Stream-K: leading cluster tiles computed whole (persistent stride)
 
   __device__ __forceinline__ bool next(const SchedParams& sp, Segment& s) {
     if (gi.num_groups > 0) {
@@ -332,6 +344,20 @@ struct SegmentIter {
     }
     s.row_base = 0;
     s.row_end = 0x7fffffff;
+    if (stream && it.cid < dp_tiles) {
+      // Data-parallel waves before the Stream-K tail: whole tiles in the persistent order.
+      s.cid = it.cid;
+      s.kb0 = 0;
+      s.kb1 = k_iters;
+      int32_t l, cid_in_problem;
+      fast_divmod(sp.dm_clusters_per_problem, s.cid, l, cid_in_problem);
+      s.batch = l;
+      s.ab_batch = l;
+      work_tile_coords(sp, s.cid, s.pid_m, s.pid_n);
+      it.cid += it.stride;
+      s.index = index++;
+      return true;
+    }
     if (stream) {
       if (pos >= end) return false;
       const int64_t tile = pos / k_iters;
@@ -369,10 +395,12 @@ __device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, 
                                                          int32_t kps, int32_t stream_k,
                                                          int32_t splits,
                                                          GroupInfo gi = GroupInfo{0, nullptr,
-                                                                                  nullptr, 1}) {
+                                                                                  nullptr, 1},
+                                                         int32_t dp_tiles = 0) {
   SegmentIter si;
   si.it = make_work_iter(sp);
   si.gi = gi;
+  si.dp_tiles = stream_k ? dp_tiles : 0;
   si.group_total = gi.num_groups > 0 ? gi.prefix[gi.num_groups] : 0;
   si.k_iters = k_iters;
   si.kps = kps;
@@ -381,10 +409,11 @@ __device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, 
   si.index = 0;
   si.pos = si.end = 0;
   if (stream_k) {
-    const int64_t total = static_cast<int64_t>(sched_total_clusters(sp)) * k_iters;
+    const int64_t base = static_cast<int64_t>(si.dp_tiles) * k_iters;
+    const int64_t total = static_cast<int64_t>(sched_total_clusters(sp)) * k_iters - base;
     const int64_t z = blockIdx.z, g = gridDim.z;
-    si.pos = total * z / g;
-    si.end = total * (z + 1) / g;
+    si.pos = base + total * z / g;
+    si.end = base + total * (z + 1) / g;
   }
   return si;
 }
@@ -500,7 +529,8 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               const ptx::WaitCtx& ctx, int32_t l2_a = 0,
                                               int32_t l2_b = 0, int32_t stream_k = 0,
                                               int32_t b_slot_rows = 0, int32_t splits = 1,
-                                              GroupInfo gi = GroupInfo{0, nullptr, nullptr, 1}) {
+                                              GroupInfo gi = GroupInfo{0, nullptr, nullptr, 1},
+                                              int32_t dp_tiles = 0) {
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
@@ -512,7 +542,8 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t phase = 0;
   uint32_t fills = 0;
   bool ok = true;
-  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits, gi);
+  SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits, gi,
+                                     dp_tiles);
   Segment sg;
   while (ok && si.next(sp, sg)) {
     const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
@@ -588,7 +619,8 @@ template <int BN, int CtaGroup, typename AB, typename OutT>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b,
-                      const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tm_d,
+                      const __grid_constant__ CUtensorMap tm_ws, const GemmParams p) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using L = GemmSmem<BN, CtaGroup>;
   using OT = OperandTraits<AB>;
@@ -661,7 +693,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
           leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0,
-          p.num_splits, group_info(p));
+          p.num_splits, group_info(p), p.dp_tiles);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -673,7 +705,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k,
-                                         p.num_splits, group_info(p));
+                                         p.num_splits, group_info(p), p.dp_tiles);
       Segment sg;
       while (ok && si.next(sp, sg)) {
         const int kb0 = sg.kb0, kb1 = sg.kb1;
@@ -769,12 +801,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     };
     SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k,
-                                       p.num_splits, group_info(p));
+                                       p.num_splits, group_info(p), p.dp_tiles);
     Segment sg;
+    const int32_t cluster_ctas = sp.cluster_m * sp.cluster_n;
+    const int32_t cta_in_cluster = static_cast<int32_t>(ptx::cluster_ctaid_x()) +
+                                   static_cast<int32_t>(ptx::cluster_ctaid_y()) * sp.cluster_m;
     while (si.next(sp, sg)) {
       const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
-      // Split-K / Stream-K: only the segment holding a tile's first k-block adds the bias.
+      // Split-K / Stream-K into D: only the segment holding a tile's first k-block adds the bias.
       const bool add_bias = has_bias && sg.kb0 == 0;
+      // Stream-K with fixup: a segment with part of a tile's k-blocks adds into the workspace.
+      const bool partial = p.fixup != 0 && (sg.kb0 != 0 || sg.kb1 != p.k_iters);
       bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -796,6 +833,73 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // 256 output columns.
       const int out_cols = gated ? BN / 2 : BN;
       const int n_chunks = out_cols / kStoreCols;
+      // This warp's 32 workspace rows (the CTA tile's workspace tile; partial segments only).
+      const int32_t ws_tile = partial ? (sg.cid - si.dp_tiles) * cluster_ctas + cta_in_cluster : 0;
+      const int32_t ws_row = ws_tile * kBM + static_cast<int32_t>(row_in_tile);
+
+      // Stage 32 rows x 128 bytes of this warp's output (thread = row) in the next staging
+      // buffer; returns the buffer's shared-memory address.
+      auto stage = [&](const uint32_t (&words)[32]) -> uint32_t {
+        const int buf = epi_idx % p.epi_stages;
+        const uint32_t sbuf =
+            epi_base + static_cast<uint32_t>((ew * p.epi_stages + buf) * kEpiBufBytes);
+        if (lane == 0) epi_wait_buffer(p.epi_stages);
+        __syncwarp();
+        const uint32_t row_addr = sbuf + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t chunk = static_cast<uint32_t>(j) ^ (lane & 7u);
+          ptx::st_shared_v4(row_addr + (chunk << 4), words[4 * j], words[4 * j + 1],
+                            words[4 * j + 2], words[4 * j + 3]);
+        }
+        ptx::fence_proxy_async_shared();
+        __syncwarp();
+        ++epi_idx;
+        return sbuf;
+      };
+      // Round x (kStoreCols columns of this thread's row, from column col0) to D's type and
+      // store it.
+      auto store_chunk = [&](const float (&x)[kStoreCols], int32_t col0) {
+        uint32_t packed[32];  // 128 bytes of this thread's output row
+        if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) packed[i] = ptx::pack_bf16x2(x[2 * i], x[2 * i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) packed[i] = __float_as_uint(x[i]);
+        }
+        const uint32_t sbuf = stage(packed);
+        // The TMA box covers this warp's 32 rows and is clipped at D's last row; a grouped
+        // tile whose group ends inside the box (before D ends) would write the next group's
+        // rows with it, so there each thread stores its own row if it is in the group.
+        // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
+        const bool box = g_row + 32 <= row_end || (g_row < row_end && row_end == p.m);
+        if (!box && g_row < row_end && col0 < p.n)
+          store_row_chunk<OutT>(p, my_row, row_end, col0, packed);
+        if (lane == 0) {
+          if (box && col0 < p.n) {
+            if (p.reduce_add) {
+              ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
+            } else {
+              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
+            }
+          }
+          ptx::bulk_commit_group();
+        }
+        __syncwarp();
+      };
+      auto add_bias_row = [&](float (&x)[kStoreCols], int32_t col0) {
+        // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
+        // they are broadcast across the warp with shuffles.
+#pragma unroll
+        for (int h = 0; h < kStoreCols / 32; ++h) {
+          const int32_t n = col0 + 32 * h + static_cast<int32_t>(lane);
+          const float bl = (n < p.n) ? __bfloat162float(p.bias[n]) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) x[32 * h + j] += __shfl_sync(0xffffffffu, bl, j);
+        }
+      };
+
 #pragma unroll 1
       for (int c = 0; c < n_chunks; ++c) {
         const int32_t col0 = pid_n * out_cols + c * kStoreCols;
@@ -834,60 +938,66 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             for (int j = 0; j < 32; ++j) x[32 * h + j] = gv[j] * (__uint_as_float(vu[j]) * alpha);
           }
         }
-        if (add_bias) {
-          // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
-          // they are broadcast across the warp with shuffles.
+        if (partial) {
+          // Add alpha * acc into the workspace, 32 FP32 columns (128 bytes) per TMA reduce.
 #pragma unroll
-          for (int h = 0; h < kStoreCols / 32; ++h) {
-            const int32_t n = col0 + 32 * h + static_cast<int32_t>(lane);
-            const float bl = (n < p.n) ? __bfloat162float(p.bias[n]) : 0.f;
+          for (int sub = 0; sub < kStoreCols / 32; ++sub) {
+            uint32_t words[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) x[32 * h + j] += __shfl_sync(0xffffffffu, bl, j);
+            for (int i = 0; i < 32; ++i) words[i] = __float_as_uint(x[32 * sub + i]);
+            const uint32_t sbuf = stage(words);
+            if (lane == 0) {
+              ptx::tma_reduce_add_3d(&tm_ws, sbuf, c * kStoreCols + 32 * sub, ws_row, 0);
+              ptx::bulk_commit_group();
+            }
+            __syncwarp();
           }
+          continue;
         }
+        if (add_bias) add_bias_row(x, col0);
         if (has_src) add_row_chunk<OutT>(p.beta, cs, x);
         if (!gated) act_inplace(p.act, x);
-        uint32_t packed[32];  // 128 bytes of this thread's output row
-        if constexpr (sizeof(OutT) == 2) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) packed[i] = ptx::pack_bf16x2(x[2 * i], x[2 * i + 1]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) packed[i] = __float_as_uint(x[i]);
-        }
-        const int buf = epi_idx % p.epi_stages;
-        const uint32_t sbuf =
-            epi_base + static_cast<uint32_t>((ew * p.epi_stages + buf) * kEpiBufBytes);
-        if (lane == 0) epi_wait_buffer(p.epi_stages);
-        __syncwarp();
-        const uint32_t row_addr = sbuf + lane * 128u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t chunk = static_cast<uint32_t>(j) ^ (lane & 7u);
-          ptx::st_shared_v4(row_addr + (chunk << 4), packed[4 * j], packed[4 * j + 1],
-                            packed[4 * j + 2], packed[4 * j + 3]);
-        }
-        ptx::fence_proxy_async_shared();
-        __syncwarp();
-        // The TMA box covers this warp's 32 rows and is clipped at D's last row; a grouped
-        // tile whose group ends inside the box (before D ends) would write the next group's
-        // rows with it, so there each thread stores its own row if it is in the group.
-        // Boxes wholly outside D (the odd CTA of a pair past the last row tile) store nothing.
-        const bool box = g_row + 32 <= row_end || (g_row < row_end && row_end == p.m);
-        if (!box && g_row < row_end && col0 < p.n)
-          store_row_chunk<OutT>(p, my_row, row_end, col0, packed);
+        store_chunk(x, col0);
+      }
+      if (partial) {
+        // Count this segment's k-blocks for its 32 rows; the warp that completes the count owns
+        // every other segment's sum (their reduces completed before their counts were added).
+        const int32_t cnt_idx = ws_tile * 4 + static_cast<int32_t>(ew);
+        const int32_t mine = sg.kb1 - sg.kb0;
+        int32_t last = 0;
         if (lane == 0) {
-          if (box && col0 < p.n) {
-            if (p.reduce_add) {
-              ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
-            } else {
-              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
-            }
-          }
-          ptx::bulk_commit_group();
+          ptx::bulk_wait_group<0>();
+          ptx::fence_proxy_async_global();
+          __threadfence();
+          const int32_t before = atomicAdd(p.fixup_count + cnt_idx, mine);
+          last = before + mine == p.k_iters ? 1 : 0;
+          if (last) __threadfence();
         }
-        __syncwarp();
-        ++epi_idx;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          float* wrow = p.fixup_ws + static_cast<int64_t>(ws_row + static_cast<int32_t>(lane)) *
+                                         p.ws_cols;
+#pragma unroll 1
+          for (int c = 0; c < n_chunks; ++c) {
+            const int32_t col0 = pid_n * out_cols + c * kStoreCols;
+            float x[kStoreCols];
+            float* src = wrow + c * kStoreCols;
+#pragma unroll
+            for (int q = 0; q < kStoreCols / 4; ++q) {
+              const uint4 v = ptx::ld_global_cg_v4(src + 4 * q);
+              x[4 * q] = __uint_as_float(v.x);
+              x[4 * q + 1] = __uint_as_float(v.y);
+              x[4 * q + 2] = __uint_as_float(v.z);
+              x[4 * q + 3] = __uint_as_float(v.w);
+            }
+            // Clear the workspace tile for the next launch.
+#pragma unroll
+            for (int q = 0; q < kStoreCols / 4; ++q) ptx::st_global_v4(src + 4 * q, 0u, 0u, 0u, 0u);
+            if (has_bias) add_bias_row(x, col0);
+            store_chunk(x, col0);
+          }
+          if (lane == 0) p.fixup_count[cnt_idx] = 0;
+        }
       }
       if (++acc == kAccStages) {
         acc = 0;

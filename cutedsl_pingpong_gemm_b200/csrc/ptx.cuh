@@ -456,6 +456,22 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void* ptr) {
   return r;
 }
 
+// 16-byte global load cached in L2 only (data other SMs wrote during this kernel).
+__device__ __forceinline__ uint4 ld_global_cg_v4(const void* ptr) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(ptr)
+               : "memory");
+  return r;
+}
+
+// Orders this thread's completed async-proxy (TMA) global writes before its later generic
+// accesses, e.g. the release of a flag other CTAs acquire.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // 16-byte global store (the address must be 16-byte aligned).
 __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {

@@ -110,7 +110,10 @@ typedef struct cpg_gemm_problem {
                             dimension, and the ranges add their FP32 partial sums into D
                             (dtype_d must be CPG_DTYPE_F32; D is cleared by cpg_gemm_run);
                             CPG_SPLIT_K_STREAM: Stream-K, every resident cluster takes an equal
-                            share of all (tile, k-block) pairs and adds into FP32 D */
+                            share of all (tile, k-block) pairs; with FP32 D the shares add into
+                            D, with BF16 D the last contributor of each tile finishes it from
+                            an FP32 workspace the plan owns (no memset, no cast);
+                            CPG_SPLIT_K_HYBRID: see below.  Activations, C and gated need 0/1 */
   int32_t gated;         /* 0, or 1: gated FFN (e.g. SwiGLU).  B holds [W_gate; W_up] as 2N rows
                             of K (ldb its row stride), D is M x N and
                             D[:, n] = act(alpha s_a s_b A . W_gate[n]) * alpha s_a s_b A . W_up[n];
@@ -131,6 +134,11 @@ typedef struct cpg_gemm_problem {
 } cpg_gemm_problem;
 
 #define CPG_SPLIT_K_STREAM (-1)
+/* Data-parallel waves + Stream-K tail: the tiles of all full waves but the last are computed
+ * whole; the k-blocks of the remaining tiles are shared evenly by the resident clusters, and
+ * the last contributor of a split tile finishes it (bias, rounding, store) from an FP32
+ * workspace the plan owns.  For problems whose tiles leave the last wave partly idle. */
+#define CPG_SPLIT_K_HYBRID (-2)
 
 /* Per-call epilogue options:
  *   D = act(alpha * s_a * s_b * (A . B^T) + bias + beta * C), rounded to D's type.
