@@ -91,6 +91,9 @@ def parse_args():
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each timed step from a CUDA graph captured through the public "
                          "API (auto: for the launch-bound small-M workload)")
+    ap.add_argument("--scheduler", choices=["static", "dynamic"], default="static",
+                    help="tile schedule: the reference's static persistent schedule, or dynamic "
+                         "(cluster launch control; not with block-scaled FP8)")
     ap.add_argument("--activation", default=None,
                     choices=["relu", "silu", "gelu", "gelu_tanh"],
                     help="fused epilogue activation for the GEMM workloads")
@@ -343,7 +346,8 @@ def run_tallk(args, world, rank, local):
     stages = args.stages or (6 if cm == 2 else 4)
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
-                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True)
+                    epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True,
+                    dynamic_scheduler=args.scheduler == "dynamic")
     chunks = max(1, args.chunks)
     # The in-GPU split of each (chunk's) GEMM is picked from its tile count (auto_split_k).
     sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=0, chunks=chunks)
@@ -387,7 +391,7 @@ def run_tallk(args, world, rank, local):
             "data": "synthetic",
             "config": {"workload": args.workload, "m": m, "n": n, "k": k,
                        "parallelism": f"split-K x{world} (NCCL reduce-scatter), auto in-GPU split",
-                       "rs_chunks": chunks,
+                       "rs_chunks": chunks, "scheduler": args.scheduler,
                        "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
                        "rows_per_rank": s1 - s0, "l2": "inputs 512 MiB per rank at 1 GPU; no flush"},
             "roofline": {"bound": "tensor", "achieved": total_flops / world / (ms_local * 1e-3) / 1e12,
@@ -441,7 +445,7 @@ def run_grouped(args, world, rank, local):
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False,
-                    is_persistent=True)
+                    is_persistent=True, dynamic_scheduler=args.scheduler == "dynamic")
 
     def step():
         gemm.grouped(a, b, d, offs, stream, activation=act, gated=gated)
@@ -478,7 +482,8 @@ def run_grouped(args, world, rank, local):
             "config": {"workload": args.workload, "rows_per_gpu": t, "n": n, "k": k,
                        "groups": groups, "group_rows": sizes, "tile": [128, tile_n],
                        "cluster": [cm, 1, 1], "ab_stage": stages, "activation": act,
-                       "gated": gated, "parallelism": f"tokens per GPU x{world}, experts replicated",
+                       "gated": gated, "scheduler": args.scheduler,
+                       "parallelism": f"tokens per GPU x{world}, experts replicated",
                        "l2": "B is 1.9 GB; no flush"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
@@ -544,7 +549,8 @@ def run_cpg(args, world, rank, local):
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
-                    is_persistent=True)
+                    is_persistent=True,
+                    dynamic_scheduler=args.scheduler == "dynamic" and w["fp8"] != "block")
     compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
     # The split is picked from the tile count (small M: K ranges or Stream-K; a partial last
     # wave: data-parallel waves + Stream-K tail); fused epilogues and block scales run whole.
@@ -719,6 +725,7 @@ def run_cpg(args, world, rank, local):
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
                        "bias": bool(w["bias"]), "activation": act, "gated": gated,
                        "split_k": split_k,
+                       "scheduler": gemm.dynamic_scheduler and "dynamic" or "static",
                        "cuda_graph": use_graph},
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -41,7 +41,7 @@ CPG_ACT_GELU_TANH = 4
 ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
                "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
 
-ABI_VERSION = 10
+ABI_VERSION = 11
 
 
 class CpgError(RuntimeError):
@@ -82,6 +82,7 @@ class GemmConfigC(ctypes.Structure):
         ("reuse_ab", ctypes.c_int32), ("is_persistent", ctypes.c_int32),
         ("gemm_n_prologue", ctypes.c_int32),
         ("group_size", ctypes.c_int32),
+        ("dynamic_scheduler", ctypes.c_int32),
     ]
 
 

@@ -340,7 +340,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 10; }
+int cpg_abi_version(void) { return 11; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -390,6 +390,12 @@ int cpg_config_validate(const cpg_gemm_config* c) {
     return fail(CPG_ERR_INVALID_CONFIG, "tile, cluster, stage and group sizes must be positive");
   if (c->raster_order != CPG_RASTER_ALONG_M && c->raster_order != CPG_RASTER_ALONG_N)
     return fail(CPG_ERR_INVALID_CONFIG, "raster_order must be 0 (AlongM) or 1 (AlongN)");
+  if (c->dynamic_scheduler != 0 && c->dynamic_scheduler != 1)
+    return fail(CPG_ERR_INVALID_CONFIG, "dynamic_scheduler must be 0 or 1");
+  if (c->dynamic_scheduler && c->reuse_ab)
+    return fail(CPG_ERR_INVALID_CONFIG,
+                "the dynamic scheduler runs several tiles per CTA and can't reuse AB for the "
+                "epilogue");
   return CPG_OK;
 }
 
@@ -467,6 +473,9 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return fail(CPG_ERR_UNSUPPORTED, "split-K ranges accumulate into an FP32 D (no block scales)");
   if (sk_any && v.scale_mode != CPG_SCALE_TENSOR)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K is not available with block scales");
+  if (cfg->dynamic_scheduler && (sk_any || v.scale_mode != CPG_SCALE_TENSOR))
+    return fail(CPG_ERR_UNSUPPORTED,
+                "the dynamic scheduler is not available with Stream-K or block scales");
   if (sk_any && !cfg->is_persistent)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K needs a persistent kernel");
   if (prob->gated != 0 && prob->gated != 1)
@@ -603,6 +612,19 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     }
     g->group_n_clusters = static_cast<int32_t>(ncol);
     grid[2] = static_cast<int32_t>(bound < mac ? (bound > 0 ? bound : 1) : mac);
+  }
+  if (cfg->dynamic_scheduler) {
+    // One cluster per cluster tile (the grouped GEMM's bound), along x.
+    const int64_t tiles = groups > 0 ? (((prob->m + 128 * cfg->cluster_m - 1) /
+                                         (128 * cfg->cluster_m)) + groups) * g->group_n_clusters
+                                     : int64_t(cpg::sched_total_clusters(g->sched));
+    if (tiles * cfg->cluster_m > (int64_t(1) << 31) - 1) {
+      delete g;
+      return fail(CPG_ERR_INVALID_SHAPE, "dynamic scheduler: more than 2^31 - 1 CTAs along x");
+    }
+    grid[0] = static_cast<int32_t>((tiles > 0 ? tiles : 1) * cfg->cluster_m);
+    grid[1] = cfg->cluster_n;
+    grid[2] = 1;
   }
   for (int i = 0; i < 3; ++i) g->grid[i] = grid[i];
   g->cluster[0] = cfg->cluster_m;
@@ -878,6 +900,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
   p.ab_stages = g->cfg.ab_stage;
   p.epi_stages = g->cfg.epi_stage;
   p.reuse_ab = g->cfg.reuse_ab;
+  p.dynamic = g->cfg.dynamic_scheduler;
   p.alpha = alpha;
   const bool block = g->v.scale_mode == CPG_SCALE_BLOCK;
   cpg::BlockScales bs{nullptr, nullptr};
@@ -1101,12 +1124,35 @@ int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols
     } else if (row_block) {
       const int64_t warps = rows * ((cols + 127) / 128);
       const int64_t blocks = (warps * 32 + threads - 1) / threads;
-      cpg::quant_row_block_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
-          xx, rows, cols, ldx, qq, ldq, scales);
+      // 16-byte loads of x and V-byte stores of q: row starts aligned to V elements of both.
+      constexpr int V = cpg::Vec16<T>::kElems;
+      const bool vec = ldx % V == 0 && ldq % V == 0 &&
+                       (reinterpret_cast<uintptr_t>(xx) & 15u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(qq) & static_cast<uintptr_t>(V - 1)) == 0;
+      if (vec) {
+        constexpr int kPerWarp = cpg::row_blocks_per_warp<T>();
+        const int64_t groups = (((cols + 127) / 128) + kPerWarp - 1) / kPerWarp;
+        const int64_t vblocks = (rows * groups * 32 + threads - 1) / threads;
+        cpg::quant_row_block_vec_kernel<T><<<static_cast<unsigned>(vblocks), threads, 0, st>>>(
+            xx, rows, cols, ldx, qq, ldq, scales);
+      } else {
+        cpg::quant_row_block_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+            xx, rows, cols, ldx, qq, ldq, scales);
+      }
     } else {
       const int64_t blocks = ((rows + 127) / 128) * ((cols + 127) / 128);
-      cpg::quant_tile_block_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-          xx, rows, cols, ldx, qq, ldq, scales);
+      constexpr int V = cpg::Vec16<T>::kElems;
+      const bool vec = ldx % V == 0 && ldq % V == 0 &&
+                       (reinterpret_cast<uintptr_t>(xx) & 15u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(qq) & static_cast<uintptr_t>(V - 1)) == 0;
+      if (vec) {
+        cpg::quant_tile_block_vec_kernel<T>
+            <<<static_cast<unsigned>(blocks), cpg::kTileBlockThreads, 0, st>>>(
+            xx, rows, cols, ldx, qq, ldq, scales);
+      } else {
+        cpg::quant_tile_block_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+            xx, rows, cols, ldx, qq, ldq, scales);
+      }
     }
   };
   if (dtype_x == CPG_DTYPE_BF16) {
@@ -1177,6 +1223,8 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   if (cfg == nullptr || prob == nullptr) return fail(CPG_ERR_NULL, "cfg and prob must be non-NULL");
   int rc = cpg_config_validate(cfg);
   if (rc != CPG_OK) return rc;
+  if (cfg->dynamic_scheduler)
+    return fail(CPG_ERR_UNSUPPORTED, "the dynamic scheduler is not available on this entry point");
   if (cfg->tile_m != 128 ||
       (cfg->tile_n != 64 && cfg->tile_n != 128 && cfg->tile_n != 256 && cfg->tile_n != 512) ||
       cfg->cluster_m > 2 || cfg->cluster_n > 2 || cfg->ab_stage > cpg::kMaxStages ||

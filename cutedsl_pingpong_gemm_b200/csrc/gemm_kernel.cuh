@@ -81,6 +81,8 @@ struct OutputTraits<float> {
 constexpr int kMaxStages = 12;
 constexpr int kMaxEpiStages = 4;
 constexpr int kMinSmemForOneCtaPerSm = 116 * 1024;
+constexpr int kWorkSlots = 4;    // dynamic scheduling: entries of the work ring
+constexpr int kDynBytes = 16 * kWorkSlots + 16 + 16 + 4 * kWorkSlots;  // DynLayout
 
 // Wait-site identifiers recorded in the status word on a timeout.
 enum WaitSite : int32_t {
@@ -90,6 +92,9 @@ enum WaitSite : int32_t {
   kSiteEpiTmemFull = 4,
   kSiteDrainLoads = 5,
   kSiteDrainMma = 6,
+  kSiteWorkFull = 7,    // dynamic scheduling: waiting for the next work entry
+  kSiteWorkEmpty = 8,   // dynamic scheduling: waiting for a free work entry
+  kSiteClc = 9,         // dynamic scheduling: waiting for a cluster launch control response
 };
 
 struct GemmParams {
@@ -142,6 +147,9 @@ struct GemmParams {
   int32_t* fixup_count;           // [sk tiles * CTAs per cluster], zero between launches
   float* fixup_ws;                // FP32 workspace the fixup reads (and clears)
   int32_t ws_cols;                // row length of a workspace tile (the tile's output columns)
+  // Dynamic scheduling (cluster launch control, WorkScheduler): the grid holds one cluster per
+  // cluster tile along x and running clusters take over clusters that have not started.
+  int32_t dynamic;
 };
 
 // The grouped mode of the segment iterator (num_groups == 0: the scheduler's tiles).
@@ -230,9 +238,13 @@ struct GemmSmem {
     int end_epi = epi_offset(stages, reuse_ab) + kEpiWarps * epi_stages * kEpiBufBytes;
     return end_stages > end_epi ? end_stages : end_epi;
   }
-  // full[S], empty[S], tmem_full[2], tmem_empty[2], drain[1]; then tmem slot and abort flag.
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], drain[1]; then tmem slot and abort flag;
+  // then (16-byte aligned) the dynamic scheduler's kDynBytes (DynLayout).
+  static __host__ __device__ int dyn_offset(int stages, int epi_stages, int reuse_ab) {
+    return (barrier_offset(stages, epi_stages, reuse_ab) + (2 * stages + 5) * 8 + 16 + 15) & ~15;
+  }
   static __host__ __device__ int bytes(int stages, int epi_stages, int reuse_ab) {
-    int b = barrier_offset(stages, epi_stages, reuse_ab) + (2 * stages + 5) * 8 + 16;
+    int b = dyn_offset(stages, epi_stages, reuse_ab) + kDynBytes;
     b += 1024;  // alignment slack for the dynamic shared memory base
     return b < kMinSmemForOneCtaPerSm ? kMinSmemForOneCtaPerSm : b;
   }
@@ -396,9 +408,12 @@ __device__ __forceinline__ SegmentIter make_segment_iter(const SchedParams& sp, 
                                                          int32_t splits,
                                                          GroupInfo gi = GroupInfo{0, nullptr,
                                                                                   nullptr, 1},
-                                                         int32_t dp_tiles = 0) {
+                                                         int32_t dp_tiles = 0,
+                                                         int32_t dynamic = 0) {
   SegmentIter si;
   si.it = make_work_iter(sp);
+  // Dynamic scheduling sets it.cid before every next(); a tile is valid below the total.
+  if (dynamic) si.it.persistent = 1;
   si.gi = gi;
   si.dp_tiles = stream_k ? dp_tiles : 0;
   si.group_total = gi.num_groups > 0 ? gi.prefix[gi.num_groups] : 0;
@@ -516,6 +531,135 @@ __device__ __forceinline__ uint64_t l2_policy(int32_t which) {
                     : (which == 2 ? ptx::policy_evict_last() : ptx::policy_evict_normal());
 }
 
+// ------------------------------------------------------------------ dynamic scheduling
+// Cluster launch control.  The grid holds one cluster per cluster tile (x = tile * cluster_m).
+// A cluster starts with its own tile (%clusterid.x) and then takes over clusters of the grid that
+// have not started: the producer lane of CTA 0 asks for one (clusterlaunchcontrol.try_cancel)
+// when it starts loading a tile and, once that tile's loads are issued, publishes the answer --
+// the cancelled cluster's tile, or -1 when none was left -- to every CTA of the cluster through a
+// ring of kWorkSlots entries in shared memory.  full[i] of a CTA completes when its entry i is
+// written (CTA 0 stores it, by distributed shared memory for the other CTAs, and arrives with
+// cluster-scope release); empty[i] of CTA 0 completes when every consumer of the cluster has read
+// entry i: the producer lanes of the other CTAs, the MMA lanes and the four epilogue warps of
+// every CTA.  Tiles keep the scheduler's linear-id -> (m, n, l) map; only which cluster runs a
+// tile is decided at run time, so CTAs that start late (SMs busy with other work) take fewer.
+struct DynLayout {
+  uint32_t full;      // mbarrier[kWorkSlots]
+  uint32_t empty;     // mbarrier[kWorkSlots], used in CTA 0
+  uint32_t clc_bar;   // mbarrier of the cluster launch control response
+  uint32_t clc_resp;  // 16-byte response
+  uint32_t cids;      // int32[kWorkSlots]
+};
+
+__device__ __forceinline__ DynLayout dyn_layout(uint32_t base) {
+  return DynLayout{base, base + 8u * kWorkSlots, base + 16u * kWorkSlots,
+                   base + 16u * kWorkSlots + 16u, base + 16u * kWorkSlots + 32u};
+}
+
+// Readers of the work ring per CTA: its producer lane (CTAs other than 0), its MMA lane (CTAs
+// that issue MMAs) and its four epilogue warps.
+__device__ __forceinline__ uint32_t dyn_consumers(int32_t cluster_ctas, int32_t cta_group) {
+  return static_cast<uint32_t>(cluster_ctas * kEpiWarps + (cluster_ctas - 1) +
+                               cluster_ctas / cta_group);
+}
+
+// A consumer's view: its own tile first, then the ring's entries in order.  CTA 0 addresses
+// its own barriers by their shared::cta address (part of the shared::cluster window), so a grid
+// without clusters needs no mapa.
+struct WorkReader {
+  DynLayout l;
+  int slot;
+  uint32_t phase;
+  bool first;
+  uint32_t rank;
+  __device__ __forceinline__ WorkReader(const DynLayout& layout, uint32_t cta_rank)
+      : l(layout), slot(0), phase(0), first(true), rank(cta_rank) {}
+  // False on a timeout (recorded in the status word); cid = -1 when no work is left.
+  __device__ __forceinline__ bool next(int32_t& cid, const ptx::WaitCtx& ctx) {
+    if (first) {
+      first = false;
+      cid = static_cast<int32_t>(ptx::clusterid_x());
+      return true;
+    }
+    if (!ptx::mbar_wait_acquire_cluster(l.full + 8u * slot, phase, ctx, kSiteWorkFull))
+      return false;
+    cid = static_cast<int32_t>(ptx::ld_shared_u32(l.cids + 4u * slot));
+    const uint32_t e = l.empty + 8u * slot;
+    ptx::mbar_arrive_release_cluster(rank == 0 ? e : ptx::mapa_shared(e, 0));
+    if (++slot == kWorkSlots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return true;
+  }
+};
+
+// CTA 0's producer lane: requests clusters and publishes the answers.
+struct WorkScheduler {
+  DynLayout l;
+  int slot;
+  uint32_t phase, clc_phase;
+  bool live, pending;
+  int32_t cluster_ctas, cluster_m;
+  __device__ __forceinline__ WorkScheduler(const DynLayout& layout, int32_t ctas, int32_t cm)
+      : l(layout), slot(0), phase(0), clc_phase(0), live(true), pending(false),
+        cluster_ctas(ctas), cluster_m(cm) {}
+  __device__ __forceinline__ void request() {
+    if (!live || pending) return;
+    ptx::mbar_arrive_expect_tx(l.clc_bar, 16u);
+    ptx::clc_try_cancel(l.clc_resp, l.clc_bar);
+    pending = true;
+  }
+  // The answer to the outstanding request (-1: none left, or no request outstanding).
+  __device__ __forceinline__ bool answer(int32_t& cid, const ptx::WaitCtx& ctx) {
+    cid = -1;
+    if (!pending) return true;
+    if (!ptx::mbar_wait(l.clc_bar, clc_phase, ctx, kSiteClc)) return false;
+    pending = false;
+    clc_phase ^= 1u;
+    const int32_t x = ptx::clc_query_first_x(l.clc_resp);
+    ptx::fence_proxy_async_shared();  // this read before the next request's async write
+    if (x < 0) {
+      live = false;  // no request may follow a failed one
+    } else {
+      cid = x / cluster_m;
+    }
+    return true;
+  }
+  __device__ __forceinline__ bool publish(int32_t cid, const ptx::WaitCtx& ctx) {
+    if (!ptx::mbar_wait_acquire_cluster(l.empty + 8u * slot, phase ^ 1u, ctx, kSiteWorkEmpty))
+      return false;
+    for (int32_t r = 0; r < cluster_ctas; ++r) {
+      const uint32_t rr = static_cast<uint32_t>(r);
+      const uint32_t c = l.cids + 4u * slot, f = l.full + 8u * slot;
+      ptx::st_shared_cluster_u32(r == 0 ? c : ptx::mapa_shared(c, rr), static_cast<uint32_t>(cid));
+      ptx::mbar_arrive_release_cluster(r == 0 ? f : ptx::mapa_shared(f, rr));
+    }
+    if (++slot == kWorkSlots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return true;
+  }
+  // Before the CTA exits: a response still in flight must land in shared memory first.
+  __device__ __forceinline__ void drain(const ptx::WaitCtx& ctx) {
+    if (!pending) return;
+    ptx::WaitCtx dctx{ctx.abort_flag, ctx.status, ctx.timeout_ns};
+    volatile int32_t no_abort = 0;
+    dctx.abort_flag = &no_abort;
+    if (ptx::mbar_wait(l.clc_bar, clc_phase, dctx, kSiteClc)) pending = false;
+  }
+};
+
+// What the roles need to know of the dynamic mode.
+struct DynArgs {
+  int32_t enabled;
+  DynLayout layout;
+  int32_t cluster_ctas;
+  int32_t cluster_m;
+  uint32_t rank;  // %cluster_ctarank
+};
+
 // TMA producer (one lane): streams the k-blocks of A (128 rows) and B (BN / CtaGroup rows) of
 // every tile of this CTA into the shared-memory stage ring, then drains its in-flight loads.
 // B is loaded as BN / kMmaN slots, one per MMA of width kMmaN.
@@ -530,7 +674,8 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
                                               int32_t l2_b = 0, int32_t stream_k = 0,
                                               int32_t b_slot_rows = 0, int32_t splits = 1,
                                               GroupInfo gi = GroupInfo{0, nullptr, nullptr, 1},
-                                              int32_t dp_tiles = 0) {
+                                              int32_t dp_tiles = 0,
+                                              DynArgs dyn = DynArgs{}) {
   constexpr int kNumMma = BN / kMmaN;
   constexpr int kBRowsPerMma = kMmaN / CtaGroup;
   constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes * CtaGroup);
@@ -543,9 +688,55 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
   uint32_t fills = 0;
   bool ok = true;
   SegmentIter si = make_segment_iter(sp, k_iters, k_iters_per_split, stream_k, splits, gi,
-                                     dp_tiles);
+                                     dp_tiles, dyn.enabled);
+  // Dynamic mode: CTA 0 schedules (and needs no reader), the other CTAs read the ring.
+  const bool scheduler = dyn.enabled && dyn.rank == 0;
+  WorkScheduler sched(dyn.layout, dyn.cluster_ctas, dyn.cluster_m);
+  WorkReader reader(dyn.layout, dyn.rank);
+  const int32_t valid_tiles = gi.num_groups > 0 ? si.group_total : 0x7fffffff;
+  bool first = true;
+  auto fetch = [&](Segment& out) -> bool {
+    if (!dyn.enabled) return si.next(sp, out);
+    int32_t cid;
+    if (scheduler) {
+      if (first) {
+        first = false;
+        cid = static_cast<int32_t>(ptx::clusterid_x());
+        if (cid >= valid_tiles) {  // an empty cluster of a grouped GEMM's bound
+          sched.publish(-1, ctx);
+          return false;
+        }
+      } else {
+        // The answer to the request made when the previous tile started; clusters past the
+        // grouped GEMM's tiles are skipped by asking again.
+        while (true) {
+          if (!sched.answer(cid, ctx)) {
+            ok = false;
+            sched.publish(-1, ctx);
+            return false;
+          }
+          if (cid < valid_tiles) break;
+          sched.request();
+        }
+        if (!sched.publish(cid, ctx)) {
+          ok = false;
+          return false;
+        }
+        if (cid < 0) return false;
+      }
+      sched.request();  // for the tile after this one, answered while this one loads
+    } else {
+      if (!reader.next(cid, ctx)) {
+        ok = false;
+        return false;
+      }
+      if (cid < 0) return false;
+    }
+    si.it.cid = cid;
+    return si.next(sp, out);
+  };
   Segment sg;
-  while (ok && si.next(sp, sg)) {
+  while (ok && fetch(sg)) {
     const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
     const int32_t a_row = sg.row_base + pid_m * kBM;
     // B rows of MMA j: [pid_n * BN + j * kMmaN, +kMmaN), of which this CTA of a pair loads its
@@ -585,6 +776,11 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
         phase ^= 1u;
       }
     }
+  }
+  if (scheduler) {
+    // Error paths: finish the ring (consumers stop at -1) and let a pending response land.
+    if (!ok) sched.publish(-1, ctx);
+    sched.drain(ctx);
   }
   // Drain: wait (bounded) until every issued fill has landed so no TMA write into this CTA's
   // shared memory is outstanding when the CTA exits.  Immediate on the normal path.
@@ -653,11 +849,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const bool leader = (CtaGroup == 1) || ((rank & 1u) == 0u);
   const uint32_t leader_rank = rank & ~1u;
   const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);  // both CTAs of the pair
+  const int32_t cluster_ctas = p.sched.cluster_m * p.sched.cluster_n;
+  DynArgs dyn;
+  dyn.enabled = p.dynamic;
+  dyn.layout = dyn_layout(base + L::dyn_offset(stages, p.epi_stages, p.reuse_ab));
+  dyn.cluster_ctas = cluster_ctas;
+  dyn.cluster_m = p.sched.cluster_m;
+  dyn.rank = cluster_ctas > 1 ? ptx::cluster_ctarank() : 0u;
+  // Cluster-wide barrier after the barrier initialisation and before exit: CTA pairs share
+  // barriers and TMEM; the dynamic mode writes the other CTAs' work rings.
+  const bool cluster_barriers = CtaGroup == 2 || (p.dynamic != 0 && cluster_ctas > 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       ptx::mbar_init(full_bar + 8u * s, 1);
       ptx::mbar_init(empty_bar + 8u * s, 1);
+    }
+    if (p.dynamic) {
+      for (int i = 0; i < kWorkSlots; ++i) {
+        ptx::mbar_init(dyn.layout.full + 8u * i, 1);
+        ptx::mbar_init(dyn.layout.empty + 8u * i, dyn_consumers(cluster_ctas, CtaGroup));
+      }
+      ptx::mbar_init(dyn.layout.clc_bar, 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(tfull_bar + 8u * b, 1);
@@ -679,7 +892,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CtaGroup == 2) ptx::cluster_sync();  // peer barriers initialised before use
+  if (cluster_barriers) ptx::cluster_sync();  // peer barriers initialised before use
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -693,7 +906,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
           &tm_a, &tm_b, sp, k_iters, p.k_iters_per_split, stages, base, full_bar, empty_bar, rank,
           leader, ctx, p.l2_policy_a, p.l2_policy_b, p.stream_k, p.gated ? p.n : 0,
-          p.num_splits, group_info(p), p.dp_tiles);
+          p.num_splits, group_info(p), p.dp_tiles, dyn);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -705,9 +918,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       SegmentIter si = make_segment_iter(sp, k_iters, p.k_iters_per_split, p.stream_k,
-                                         p.num_splits, group_info(p), p.dp_tiles);
+                                         p.num_splits, group_info(p), p.dp_tiles, p.dynamic);
+      WorkReader reader(dyn.layout, dyn.rank);
+      auto fetch = [&](Segment& out) -> bool {
+        if (!dyn.enabled) return si.next(sp, out);
+        int32_t cid;
+        if (!reader.next(cid, ctx)) {
+          ok = false;
+          return false;
+        }
+        if (cid < 0) return false;
+        si.it.cid = cid;
+        return si.next(sp, out);
+      };
       Segment sg;
-      while (ok && si.next(sp, sg)) {
+      while (ok && fetch(sg)) {
         const int kb0 = sg.kb0, kb1 = sg.kb1;
         if (!ptx::mbar_wait(tempty_bar + 8u * acc, acc_phase ^ 1u, ctx, kSiteMmaTmemEmpty)) {
           ok = false;
@@ -801,12 +1026,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     };
     SegmentIter si = make_segment_iter(sp, p.k_iters, p.k_iters_per_split, p.stream_k,
-                                       p.num_splits, group_info(p), p.dp_tiles);
+                                       p.num_splits, group_info(p), p.dp_tiles, p.dynamic);
+    // Dynamic mode: lane 0 reads the work ring and hands each entry to the warp.
+    WorkReader reader(dyn.layout, dyn.rank);
+    auto fetch = [&](Segment& out) -> bool {
+      if (!dyn.enabled) return si.next(sp, out);
+      int32_t cid = 0;
+      int32_t got = 1;
+      if (lane == 0) got = reader.next(cid, ctx) ? 1 : 0;
+      cid = __shfl_sync(0xffffffffu, cid, 0);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got || cid < 0) return false;
+      si.it.cid = cid;
+      return si.next(sp, out);
+    };
     Segment sg;
-    const int32_t cluster_ctas = sp.cluster_m * sp.cluster_n;
     const int32_t cta_in_cluster = static_cast<int32_t>(ptx::cluster_ctaid_x()) +
                                    static_cast<int32_t>(ptx::cluster_ctaid_y()) * sp.cluster_m;
-    while (si.next(sp, sg)) {
+    while (fetch(sg)) {
       const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
       // Split-K / Stream-K into D: only the segment holding a tile's first k-block adds the bias.
       const bool add_bias = has_bias && sg.kb0 == 0;
@@ -1011,7 +1248,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // ------------------------------------------------------------------ teardown
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CtaGroup == 2) ptx::cluster_sync();  // peer done with our barriers and TMEM
+  if (cluster_barriers) ptx::cluster_sync();  // peers done with our barriers, TMEM and ring
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc<CtaGroup>(tmem_base, L::kTmemCols);

@@ -487,6 +487,76 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// ---------------------------------------------------------------- cluster launch control
+// Ask to cancel the launch of a cluster of this grid that has not started yet.  The 16-byte
+// response is written (async proxy) to this CTA's shared memory at `resp` and completes 16 bytes
+// of transaction on `bar`.  After a response reported failure no further request may be issued.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 "
+      "[%0], [%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+
+// Decode the response at `resp`: the x index of the cancelled cluster's first CTA, or -1 when
+// the request failed (no cluster left to cancel).
+__device__ __forceinline__ int32_t clc_query_first_x(uint32_t resp) {
+  uint64_t lo, hi;
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(resp) : "memory");
+  uint32_t ok, x;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "mov.b128 r, {%2, %3};\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "mov.u32 %1, 0;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+      : "=r"(ok), "=r"(x)
+      : "l"(lo), "l"(hi));
+  return ok ? static_cast<int32_t>(x) : -1;
+}
+
+// Store / arrive on another CTA's shared memory (addresses from mapa_shared) with cluster-scope
+// release, and wait with cluster-scope acquire: for data handed between the CTAs of a cluster.
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acquire_cluster(uint32_t bar, uint32_t parity,
+                                                              uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded like mbar_wait, with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_acquire_cluster(uint32_t bar, uint32_t parity,
+                                                          const WaitCtx& ctx, int32_t site) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_acquire_cluster(bar, parity, kWaitSuspendNs)) return true;
+    if (*ctx.abort_flag) return false;
+    if (globaltimer() - t0 > ctx.timeout_ns) {
+      record_timeout(ctx, site);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -45,6 +45,49 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// x / s for the vector kernels, exact to the E4M3 byte without a division per element.  With
+// y = RN(1 / s) (__frcp_rn) and q = RN(x * y), |q - x / s| < ulp(x * y) / 2 + ulp(x / s), so q and
+// t = RN(x / s) are at most two fp32 steps apart; e4m3(q) != e4m3(t) (round to nearest even is
+// monotone) needs an E4M3 rounding midpoint in between.  Midpoints of the normal E4M3 range
+// (>= 2^-6) are the fp32 values whose low 20 fraction bits are 0x80000.  So q whose low bits are
+// within 8 steps of that pattern, and nonzero q below 2^-6 (the subnormal E4M3 grid has other
+// midpoints), make the whole vector take the IEEE division; all other q give the same byte.
+__device__ __forceinline__ bool e4m3_midpoint_risk(float q) {
+  const uint32_t b = __float_as_uint(q);
+  // Low 20 bits within [0x80000 - 8, 0x80000 + 8] (any exponent: a superset of the normal range),
+  // or 0 < |q| < 2^-6 (b << 1 drops the sign: 2 <= 2|q|bits <= 2 * 0x3c7fffff).
+  return ((b - 0x7fff8u) & 0xfffffu) <= 16u || (b << 1) - 2u <= 0x78fffffcu;
+}
+
+template <int N>
+__device__ __forceinline__ void div_by_scale(float (&x)[N], float s, float y) {
+  float q[N];
+  bool slow = false;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    q[j] = __fmul_rn(x[j], y);
+    slow |= e4m3_midpoint_risk(q[j]);
+  }
+  if (slow) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[j] = x[j] / s;
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) x[j] = q[j];
+  }
+}
+
+// N (a multiple of 4) floats already divided by the scale -> N E4M3 bytes, packed 4 per word.
+template <int N>
+__device__ __forceinline__ void pack_e4m3(const float (&x)[N], uint32_t (&w)[N / 4]) {
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const uint32_t lo = cvt_e4m3x2(x[4 * i], x[4 * i + 1]);
+    const uint32_t hi = cvt_e4m3x2(x[4 * i + 2], x[4 * i + 3]);
+    w[i] = lo | (hi << 16);
+  }
+}
+
 // Grid-stride over rows, block-stride over columns (no per-element division).
 #define CPG_ROW_LOOP(body)                                                             \
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)                              \
@@ -114,6 +157,31 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return r;
 }
 
+// The first n (< V) elements at p as a 16-byte vector of raw bits, zeros (+0.0) after them.
+template <typename T>
+__device__ __forceinline__ uint4 ld_partial_vec(const T* p, int n) {
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < n) w[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(p[j])) << (16 * (j & 1));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < n) w[j] = __float_as_uint(p[j]);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T>
+__device__ __forceinline__ float amax_vec(const uint4& raw, float m) {
+  float f[Vec16<T>::kElems];
+  Vec16<T>::unpack(raw, f);
+#pragma unroll
+  for (int j = 0; j < Vec16<T>::kElems; ++j) m = fmaxf(m, fabsf(f[j]));
+  return m;
+}
+
 template <typename T>
 __global__ void amax_vec_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
                                 unsigned int* amax_bits) {
@@ -148,6 +216,7 @@ __global__ void quant_per_tensor_vec_kernel(const T* __restrict__ x, int64_t row
                                             const unsigned int* amax_bits) {
   constexpr int V = Vec16<T>::kElems;
   const float s = fmaxf(__uint_as_float(*amax_bits), kAmaxFloor) / kE4M3Max;
+  const float y = __frcp_rn(s);
   const int64_t vcols = cols / V;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* row = x + r * ldx;
@@ -156,13 +225,9 @@ __global__ void quant_per_tensor_vec_kernel(const T* __restrict__ x, int64_t row
     for (int64_t c = threadIdx.x; c < vcols; c += blockDim.x) {
       float f[V];
       Vec16<T>::unpack(ld_nc_v4(row + c * V), f);
+      div_by_scale(f, s, y);
       uint32_t w[V / 4];
-#pragma unroll
-      for (int i = 0; i < V / 4; ++i) {
-        const uint32_t lo = cvt_e4m3x2(f[4 * i] / s, f[4 * i + 1] / s);
-        const uint32_t hi = cvt_e4m3x2(f[4 * i + 2] / s, f[4 * i + 3] / s);
-        w[i] = lo | (hi << 16);
-      }
+      pack_e4m3(f, w);
       if constexpr (V == 8) {
         *reinterpret_cast<uint2*>(qrow + c * V) = make_uint2(w[0], w[1]);
       } else {
@@ -206,39 +271,185 @@ __global__ void quant_row_block_kernel(const T* __restrict__ x, int64_t rows, in
   if (lane == 0) scales[kb * rows + r] = s;
 }
 
-// 128 x 128 blocks: one 256-thread CTA per block; thread t owns column (t & 127) of rows
-// (t >> 7), (t >> 7) + 2, ... (64 values).
+// 128 x 128 blocks: one CTA per block (a multiple of 128 threads, at most 512); thread t owns
+// column (t & 127) of rows (t >> 7), (t >> 7) + blockDim.x / 128, ...
 template <typename T>
-__global__ void quant_tile_block_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
-                                        int64_t ldx, uint8_t* __restrict__ q, int64_t ldq,
-                                        float* __restrict__ scales) {
+__device__ __forceinline__ void quant_tile_block_elems(const T* __restrict__ x, int64_t rows,
+                                                       int64_t cols, int64_t ldx,
+                                                       uint8_t* __restrict__ q, int64_t ldq,
+                                                       float* __restrict__ scales) {
   const int64_t nkb = (cols + 127) / 128;
   const int64_t rb = blockIdx.x / nkb, kb = blockIdx.x - (blockIdx.x / nkb) * nkb;
   const int col = threadIdx.x & 127;
   const int r0 = threadIdx.x >> 7;
+  const int rstep = blockDim.x >> 7;
   const int64_t c = kb * 128 + col;
   float m = 0.f;
-  for (int rr = r0; rr < 128; rr += 2) {
+  for (int rr = r0; rr < 128; rr += rstep) {
     const int64_t r = rb * 128 + rr;
     if (r < rows && c < cols) m = fmaxf(m, fabsf(to_f32(x[r * ldx + c])));
   }
   m = warp_max(m);
-  __shared__ float red[8];
+  __shared__ float red[16];
   __shared__ float s_sh;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (lane == 0) red[warp] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
     float mm = 0.f;
-    for (int w = 0; w < 8; ++w) mm = fmaxf(mm, red[w]);
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
     s_sh = fmaxf(mm, kAmaxFloor) / kE4M3Max;
     scales[rb * nkb + kb] = s_sh;
   }
   __syncthreads();
   const float s = s_sh;
-  for (int rr = r0; rr < 128; rr += 2) {
+  for (int rr = r0; rr < 128; rr += rstep) {
     const int64_t r = rb * 128 + rr;
     if (r < rows && c < cols) q[r * ldq + c] = cvt_e4m3(to_f32(x[r * ldx + c]) / s);
+  }
+}
+
+template <typename T>
+__global__ void quant_tile_block_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                        int64_t ldx, uint8_t* __restrict__ q, int64_t ldq,
+                                        float* __restrict__ scales) {
+  quant_tile_block_elems(x, rows, cols, ldx, q, ldq, scales);
+}
+
+// 128 x 128 blocks with 16-byte loads: one kTileBlockThreads-thread CTA per block; a thread owns
+// one vector (8 BF16 / 4 FP32 columns) of 128 * V / kTileBlockThreads rows and keeps them, packed,
+// in registers between the amax and the quantisation, so the block is read once.  Blocks at a
+// ragged edge use the element form.
+constexpr int kTileBlockThreads = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(kTileBlockThreads)
+    quant_tile_block_vec_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+                                uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scales) {
+  constexpr int V = Vec16<T>::kElems;
+  constexpr int kThreadsPerRow = 128 / V;                             // 16 or 32
+  constexpr int kRowsPerPass = kTileBlockThreads / kThreadsPerRow;    // 32 or 16
+  constexpr int kPasses = 128 / kRowsPerPass;                         // 4 or 8
+  constexpr int kWarps = kTileBlockThreads / 32;
+  const int64_t nkb = (cols + 127) / 128;
+  const int64_t rb = blockIdx.x / nkb, kb = blockIdx.x - rb * nkb;
+  if ((rb + 1) * 128 > rows || (kb + 1) * 128 > cols) {
+    quant_tile_block_elems(x, rows, cols, ldx, q, ldq, scales);
+    return;
+  }
+  const int cg = threadIdx.x % kThreadsPerRow;
+  const int r0 = threadIdx.x / kThreadsPerRow;
+  const T* xp = x + (rb * 128 + r0) * ldx + kb * 128 + cg * V;
+  uint8_t* qp = q + (rb * 128 + r0) * ldq + kb * 128 + cg * V;
+  uint4 raw[kPasses];
+#pragma unroll
+  for (int i = 0; i < kPasses; ++i) raw[i] = ld_nc_v4(xp + i * kRowsPerPass * ldx);
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPasses; ++i) m = amax_vec<T>(raw[i], m);
+  m = warp_max(m);
+  __shared__ float red[kWarps];
+  __shared__ float s_sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = 0.f;
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, red[w]);
+    s_sh = fmaxf(mm, kAmaxFloor) / kE4M3Max;
+    scales[rb * nkb + kb] = s_sh;
+  }
+  __syncthreads();
+  const float s = s_sh;
+  const float y = __frcp_rn(s);
+#pragma unroll
+  for (int i = 0; i < kPasses; ++i) {
+    float v[V];
+    Vec16<T>::unpack(raw[i], v);
+    div_by_scale(v, s, y);
+    uint32_t w[V / 4];
+    pack_e4m3(v, w);
+    uint8_t* dst = qp + i * kRowsPerPass * ldq;
+    if constexpr (V == 8) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = w[0];
+    }
+  }
+}
+
+// 1 x 128 blocks with 16-byte loads: lane l holds V consecutive values (8 BF16 / 4 FP32) of a
+// block, 128 / V lanes cover one block, and a warp quantises kRowBlockLoads such loads of
+// consecutive blocks of one row (8 BF16 / 4 FP32 blocks), issued before the first reduction so
+// that each warp keeps kRowBlockLoads 16-byte loads per lane in flight.  Blocks at a ragged right
+// edge use element accesses.
+constexpr int kRowBlockLoads = 4;
+
+template <typename T>
+__host__ __device__ constexpr int row_blocks_per_warp() {
+  return kRowBlockLoads * (32 / (128 / Vec16<T>::kElems));
+}
+
+template <typename T>
+__global__ void quant_row_block_vec_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                           int64_t ldx, uint8_t* __restrict__ q, int64_t ldq,
+                                           float* __restrict__ scales) {
+  constexpr int V = Vec16<T>::kElems;
+  constexpr int kLanesPerBlock = 128 / V;              // 16 or 32
+  constexpr int kBlocksPerLoad = 32 / kLanesPerBlock;  // 2 or 1
+  constexpr int kPerWarp = row_blocks_per_warp<T>();
+  const int64_t nkb = (cols + 127) / 128;
+  const int64_t ngroups = (nkb + kPerWarp - 1) / kPerWarp;
+  const int64_t warp_id = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= rows * ngroups) return;  // whole warps
+  const int64_t r = warp_id / ngroups;
+  const int64_t kb_first = (warp_id - r * ngroups) * kPerWarp + lane / kLanesPerBlock;
+  const int li = lane % kLanesPerBlock;
+  uint4 raw[kRowBlockLoads];
+#pragma unroll
+  for (int i = 0; i < kRowBlockLoads; ++i) {
+    const int64_t kb = kb_first + i * kBlocksPerLoad;
+    const int64_t c0 = kb * 128 + li * V;
+    if ((kb + 1) * 128 <= cols) {
+      raw[i] = ld_nc_v4(x + r * ldx + c0);
+    } else {
+      const int64_t n = kb < nkb ? cols - c0 : 0;
+      raw[i] = ld_partial_vec(x + r * ldx + c0, n < 0 ? 0 : (n > V ? V : static_cast<int>(n)));
+    }
+  }
+  // Block amax: reductions over each block's lanes, all lanes taking part in every shuffle.
+  float m[kRowBlockLoads];
+#pragma unroll
+  for (int i = 0; i < kRowBlockLoads; ++i) {
+    m[i] = amax_vec<T>(raw[i], 0.f);
+#pragma unroll
+    for (int o = kLanesPerBlock / 2; o > 0; o >>= 1)
+      m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+  }
+#pragma unroll
+  for (int i = 0; i < kRowBlockLoads; ++i) {
+    const int64_t kb = kb_first + i * kBlocksPerLoad;
+    if (kb >= nkb) continue;
+    const int64_t c0 = kb * 128 + li * V;
+    const float s = fmaxf(m[i], kAmaxFloor) / kE4M3Max;
+    float v[V];
+    Vec16<T>::unpack(raw[i], v);
+    div_by_scale(v, s, __frcp_rn(s));
+    if ((kb + 1) * 128 <= cols) {
+      uint32_t w[V / 4];
+      pack_e4m3(v, w);
+      if constexpr (V == 8) {
+        *reinterpret_cast<uint2*>(q + r * ldq + c0) = make_uint2(w[0], w[1]);
+      } else {
+        *reinterpret_cast<uint32_t*>(q + r * ldq + c0) = w[0];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j)
+        if (c0 + j < cols) q[r * ldq + c0 + j] = cvt_e4m3(v[j]);
+    }
+    if (li == 0) scales[kb * rows + r] = s;
   }
 }
 

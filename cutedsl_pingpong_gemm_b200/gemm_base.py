@@ -289,7 +289,7 @@ class CompiledGemm:
         s = wave_split_k(tiles, kblocks, slots, min_fill=0.85 if kblocks >= 256 else 0.95)
         if s is not None:
             return s
-        if gemm.is_persistent and kblocks >= 8:
+        if gemm.is_persistent and not gemm.dynamic_scheduler and kblocks >= 8:
             return _lib.CPG_SPLIT_K_STREAM
         want = -(-3 * slots // tiles)
         return max(1, min(want, kblocks // 4))
@@ -440,7 +440,12 @@ class GemmSM90:
         reuse_ab: bool = True,
         is_persistent: bool = False,
         gemm_n_prologue: int = 0,
+        *,
+        dynamic_scheduler: bool = False,
     ):
+        """dynamic_scheduler (not in the reference): one cluster per cluster tile in the grid and
+        cluster launch control, so running clusters take over the tiles of clusters that have
+        not started (the tile map is the same; is_persistent is then ignored)."""
         import torch
         self.acc_dtype = torch.float32
         self.raster_order = raster_order
@@ -482,6 +487,9 @@ class GemmSM90:
         self.gemm_n_prologue = gemm_n_prologue
 
         assert not (self.reuse_ab and self.is_persistent), "Persistent kernel can't reuse AB for epilogue"
+        self.dynamic_scheduler = bool(dynamic_scheduler)
+        assert not (self.reuse_ab and self.dynamic_scheduler), \
+            "Dynamic scheduler runs several tiles per CTA and can't reuse AB for epilogue"
         self._compiled: Optional[CompiledGemm] = None
 
     @property
@@ -500,7 +508,7 @@ class GemmSM90:
             self.atom_layout_mnk[0], self.atom_layout_mnk[1],
             self.ab_stage, self.epi_stage, int(self.raster_order),
             int(bool(self.reuse_ab)), int(bool(self.is_persistent)), int(self.gemm_n_prologue),
-            int(self.scheduler_group_size))
+            int(self.scheduler_group_size), int(self.dynamic_scheduler))
 
     def validate(self) -> None:
         """Run the C ABI's copy of the constructor checks (no GPU needed)."""

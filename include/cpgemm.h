@@ -86,7 +86,7 @@ typedef struct cpg_sched_params {
 } cpg_sched_params;
 
 /* GemmSM90 constructor arguments (gemm_base.py:50-62) plus the scheduler group size, which the
- * reference fixes at 8 (gemm_base.py:65). */
+ * reference fixes at 8 (gemm_base.py:65), and the scheduling mode. */
 typedef struct cpg_gemm_config {
   int32_t tile_m, tile_n;
   int32_t epi_tile_m, epi_tile_n;
@@ -96,6 +96,12 @@ typedef struct cpg_gemm_config {
   int32_t raster_order;
   int32_t reuse_ab, is_persistent, gemm_n_prologue;
   int32_t group_size;
+  int32_t dynamic_scheduler; /* 0: the static schedule of tile_scheduler.py (persistent or one
+                                tile per cluster); 1: dynamic (cluster launch control): the grid
+                                holds one cluster per cluster tile and running clusters take over
+                                clusters that have not started, so SMs busy with other work take
+                                fewer tiles.  Same tile map; needs reuse_ab = 0 and no Stream-K or
+                                block scales; ignores is_persistent. */
 } cpg_gemm_config;
 
 /* Problem description fixed at create time (the reference fixes dtypes and layouts at compile

@@ -131,3 +131,22 @@ def test_fused_epilogue_rejections():
     odd = torch.empty(m, n + 1, dtype=torch.bfloat16, device="cuda")[:, :n]
     with pytest.raises(_lib.CpgError):  # C rows not 16-byte aligned
         make_gemm(256, (1, 1, 1))(a, b[:n], d, None, source=odd)
+
+
+@pytest.mark.parametrize("act", ["relu", "gelu"])
+def test_fp8_per_tensor_with_bias_and_activation(act):
+    m, n, k = 384, 768, 512
+    g = torch.Generator().manual_seed(33)
+    a = torch.randn(m, k, generator=g)
+    b = torch.randn(n, k, generator=g) * k ** -0.5
+    bias = torch.randn(n, generator=g).to(torch.bfloat16)
+    qa, sa = quantize_e4m3(a.cuda())
+    qb, sb = quantize_e4m3(b.cuda())
+    d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    make_gemm(512, (2, 1, 1), stages=4)(qa, qb, d, None, scale_a=sa, scale_b=sb,
+                                        bias=bias.cuda(), activation=act)
+    torch.cuda.synchronize()
+    res = gemm_ref.check_epilogue(d.cpu(), qa.cpu().float() * sa.cpu(),
+                                  qb.cpu().float() * sb.cpu(), bias=bias, act=act,
+                                  frob_tol=gemm_ref.FROB_TOL_FP8)
+    assert res["ok"], res

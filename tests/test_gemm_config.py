@@ -9,10 +9,14 @@ from cutedsl_pingpong_gemm_b200 import GemmSM90, GemmSM100, RasterOrder, _lib
 
 def test_signature_matches_reference():
     sig = inspect.signature(GemmSM90.__init__)
-    names = list(sig.parameters)[1:]
-    assert names == ["tile_shape_mn", "epi_tile_mn", "cluster_shape_mnk", "atom_layout_mn",
-                     "ab_stage", "epi_stage", "raster_order", "reuse_ab", "is_persistent",
-                     "gemm_n_prologue"]
+    positional = [k for k, v in sig.parameters.items()
+                  if v.kind == inspect.Parameter.POSITIONAL_OR_KEYWORD][1:]
+    assert positional == ["tile_shape_mn", "epi_tile_mn", "cluster_shape_mnk", "atom_layout_mn",
+                          "ab_stage", "epi_stage", "raster_order", "reuse_ab", "is_persistent",
+                          "gemm_n_prologue"]
+    # Additions of this build are keyword-only, with defaults that keep the reference behaviour.
+    extra = {k: v for k, v in sig.parameters.items() if v.kind == inspect.Parameter.KEYWORD_ONLY}
+    assert extra.keys() == {"dynamic_scheduler"} and extra["dynamic_scheduler"].default is False
     d = {k: v.default for k, v in sig.parameters.items()}
     assert d["ab_stage"] == 2 and d["epi_stage"] == 2
     assert d["raster_order"] == RasterOrder.AlongN
