@@ -93,7 +93,7 @@ def parse_args():
                          "API (auto: for the launch-bound small-M workload)")
     ap.add_argument("--scheduler", choices=["auto", "static", "dynamic"], default="auto",
                     help="tile schedule: the reference's static persistent schedule, or dynamic "
-                         "(cluster launch control; not with block-scaled FP8 or Stream-K).  auto: "
+                         "(cluster launch control; not with Stream-K).  auto: "
                          "dynamic for the dense single-GEMM workloads (measured 3-10%% faster "
                          "there under the power cap), static for the others")
     ap.add_argument("--activation", default=None,
@@ -557,7 +557,7 @@ def run_cpg(args, world, rank, local):
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
                     is_persistent=True,
-                    dynamic_scheduler=args.scheduler == "dynamic" and w["fp8"] != "block")
+                    dynamic_scheduler=args.scheduler == "dynamic")
     compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
     # The split is picked from the tile count (small M: K ranges or Stream-K; a partial last
     # wave: data-parallel waves + Stream-K tail); fused epilogues and block scales run whole.

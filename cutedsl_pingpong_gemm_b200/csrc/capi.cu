@@ -473,9 +473,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return fail(CPG_ERR_UNSUPPORTED, "split-K ranges accumulate into an FP32 D (no block scales)");
   if (sk_any && v.scale_mode != CPG_SCALE_TENSOR)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K is not available with block scales");
-  if (cfg->dynamic_scheduler && (sk_any || v.scale_mode != CPG_SCALE_TENSOR))
-    return fail(CPG_ERR_UNSUPPORTED,
-                "the dynamic scheduler is not available with Stream-K or block scales");
+  if (cfg->dynamic_scheduler && sk_any)
+    return fail(CPG_ERR_UNSUPPORTED, "the dynamic scheduler is not available with Stream-K");
   if (sk_any && !cfg->is_persistent)
     return fail(CPG_ERR_UNSUPPORTED, "Stream-K needs a persistent kernel");
   if (prob->gated != 0 && prob->gated != 1)

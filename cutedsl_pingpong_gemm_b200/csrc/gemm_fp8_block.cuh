@@ -56,10 +56,14 @@ struct BlockSmem {
   static __host__ __device__ int barrier_offset(int stages, int epi_stages) {
     return epi_offset(stages) + kBlockEpiWarps * epi_stages * kEpiBufBytes;
   }
-  // full[S], empty[S], part_full[P], part_empty[P], drain[1]; then tmem slot and abort flag.
+  // full[S], empty[S], part_full[P], part_empty[P], drain[1]; then tmem slot and abort flag;
+  // then (16-byte aligned) the dynamic scheduler's kDynBytes (DynLayout).
+  static __host__ __device__ int dyn_offset(int stages, int epi_stages) {
+    return (barrier_offset(stages, epi_stages) + (2 * stages + 2 * BlockShape<BN>::kParts + 1) * 8 +
+            16 + 15) & ~15;
+  }
   static __host__ __device__ int bytes(int stages, int epi_stages, int /*reuse_ab*/) {
-    int b = barrier_offset(stages, epi_stages) +
-            (2 * stages + 2 * BlockShape<BN>::kParts + 1) * 8 + 16 + 1024;
+    int b = dyn_offset(stages, epi_stages) + kDynBytes + 1024;
     return b < kMinSmemForOneCtaPerSm ? kMinSmemForOneCtaPerSm : b;
   }
 };
@@ -114,6 +118,14 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
   const bool leader = (CtaGroup == 1) || ((rank & 1u) == 0u);
   const uint32_t leader_rank = rank & ~1u;
   const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);
+  const int32_t cluster_ctas = p.sched.cluster_m * p.sched.cluster_n;
+  DynArgs dyn;
+  dyn.enabled = p.dynamic;
+  dyn.layout = dyn_layout(base + L::dyn_offset(stages, p.epi_stages));
+  dyn.cluster_ctas = cluster_ctas;
+  dyn.cluster_m = p.sched.cluster_m;
+  dyn.rank = cluster_ctas > 1 ? ptx::cluster_ctarank() : 0u;
+  const bool cluster_barriers = CtaGroup == 2 || (p.dynamic != 0 && cluster_ctas > 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -123,6 +135,14 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
     for (int b = 0; b < kParts; ++b) {
       ptx::mbar_init(pfull_bar + 8u * b, 1);
       ptx::mbar_init(pempty_bar + 8u * b, kBlockEpiWarps * CtaGroup);
+    }
+    if (p.dynamic) {
+      for (int i = 0; i < kWorkSlots; ++i) {
+        ptx::mbar_init(dyn.layout.full + 8u * i, 1);
+        ptx::mbar_init(dyn.layout.empty + 8u * i,
+                       dyn_consumers(cluster_ctas, CtaGroup, kBlockEpiWarps));
+      }
+      ptx::mbar_init(dyn.layout.clc_bar, 1);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -140,7 +160,7 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CtaGroup == 2) ptx::cluster_sync();
+  if (cluster_barriers) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -156,7 +176,8 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
       if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
         producer_loop<BN, CtaGroup, kBK, L::kStageBytes, L::kAStageBytes>(
             &tm_a, &tm_b, sp, k_iters, k_iters, stages, base, full_bar, empty_bar, rank, leader,
-            ctx, p.l2_policy_a, p.l2_policy_b);
+            ctx, p.l2_policy_a, p.l2_policy_b, 0, 0, 1, GroupInfo{0, nullptr, nullptr, 1}, 0,
+            dyn);
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -166,7 +187,9 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
         int part = 0;
         uint32_t part_phase = 0;
         bool ok = true;
-        for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+        TileSource tiles(sp, dyn);
+        int32_t cid;
+        while (ok && tiles.next(cid, ctx, ok, false)) {
           for (int kb = 0; kb < k_iters; ++kb) {
             if (!ptx::mbar_wait(pempty_bar + 8u * part, part_phase ^ 1u, ctx, kSiteMmaTmemEmpty) ||
                 !ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) {
@@ -223,13 +246,16 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
     uint32_t part_phase = 0;
     int epi_idx = 0;
     bool ok = true;
-    for (WorkIter it = make_work_iter(sp); ok && it.valid(); it.advance()) {
+    TileSource tiles(sp, dyn);
+    int32_t cid;
+    int32_t executed = 0;
+    for (; ok && tiles.next(cid, ctx, ok, true); ++executed) {
       int32_t pid_m, pid_n;
-      work_tile_coords(sp, it.cid, pid_m, pid_n);
-      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && it.executed < p.trace_stride) {
+      work_tile_coords(sp, cid, pid_m, pid_n);
+      if (p.tile_trace != nullptr && ew == 0 && lane == 0 && executed < p.trace_stride) {
         const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) *
                                              (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
-        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + it.executed);
+        int32_t* t = p.tile_trace + 2 * (cta * p.trace_stride + executed);
         t[0] = pid_m;
         t[1] = pid_n;
       }
@@ -363,7 +389,7 @@ __global__ void __launch_bounds__(BlockShape<BN>::kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CtaGroup == 2) ptx::cluster_sync();
+  if (cluster_barriers) ptx::cluster_sync();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc<CtaGroup>(tmem_base, L::kTmemCols);

@@ -557,9 +557,10 @@ __device__ __forceinline__ DynLayout dyn_layout(uint32_t base) {
 }
 
 // Readers of the work ring per CTA: its producer lane (CTAs other than 0), its MMA lane (CTAs
-// that issue MMAs) and its four epilogue warps.
-__device__ __forceinline__ uint32_t dyn_consumers(int32_t cluster_ctas, int32_t cta_group) {
-  return static_cast<uint32_t>(cluster_ctas * kEpiWarps + (cluster_ctas - 1) +
+// that issue MMAs) and its epilogue warps.
+__device__ __forceinline__ uint32_t dyn_consumers(int32_t cluster_ctas, int32_t cta_group,
+                                                  int32_t epi_warps) {
+  return static_cast<uint32_t>(cluster_ctas * epi_warps + (cluster_ctas - 1) +
                                cluster_ctas / cta_group);
 }
 
@@ -658,6 +659,40 @@ struct DynArgs {
   int32_t cluster_ctas;
   int32_t cluster_m;
   uint32_t rank;  // %cluster_ctarank
+};
+
+// The cluster tiles of a role that walks whole tiles: the static WorkIter, or the work ring.
+// With `broadcast`, lane 0 reads the ring and the warp shares the entry (all lanes must call).
+struct TileSource {
+  WorkIter it;
+  WorkReader reader;
+  bool dynamic, started;
+  __device__ __forceinline__ TileSource(const SchedParams& sp, const DynArgs& dyn)
+      : it(make_work_iter(sp)), reader(dyn.layout, dyn.rank), dynamic(dyn.enabled != 0),
+        started(false) {}
+  // False at the end, or on a timeout (then `ok` is cleared).
+  __device__ __forceinline__ bool next(int32_t& cid, const ptx::WaitCtx& ctx, bool& ok,
+                                       bool broadcast) {
+    if (!dynamic) {
+      if (started) it.advance();
+      started = true;
+      if (!it.valid()) return false;
+      cid = it.cid;
+      return true;
+    }
+    int32_t got = 1;
+    cid = 0;
+    if (!broadcast || ptx::lane_id() == 0) got = reader.next(cid, ctx) ? 1 : 0;
+    if (broadcast) {
+      cid = __shfl_sync(0xffffffffu, cid, 0);
+      got = __shfl_sync(0xffffffffu, got, 0);
+    }
+    if (!got) {
+      ok = false;
+      return false;
+    }
+    return cid >= 0;
+  }
 };
 
 // TMA producer (one lane): streams the k-blocks of A (128 rows) and B (BN / CtaGroup rows) of
@@ -868,7 +903,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (p.dynamic) {
       for (int i = 0; i < kWorkSlots; ++i) {
         ptx::mbar_init(dyn.layout.full + 8u * i, 1);
-        ptx::mbar_init(dyn.layout.empty + 8u * i, dyn_consumers(cluster_ctas, CtaGroup));
+        ptx::mbar_init(dyn.layout.empty + 8u * i,
+                       dyn_consumers(cluster_ctas, CtaGroup, kEpiWarps));
       }
       ptx::mbar_init(dyn.layout.clc_bar, 1);
     }

@@ -100,8 +100,8 @@ typedef struct cpg_gemm_config {
                                 tile per cluster); 1: dynamic (cluster launch control): the grid
                                 holds one cluster per cluster tile and running clusters take over
                                 clusters that have not started, so SMs busy with other work take
-                                fewer tiles.  Same tile map; needs reuse_ab = 0 and no Stream-K or
-                                block scales; ignores is_persistent. */
+                                fewer tiles.  Same tile map; needs reuse_ab = 0 and no Stream-K;
+                                ignores is_persistent. */
 } cpg_gemm_config;
 
 /* Problem description fixed at create time (the reference fixes dtypes and layouts at compile

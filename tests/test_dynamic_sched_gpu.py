@@ -176,7 +176,29 @@ def test_dynamic_rejections():
                  dynamic_scheduler=True)
     with pytest.raises(_lib.CpgError):  # Stream-K partitions the k-blocks statically
         make_gemm(256)(a, b, d, None, split_k=-1)
-    qa, sa = quantize_e4m3(a, (1, 128))
-    qb, sb = quantize_e4m3(b, (128, 128))
-    with pytest.raises(_lib.CpgError):  # block scales
-        make_gemm(128)(qa, qb, d, None, scale_a=sa, scale_b=sb)
+
+
+@pytest.mark.parametrize("tile_n,cluster,stages,epi", [(128, (1, 1, 1), 5, 2),
+                                                       (256, (2, 1, 1), 6, 1)])
+def test_dynamic_fp8_block_scales(tile_n, cluster, stages, epi):
+    """The block-scaled FP8 kernel under the dynamic schedule: identical bytes to the static one
+    and within the FP8 tolerance of the dequantised oracle."""
+    m, n, k = 2048 + 128, 3072 - 64, 1024
+    g = torch.Generator().manual_seed(78)
+    qa, sa = quantize_e4m3(torch.randn(m, k, generator=g).cuda(), (1, 128))
+    qb, sb = quantize_e4m3(torch.randn(n, k, generator=g).cuda(), (128, 128))
+    outs = []
+    for dyn in (False, True):
+        gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
+                        cluster_shape_mnk=cluster, atom_layout_mn=(1, 1), ab_stage=stages,
+                        epi_stage=epi, raster_order=RasterOrder.AlongN, reuse_ab=False,
+                        is_persistent=True, dynamic_scheduler=dyn)
+        d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        gemm(qa, qb, d, None, scale_a=sa, scale_b=sb)
+        outs.append(d)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    da = gemm_ref.dequantize_blocks(qa.cpu(), sa.cpu(), (1, 128))
+    db = gemm_ref.dequantize_blocks(qb.cpu(), sb.cpu(), (128, 128))
+    res = gemm_ref.check(outs[1].cpu(), da, db, frob_tol=gemm_ref.FROB_TOL_FP8)
+    assert res["ok"], res
