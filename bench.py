@@ -94,8 +94,9 @@ def parse_args():
     ap.add_argument("--scheduler", choices=["auto", "static", "dynamic"], default="auto",
                     help="tile schedule: the reference's static persistent schedule, or dynamic "
                          "(cluster launch control; not with Stream-K).  auto: "
-                         "dynamic for the dense single-GEMM workloads (measured 3-10%% faster "
-                         "there under the power cap), static for the others")
+                         "dynamic for the dense GEMM workloads (measured 3-10%% faster there "
+                         "under the power cap), static for small M (Stream-K), the grouped MoE "
+                         "and block-scaled FP8 (measured equal or slower)")
     ap.add_argument("--activation", default=None,
                     choices=["relu", "silu", "gelu", "gelu_tanh"],
                     help="fused epilogue activation for the GEMM workloads")
@@ -762,8 +763,7 @@ def main():
     args = parse_args()
     if args.scheduler == "auto":
         w = WORKLOADS[args.workload]
-        dense = not (w.get("small_m") or w.get("groups") or w.get("split") == "k"
-                     or w["fp8"] == "block")
+        dense = not (w.get("small_m") or w.get("groups") or w["fp8"] == "block")
         args.scheduler = "dynamic" if dense else "static"
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
