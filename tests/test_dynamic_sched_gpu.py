@@ -202,3 +202,28 @@ def test_dynamic_fp8_block_scales(tile_n, cluster, stages, epi):
     db = gemm_ref.dequantize_blocks(qb.cpu(), sb.cpu(), (128, 128))
     res = gemm_ref.check(outs[1].cpu(), da, db, frob_tol=gemm_ref.FROB_TOL_FP8)
     assert res["ok"], res
+
+
+def test_dynamic_in_cuda_graph():
+    """A dynamic-schedule GEMM captured into a CUDA graph and replayed: each replay cancels
+    clusters of its own launch."""
+    m, n, k = 1024, 4096, 1024
+    a, b, _ = gemm_ref.make_inputs(m, n, k, seed=79, b_scale=k ** -0.5)
+    da, db = a.cuda(), b.cuda()
+    d = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    gemm = make_gemm(256, (2, 1, 1))
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        gemm(da, db, d, None)  # plan and tensor maps built before capture
+    torch.cuda.synchronize()
+    ref = d.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        gemm(da, db, d, None)
+    for _ in range(3):
+        d.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(d, ref)
+    res = gemm_ref.check(ref.cpu(), a, b)
+    assert res["ok"], res

@@ -104,3 +104,41 @@ def test_wave_split_k_choices():
         assert kblocks // s >= 32
         assert units / (-(-units // slots) * slots) >= 0.85
     assert wave_split_k(4, 40, 148) is None  # too few k-blocks to split
+
+
+def test_capi_validate_dynamic_scheduler(lib):
+    """dynamic_scheduler is 0 or 1 and excludes reuse_ab (several tiles per CTA); the Python
+    constructor asserts the same."""
+    import ctypes
+    cfg = _lib.GemmConfigC(128, 256, 128, 32, 2, 1, 1, 1, 1, 4, 2, 1, 0, 1, 0, 8, 1)
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_OK
+    cfg.dynamic_scheduler = 2
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_ERR_INVALID_CONFIG
+    cfg.dynamic_scheduler = 1
+    cfg.reuse_ab, cfg.is_persistent = 1, 0
+    assert lib.cpg_config_validate(ctypes.byref(cfg)) == _lib.CPG_ERR_INVALID_CONFIG
+    with pytest.raises(AssertionError):
+        GemmSM90(tile_shape_mn=(128, 256), epi_tile_mn=(128, 32), cluster_shape_mnk=(1, 1, 1),
+                 atom_layout_mn=(1, 1), reuse_ab=True, is_persistent=False,
+                 dynamic_scheduler=True)
+    g = GemmSM90(tile_shape_mn=(128, 256), epi_tile_mn=(128, 32), cluster_shape_mnk=(2, 1, 1),
+                 atom_layout_mn=(1, 1), reuse_ab=False, is_persistent=False,
+                 dynamic_scheduler=True)
+    assert g._config_c().dynamic_scheduler == 1
+    g.validate()
+
+
+def test_auto_split_k_avoids_stream_k_when_dynamic(monkeypatch):
+    """Stream-K partitions the k-blocks statically, so the automatic split of a dynamic-schedule
+    GEMM picks K ranges instead (decode-like M = 128, N = K = 8192 would take Stream-K)."""
+    from cutedsl_pingpong_gemm_b200.gemm_base import CompiledGemm
+    for dyn, want_stream in ((False, True), (True, False)):
+        g = GemmSM90(tile_shape_mn=(128, 128), epi_tile_mn=(128, 32), cluster_shape_mnk=(1, 1, 1),
+                     atom_layout_mn=(1, 1), ab_stage=6, reuse_ab=False, is_persistent=True,
+                     dynamic_scheduler=dyn)
+        g._max_active_clusters = 148  # B200: one CTA per SM (no GPU here)
+        c = CompiledGemm.__new__(CompiledGemm)
+        c.gemm = g
+        s = c.auto_split_k(128, 8192, 8192)
+        assert (s == _lib.CPG_SPLIT_K_STREAM) == want_stream, (dyn, s)
+        assert s != 0
