@@ -17,9 +17,10 @@ LIB_NAME = "libcpgemm.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
 SOURCES = [os.path.join(CSRC, "capi.cu")]
-DEPENDS = SOURCES + [
-    os.path.join(CSRC, f) for f in ("gemm_kernel.cuh", "ptx.cuh", "tile_scheduler.h", "fast_divmod.h")
-] + [os.path.join(INCLUDE, "cpgemm.h")]
+# Every source and header of csrc/ and the public header: a change to any of them rebuilds.
+DEPENDS = SOURCES + sorted(
+    os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))
+) + [os.path.join(INCLUDE, "cpgemm.h")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
