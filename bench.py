@@ -91,6 +91,9 @@ def parse_args():
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each timed step from a CUDA graph captured through the public "
                          "API (auto: for the launch-bound small-M workload)")
+    ap.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
+                    help="tallk at N > 1: NCCL reduce-scatter of the FP32 partials, or p2p: the "
+                         "GEMM epilogue adds them into the owning rank's memory over NVLink")
     ap.add_argument("--scheduler", choices=["auto", "static", "dynamic"], default="auto",
                     help="tile schedule: the reference's static persistent schedule, or dynamic "
                          "(cluster launch control; not with Stream-K).  auto: "
@@ -339,7 +342,7 @@ def run_tallk(args, world, rank, local):
     into fp32 partials, one NCCL reduce-scatter sums them, the cast kernel writes BF16 rows."""
     import torch
     from cutedsl_pingpong_gemm_b200 import GemmSM90, RasterOrder
-    from cutedsl_pingpong_gemm_b200.sharding import SplitKGemm, k_ranges, row_range
+    from cutedsl_pingpong_gemm_b200.sharding import PeerSplitK, SplitKGemm, k_ranges, row_range
 
     w = WORKLOADS[args.workload]
     m, n, k = w["m"], w["n"], w["k"]
@@ -357,14 +360,23 @@ def run_tallk(args, world, rank, local):
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True,
                     dynamic_scheduler=args.scheduler == "dynamic")
     chunks = max(1, args.chunks)
-    # The in-GPU split of each (chunk's) GEMM is picked from its tile count (auto_split_k).
-    sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=0, chunks=chunks)
+    peer = args.exchange == "p2p" and world > 1
+    if peer:
+        # The GEMM epilogue adds the partials into the owners' memory; one finish kernel each.
+        sk = PeerSplitK(gemm, world, rank, local_split_k=0)
+        chunks = 1
+    else:
+        # The in-GPU split of each (chunk's) GEMM is picked from its tile count (auto_split_k).
+        sk = SplitKGemm.on_gpu(gemm, world, rank, local_split_k=0, chunks=chunks)
 
     launches = [0]
 
     def step():
         out = sk(a_k, b_k, m, n)
-        launches[0] += 2 * len(sk.column_chunks(n)) if chunks > 1 else 2  # GEMM + cast each
+        if peer:
+            launches[0] += 2  # GEMM (exchange in its epilogue) + finish
+        else:
+            launches[0] += 2 * len(sk.column_chunks(n)) if chunks > 1 else 2  # GEMM + cast each
         return out
 
     for _ in range(args.warmup):
@@ -398,7 +410,10 @@ def run_tallk(args, world, rank, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": args.workload, "m": m, "n": n, "k": k,
-                       "parallelism": f"split-K x{world} (NCCL reduce-scatter), auto in-GPU split",
+                       "parallelism": (f"split-K x{world} (GEMM epilogue adds partials into the "
+                                       f"owners' memory over NVLink), auto in-GPU split" if peer
+                                       else f"split-K x{world} (NCCL reduce-scatter), auto "
+                                       f"in-GPU split"),
                        "rs_chunks": chunks, "scheduler": args.scheduler,
                        "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
                        "rows_per_rank": s1 - s0, "l2": "inputs 512 MiB per rank at 1 GPU; no flush"},
@@ -412,6 +427,9 @@ def run_tallk(args, world, rank, local):
         }
         print(json.dumps(line), flush=True)
     del out
+    if peer:
+        sk.check_status()
+        sk.close()
 
 
 # ------------------------------------------------------------------ GPU arm: grouped (MoE)

@@ -41,7 +41,7 @@ CPG_ACT_GELU_TANH = 4
 ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
                "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
 
-ABI_VERSION = 11
+ABI_VERSION = 12
 
 
 class CpgError(RuntimeError):
@@ -108,6 +108,20 @@ class EpilogueC(ctypes.Structure):
                 ("batch_stride_source", ctypes.c_int64)]
 
 
+CPG_MAX_PEERS = 8
+
+
+class IpcHandleC(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint8 * 64)]
+
+
+class ReduceScatterC(ctypes.Structure):
+    _fields_ = [("ranks", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("row_start", ctypes.c_int64 * (CPG_MAX_PEERS + 1)), ("ld", ctypes.c_int64),
+                ("dst", ctypes.c_void_p * CPG_MAX_PEERS),
+                ("count", ctypes.c_void_p * CPG_MAX_PEERS)]
+
+
 _P = ctypes.POINTER
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -140,6 +154,15 @@ SIGNATURES = {
     "cpg_cast_f32_bf16": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "cpg_gemm_splitk_static": (ctypes.c_int, [_P(GemmConfigC), _P(GemmProblemC), _vp, _vp, _vp,
                                               _P(EpilogueC), _vp]),
+    "cpg_peer_alloc": (ctypes.c_int, [_i64, _P(_vp), _P(IpcHandleC)]),
+    "cpg_peer_open": (ctypes.c_int, [_P(IpcHandleC), _P(_vp)]),
+    "cpg_peer_close": (ctypes.c_int, [_vp]),
+    "cpg_peer_free": (ctypes.c_int, [_vp]),
+    "cpg_gemm_run_reduce_scatter": (ctypes.c_int, [_vp, _vp, _vp, _P(ReduceScatterC),
+                                                   _P(EpilogueC), _vp]),
+    "cpg_gemm_rs_arrivals": (ctypes.c_int, [_vp, _P(ReduceScatterC), _P(ctypes.c_uint32)]),
+    "cpg_peer_finish": (ctypes.c_int, [_vp, _i64, _vp, ctypes.c_uint32, _i64, _i64, _vp, _i64,
+                                       _vp, _vp, _i32, _vp]),
     "cpg_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "cpg_last_error_message": (ctypes.c_char_p, []),
     "cpg_abi_version": (ctypes.c_int, []),

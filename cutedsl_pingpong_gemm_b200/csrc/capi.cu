@@ -14,6 +14,7 @@
 #include "cpgemm.h"
 #include "gemm_fp8_block.cuh"
 #include "gemm_kernel.cuh"
+#include "peer_kernels.cuh"
 #include "quant_kernels.cuh"
 
 namespace {
@@ -340,7 +341,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 11; }
+int cpg_abi_version(void) { return 12; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -772,7 +773,8 @@ int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
 }
 
 static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
-                    void* stream, const int32_t* group_offsets);
+                    void* stream, const int32_t* group_offsets,
+                    const cpg_reduce_scatter* rs = nullptr);
 
 int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
                  void* stream) {
@@ -794,7 +796,7 @@ int cpg_gemm_run_grouped(cpg_gemm* g, const void* a, const void* b, void* d,
 }
 
 static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
-                    void* stream, const int32_t* group_offsets) {
+                    void* stream, const int32_t* group_offsets, const cpg_reduce_scatter* rs) {
   const cpg_gemm_problem& pr = g->prob;
   if (pr.m == 0 || pr.n == 0) return CPG_OK;
   if (d == nullptr) return fail(CPG_ERR_NULL, "D is NULL");
@@ -929,6 +931,18 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
   p.num_splits = g->splits;
   p.d = d;
   p.ldd = pr.ldd;
+  if (rs != nullptr) {
+    // Peer reduce-scatter: the epilogue adds into the owners' buffers (checked by the caller);
+    // D is not written, so nothing is cleared here.
+    p.reduce_add = 0;
+    p.rs_ranks = rs->ranks;
+    for (int q = 0; q <= rs->ranks; ++q) p.rs_row_start[q] = static_cast<int32_t>(rs->row_start[q]);
+    p.rs_ld = rs->ld;
+    for (int q = 0; q < rs->ranks; ++q) {
+      p.rs_dst[q] = rs->dst[q];
+      p.rs_count[q] = rs->count[q];
+    }
+  }
   if (g->groups > 0) {
     p.num_groups = static_cast<int32_t>(g->groups);
     p.group_offsets = group_offsets;
@@ -941,7 +955,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     if (e != cudaSuccess) return cuda_fail(e, "group tile prefix launch");
   }
 
-  if (g->splits > 1 || (g->stream_k && !g->fixup)) {
+  if ((g->splits > 1 || (g->stream_k && !g->fixup)) && rs == nullptr) {
     // The splits / Stream-K segments add their partial sums into D.
     for (int64_t bt = 0; bt < g->batches; ++bt) {
       cudaError_t e = cudaMemset2DAsync(static_cast<char*>(d) + bt * pr.batch_stride_d * ed,
@@ -1161,6 +1175,145 @@ int cpg_quantize_e4m3(const void* x, int32_t dtype_x, int64_t rows, int64_t cols
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CPG_OK : cuda_fail(e, "quantize launch");
+}
+
+// ------------------------------------------------------------ reduce-scatter over peer memory
+static_assert(sizeof(cpg_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+static_assert(CPG_MAX_PEERS == cpg::kMaxPeers, "peer count");
+
+int cpg_peer_alloc(int64_t bytes, void** dev_ptr, cpg_ipc_handle* handle) {
+  if (dev_ptr == nullptr || handle == nullptr) return fail(CPG_ERR_NULL, "NULL argument");
+  *dev_ptr = nullptr;
+  if (bytes <= 0) return fail(CPG_ERR_INVALID_SHAPE, "bytes must be positive");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer buffer)");
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer buffer setup");
+  }
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *dev_ptr = p;
+  return CPG_OK;
+}
+
+int cpg_peer_open(const cpg_ipc_handle* handle, void** dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr) return fail(CPG_ERR_NULL, "NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *dev_ptr = p;
+  return CPG_OK;
+}
+
+int cpg_peer_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) return CPG_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int cpg_peer_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return CPG_OK;
+  cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "cudaFree(peer buffer)");
+}
+
+static int check_reduce_scatter(const cpg_gemm* g, const cpg_reduce_scatter* rs) {
+  if (g == nullptr || rs == nullptr) return fail(CPG_ERR_NULL, "plan and rs must be non-NULL");
+  const cpg_gemm_problem& pr = g->prob;
+  if (pr.dtype_d != CPG_DTYPE_F32 || g->stream_k || g->groups > 0 || g->batches > 1 ||
+      pr.gated || g->v.scale_mode != CPG_SCALE_TENSOR)
+    return fail(CPG_ERR_UNSUPPORTED,
+                "the peer reduce-scatter needs an FP32-output plan without Stream-K, batches, "
+                "groups, gating or block scales");
+  if (rs->ranks < 1 || rs->ranks > CPG_MAX_PEERS || rs->rank < 0 || rs->rank >= rs->ranks)
+    return fail(CPG_ERR_INVALID_CONFIG, "rank %d of %d ranks (at most %d)", rs->rank, rs->ranks,
+                CPG_MAX_PEERS);
+  if (rs->row_start[0] != 0 || rs->row_start[rs->ranks] != pr.m)
+    return fail(CPG_ERR_INVALID_SHAPE, "row_start must run from 0 to M = %lld",
+                static_cast<long long>(pr.m));
+  for (int q = 0; q < rs->ranks; ++q) {
+    if (rs->row_start[q + 1] < rs->row_start[q])
+      return fail(CPG_ERR_INVALID_SHAPE, "row_start must not decrease");
+    if (q > 0 && rs->row_start[q] != pr.m && rs->row_start[q] % cpg::kBM != 0)
+      return fail(CPG_ERR_ALIGNMENT, "row blocks must start on 128-row tiles (or at M)");
+    if (rs->dst[q] == nullptr || rs->count[q] == nullptr)
+      return fail(CPG_ERR_NULL, "dst[%d] and count[%d] must be non-NULL", q, q);
+    if ((reinterpret_cast<uintptr_t>(rs->dst[q]) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(rs->count[q]) & 3u) != 0)
+      return fail(CPG_ERR_ALIGNMENT, "dst 16-byte and count 4-byte aligned");
+  }
+  if (pr.n % 4 != 0 || rs->ld < pr.n || rs->ld % 4 != 0)
+    return fail(CPG_ERR_ALIGNMENT, "N and ld must be multiples of 4 (16-byte atomics), ld >= N");
+  return CPG_OK;
+}
+
+int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
+                                const cpg_reduce_scatter* rs, const cpg_epilogue* epi,
+                                void* stream) {
+  int rc = check_reduce_scatter(g, rs);
+  if (rc != CPG_OK) return rc;
+  const cpg_gemm_problem& pr = g->prob;
+  if (epi != nullptr &&
+      (epi->bias != nullptr || epi->activation != CPG_ACT_NONE || epi->source != nullptr))
+    return fail(CPG_ERR_UNSUPPORTED, "bias, activations and C belong to cpg_peer_finish");
+  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;  // no arrivals (cpg_gemm_rs_arrivals)
+  // The output tensor map is built on this rank's buffer and never used for stores.
+  return run_impl(g, a, b, rs->dst[rs->rank], epi, stream, nullptr, rs);
+}
+
+int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32_t* per_rank) {
+  int rc = check_reduce_scatter(g, rs);
+  if (rc != CPG_OK) return rc;
+  if (per_rank == nullptr) return fail(CPG_ERR_NULL, "per_rank is NULL");
+  for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
+  const cpg_gemm_problem& pr = g->prob;
+  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
+  // Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
+  // runs once per K range; each of its 4 epilogue warps arrives once on its rows' owner.
+  const int64_t cta_rows = int64_t(g->sched.ncluster_m) * g->cfg.cluster_m;
+  const int64_t cta_cols = int64_t(g->sched.ncluster_n) * g->cfg.cluster_n;
+  const int64_t per_tile = int64_t(cpg::kEpiWarps) * cta_cols * g->sched.ncluster_l;
+  for (int64_t i = 0; i < cta_rows; ++i) {
+    const int64_t row = i * cpg::kBM;
+    int owner = rs->ranks - 1;
+    for (int q = 0; q < rs->ranks; ++q) {
+      if (row < rs->row_start[q + 1]) {
+        owner = q;
+        break;
+      }
+    }
+    per_rank[owner] += static_cast<uint32_t>(per_tile);
+  }
+  return CPG_OK;
+}
+
+int cpg_peer_finish(float* w, int64_t ldw, const uint32_t* count, uint32_t target, int64_t rows,
+                    int64_t cols, void* d, int64_t ldd, const void* bias, int32_t* status,
+                    int32_t timeout_ms, void* stream) {
+  if (rows < 0 || cols < 0 || ldw < cols || ldd < cols)
+    return fail(CPG_ERR_INVALID_SHAPE, "bad extents");
+  if (cols % 4 != 0 || ldw % 4 != 0 || ldd % 4 != 0)
+    return fail(CPG_ERR_ALIGNMENT, "cols, ldw and ldd must be multiples of 4");
+  if (count == nullptr || status == nullptr) return fail(CPG_ERR_NULL, "count and status");
+  if (timeout_ms <= 0) return fail(CPG_ERR_INVALID_SHAPE, "timeout must be positive");
+  if (rows > 0 && cols > 0 && (w == nullptr || d == nullptr))
+    return fail(CPG_ERR_NULL, "w and d must be non-NULL");
+  if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (reinterpret_cast<uintptr_t>(d) & 7u) != 0)
+    return fail(CPG_ERR_ALIGNMENT, "w 16-byte and d 8-byte aligned");
+  // At least one CTA waits even without rows, so a finish always observes its call's arrivals.
+  const int64_t blocks = rows < 1 ? 1 : (rows < 1024 ? rows : 1024);
+  cpg::peer_finish_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(
+      w, ldw, count, target, rows, cols, static_cast<__nv_bfloat16*>(d), ldd,
+      static_cast<const __nv_bfloat16*>(bias), status, uint64_t(timeout_ms) * 1000000ull);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "peer finish launch");
 }
 
 int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, void* y,

@@ -82,6 +82,7 @@ constexpr int kMaxStages = 12;
 constexpr int kMaxEpiStages = 4;
 constexpr int kMinSmemForOneCtaPerSm = 116 * 1024;
 constexpr int kWorkSlots = 4;    // dynamic scheduling: entries of the work ring
+constexpr int kMaxPeers = 8;     // reduce-scatter over peer memory: ranks
 constexpr int kDynBytes = 16 * kWorkSlots + 16 + 16 + 4 * kWorkSlots;  // DynLayout
 
 // Wait-site identifiers recorded in the status word on a timeout.
@@ -95,6 +96,7 @@ enum WaitSite : int32_t {
   kSiteWorkFull = 7,    // dynamic scheduling: waiting for the next work entry
   kSiteWorkEmpty = 8,   // dynamic scheduling: waiting for a free work entry
   kSiteClc = 9,         // dynamic scheduling: waiting for a cluster launch control response
+  kSitePeerArrivals = 10,  // peer reduce-scatter: the owner waiting for the ranks' tiles
 };
 
 struct GemmParams {
@@ -150,6 +152,15 @@ struct GemmParams {
   // Dynamic scheduling (cluster launch control, WorkScheduler): the grid holds one cluster per
   // cluster tile along x and running clusters take over clusters that have not started.
   int32_t dynamic;
+  // Reduce-scatter over peer memory (rs_ranks > 0): every segment adds alpha * acc into the FP32
+  // buffer of the rank that owns its rows (rows [rs_row_start[q], rs_row_start[q + 1]) belong to
+  // rank q, stored from row 0 of rs_dst[q] with row stride rs_ld), with system-scope atomics
+  // over NVLink, then each epilogue warp counts itself on the owner's rs_count (release).
+  int32_t rs_ranks;
+  int32_t rs_row_start[kMaxPeers + 1];
+  int64_t rs_ld;
+  float* rs_dst[kMaxPeers];
+  uint32_t* rs_count[kMaxPeers];
 };
 
 // The grouped mode of the segment iterator (num_groups == 0: the scheduler's tiles).
@@ -1109,6 +1120,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // This warp's 32 workspace rows (the CTA tile's workspace tile; partial segments only).
       const int32_t ws_tile = partial ? (sg.cid - si.dp_tiles) * cluster_ctas + cta_in_cluster : 0;
       const int32_t ws_row = ws_tile * kBM + static_cast<int32_t>(row_in_tile);
+      // Reduce-scatter over peer memory: the rank owning this warp's rows (row blocks are whole
+      // 128-row tiles, so all 32 rows have one owner; rows past M count for the last rank) and
+      // the first of its rows in that rank's buffer.
+      const bool rs = sizeof(OutT) == 4 && p.rs_ranks > 0;  // FP32 partial sums only
+      int32_t rs_owner = 0;
+      float* rs_rows = nullptr;
+      if (rs) {
+        rs_owner = p.rs_ranks - 1;
+        for (int32_t q = 0; q < p.rs_ranks; ++q) {
+          if (g_row < p.rs_row_start[q + 1]) {
+            rs_owner = q;
+            break;
+          }
+        }
+        rs_rows = p.rs_dst[rs_owner] +
+                  static_cast<int64_t>(g_row - p.rs_row_start[rs_owner]) * p.rs_ld;
+      }
 
       // Stage 32 rows x 128 bytes of this warp's output (thread = row) in the next staging
       // buffer; returns the buffer's shared-memory address.
@@ -1227,10 +1255,41 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           continue;
         }
+        if (rs) {
+          // Add alpha * acc into the owner's buffer, 32 FP32 columns (128 bytes) per staging
+          // buffer, copied out 4 rows x 128 bytes per warp instruction (coalesced atomics).
+#pragma unroll
+          for (int sub = 0; sub < kStoreCols / 32; ++sub) {
+            uint32_t words[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) words[i] = __float_as_uint(x[32 * sub + i]);
+            const uint32_t sbuf = stage(words);
+            const int32_t cbase = col0 + 32 * sub;
+            const int32_t ch = static_cast<int32_t>(lane & 7u);
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int32_t r = it * 4 + static_cast<int32_t>(lane >> 3);
+              const int32_t col = cbase + 4 * ch;
+              if (g_row + r < row_end && col < p.n) {
+                const uint4 v = ptx::ld_shared_v4(
+                    sbuf + static_cast<uint32_t>(r * 128 + ((ch ^ (r & 7)) << 4)));
+                ptx::red_add_sys_v4(rs_rows + static_cast<int64_t>(r) * p.rs_ld + col, v);
+              }
+            }
+            __syncwarp();
+          }
+          continue;
+        }
         if (add_bias) add_bias_row(x, col0);
         if (has_src) add_row_chunk<OutT>(p.beta, cs, x);
         if (!gated) act_inplace(p.act, x);
         store_chunk(x, col0);
+      }
+      if (rs) {
+        // Every lane's atomics before the warp's arrival on the owner's count (system scope).
+        ptx::fence_sc_sys();
+        __syncwarp();
+        if (lane == 0) ptx::red_release_sys_add_u32(p.rs_count[rs_owner], 1u);
       }
       if (partial) {
         // Count this segment's k-blocks for its 32 rows; the warp that completes the count owns

@@ -9,6 +9,10 @@ Two decompositions of D = A . B^T (the reference has none; it is a single-GPU ke
   an fp32 partial [M, N] with the same kernel (fp32 epilogue), the partials are summed with one
   NCCL reduce-scatter over NVLink (rank r receives rows ``row_range(M, world, r)``), and a cast
   kernel rounds the reduced rows to BF16.
+* ``PeerSplitK`` -- the same split-K without the collective: each rank's GEMM epilogue adds its
+  FP32 partial tiles straight into the buffer of the rank owning their rows (NVLink atomics into
+  memory mapped between the processes), overlapping the exchange with the next tiles' math, and
+  each rank rounds its own rows once every rank's tiles have arrived.
 
 The range arithmetic is plain Python so that the decomposition can be exercised on CPU ranks
 (gloo) with any per-rank compute function; the GPU compute always goes through the C ABI.
@@ -197,3 +201,182 @@ class SplitKGemm:
         else:
             self.cast_fn(rows, cs, ce, out[:, cs:ce])
         return out
+
+
+def peer_row_starts(m: int, world: int) -> List[int]:
+    """Row block boundaries of the split-K output: rank q owns rows [starts[q], starts[q + 1])
+    (``row_range``), so starts[0] = 0 and starts[world] = m."""
+    return [row_range(m, world, q)[0] for q in range(world)] + [m]
+
+
+class PeerSplitK:
+    """Split-K across ranks with the reduce-scatter done by the GEMM's epilogue over peer memory.
+
+    Rank r passes its K range of A and B (``k_ranges``); the sm_100a GEMM adds every FP32
+    partial tile into the owning rank's buffer (``cpg_gemm_run_reduce_scatter``) and counts
+    itself there; ``cpg_peer_finish`` then waits on this rank's counter for every rank's tiles
+    and writes this rank's rows of D in BF16 (+ bias), clearing its buffer.  Two buffers per rank
+    alternate between calls, so a rank that runs one call ahead adds into the other one; the
+    counter only grows, and each finish waits for the running total of arrivals.
+
+    The buffers are ``cudaMalloc`` memory mapped into the other processes with CUDA IPC handles
+    exchanged once per shape over ``group`` (no multicast objects).  Needs N a multiple of 4 and
+    GPUs that can map each other's memory (NVLink / NVSwitch).  ``close()`` (collective) frees
+    everything; call it on every rank before the process group goes away.
+    """
+
+    def __init__(self, gemm, world: int, rank: int, group=None, bias=None, local_split_k: int = 0,
+                 timeout_ms: int = 10000):
+        if world > 8:
+            raise ValueError("at most 8 ranks")
+        self.gemm = gemm
+        self.world, self.rank, self.group = world, rank, group
+        self.bias = bias
+        self.local_split_k = local_split_k
+        self.timeout_ms = int(timeout_ms)
+        self._states = {}
+        self._status = None
+
+    # -------------------------------------------------------------- setup (once per shape)
+    def _split(self, compiled, m: int, n: int, k: int) -> int:
+        from . import _lib
+        if self.local_split_k > 0:
+            return self.local_split_k
+        s = compiled.auto_split_k(m, n, k)
+        if s < 1:
+            # Stream-K cuts tiles into partial ranges; the exchange counts whole (tile, K range)
+            # segments, so take K ranges (about three waves of them) instead.
+            gemm = self.gemm
+            cm, cn, _ = gemm.cluster_shape_mnk
+            col_tiles = -(-n // gemm.cta_tile_shape_mnk[1])
+            tiles = -(-m // (128 * cm)) * -(-col_tiles // cn)
+            kblocks = -(-k // 64)
+            s = max(1, min(-(-3 * gemm.max_active_clusters // max(tiles, 1)), kblocks // 4))
+        return s
+
+    def _state(self, a_k, b_k, m: int, n: int):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        from .gemm_base import CompiledGemm, _Plan
+        k = a_k.shape[1]
+        dev = a_k.device
+        key = (m, n, k, a_k.stride(0), b_k.stride(0), dev.index)
+        st = self._states.get(key)
+        if st is not None:
+            return st
+        if n % 4 != 0:
+            raise _lib.CpgError(_lib.CPG_ERR_ALIGNMENT, "the peer reduce-scatter needs N % 4 == 0")
+        lib = _lib.load()
+        starts = peer_row_starts(m, self.world)
+        ld = n
+        rows_max = max(starts[q + 1] - starts[q] for q in range(self.world))
+        compiled = CompiledGemm(self.gemm)
+        split = self._split(compiled, m, n, k)
+        dt_ab = {torch.bfloat16: _lib.CPG_DTYPE_BF16, torch.float8_e4m3fn: _lib.CPG_DTYPE_E4M3}[a_k.dtype]
+        lda = a_k.stride(0) if m > 1 else max(8, k)
+        ldb = b_k.stride(0) if n > 1 else max(8, k)
+        plan = _Plan(self.gemm, m, n, k, lda, ldb, ld, dev.index, dt_ab, _lib.CPG_DTYPE_F32, 0,
+                     split)
+        # Two buffers of this rank's rows and one 64-byte counter, mapped by every rank.
+        own, handles = [], []
+        for nbytes in (max(rows_max, 1) * ld * 4, max(rows_max, 1) * ld * 4, 64):
+            ptr, h = ctypes.c_void_p(), _lib.IpcHandleC()
+            _lib.check(lib.cpg_peer_alloc(nbytes, ctypes.byref(ptr), ctypes.byref(h)), "peer_alloc")
+            own.append(ptr.value)
+            handles.append(bytes(h.bytes))
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=self.group)
+        opened, mapped = [], []
+        for q in range(self.world):
+            if q == self.rank:
+                mapped.append(list(own))
+                continue
+            row = []
+            for hb in gathered[q]:
+                h = _lib.IpcHandleC()
+                ctypes.memmove(h.bytes, hb, 64)
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.cpg_peer_open(ctypes.byref(h), ctypes.byref(ptr)), "peer_open")
+                opened.append(ptr.value)
+                row.append(ptr.value)
+            mapped.append(row)
+        rs = []
+        for buf in range(2):
+            r = _lib.ReduceScatterC()
+            r.ranks, r.rank, r.ld = self.world, self.rank, ld
+            for q in range(self.world + 1):
+                r.row_start[q] = starts[q]
+            for q in range(self.world):
+                r.dst[q] = mapped[q][buf]
+                r.count[q] = mapped[q][2]
+            rs.append(r)
+        per_rank = (ctypes.c_uint32 * self.world)()
+        _lib.check(lib.cpg_gemm_rs_arrivals(plan.handle, ctypes.byref(rs[0]), per_rank),
+                   "rs_arrivals")
+        all_arrivals = [None] * self.world
+        dist.all_gather_object(all_arrivals, list(per_rank), group=self.group)
+        expected = sum(arr[self.rank] for arr in all_arrivals) & 0xFFFFFFFF
+        if self._status is None:
+            self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = dict(plan=plan, rs=rs, own=own, opened=opened, expected=expected, calls=0,
+                  rows=(starts[self.rank], starts[self.rank + 1]), ld=ld, split=split)
+        self._states[key] = st
+        return st
+
+    # -------------------------------------------------------------- one call
+    def __call__(self, a_k, b_k, m: int, n: int, stream=None):
+        """This rank's rows of D = A . B^T (BF16, + bias), from its K range ``a_k`` [M, k_r],
+        ``b_k`` [N, k_r]."""
+        import ctypes
+        import torch
+        from . import _lib
+        from .gemm_base import _stream_handle
+        st = self._state(a_k, b_k, m, n)
+        lib = _lib.load()
+        dev = a_k.device
+        h = _stream_handle(stream, dev)
+        buf = st["calls"] % 2
+        epi = _lib.EpilogueC(1.0, None, None, None, 0.0, 0, None, 0, 0)
+        _lib.check(lib.cpg_gemm_run_reduce_scatter(
+            st["plan"].handle, a_k.data_ptr() if a_k.numel() else None,
+            b_k.data_ptr() if b_k.numel() else None, ctypes.byref(st["rs"][buf]),
+            ctypes.byref(epi), h), "gemm_run_reduce_scatter")
+        st["calls"] += 1
+        target = (st["calls"] * st["expected"]) & 0xFFFFFFFF
+        r0, r1 = st["rows"]
+        out = torch.empty(r1 - r0, n, dtype=torch.bfloat16, device=dev)
+        bias = self.bias
+        _lib.check(lib.cpg_peer_finish(st["own"][buf], st["ld"], st["own"][2], target, r1 - r0, n,
+                                       out.data_ptr() if out.numel() else None, n,
+                                       None if bias is None else bias.data_ptr(),
+                                       self._status.data_ptr(), self.timeout_ms, h),
+                   "peer_finish")
+        return out
+
+    def check_status(self) -> None:
+        """Raise if a finish gave up waiting for the other ranks (synchronises)."""
+        from . import _lib
+        if self._status is not None and int(self._status.item()) != 0:
+            raise _lib.CpgError(_lib.CPG_ERR_DEVICE_TIMEOUT,
+                                f"peer reduce-scatter status {int(self._status.item()):#x}")
+
+    def close(self) -> None:
+        """Collective: wait for every rank, then unmap the peers' buffers and free this rank's."""
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        if not self._states:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = _lib.load()
+        for st in self._states.values():
+            for ptr in st["opened"]:
+                lib.cpg_peer_close(ptr)
+        dist.barrier(group=self.group)
+        for st in self._states.values():
+            for ptr in st["own"]:
+                lib.cpg_peer_free(ptr)
+        self._states.clear()

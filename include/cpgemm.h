@@ -290,6 +290,57 @@ int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm_problem* p
                            const void* a, const void* b, void* d, const cpg_epilogue* epi,
                            void* stream);
 
+/* ---- Split-K reduce-scatter over peer memory (NVLink) -------------------------------------
+ * The tall-K multi-GPU path without a separate collective: rank r multiplies its K range and
+ * its GEMM's epilogue adds every FP32 partial tile straight into the buffer of the rank that
+ * owns the tile's rows (system-scope atomics into the peer's memory, overlapping the next tiles'
+ * math), then counts itself on that rank's arrival counter; each rank finishes its own rows with
+ * cpg_peer_finish.  Replaces the NCCL reduce-scatter of the partials for ranks whose GPUs can
+ * map each other's memory.  No counterpart in the reference. */
+#define CPG_MAX_PEERS 8
+
+/* Opaque inter-process handle of a peer buffer (cudaIpcMemHandle_t). */
+typedef struct cpg_ipc_handle {
+  uint8_t bytes[64];
+} cpg_ipc_handle;
+
+/* Zeroed device memory other processes can map: cudaMalloc + memset + an IPC handle. */
+int cpg_peer_alloc(int64_t bytes, void** dev_ptr, cpg_ipc_handle* handle);
+/* Map another process's cpg_peer_alloc buffer into this one (on the current device). */
+int cpg_peer_open(const cpg_ipc_handle* handle, void** dev_ptr);
+int cpg_peer_close(void* dev_ptr);  /* unmap a cpg_peer_open mapping */
+int cpg_peer_free(void* dev_ptr);   /* free a cpg_peer_alloc buffer */
+
+typedef struct cpg_reduce_scatter {
+  int32_t ranks;                       /* 1..CPG_MAX_PEERS */
+  int32_t rank;                        /* this process's rank */
+  int64_t row_start[CPG_MAX_PEERS + 1]; /* rank q owns D rows [row_start[q], row_start[q + 1]):
+                                          row_start[0] = 0, row_start[ranks] = M, interior
+                                          boundaries multiples of 128 */
+  int64_t ld;                          /* row stride (elements) of every rank's buffer, >= N,
+                                          a multiple of 4 */
+  float* dst[CPG_MAX_PEERS];           /* rank q's FP32 buffer ([its rows, ld], zero before the
+                                          call) as mapped in this process */
+  uint32_t* count[CPG_MAX_PEERS];      /* rank q's arrival counter as mapped in this process */
+} cpg_reduce_scatter;
+
+/* Run a plan (dtype_d = CPG_DTYPE_F32, split_k >= 0, no Stream-K / batches / groups / gating,
+ * per-tensor scales only, N a multiple of 4) on this rank's K range, adding the partial sums
+ * into the owners' buffers; epi may carry alpha and FP8 scales (no bias, activation or C). */
+int cpg_gemm_run_reduce_scatter(cpg_gemm* plan, const void* a, const void* b,
+                                const cpg_reduce_scatter* rs, const cpg_epilogue* epi,
+                                void* stream);
+/* How much one cpg_gemm_run_reduce_scatter of this plan raises each rank's counter:
+ * per_rank[q] for q < rs->ranks (4 per CTA tile and K range whose rows rank q owns). */
+int cpg_gemm_rs_arrivals(const cpg_gemm* plan, const cpg_reduce_scatter* rs, uint32_t* per_rank);
+/* Owner side: wait (bounded by timeout_ms; on a timeout *status gets a nonzero code and nothing
+ * is written) until *count reaches target (modulo 2^32; the sum of every rank's arrivals on this
+ * rank over all calls so far), then d = bf16(w + bias) for rows x cols and w = 0.  cols, ldw and
+ * ldd multiples of 4; bias optional (BF16, length cols). */
+int cpg_peer_finish(float* w, int64_t ldw, const uint32_t* count, uint32_t target, int64_t rows,
+                    int64_t cols, void* d, int64_t ldd, const void* bias, int32_t* status,
+                    int32_t timeout_ms, void* stream);
+
 const char* cpg_strerror(int code);
 const char* cpg_last_error_message(void);
 /* ABI version, bumped on any incompatible change of this header. */

@@ -1,5 +1,6 @@
-"""Multi-GPU paths on real GPUs (NCCL): M-sharding with B replicated, and split-K with an NCCL
-reduce-scatter of fp32 partials followed by the BF16 cast kernel.
+"""Multi-GPU paths on real GPUs (NCCL): M-sharding with B replicated, split-K with an NCCL
+reduce-scatter of fp32 partials followed by the BF16 cast kernel, and split-K whose GEMM epilogue
+adds the partials into the owning ranks' memory over NVLink (PeerSplitK).
 
 Runs one process per visible GPU (at least two, otherwise skipped) with a short process-group
 timeout; each rank checks its rows against the fp32 CPU oracle.  NVLS is switched off
@@ -59,10 +60,37 @@ WORKER = textwrap.dedent(r'''
     torch.cuda.synchronize()
     res3 = gemm_ref.check(rows_c.cpu(), a2[r0:r1], b2)
     ok &= res3["ok"]
+    # Split-K with the reduce-scatter done by the GEMM epilogue over peer memory: three calls
+    # (alternating buffers, running arrival count), then a ragged M with bias under the dynamic
+    # schedule and an automatic in-GPU split.
+    from cutedsl_pingpong_gemm_b200.sharding import PeerSplitK
+    pk = PeerSplitK(gemm, world, rank, local_split_k=2)
+    res4 = None
+    for it in range(3):
+        rows_p = pk(a2[:, ks:ke].cuda().contiguous(), b2[:, ks:ke].cuda().contiguous(), m2, n2)
+        torch.cuda.synchronize()
+        res4 = gemm_ref.check(rows_p.cpu(), a2[r0:r1], b2)
+        ok &= res4["ok"] and rows_p.shape == (r1 - r0, n2)
+    pk.check_status()
+    m3, n3, k3 = 128 * (2 * world + 1) - 40, 1000, 6144
+    a3, b3, bias3 = gemm_ref.make_inputs(m3, n3, k3, seed=7, b_scale=k3 ** -0.5, with_bias=True)
+    ks3, ke3 = k_ranges(k3, world)[rank]
+    gemm_dyn = GemmSM90((128, 256), (128, 32), (2, 1, 1), (1, 1), ab_stage=6, reuse_ab=False,
+                        is_persistent=True, dynamic_scheduler=True)
+    pk3 = PeerSplitK(gemm_dyn, world, rank, bias=bias3.cuda(), local_split_k=0)
+    for it in range(2):
+        rows3 = pk3(a3[:, ks3:ke3].cuda().contiguous(), b3[:, ks3:ke3].cuda().contiguous(), m3, n3)
+        torch.cuda.synchronize()
+        q0, q1 = row_range(m3, world, rank)
+        res5 = gemm_ref.check(rows3.cpu(), a3[q0:q1], b3, bias=bias3)
+        ok &= res5["ok"] and rows3.shape == (q1 - q0, n3)
+    pk3.check_status()
+    pk.close()
+    pk3.close()
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
-        print("RESULT", int(flag.item()), res, res2, res3, flush=True)
+        print("RESULT", int(flag.item()), res, res2, res3, res4, res5, flush=True)
     dist.destroy_process_group()
     sys.exit(0 if ok else 1)
 ''')

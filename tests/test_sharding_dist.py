@@ -9,7 +9,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from cutedsl_pingpong_gemm_b200.sharding import (MShardedGemm, SplitKGemm, k_ranges,
-                                                  reduce_scatter_rows, row_range)
+                                                  peer_row_starts, reduce_scatter_rows, row_range)
 
 
 def test_row_range_partitions():
@@ -26,6 +26,20 @@ def test_row_range_partitions():
                 assert s % 128 == 0 or s == m
     # The LLM shape splits into equal 2048-row shards on 8 GPUs.
     assert [row_range(16384, 8, r) for r in range(8)] == [(2048 * r, 2048 * (r + 1)) for r in range(8)]
+
+
+def test_peer_row_starts():
+    """Row blocks of the peer reduce-scatter: contiguous, from 0 to M, interior boundaries on
+    128-row tiles (or at M for ranks left without rows), as cpg_gemm_run_reduce_scatter
+    requires."""
+    for m in (1, 129, 600, 2048, 16384 + 40):
+        for world in (1, 2, 3, 8):
+            st = peer_row_starts(m, world)
+            assert len(st) == world + 1 and st[0] == 0 and st[-1] == m
+            assert all(a <= b for a, b in zip(st, st[1:]))
+            assert all(x % 128 == 0 or x == m for x in st[1:-1])
+            assert [(st[q], st[q + 1]) for q in range(world)] == \
+                [row_range(m, world, q) for q in range(world)]
 
 
 def test_k_ranges_aligned():
