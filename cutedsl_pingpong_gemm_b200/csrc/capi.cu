@@ -400,6 +400,33 @@ int cpg_config_validate(const cpg_gemm_config* c) {
   return CPG_OK;
 }
 
+// One FP32 workspace tile (128 rows x the tile's output columns) and four k-block counts (one
+// per epilogue warp) per CTA of `tiles` cluster tiles, zero between launches: the tiles whose
+// k-blocks are shared by several segments (Stream-K, or split-K into peer memory) sum there.
+static int alloc_fixup_workspace(cpg_gemm* g, int64_t tiles) {
+  const int64_t ctas = int64_t(g->cfg.cluster_m) * g->cfg.cluster_n;
+  const int64_t ws_rows = tiles * ctas * 128;
+  const int64_t ws_cols = g->cfg.tile_n;
+  g->ws_bytes = ws_rows * ws_cols * 4;
+  g->cnt_bytes = tiles * ctas * 4 * 4;
+  cudaError_t e = cudaMalloc(&g->ws_dev, g->ws_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&g->cnt_dev, g->cnt_bytes);
+  if (e == cudaSuccess) e = cudaMemset(g->ws_dev, 0, g->ws_bytes);
+  if (e == cudaSuccess) e = cudaMemset(g->cnt_dev, 0, g->cnt_bytes);
+  const int rc = e == cudaSuccess
+                     ? encode_tiled(&g->tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g->ws_dev,
+                                    ws_rows, ws_cols, ws_cols, 32, cpg::kRowBytes / 4)
+                     : cuda_fail(e, "fixup workspace");
+  if (rc != CPG_OK) {
+    if (g->ws_dev) cudaFree(g->ws_dev);
+    if (g->cnt_dev) cudaFree(g->cnt_dev);
+    g->ws_dev = nullptr;
+    g->cnt_dev = nullptr;
+    g->ws_bytes = g->cnt_bytes = 0;
+  }
+  return rc;
+}
+
 int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
                     cpg_gemm** out) {
   if (cfg == nullptr || prob == nullptr || out == nullptr)
@@ -658,24 +685,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return cuda_fail(e, "cudaMemset(status word)");
   }
   if (sk_tiles > 0) {
-    // One FP32 workspace tile (128 rows x the tile's output columns) and four k-block counts
-    // (one per epilogue warp) per CTA of every Stream-K tile, zero between launches.
-    const int64_t ctas = int64_t(cfg->cluster_m) * cfg->cluster_n;
-    const int64_t ws_rows = sk_tiles * ctas * 128;
-    const int64_t ws_cols = cfg->tile_n;
-    g->ws_bytes = ws_rows * ws_cols * 4;
-    g->cnt_bytes = sk_tiles * ctas * 4 * 4;
-    e = cudaMalloc(&g->ws_dev, g->ws_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&g->cnt_dev, g->cnt_bytes);
-    if (e == cudaSuccess) e = cudaMemset(g->ws_dev, 0, g->ws_bytes);
-    if (e == cudaSuccess) e = cudaMemset(g->cnt_dev, 0, g->cnt_bytes);
-    int rc2 = e == cudaSuccess
-                  ? encode_tiled(&g->tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g->ws_dev, ws_rows,
-                                 ws_cols, ws_cols, 32, cpg::kRowBytes / 4)
-                  : cuda_fail(e, "Stream-K workspace");
+    const int rc2 = alloc_fixup_workspace(g, sk_tiles);
     if (rc2 != CPG_OK) {
-      if (g->ws_dev) cudaFree(g->ws_dev);
-      if (g->cnt_dev) cudaFree(g->cnt_dev);
       cudaFree(g->status_dev);
       delete g;
       return rc2;
@@ -935,6 +946,9 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     // Peer reduce-scatter: the epilogue adds into the owners' buffers (checked by the caller);
     // D is not written, so nothing is cleared here.
     p.reduce_add = 0;
+    // K ranges of a tile sum in the plan's workspace first; the last one sends the tile.
+    p.fixup = g->splits > 1 ? 1 : 0;
+    p.dp_tiles = 0;
     p.rs_ranks = rs->ranks;
     for (int q = 0; q <= rs->ranks; ++q) p.rs_row_start[q] = static_cast<int32_t>(rs->row_start[q]);
     p.rs_ld = rs->ld;
@@ -1263,6 +1277,18 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
       (epi->bias != nullptr || epi->activation != CPG_ACT_NONE || epi->source != nullptr))
     return fail(CPG_ERR_UNSUPPORTED, "bias, activations and C belong to cpg_peer_finish");
   if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;  // no arrivals (cpg_gemm_rs_arrivals)
+  if (g->splits > 1 && g->ws_dev == nullptr) {
+    // The K ranges of a tile are summed in this GPU's L2 first (the Stream-K fixup workspace,
+    // one tile per cluster tile of the problem), so each tile crosses to its owner once.
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != g->device)
+      return fail(CPG_ERR_NO_DEVICE, "current device %d differs from the plan's device %d", cur,
+                  g->device);
+    const int rc2 = alloc_fixup_workspace(
+        g, int64_t(g->sched.ncluster_m) * g->sched.ncluster_n);
+    if (rc2 != CPG_OK) return rc2;
+  }
   // The output tensor map is built on this rank's buffer and never used for stores.
   return run_impl(g, a, b, rs->dst[rs->rank], epi, stream, nullptr, rs);
 }
@@ -1275,10 +1301,11 @@ int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32
   const cpg_gemm_problem& pr = g->prob;
   if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
   // Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
-  // runs once per K range; each of its 4 epilogue warps arrives once on its rows' owner.
+  // sends its sum once (with K ranges, the last range to finish sends it); each of its 4
+  // epilogue warps then arrives once on its rows' owner.
   const int64_t cta_rows = int64_t(g->sched.ncluster_m) * g->cfg.cluster_m;
   const int64_t cta_cols = int64_t(g->sched.ncluster_n) * g->cfg.cluster_n;
-  const int64_t per_tile = int64_t(cpg::kEpiWarps) * cta_cols * g->sched.ncluster_l;
+  const int64_t per_tile = int64_t(cpg::kEpiWarps) * cta_cols;
   for (int64_t i = 0; i < cta_rows; ++i) {
     const int64_t row = i * cpg::kBM;
     int owner = rs->ranks - 1;

@@ -1094,7 +1094,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int32_t pid_m = sg.pid_m, pid_n = sg.pid_n;
       // Split-K / Stream-K into D: only the segment holding a tile's first k-block adds the bias.
       const bool add_bias = has_bias && sg.kb0 == 0;
-      // Stream-K with fixup: a segment with part of a tile's k-blocks adds into the workspace.
+      // Stream-K with fixup, and split-K into peer memory: a segment with part of a tile's
+      // k-blocks adds into the workspace.
       const bool partial = p.fixup != 0 && (sg.kb0 != 0 || sg.kb1 != p.k_iters);
       bool ok = ptx::mbar_wait(tfull_bar + 8u * acc, acc_phase, ctx, kSiteEpiTmemFull);
       ok = __all_sync(0xffffffffu, ok);
@@ -1118,7 +1119,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int out_cols = gated ? BN / 2 : BN;
       const int n_chunks = out_cols / kStoreCols;
       // This warp's 32 workspace rows (the CTA tile's workspace tile; partial segments only).
-      const int32_t ws_tile = partial ? (sg.cid - si.dp_tiles) * cluster_ctas + cta_in_cluster : 0;
+      // Stream-K numbers the split tiles after the data-parallel ones; split-K (L = K range)
+      // shares one workspace tile between the K ranges of a tile.
+      int32_t ws_cid = sg.cid - si.dp_tiles;
+      if (partial && !p.stream_k) {
+        int32_t l_idx;
+        fast_divmod(sp.dm_clusters_per_problem, sg.cid, l_idx, ws_cid);
+      }
+      const int32_t ws_tile = partial ? ws_cid * cluster_ctas + cta_in_cluster : 0;
       const int32_t ws_row = ws_tile * kBM + static_cast<int32_t>(row_in_tile);
       // Reduce-scatter over peer memory: the rank owning this warp's rows (row blocks are whole
       // 128-row tiles, so all 32 rows have one owner; rows past M count for the last rank) and
@@ -1189,6 +1197,38 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         __syncwarp();
       };
+      // Peer reduce-scatter: add x (kStoreCols FP32 columns of this thread's row) into the
+      // owner's buffer, 32 columns (128 bytes) per staging buffer, copied out 4 rows x 128 bytes
+      // per warp instruction (coalesced system-scope atomics).
+      auto rs_add_chunk = [&](const float (&x)[kStoreCols], int32_t col0) {
+#pragma unroll
+        for (int sub = 0; sub < kStoreCols / 32; ++sub) {
+          uint32_t words[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) words[i] = __float_as_uint(x[32 * sub + i]);
+          const uint32_t sbuf = stage(words);
+          const int32_t cbase = col0 + 32 * sub;
+          const int32_t ch = static_cast<int32_t>(lane & 7u);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int32_t r = it * 4 + static_cast<int32_t>(lane >> 3);
+            const int32_t col = cbase + 4 * ch;
+            if (g_row + r < row_end && col < p.n) {
+              const uint4 v = ptx::ld_shared_v4(
+                  sbuf + static_cast<uint32_t>(r * 128 + ((ch ^ (r & 7)) << 4)));
+              ptx::red_add_sys_v4(rs_rows + static_cast<int64_t>(r) * p.rs_ld + col, v);
+            }
+          }
+          __syncwarp();
+        }
+      };
+      // After this warp's last atomics of a tile: every lane's atomics before the warp's arrival
+      // on the owner's count (system scope).
+      auto rs_arrive = [&]() {
+        ptx::fence_sc_sys();
+        __syncwarp();
+        if (lane == 0) ptx::red_release_sys_add_u32(p.rs_count[rs_owner], 1u);
+      };
       auto add_bias_row = [&](float (&x)[kStoreCols], int32_t col0) {
         // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
         // they are broadcast across the warp with shuffles.
@@ -1256,28 +1296,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           continue;
         }
         if (rs) {
-          // Add alpha * acc into the owner's buffer, 32 FP32 columns (128 bytes) per staging
-          // buffer, copied out 4 rows x 128 bytes per warp instruction (coalesced atomics).
-#pragma unroll
-          for (int sub = 0; sub < kStoreCols / 32; ++sub) {
-            uint32_t words[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) words[i] = __float_as_uint(x[32 * sub + i]);
-            const uint32_t sbuf = stage(words);
-            const int32_t cbase = col0 + 32 * sub;
-            const int32_t ch = static_cast<int32_t>(lane & 7u);
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-              const int32_t r = it * 4 + static_cast<int32_t>(lane >> 3);
-              const int32_t col = cbase + 4 * ch;
-              if (g_row + r < row_end && col < p.n) {
-                const uint4 v = ptx::ld_shared_v4(
-                    sbuf + static_cast<uint32_t>(r * 128 + ((ch ^ (r & 7)) << 4)));
-                ptx::red_add_sys_v4(rs_rows + static_cast<int64_t>(r) * p.rs_ld + col, v);
-              }
-            }
-            __syncwarp();
-          }
+          rs_add_chunk(x, col0);
           continue;
         }
         if (add_bias) add_bias_row(x, col0);
@@ -1285,12 +1304,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (!gated) act_inplace(p.act, x);
         store_chunk(x, col0);
       }
-      if (rs) {
-        // Every lane's atomics before the warp's arrival on the owner's count (system scope).
-        ptx::fence_sc_sys();
-        __syncwarp();
-        if (lane == 0) ptx::red_release_sys_add_u32(p.rs_count[rs_owner], 1u);
-      }
+      if (rs && !partial) rs_arrive();
       if (partial) {
         // Count this segment's k-blocks for its 32 rows; the warp that completes the count owns
         // every other segment's sum (their reduces completed before their counts were added).
@@ -1325,9 +1339,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             // Clear the workspace tile for the next launch.
 #pragma unroll
             for (int q = 0; q < kStoreCols / 4; ++q) ptx::st_global_v4(src + 4 * q, 0u, 0u, 0u, 0u);
+            if (rs) {
+              rs_add_chunk(x, col0);  // the tile's sum crosses to its owner once
+              continue;
+            }
             if (has_bias) add_bias_row(x, col0);
             store_chunk(x, col0);
           }
+          if (rs) rs_arrive();
           if (lane == 0) p.fixup_count[cnt_idx] = 0;
         }
       }
