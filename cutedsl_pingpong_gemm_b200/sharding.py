@@ -220,9 +220,11 @@ class PeerSplitK:
     counter only grows, and each finish waits for the running total of arrivals.
 
     The buffers are ``cudaMalloc`` memory mapped into the other processes with CUDA IPC handles
-    exchanged once per shape over ``group`` (no multicast objects).  Needs N a multiple of 4 and
-    GPUs that can map each other's memory (NVLink / NVSwitch).  ``close()`` (collective) frees
-    everything; call it on every rank before the process group goes away.
+    exchanged once per shape over ``group`` (no multicast objects), so the first call with a new
+    shape is collective: every rank makes its calls with the same shapes in the same order.
+    Needs N a multiple of 4 and GPUs that can map each other's memory (NVLink / NVSwitch).
+    ``check_status()`` raises if a finish gave up waiting (a rank missing); ``close()``
+    (collective) frees everything: call it on every rank before the process group goes away.
     """
 
     def __init__(self, gemm, world: int, rank: int, group=None, bias=None, local_split_k: int = 0,
