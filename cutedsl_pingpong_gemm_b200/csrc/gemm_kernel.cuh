@@ -24,7 +24,12 @@
 // Tile order: every role walks the same sequence of segments (SegmentIter): the tiles of the
 // shared scheduler header, identical to the reference's SimpleTileScheduler
 // (tile_scheduler.py:94-183) with its L index carrying batches and split-K ranges; Stream-K
-// ranges of the (tile, k-block) space; or the tiles of a grouped GEMM's ragged groups.
+// ranges of the (tile, k-block) space; or the tiles of a grouped GEMM's ragged groups.  With
+// the dynamic schedule the same linear tile ids come from cluster launch control instead of a
+// fixed stride (WorkScheduler / WorkReader below).
+//
+// FP32 outputs can also go to other GPUs: with rs_ranks > 0 the epilogue adds each tile into
+// the buffer of the rank that owns its rows, over NVLink (the split-K reduce-scatter).
 //
 // Every mbarrier wait is bounded (WaitCtx): on a timeout the kernel records an error code in the
 // status word, the other roles stop at their next wait, in-flight TMA loads and MMAs are drained
