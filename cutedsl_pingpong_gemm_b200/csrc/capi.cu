@@ -315,7 +315,7 @@ struct cpg_gemm {
   int32_t trace_stride;
   uint64_t timeout_ns;
   int32_t fault_inject;
-  int32_t l2_policy_a, l2_policy_b;
+  int32_t l2_policy_a, l2_policy_b, l2_policy_d;
   int32_t k_iters;
   int32_t k_iters_per_split;
   int32_t splits;
@@ -585,10 +585,14 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
       g->l2_policy_b = 2;
     }
   }
+  // D tiles are written once and never read back by the kernel.
+  g->l2_policy_d = 1;
   const char* pa = std::getenv("CPG_L2_POLICY_A");
   const char* pb = std::getenv("CPG_L2_POLICY_B");
+  const char* pd = std::getenv("CPG_L2_POLICY_D");
   if (pa != nullptr) g->l2_policy_a = std::atoi(pa);
   if (pb != nullptr) g->l2_policy_b = std::atoi(pb);
+  if (pd != nullptr) g->l2_policy_d = std::atoi(pd);
 
   const int64_t ntm = prob->m > 0 ? (prob->m + 127) / 128 : 1;
   // A gated tile stores 256 output columns (its 512 accumulator columns are gate and up).
@@ -933,6 +937,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
   p.fault_inject = g->fault_inject;
   p.l2_policy_a = g->l2_policy_a;
   p.l2_policy_b = g->l2_policy_b;
+  p.l2_policy_d = g->l2_policy_d;
   p.act = act;
   p.beta = epi != nullptr ? epi->beta : 0.f;
   p.src = src;

@@ -125,6 +125,7 @@ struct GemmParams {
   int32_t fault_inject;   // test hook: kInjectSkipLoads makes the producer issue no loads
   int32_t l2_policy_a;    // L2 eviction priority of A / B tile loads: 0 normal, 1 first, 2 last
   int32_t l2_policy_b;
+  int32_t l2_policy_d;    // ... of the D tile stores (D is written once and not read back)
   // Fused epilogue: D = act(alpha * acc + bias + beta * C); gated (512-wide tiles only):
   // D[:, n] = act(alpha * acc_gate[:, n]) * alpha * acc_up[:, n] with B = [W_gate; W_up].
   int32_t act;            // kActNone, kActRelu, kActSilu, kActGelu, kActGeluTanh
@@ -1061,7 +1062,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     float alpha = p.alpha;
     if (p.scale_a != nullptr) alpha *= *p.scale_a;
     if (p.scale_b != nullptr) alpha *= *p.scale_b;
+    const uint64_t pol_d = l2_policy(p.l2_policy_d);
     const bool has_bias = p.bias != nullptr;
+    // 16-byte aligned bias: the epilogue reads whole chunks of it with vector loads.
+    const bool bias_vec = has_bias && (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0;
     const bool has_src = p.src != nullptr;
     const bool gated = (BN == 512) && p.gated != 0;
     // Accumulator fully read into registers: hand the TMEM buffer back to the MMA warp.
@@ -1195,7 +1199,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (p.reduce_add) {
               ptx::tma_reduce_add_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
             } else {
-              ptx::tma_store_3d(&tm_d, sbuf, col0, g_row, sg.ab_batch);
+              ptx::tma_store_3d_hint(&tm_d, sbuf, col0, g_row, sg.ab_batch, pol_d);
             }
           }
           ptx::bulk_commit_group();
@@ -1235,8 +1239,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (lane == 0) ptx::red_release_sys_add_u32(p.rs_count[rs_owner], 1u);
       };
       auto add_bias_row = [&](float (&x)[kStoreCols], int32_t col0) {
-        // Lane l fetches bias[col0 + 32 h + l] (coalesced); every row needs all of them, so
-        // they are broadcast across the warp with shuffles.
+        if (bias_vec && col0 + kStoreCols <= p.n) {
+          // Every row needs the same kStoreCols values: all lanes load them with the same
+          // 16-byte loads (one broadcast request each) and unpack the BF16 pairs.
+          const __nv_bfloat16* bp = p.bias + col0;
+#pragma unroll
+          for (int q = 0; q < kStoreCols / 8; ++q) {
+            const uint4 w = ptx::ld_global_nc_v4(bp + 8 * q);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              x[8 * q + 2 * i] += __uint_as_float(ws[i] << 16);
+              x[8 * q + 2 * i + 1] += __uint_as_float(ws[i] & 0xffff0000u);
+            }
+          }
+          return;
+        }
+        // Otherwise lane l fetches bias[col0 + 32 h + l] (coalesced, bounds-checked) and the
+        // values are broadcast across the warp with shuffles.
 #pragma unroll
         for (int h = 0; h < kStoreCols / 32; ++h) {
           const int32_t n = col0 + 32 * h + static_cast<int32_t>(lane);

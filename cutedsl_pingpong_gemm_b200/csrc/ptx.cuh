@@ -203,6 +203,16 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src,
       : "memory");
 }
 
+// As tma_store_3d, with an L2 eviction-priority policy for the written lines.
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* m, uint32_t src, int32_t x,
+                                                  int32_t y, int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], "
+      "[%1], %5;" ::"l"(reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // Element-wise add of a shared-memory box into global memory (fp32 split-K accumulation in L2).
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, uint32_t src, int32_t x,
                                                   int32_t y, int32_t z) {
