@@ -77,6 +77,8 @@ def parse_args():
     ap.add_argument("--tile-n", type=int, default=0, help="0 = 512 for BF16/FP8 (pairs), 256 for block FP8")
     ap.add_argument("--cluster-m", type=int, default=2)
     ap.add_argument("--stages", type=int, default=0, help="0 = deepest that fits")
+    ap.add_argument("--epi-stages", type=int, default=0,
+                    help="epilogue staging buffers per warp (0 = 2; block FP8 picks its own)")
     ap.add_argument("--split-k", type=int, default=0, help="small-M only: 0 auto, -1 Stream-K, S splits")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -567,7 +569,7 @@ def run_cpg(args, world, rank, local):
     cm = args.cluster_m
     stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
                                                                                    8 if cm == 2 else 6)
-    epi_stage = 2
+    epi_stage = args.epi_stages or 2
     if w["fp8"] == "block" and not args.stages:
         # Deepest ring that fits 227 KiB next to 8 promotion warps' epilogue staging (4 KiB per
         # warp and epilogue stage).
@@ -747,7 +749,7 @@ def run_cpg(args, world, rank, local):
             "config": {"workload": args.workload, "m_per_gpu": m, "n": n, "k": k,
                        "m_total": m * world, "parallelism": f"m-shard x{world}, B replicated",
                        "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
-                       "fp8_scales": w["fp8"],
+                       "epi_stage": epi_stage, "fp8_scales": w["fp8"],
                        "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
                        "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
                        "bias": bool(w["bias"]), "activation": act, "gated": gated,
