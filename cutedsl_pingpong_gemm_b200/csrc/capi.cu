@@ -1298,18 +1298,14 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
   return run_impl(g, a, b, rs->dst[rs->rank], epi, stream, nullptr, rs);
 }
 
-int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32_t* per_rank) {
-  int rc = check_reduce_scatter(g, rs);
-  if (rc != CPG_OK) return rc;
-  if (per_rank == nullptr) return fail(CPG_ERR_NULL, "per_rank is NULL");
+// Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
+// sends its sum once (with K ranges, the last range to finish sends it); each of its 4 epilogue
+// warps then arrives once on the counter of the rank owning its rows (rows past M: the last).
+static void rs_arrivals(const cpg::SchedParams& sp, const cpg_reduce_scatter* rs,
+                        uint32_t* per_rank) {
   for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
-  const cpg_gemm_problem& pr = g->prob;
-  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
-  // Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
-  // sends its sum once (with K ranges, the last range to finish sends it); each of its 4
-  // epilogue warps then arrives once on its rows' owner.
-  const int64_t cta_rows = int64_t(g->sched.ncluster_m) * g->cfg.cluster_m;
-  const int64_t cta_cols = int64_t(g->sched.ncluster_n) * g->cfg.cluster_n;
+  const int64_t cta_rows = int64_t(sp.ncluster_m) * sp.cluster_m;
+  const int64_t cta_cols = int64_t(sp.ncluster_n) * sp.cluster_n;
   const int64_t per_tile = int64_t(cpg::kEpiWarps) * cta_cols;
   for (int64_t i = 0; i < cta_rows; ++i) {
     const int64_t row = i * cpg::kBM;
@@ -1322,6 +1318,29 @@ int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32
     }
     per_rank[owner] += static_cast<uint32_t>(per_tile);
   }
+}
+
+int cpg_sched_rs_arrivals(const cpg_sched_params* sp, const cpg_reduce_scatter* rs,
+                          uint32_t* per_rank) {
+  if (sp == nullptr || rs == nullptr || per_rank == nullptr)
+    return fail(CPG_ERR_NULL, "NULL argument");
+  if (rs->ranks < 1 || rs->ranks > CPG_MAX_PEERS)
+    return fail(CPG_ERR_INVALID_CONFIG, "1 to %d ranks", CPG_MAX_PEERS);
+  cpg::SchedParams p;
+  static_assert(sizeof(cpg_sched_params) == sizeof(cpg::SchedParams), "layout mismatch");
+  std::memcpy(&p, sp, sizeof(p));
+  rs_arrivals(p, rs, per_rank);
+  return CPG_OK;
+}
+
+int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32_t* per_rank) {
+  int rc = check_reduce_scatter(g, rs);
+  if (rc != CPG_OK) return rc;
+  if (per_rank == nullptr) return fail(CPG_ERR_NULL, "per_rank is NULL");
+  for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
+  const cpg_gemm_problem& pr = g->prob;
+  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
+  rs_arrivals(g->sched, rs, per_rank);
   return CPG_OK;
 }
 

@@ -133,3 +133,34 @@ def _header_struct_fields(name):
 def test_ctypes_structs_match_header(c_name, py_struct):
     struct = getattr(_lib, py_struct)
     assert [f[0] for f in struct._fields_] == _header_struct_fields(c_name)
+
+
+def test_sched_rs_arrivals_match_the_counting_rule():
+    """The peer reduce-scatter's arrival count (no GPU): every CTA tile of the schedule -- the row
+    tiles of all clusters, a pair's tile past M included -- makes 4 arrivals (one per epilogue
+    warp) on the rank owning its first row; rows past M count for the last rank."""
+    import ctypes
+    from cutedsl_pingpong_gemm_b200 import _lib
+    from cutedsl_pingpong_gemm_b200.sharding import peer_row_starts
+    lib = _lib.load()
+    for m, n, tile_n, cluster, world in ((600, 1000, 256, (2, 1), 2), (2048, 2048, 256, (2, 1), 8),
+                                          (129, 64, 128, (1, 2), 3), (640, 512, 512, (1, 1), 4)):
+        ntm, ntn = -(-m // 128), -(-n // tile_n)
+        sp = _lib.SchedParamsC()
+        assert lib.cpg_sched_params_create(ntm, ntn, 1, 1, 8, cluster[0], cluster[1], 1, 1,
+                                           ctypes.byref(sp)) == 0
+        rs = _lib.ReduceScatterC()
+        rs.ranks = world
+        starts = peer_row_starts(m, world)
+        for q in range(world + 1):
+            rs.row_start[q] = starts[q]
+        out = (ctypes.c_uint32 * world)()
+        assert lib.cpg_sched_rs_arrivals(ctypes.byref(sp), ctypes.byref(rs), out) == 0
+        want = [0] * world
+        cta_rows = sp.ncluster_m * cluster[0]
+        cta_cols = sp.ncluster_n * cluster[1]
+        for i in range(cta_rows):
+            owner = next((q for q in range(world) if i * 128 < starts[q + 1]), world - 1)
+            want[owner] += 4 * cta_cols
+        assert list(out) == want, (m, n, cluster, world, list(out), want)
+        assert sum(out) == 4 * cta_rows * cta_cols
