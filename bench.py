@@ -8,7 +8,15 @@ and there is no collective on the data path ("scaling": "weak").  ``value`` is t
 TFLOP/s = total flops / max over ranks of the device time of the timed steps.
 
 Other workloads: ``llm`` (FFN up-projection 16384 x 28672 x 8192 with bias, M split over the N
-GPUs: strong scaling of the BASELINE config 3) and ``smallm`` (M = 128, N = K = 8192: HBM bound).
+GPUs: strong scaling of the BASELINE config 3), ``llm_swiglu`` (the same flops as a fused gated
+FFN), ``fp8`` / ``fp8_block`` (E4M3 16384 x 8192 x 8192, per-tensor / 1x128 + 128x128 scales),
+``smallm`` (M = 128, N = K = 8192: HBM bound), ``moe`` (grouped GEMM over 8 experts) and
+``tallk`` (2048 x 2048 x 131072, K split over the GPUs; the partial sums are exchanged by the
+GEMM epilogue over NVLink peer memory, or with ``--exchange nccl`` an NCCL reduce-scatter).
+
+The tile schedule (``--scheduler auto``) is the dynamic one (cluster launch control) for the
+dense workloads and the reference's static persistent schedule for small M (Stream-K), the
+grouped MoE and block-scaled FP8, as measured fastest for each.
 
 Timing: W untimed warm-up steps, then exactly K steps between a barrier + synchronize on both
 sides, timed with CUDA events on the launching stream, max over ranks.  Inputs are larger than
