@@ -478,7 +478,7 @@ def run_grouped(args, world, rank, local):
     offs = torch.tensor(off, dtype=torch.int32, device=dev)
     cm = args.cluster_m
     tile_n = 512 if gated else (args.tile_n or (512 if cm == 2 else 256))
-    stages = args.stages or {(512, 2): 4, (512, 1): 2}.get((tile_n, cm), 6 if cm == 2 else 4)
+    stages = args.stages or {(512, 2): 3, (512, 1): 2}.get((tile_n, cm), 6 if cm == 2 else 4)
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
                     cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
                     epi_stage=2, raster_order=RasterOrder.AlongN, reuse_ab=False,
@@ -575,7 +575,7 @@ def run_cpg(args, world, rank, local):
         torch.cuda.synchronize()
 
     cm = args.cluster_m
-    stages = args.stages or {(512, 2): 4, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
+    stages = args.stages or {(512, 2): 3, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
                                                                                    8 if cm == 2 else 6)
     epi_stage = args.epi_stages or 2
     if w["fp8"] == "block" and not args.stages:

@@ -161,7 +161,7 @@ SIGNATURES = {
     "cpg_gemm_run_reduce_scatter": (ctypes.c_int, [_vp, _vp, _vp, _P(ReduceScatterC),
                                                    _P(EpilogueC), _vp]),
     "cpg_gemm_rs_arrivals": (ctypes.c_int, [_vp, _P(ReduceScatterC), _P(ctypes.c_uint32)]),
-    "cpg_sched_rs_arrivals": (ctypes.c_int, [_P(SchedParamsC), _P(ReduceScatterC),
+    "cpg_sched_rs_arrivals": (ctypes.c_int, [_P(SchedParamsC), _i32, _P(ReduceScatterC),
                                              _P(ctypes.c_uint32)]),
     "cpg_peer_finish": (ctypes.c_int, [_vp, _i64, _vp, ctypes.c_uint32, _i64, _i64, _vp, _i64,
                                        _vp, _vp, _i32, _vp]),

@@ -113,6 +113,7 @@ struct Variant {
   const void* fn;
   int (*smem_bytes)(int, int, int);
   int threads;
+  int epi_warps;  // epilogue warps per CTA (each owns 32 rows and a share of the columns)
 };
 
 template <int BN, int CG>
@@ -133,7 +134,8 @@ template <int BN, int CG, typename AB, typename OutT>
 Variant make_variant() {
   KernelFn fn = &cpg::gemm_sm100_kernel<BN, CG, AB, OutT>;
   return Variant{BN, CG, dtype_code<AB>(), dtype_code<OutT>(), CPG_SCALE_TENSOR,
-                 reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>, cpg::kNumThreads};
+                 reinterpret_cast<const void*>(fn), &smem_bytes_of<BN, CG>,
+                 cpg::EpiShape<BN>::kThreads, cpg::EpiShape<BN>::kWarps};
 }
 
 template <int BN, int CG>
@@ -148,7 +150,7 @@ Variant make_block_variant() {
   BlockFn fn = &cpg::gemm_fp8_block_kernel<BN, CG>;
   return Variant{BN, CG, CPG_DTYPE_E4M3, CPG_DTYPE_BF16, CPG_SCALE_BLOCK,
                  reinterpret_cast<const void*>(fn), &block_smem_bytes_of<BN, CG>,
-                 cpg::BlockShape<BN>::kThreads};
+                 cpg::BlockShape<BN>::kThreads, cpg::kBlockEpiWarps};
 }
 
 template <typename AB, typename OutT>
@@ -400,15 +402,15 @@ int cpg_config_validate(const cpg_gemm_config* c) {
   return CPG_OK;
 }
 
-// One FP32 workspace tile (128 rows x the tile's output columns) and four k-block counts (one
-// per epilogue warp) per CTA of `tiles` cluster tiles, zero between launches: the tiles whose
+// One FP32 workspace tile (128 rows x the tile's output columns) and one k-block count per
+// epilogue warp per CTA of `tiles` cluster tiles, zero between launches: the tiles whose
 // k-blocks are shared by several segments (Stream-K, or split-K into peer memory) sum there.
 static int alloc_fixup_workspace(cpg_gemm* g, int64_t tiles) {
   const int64_t ctas = int64_t(g->cfg.cluster_m) * g->cfg.cluster_n;
   const int64_t ws_rows = tiles * ctas * 128;
   const int64_t ws_cols = g->cfg.tile_n;
   g->ws_bytes = ws_rows * ws_cols * 4;
-  g->cnt_bytes = tiles * ctas * 4 * 4;
+  g->cnt_bytes = tiles * ctas * g->v.epi_warps * 4;
   cudaError_t e = cudaMalloc(&g->ws_dev, g->ws_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&g->cnt_dev, g->cnt_bytes);
   if (e == cudaSuccess) e = cudaMemset(g->ws_dev, 0, g->ws_bytes);
@@ -1299,14 +1301,15 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
 }
 
 // Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
-// sends its sum once (with K ranges, the last range to finish sends it); each of its 4 epilogue
-// warps then arrives once on the counter of the rank owning its rows (rows past M: the last).
-static void rs_arrivals(const cpg::SchedParams& sp, const cpg_reduce_scatter* rs,
+// sends its sum once (with K ranges, the last range to finish sends it); each of its epilogue
+// warps (4, or 8 for 512-wide tiles) then arrives once on the counter of the rank owning its
+// rows (rows past M: the last).
+static void rs_arrivals(const cpg::SchedParams& sp, int epi_warps, const cpg_reduce_scatter* rs,
                         uint32_t* per_rank) {
   for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
   const int64_t cta_rows = int64_t(sp.ncluster_m) * sp.cluster_m;
   const int64_t cta_cols = int64_t(sp.ncluster_n) * sp.cluster_n;
-  const int64_t per_tile = int64_t(cpg::kEpiWarps) * cta_cols;
+  const int64_t per_tile = int64_t(epi_warps) * cta_cols;
   for (int64_t i = 0; i < cta_rows; ++i) {
     const int64_t row = i * cpg::kBM;
     int owner = rs->ranks - 1;
@@ -1320,16 +1323,18 @@ static void rs_arrivals(const cpg::SchedParams& sp, const cpg_reduce_scatter* rs
   }
 }
 
-int cpg_sched_rs_arrivals(const cpg_sched_params* sp, const cpg_reduce_scatter* rs,
-                          uint32_t* per_rank) {
+int cpg_sched_rs_arrivals(const cpg_sched_params* sp, int32_t tile_n,
+                          const cpg_reduce_scatter* rs, uint32_t* per_rank) {
   if (sp == nullptr || rs == nullptr || per_rank == nullptr)
     return fail(CPG_ERR_NULL, "NULL argument");
+  if (tile_n != 64 && tile_n != 128 && tile_n != 256 && tile_n != 512)
+    return fail(CPG_ERR_UNSUPPORTED, "tile_n must be 64, 128, 256 or 512");
   if (rs->ranks < 1 || rs->ranks > CPG_MAX_PEERS)
     return fail(CPG_ERR_INVALID_CONFIG, "1 to %d ranks", CPG_MAX_PEERS);
   cpg::SchedParams p;
   static_assert(sizeof(cpg_sched_params) == sizeof(cpg::SchedParams), "layout mismatch");
   std::memcpy(&p, sp, sizeof(p));
-  rs_arrivals(p, rs, per_rank);
+  rs_arrivals(p, tile_n == 512 ? cpg::EpiShape<512>::kWarps : cpg::kEpiWarps, rs, per_rank);
   return CPG_OK;
 }
 
@@ -1340,7 +1345,7 @@ int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32
   for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
   const cpg_gemm_problem& pr = g->prob;
   if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
-  rs_arrivals(g->sched, rs, per_rank);
+  rs_arrivals(g->sched, g->v.epi_warps, rs, per_rank);
   return CPG_OK;
 }
 

@@ -46,10 +46,30 @@ namespace cpg {
 
 constexpr int kBM = 128;             // rows of A / D per CTA
 constexpr int kRowBytes = 128;       // one 128-byte swizzled row of a k-block
-constexpr int kNumThreads = 192;     // 6 warps
-constexpr int kEpiWarps = 4;
-constexpr int kEpiFirstWarp = 2;
+constexpr int kEpiWarps = 4;         // epilogue warps of the narrower tiles (one per TMEM quadrant)
 constexpr int kEpiBufBytes = 32 * kRowBytes;  // 32 rows x 128 bytes = 4 KiB per staging buffer
+
+// Warp layout per tile width.  Tiles up to 256 wide: 192 threads -- producer, MMA issuer and 4
+// epilogue warps (warps 2-5, one per TMEM lane quadrant); the epilogue of one tile overlaps the
+// next tile's mainloop through two TMEM accumulators.  512-wide tiles fill TMEM with one
+// accumulator, so the next tile's MMAs wait until the epilogue has read it out; they get 8
+// epilogue warps (warps 4-11, two per lane quadrant, each reading half of the columns) behind a
+// warpgroup of producer, MMA issuer and 2 idle warps: 384 threads launched with 168 registers,
+// the first warpgroup dropping to 56 and the epilogue warpgroups rising to 224
+// (128 * 56 + 256 * 224 = 384 * 168).
+template <int BN>
+struct EpiShape {
+  static constexpr bool kWide = BN == 512;
+  static constexpr int kWarps = kWide ? 8 : 4;
+  static constexpr int kFirstWarp = kWide ? 4 : 2;
+  static constexpr int kThreads = (kFirstWarp + kWarps) * 32;  // 384 or 192
+  static constexpr int kHalves = kWarps / 4;                   // warps per TMEM lane quadrant
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kLowRegs = 56;
+  static constexpr int kHighRegs = 224;
+  static_assert(!kWide || 128 * kLowRegs + 256 * kHighRegs == kThreads * kLaunchRegs,
+                "register split must add up to the launch allocation");
+};
 
 // FP8 E4M3 storage type (one byte per element).
 struct e4m3_t {
@@ -252,7 +272,7 @@ struct GemmSmem {
   }
   static __host__ __device__ int barrier_offset(int stages, int epi_stages, int reuse_ab) {
     int end_stages = stages * kStageBytes;
-    int end_epi = epi_offset(stages, reuse_ab) + kEpiWarps * epi_stages * kEpiBufBytes;
+    int end_epi = epi_offset(stages, reuse_ab) + EpiShape<BN>::kWarps * epi_stages * kEpiBufBytes;
     return end_stages > end_epi ? end_stages : end_epi;
   }
   // full[S], empty[S], tmem_full[2], tmem_empty[2], drain[1]; then tmem slot and abort flag;
@@ -864,7 +884,7 @@ __device__ __forceinline__ void producer_loop(const CUtensorMap* tm_a, const CUt
 }
 
 template <int BN, int CtaGroup, typename AB, typename OutT>
-__global__ void __launch_bounds__(kNumThreads, 1)
+__global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_d,
@@ -921,13 +941,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int i = 0; i < kWorkSlots; ++i) {
         ptx::mbar_init(dyn.layout.full + 8u * i, 1);
         ptx::mbar_init(dyn.layout.empty + 8u * i,
-                       dyn_consumers(cluster_ctas, CtaGroup, kEpiWarps));
+                       dyn_consumers(cluster_ctas, CtaGroup, EpiShape<BN>::kWarps));
       }
       ptx::mbar_init(dyn.layout.clc_bar, 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(tfull_bar + 8u * b, 1);
-      ptx::mbar_init(tempty_bar + 8u * b, kEpiWarps * CtaGroup);
+      ptx::mbar_init(tempty_bar + 8u * b, EpiShape<BN>::kWarps * CtaGroup);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -953,6 +973,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const SchedParams& sp = p.sched;
   const int k_iters = p.k_iters;
 
+  using ES = EpiShape<BN>;
+  // Each warpgroup changes its register budget inside its own role branch (512-wide tiles), so
+  // the compiler allocates the producer / MMA code and the epilogue code separately.
+  if (warp < static_cast<uint32_t>(ES::kFirstWarp)) {
+  if constexpr (ES::kWide) ptx::setmaxnreg_dec<ES::kLowRegs>();
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && (p.fault_inject & kInjectSkipLoads) == 0) {
@@ -1051,11 +1076,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
     }
     __syncwarp();
+  }  // warps 2-3 of a 512-wide tile's first warpgroup have no role
   } else {
+    if constexpr (ES::kWide) ptx::setmaxnreg_inc<ES::kHighRegs>();
     // ------------------------------------------------------------------ epilogue
-    const uint32_t ew = warp - kEpiFirstWarp;  // 0..3
-    const uint32_t quad = warp & 3u;           // TMEM lane quadrant this warp may access
+    const uint32_t ew = warp - static_cast<uint32_t>(ES::kFirstWarp);  // 0 .. kWarps - 1
+    const uint32_t quad = warp & 3u;  // TMEM lane quadrant this warp may access
     const uint32_t row_in_tile = quad * 32u;
+    // The warp's share of the tile's columns: all of them, or (two warps per quadrant) half.
+    const int half = static_cast<int>(ew) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     int epi_idx = 0;
@@ -1127,6 +1156,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // 256 output columns.
       const int out_cols = gated ? BN / 2 : BN;
       const int n_chunks = out_cols / kStoreCols;
+      // This warp's chunks [c_begin, c_end) of the tile's columns.
+      const int c_begin = half * n_chunks / ES::kHalves;
+      const int c_end = (half + 1) * n_chunks / ES::kHalves;
       // This warp's 32 workspace rows (the CTA tile's workspace tile; partial segments only).
       // Stream-K numbers the split tiles after the data-parallel ones; split-K (L = K range)
       // shares one workspace tile between the K ranges of a tile.
@@ -1267,7 +1299,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       };
 
 #pragma unroll 1
-      for (int c = 0; c < n_chunks; ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
         const int32_t col0 = pid_n * out_cols + c * kStoreCols;
         // C (beta * C source): this thread's 128-byte row chunk, fetched before the TMEM loads
         // so that the two latencies overlap.
@@ -1283,7 +1315,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                     *reinterpret_cast<uint32_t(*)[32]>(&v[32 * h]));
           }
           ptx::tmem_ld_wait();
-          if (c == n_chunks - 1) release_tmem(acc);
+          if (c == c_end - 1) release_tmem(acc);
 #pragma unroll
           for (int j = 0; j < kStoreCols; ++j) x[j] = __uint_as_float(v[j]) * alpha;
         } else {
@@ -1295,7 +1327,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ptx::tmem_ld_32x32b_x32(tc, vg);
             ptx::tmem_ld_32x32b_x32(tc + static_cast<uint32_t>(BN / 2), vu);
             ptx::tmem_ld_wait();
-            if (c == n_chunks - 1 && h == kStoreCols / 32 - 1) release_tmem(acc);
+            if (c == c_end - 1 && h == kStoreCols / 32 - 1) release_tmem(acc);
             float gv[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) gv[j] = __uint_as_float(vg[j]) * alpha;
@@ -1333,7 +1365,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (partial) {
         // Count this segment's k-blocks for its 32 rows; the warp that completes the count owns
         // every other segment's sum (their reduces completed before their counts were added).
-        const int32_t cnt_idx = ws_tile * 4 + static_cast<int32_t>(ew);
+        const int32_t cnt_idx = ws_tile * ES::kWarps + static_cast<int32_t>(ew);
         const int32_t mine = sg.kb1 - sg.kb0;
         int32_t last = 0;
         if (lane == 0) {
@@ -1349,7 +1381,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           float* wrow = p.fixup_ws + static_cast<int64_t>(ws_row + static_cast<int32_t>(lane)) *
                                          p.ws_cols;
 #pragma unroll 1
-          for (int c = 0; c < n_chunks; ++c) {
+          for (int c = c_begin; c < c_end; ++c) {
             const int32_t col0 = pid_n * out_cols + c * kStoreCols;
             float x[kStoreCols];
             float* src = wrow + c * kStoreCols;

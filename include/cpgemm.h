@@ -331,11 +331,12 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* plan, const void* a, const void* b,
                                 const cpg_reduce_scatter* rs, const cpg_epilogue* epi,
                                 void* stream);
 /* How much one cpg_gemm_run_reduce_scatter of this plan raises each rank's counter:
- * per_rank[q] for q < rs->ranks (4 per CTA tile and K range whose rows rank q owns). */
+ * per_rank[q] for q < rs->ranks (one per epilogue warp -- 4, or 8 for tile_n 512 -- of every
+ * CTA tile whose rows rank q owns). */
 int cpg_gemm_rs_arrivals(const cpg_gemm* plan, const cpg_reduce_scatter* rs, uint32_t* per_rank);
-/* The same count from scheduler parameters alone (cpg_sched_params_create; no device needed). */
-int cpg_sched_rs_arrivals(const cpg_sched_params* sched, const cpg_reduce_scatter* rs,
-                          uint32_t* per_rank);
+/* The same count from scheduler parameters and the tile width alone (no device needed). */
+int cpg_sched_rs_arrivals(const cpg_sched_params* sched, int32_t tile_n,
+                          const cpg_reduce_scatter* rs, uint32_t* per_rank);
 /* Owner side: wait (bounded by timeout_ms; on a timeout *status gets a nonzero code and nothing
  * is written) until *count reaches target (modulo 2^32; the sum of every rank's arrivals on this
  * rank over all calls so far), then d = bf16(w + bias) for rows x cols and w = 0.  cols, ldw and

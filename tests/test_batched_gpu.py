@@ -126,7 +126,7 @@ def test_batched_fp8_per_tensor():
     qa, sa = quantize_e4m3(a.reshape(l * m, k).cuda())
     qb, sb = quantize_e4m3(b.reshape(l * n, k).cuda())
     d = torch.empty(l, m, n, dtype=torch.bfloat16, device="cuda")
-    make_gemm(512, (2, 1, 1), stages=4)(qa.view(l, m, k), qb.view(l, n, k), d, None,
+    make_gemm(512, (2, 1, 1), stages=3)(qa.view(l, m, k), qb.view(l, n, k), d, None,
                                         scale_a=sa, scale_b=sb)
     torch.cuda.synchronize()
     da = (qa.cpu().float() * sa.cpu()).view(l, m, k)

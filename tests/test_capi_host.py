@@ -137,8 +137,9 @@ def test_ctypes_structs_match_header(c_name, py_struct):
 
 def test_sched_rs_arrivals_match_the_counting_rule():
     """The peer reduce-scatter's arrival count (no GPU): every CTA tile of the schedule -- the row
-    tiles of all clusters, a pair's tile past M included -- makes 4 arrivals (one per epilogue
-    warp) on the rank owning its first row; rows past M count for the last rank."""
+    tiles of all clusters, a pair's tile past M included -- makes one arrival per epilogue warp
+    (4, or 8 for 512-wide tiles) on the rank owning its first row; rows past M count for the last
+    rank."""
     import ctypes
     from cutedsl_pingpong_gemm_b200 import _lib
     from cutedsl_pingpong_gemm_b200.sharding import peer_row_starts
@@ -155,12 +156,13 @@ def test_sched_rs_arrivals_match_the_counting_rule():
         for q in range(world + 1):
             rs.row_start[q] = starts[q]
         out = (ctypes.c_uint32 * world)()
-        assert lib.cpg_sched_rs_arrivals(ctypes.byref(sp), ctypes.byref(rs), out) == 0
+        assert lib.cpg_sched_rs_arrivals(ctypes.byref(sp), tile_n, ctypes.byref(rs), out) == 0
+        warps = 8 if tile_n == 512 else 4
         want = [0] * world
         cta_rows = sp.ncluster_m * cluster[0]
         cta_cols = sp.ncluster_n * cluster[1]
         for i in range(cta_rows):
             owner = next((q for q in range(world) if i * 128 < starts[q + 1]), world - 1)
-            want[owner] += 4 * cta_cols
+            want[owner] += warps * cta_cols
         assert list(out) == want, (m, n, cluster, world, list(out), want)
-        assert sum(out) == 4 * cta_rows * cta_cols
+        assert sum(out) == warps * cta_rows * cta_cols

@@ -136,7 +136,7 @@ def test_dynamic_fp8_per_tensor():
     qa, sa = quantize_e4m3(torch.randn(m, k, generator=g).cuda())
     qb, sb = quantize_e4m3(torch.randn(n, k, generator=g).cuda())
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    make_gemm(512, (2, 1, 1))(qa, qb, d, None, scale_a=sa, scale_b=sb)
+    make_gemm(512, (2, 1, 1), stages=3)(qa, qb, d, None, scale_a=sa, scale_b=sb)
     torch.cuda.synchronize()
     res = gemm_ref.check(d.cpu(), qa.cpu().float() * sa.cpu(), qb.cpu().float() * sb.cpu(),
                          frob_tol=gemm_ref.FROB_TOL_FP8)

@@ -105,7 +105,7 @@ def test_gated_fp8_per_tensor():
     qa, sa = quantize_e4m3(a.cuda())
     qb, sb = quantize_e4m3(b.cuda())
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    gemm = make_gemm(512, (2, 1, 1), stages=4)
+    gemm = make_gemm(512, (2, 1, 1), stages=3)
     gemm(qa, qb, d, None, scale_a=sa, scale_b=sb, activation="silu", gated=True)
     torch.cuda.synchronize()
     da = qa.cpu().float() * sa.cpu()
@@ -143,7 +143,7 @@ def test_fp8_per_tensor_with_bias_and_activation(act):
     qa, sa = quantize_e4m3(a.cuda())
     qb, sb = quantize_e4m3(b.cuda())
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    make_gemm(512, (2, 1, 1), stages=4)(qa, qb, d, None, scale_a=sa, scale_b=sb,
+    make_gemm(512, (2, 1, 1), stages=3)(qa, qb, d, None, scale_a=sa, scale_b=sb,
                                         bias=bias.cuda(), activation=act)
     torch.cuda.synchronize()
     res = gemm_ref.check_epilogue(d.cpu(), qa.cpu().float() * sa.cpu(),

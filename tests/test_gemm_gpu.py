@@ -406,7 +406,7 @@ def test_split_k_small_m_then_cast():
 
 
 # ---------------------------------------------------------------- 512-wide tiles (two MMAs per k-step)
-@pytest.mark.parametrize("cluster,stages", [((2, 1, 1), 4), ((1, 1, 1), 2), ((2, 2, 1), 4)])
+@pytest.mark.parametrize("cluster,stages", [((2, 1, 1), 3), ((1, 1, 1), 2), ((2, 2, 1), 3)])
 @pytest.mark.parametrize("shape", [(256, 512, 128), (640, 1536, 1000), (1000, 1032, 4104),
                                    (2048, 4096, 512)])
 def test_tile_n_512(shape, cluster, stages):
@@ -418,15 +418,15 @@ def test_tile_n_512_fp8_and_bias():
     m, n, k = 1024, 2048, 1024
     qa, sa, qb, sb = gemm_ref.make_fp8_inputs(m, n, k, seed=3)
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    make_gemm(512, (2, 1, 1))(qa.cuda(), qb.cuda(), d, None, scale_a=sa.reshape(1).cuda(),
+    make_gemm(512, (2, 1, 1), stages=3)(qa.cuda(), qb.cuda(), d, None, scale_a=sa.reshape(1).cuda(),
                               scale_b=sb.reshape(1).cuda())
     torch.cuda.synchronize()
     assert gemm_ref.check_fp8(d.cpu(), qa, sa, qb, sb)["ok"]
-    run_and_check(384, 1536, 512, make_gemm(512, (2, 1, 1)), bias=True)
+    run_and_check(384, 1536, 512, make_gemm(512, (2, 1, 1), stages=3), bias=True)
 
 
 def test_tile_order_512_matches_reference():
-    got, want = traced_schedule(make_gemm(512, (2, 1, 1)), 128 * 9, 512 * 5 + 64, 128)
+    got, want = traced_schedule(make_gemm(512, (2, 1, 1), stages=3), 128 * 9, 512 * 5 + 64, 128)
     assert got == want
 
 

@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 def make_gemm(tile_n, cluster, dynamic):
     return GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32), cluster_shape_mnk=cluster,
-                    atom_layout_mn=(1, 1), ab_stage=4, epi_stage=2,
+                    atom_layout_mn=(1, 1), ab_stage=3 if tile_n == 512 else 4, epi_stage=2,
                     raster_order=RasterOrder.AlongN, reuse_ab=False, is_persistent=True,
                     dynamic_scheduler=dynamic)
 

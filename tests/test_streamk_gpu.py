@@ -26,7 +26,7 @@ CASES = [
     # (tile_n, cluster, stages, m, n, k): tiles vs resident clusters (148 single CTAs, 74 pairs)
     (128, (1, 1, 1), 6, 2560, 2560, 1024),   # 400 tiles: 148 whole, 252 shared
     (256, (1, 1, 1), 4, 1280, 2816, 640),    # 110 tiles < 148: all shared
-    (512, (2, 1, 1), 4, 4096, 5120, 512),    # 160 pair tiles: 74 whole, 86 shared
+    (512, (2, 1, 1), 3, 4096, 5120, 512),    # 160 pair tiles: 74 whole, 86 shared
     (256, (2, 1, 1), 6, 2304, 4352, 768),    # 153 pair tiles, ragged N
     (128, (1, 1, 1), 6, 1024, 4736, 256),    # 296 tiles = 2 full waves: nothing shared
 ]
@@ -76,7 +76,7 @@ def test_stream_k_bf16_in_kernel_fixup_and_auto_choice():
     res = gemm_ref.check(d.cpu(), a, b, bias=bias)
     assert res["ok"], res
     assert plan.status() == 0
-    pair = make_gemm(512, (2, 1, 1), 4)
+    pair = make_gemm(512, (2, 1, 1), 3)
     big = cpg_compile(pair, torch.empty(256, 64, dtype=torch.bfloat16, device="cuda"),
                       torch.empty(512, 64, dtype=torch.bfloat16, device="cuda"),
                       torch.empty(256, 512, dtype=torch.bfloat16, device="cuda"))
