@@ -1,7 +1,7 @@
 // Warp-specialised persistent GEMM for sm_100a (BF16 or FP8 E4M3 operands, BF16 or FP32 D):
 //   D[M,N] = act(alpha * s_a * s_b * A[M,K] . B[N,K]^T + bias[N] + beta * C)
 //
-// Role of each warp (192 threads per CTA):
+// Role of each warp (192 threads per CTA; 512-wide tiles: 384, see EpiShape):
 //   warp 0     TMA producer: one lane streams A/B k-blocks into an `ab_stages`-deep ring of
 //              128B-swizzled shared-memory stages (full/empty mbarrier pairs).  This replaces the
 //              reference's producer warp (gemm_base.py:204-229, produce_mainloop :365-388).
@@ -11,7 +11,8 @@
 //              (consume_mainloop, gemm_base.py:390-428).  Tiles up to 256 wide keep two
 //              accumulators, so the epilogue of tile i overlaps the mainloop of tile i+1; a
 //              512-wide tile (two N = 256 MMAs per k-step) fills TMEM with one.
-//   warps 2-5  epilogue: tcgen05.ld the accumulator (each warp owns a 32-lane TMEM quadrant),
+//   warps 2-5  epilogue (512-wide tiles: warps 4-11, two per quadrant, each half the columns):
+//              tcgen05.ld the accumulator (each warp owns a 32-lane TMEM quadrant),
 //              scale, add bias and beta * C, apply the activation (or the gated product of a
 //              gate / up accumulator pair), round, write 128B-swizzled staging buffers and
 //              TMA-store or TMA-reduce-add them (epilogue, gemm_base.py:270-363).

@@ -39,7 +39,10 @@ from . import _lib
 from .tile_scheduler import RasterOrder, SimpleTileScheduler, get_max_active_clusters
 
 THREADS_PER_WG = 128
-THREADS_PER_CTA_SM100 = 192  # TMA warp + MMA warp + 4 epilogue warps
+# Threads per CTA of the sm_100a kernel: TMA warp + MMA warp + 4 epilogue warps; 512-wide tiles
+# add 2 idle warps to complete the first warpgroup and use 8 epilogue warps.
+THREADS_PER_CTA_SM100 = 192
+THREADS_PER_CTA_SM100_WIDE = 384
 
 
 @functools.lru_cache(maxsize=None)
@@ -470,7 +473,7 @@ class GemmSM90:
         self.occupancy = 1
         self.mma_warpgroups = math.prod(self.atom_layout_mnk)
         assert self.mma_warpgroups in [1, 2, 3]
-        self.threads_per_cta = THREADS_PER_CTA_SM100
+        self.threads_per_cta = THREADS_PER_CTA_SM100_WIDE if tile_N == 512 else THREADS_PER_CTA_SM100
 
         self.ab_stage = ab_stage
         self.epi_stage = epi_stage
