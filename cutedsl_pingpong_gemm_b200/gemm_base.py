@@ -74,7 +74,12 @@ class CompiledGemm:
 
     Plans (validated problem + launch shape) are cached per (M, N, K, strides, device), so a
     compiled GEMM accepts any shape its configuration supports, like the reference's kernel
-    compiled on symbolic shapes.
+    compiled on symbolic shapes.  The FP32 split-K workspaces are cached per stream as well, so
+    launches on two streams never share one.  A plan's own device state (the grouped GEMM's tile
+    prefix, the hybrid split's fixup workspace and counters) is rebuilt by each launch, so
+    launches of such a plan must be stream-ordered: concurrent streams use one ``CompiledGemm``
+    each.  (Plans are not keyed by stream: creating one allocates device memory, which a CUDA
+    graph capture on a fresh stream would forbid.)  ``release()`` drops the caches.
     """
 
     def __init__(self, gemm: "GemmSM90"):
@@ -180,7 +185,7 @@ class CompiledGemm:
             if c.dim() == 3 and not c.is_contiguous():
                 raise _lib.CpgError(_lib.CPG_ERR_UNSUPPORTED,
                                     "batched split-K into BF16 needs a contiguous D")
-            ws = self._workspace(c)
+            ws = self._workspace(c, stream)
             plan = self._plan(a, b, ws, mode, split_k)
             plan.run(a, b, ws, stream, bias=None, alpha=alpha, scale_a=scale_a, scale_b=scale_b)
             from .quant import cast_f32_bf16
@@ -255,15 +260,23 @@ class CompiledGemm:
             self._plans[key] = plan
         return plan
 
-    def _workspace(self, c):
-        """FP32 [M, N] buffer for split-K partial sums (kept and reused per shape/device)."""
+    def _workspace(self, c, stream=None):
+        """FP32 [M, N] buffer for split-K partial sums (kept and reused per shape, device and
+        stream: each launch clears it on its own stream first)."""
         import torch
-        key = (tuple(c.shape), c.device)
+        key = (tuple(c.shape), c.device, _stream_handle(stream, c.device))
         ws = self._workspaces.get(key)
         if ws is None:
             ws = torch.empty(c.shape, dtype=torch.float32, device=c.device)
             self._workspaces[key] = ws
         return ws
+
+    def release(self) -> None:
+        """Drop the cached plans and split-K workspaces; their device memory is freed and the next
+        call plans again.  Call it only when no launch that uses them is still running and no
+        captured CUDA graph will replay them (a graph keeps the pointers it was captured with)."""
+        self._plans.clear()
+        self._workspaces.clear()
 
     def auto_split_k(self, m: int, n: int, k: int, batches: int = 1) -> int:
         """When the output tiles alone cannot fill the GPU: K ranges that fill whole waves of
@@ -530,6 +543,12 @@ class GemmSM90:
                           gated=gated)
         self._compiled = compiled
         return compiled
+
+    def release(self) -> None:
+        """Free what the implicit compiled GEMM of ``__call__`` / ``grouped`` caches (see
+        ``CompiledGemm.release``)."""
+        if self._compiled is not None:
+            self._compiled.release()
 
     def grouped(self, a, b, c, group_offsets, stream=None, **epilogue):
         """Grouped GEMM (see ``CompiledGemm.grouped``)."""

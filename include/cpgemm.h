@@ -184,7 +184,11 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
                     cpg_gemm** out);
 
 /* Launch D = alpha * A . B^T (+ bias) on `stream` (a cudaStream_t, NULL = legacy default
- * stream).  Replaces compiled_gemm(a, b, c, stream) (gemm_base.py:609).  epi may be NULL. */
+ * stream).  Replaces compiled_gemm(a, b, c, stream) (gemm_base.py:609).  epi may be NULL.
+ * A plan holds device state that its launches reuse (the status word; for the Stream-K fixup and
+ * hybrid splits a workspace and counters; for grouped plans the tile prefix): launches of one
+ * plan must be ordered on the device (one stream, or streams joined by events).  Concurrent
+ * streams use one plan each; plans are independent of one another. */
 int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
                  void* stream);
 

@@ -142,3 +142,16 @@ def test_auto_split_k_avoids_stream_k_when_dynamic(monkeypatch):
         s = c.auto_split_k(128, 8192, 8192)
         assert (s == _lib.CPG_SPLIT_K_STREAM) == want_stream, (dyn, s)
         assert s != 0
+
+
+def test_release_drops_cached_plans_and_workspaces():
+    from cutedsl_pingpong_gemm_b200.gemm_base import CompiledGemm
+    gemm = GemmSM90(tile_shape_mn=(128, 256), epi_tile_mn=(128, 32), cluster_shape_mnk=(2, 1, 1),
+                    atom_layout_mn=(1, 1), ab_stage=4, reuse_ab=False, is_persistent=True)
+    gemm.release()  # nothing compiled yet: no-op
+    compiled = CompiledGemm(gemm)
+    gemm._compiled = compiled
+    compiled._plans["plan"] = object()
+    compiled._workspaces["workspace"] = object()
+    gemm.release()
+    assert compiled._plans == {} and compiled._workspaces == {}

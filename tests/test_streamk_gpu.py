@@ -91,3 +91,30 @@ def test_fused_epilogue_rejects_stream_k():
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.CpgError):
         make_gemm(256, (1, 1, 1), 4)(a.cuda(), b.cuda(), d, None, activation="silu", split_k=-2)
+
+
+def test_split_k_bf16_on_two_streams():
+    """The same split-K shape launched on two streams at once: each stream adds its partial sums
+    into its own FP32 workspace, so neither output sees the other's sums."""
+    m, n, k = 256, 2048, 4096
+    gemm = make_gemm(256, (2, 1, 1), 6)
+    inputs = [gemm_ref.make_inputs(m, n, k, seed=90 + i, b_scale=k ** -0.5) for i in range(2)]
+    dev = [(a.cuda(), b.cuda()) for a, b, _ in inputs]
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for it in range(3):
+        for (da, db), d, s in zip(dev, outs, streams):
+            with torch.cuda.stream(s):
+                gemm(da, db, d, None, split_k=4)
+        torch.cuda.synchronize()
+        for (a, b, _), d in zip(inputs, outs):
+            res = gemm_ref.check(d.cpu(), a, b)
+            assert res["ok"], (it, res)
+    assert len(gemm._compiled._workspaces) == 2
+    gemm.release()
+    assert not gemm._compiled._workspaces and not gemm._compiled._plans
+    gemm(dev[0][0], dev[0][1], outs[0], None, split_k=4)  # plans again after release
+    torch.cuda.synchronize()
+    res = gemm_ref.check(outs[0].cpu(), inputs[0][0], inputs[0][1])
+    assert res["ok"], res
