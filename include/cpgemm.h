@@ -100,7 +100,10 @@ typedef struct cpg_gemm_config {
                                 tile per cluster); 1: dynamic (cluster launch control): the grid
                                 holds one cluster per cluster tile and running clusters take over
                                 clusters that have not started, so SMs busy with other work take
-                                fewer tiles.  Same tile map; needs reuse_ab = 0 and no Stream-K;
+                                fewer tiles.  The cluster id -> tile map of the static schedule,
+                                except that group_size is lowered until a group's re-read
+                                operand panel (AlongN: its B rows over one K range; AlongM: its A
+                                rows) is at most 32 MiB; needs reuse_ab = 0 and no Stream-K;
                                 ignores is_persistent. */
 } cpg_gemm_config;
 

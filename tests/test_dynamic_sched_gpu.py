@@ -41,7 +41,9 @@ def test_dynamic_tiles_once_and_numerics(tile_n, cluster):
     grid = plan.launch_info()["grid"]
     cm, cn = cluster[0], cluster[1]
     ntm, ntn = -(-m // 128), -(-n // tile_n)
-    p = ts.params_create((ntm, ntn, 1), int(gemm.raster_order), 8, cluster, True)
+    # The plan's group size (the dynamic schedule may lower the reference's 8 for long K).
+    group = plan.sched_params().dm_group_size.divisor
+    p = ts.params_create((ntm, ntn, 1), int(gemm.raster_order), group, cluster, True)
     nclusters = grid[0] // cm
     assert grid[1] == cn and grid[2] == 1
     nctas = grid[0] * grid[1]
@@ -227,3 +229,24 @@ def test_dynamic_in_cuda_graph():
         assert torch.equal(d, ref)
     res = gemm_ref.check(ref.cpu(), a, b)
     assert res["ok"], res
+
+
+@pytest.mark.parametrize("dtype,k,dynamic,want", [
+    (torch.bfloat16, 8192, True, 4),         # B panel of a cluster column: 512 x 8192 x 2 = 8 MiB
+    (torch.float8_e4m3fn, 8192, True, 8),    # 4 MiB per column: the reference's 8
+    (torch.bfloat16, 16384, True, 2),
+    (torch.bfloat16, 8192, False, 8),        # static schedule: always the reference's 8
+    (torch.bfloat16, 320, True, 8),
+])
+def test_dynamic_group_size_keeps_the_panel_in_l2(dtype, k, dynamic, want):
+    """The dynamic schedule lowers the group size until the B rows of a group's cluster columns
+    over one K range take at most 32 MiB (256 x 512 pair tiles: 512 rows of B per column)."""
+    m, n = 256, 512 * 12
+    gemm = GemmSM90(tile_shape_mn=(128, 512), epi_tile_mn=(128, 32), cluster_shape_mnk=(2, 1, 1),
+                    atom_layout_mn=(1, 1), ab_stage=3, reuse_ab=False, is_persistent=True,
+                    dynamic_scheduler=dynamic)
+    a = torch.empty(m, k, dtype=dtype, device="cuda")
+    b = torch.empty(n, k, dtype=dtype, device="cuda")
+    d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    plan = cpg_compile(gemm, a, b, d, None).plan_for(a, b, d)
+    assert plan.sched_params().dm_group_size.divisor == want
