@@ -146,6 +146,7 @@ SIGNATURES = {
     "cpg_sched_params_create": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                                _P(SchedParamsC)]),
     "cpg_sched_grid_shape": (ctypes.c_int, [_P(SchedParamsC), _i32, _P(_i32)]),
+    "cpg_sched_plan_group_size": (ctypes.c_int, [_P(GemmConfigC), ctypes.c_int64, _i32, _P(_i32)]),
     "cpg_sched_cluster_map": (ctypes.c_int, [_P(SchedParamsC), _P(_i32), _i64]),
     "cpg_sched_cluster_map_device": (ctypes.c_int, [_P(SchedParamsC), _vp, _i64, _vp]),
     "cpg_max_active_clusters": (ctypes.c_int, [_i32, _P(_i32)]),

@@ -195,6 +195,25 @@ bool find_variant(int bn, int cta_group, int dtype_ab, int dtype_d, int scale_mo
 
 int elem_bytes(int dtype) { return dtype == CPG_DTYPE_E4M3 ? 1 : (dtype == CPG_DTYPE_F32 ? 4 : 2); }
 
+// Raster group size of a plan whose K ranges hold k_iters k-blocks.  The dynamic schedule starts
+// clusters in id order, so the clusters running at any time hold about consecutive ids: a
+// group's re-read operand panel (raster AlongN: the B rows of its cluster columns over one K
+// range; AlongM: the A rows of its cluster rows) should stay in L2 while the group's tiles pass.
+// The group size is lowered until that panel is at most 32 MiB.  Measured on B200 with 256 x 512
+// pair tiles against the reference's 8: the LLM shape (BF16, K = 8192: 8 MiB per column, so 4)
+// +1.7 %, the fused SwiGLU +1.9 %, 8192^3 equal; FP8 at K = 8192 (4 MiB per column, stays 8)
+// ran 2 % slower with 4.  The static schedule keeps the configured size.
+int32_t plan_group_size(const cpg_gemm_config* cfg, int64_t k_iters) {
+  const int64_t group_size = cfg->group_size;
+  if (!cfg->dynamic_scheduler) return cfg->group_size;
+  const int64_t panel_rows = cfg->raster_order == CPG_RASTER_ALONG_N
+                                 ? int64_t(cfg->tile_n) * cfg->cluster_n
+                                 : int64_t(128) * cfg->cluster_m;
+  const int64_t panel = panel_rows * k_iters * cpg::kRowBytes;
+  const int64_t fit = panel > 0 ? (int64_t(32) << 20) / panel : group_size;
+  return static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(group_size, fit)));
+}
+
 CUtensorMapDataType tma_dtype(int dtype) {
   switch (dtype) {
     case CPG_DTYPE_E4M3: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -623,27 +642,10 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     delete g;
     return fail(CPG_ERR_INVALID_SHAPE, "more than 2^31 - 1 tiles");
   }
-  // The dynamic schedule starts clusters in id order, so the clusters running at any time hold
-  // about consecutive ids: a group's re-read operand panel (raster AlongN: the B rows of its
-  // cluster columns over one K range; AlongM: the A rows of its cluster rows) should stay in L2
-  // while the group's tiles pass.  The group size is lowered until that panel is at most 32 MiB.
-  // Measured on B200 with 256 x 512 pair tiles against the reference's 8: the LLM shape (BF16,
-  // K = 8192: 8 MiB per column, so 4) +1.7 %, the fused SwiGLU +1.9 %, 8192^3 equal; FP8 at K =
-  // 8192 (4 MiB per column, stays 8) ran 2 % slower with 4.
-  int32_t group_size = cfg->group_size;
-  if (cfg->dynamic_scheduler) {
-    const int64_t panel_rows = cfg->raster_order == CPG_RASTER_ALONG_N
-                                   ? int64_t(cfg->tile_n) * cfg->cluster_n
-                                   : int64_t(128) * cfg->cluster_m;
-    const int64_t panel = panel_rows * g->k_iters_per_split * cpg::kRowBytes;
-    const int64_t fit = panel > 0 ? (int64_t(32) << 20) / panel : int64_t(group_size);
-    group_size = static_cast<int32_t>(
-        std::max<int64_t>(1, std::min<int64_t>(int64_t(group_size), fit)));
-  }
   g->sched = cpg::sched_params_create(static_cast<int32_t>(ntm), static_cast<int32_t>(ntn),
                                       static_cast<int32_t>(ntl), cfg->raster_order,
-                                      group_size, cfg->cluster_m, cfg->cluster_n,
-                                      cfg->is_persistent);
+                                      plan_group_size(cfg, g->k_iters_per_split),
+                                      cfg->cluster_m, cfg->cluster_n, cfg->is_persistent);
   int32_t grid[3];
   cpg::sched_grid_shape(g->sched, mac, grid);
   if (g->stream_k) {
@@ -1069,6 +1071,19 @@ int cpg_sched_params_create(int32_t ntiles_m, int32_t ntiles_n, int32_t ntiles_l
   cpg::SchedParams p = cpg::sched_params_create(ntiles_m, ntiles_n, ntiles_l, raster_order,
                                                 group_size, cluster_m, cluster_n, is_persistent);
   std::memcpy(out, &p, sizeof(*out));
+  return CPG_OK;
+}
+
+int cpg_sched_plan_group_size(const cpg_gemm_config* cfg, int64_t k, int32_t dtype_ab,
+                              int32_t* out) {
+  if (cfg == nullptr || out == nullptr) return fail(CPG_ERR_NULL, "NULL argument");
+  const int rc = cpg_config_validate(cfg);
+  if (rc != CPG_OK) return rc;
+  if (dtype_ab != CPG_DTYPE_BF16 && dtype_ab != CPG_DTYPE_E4M3)
+    return fail(CPG_ERR_DTYPE, "dtype_ab must be BF16 or E4M3, got %d", dtype_ab);
+  if (k < 0) return fail(CPG_ERR_INVALID_SHAPE, "k must be >= 0, got %lld", (long long)k);
+  const int64_t bk = cpg::kRowBytes / elem_bytes(dtype_ab);
+  *out = plan_group_size(cfg, (k + bk - 1) / bk);
   return CPG_OK;
 }
 

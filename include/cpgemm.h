@@ -247,6 +247,12 @@ int cpg_sched_params_create(int32_t ntiles_m, int32_t ntiles_n, int32_t ntiles_l
                             int32_t cluster_n, int32_t cluster_k, int32_t is_persistent,
                             cpg_sched_params* out);
 int cpg_sched_grid_shape(const cpg_sched_params* p, int32_t max_active_clusters, int32_t grid[3]);
+/* Raster group size a plan of this config uses for K ranges of k elements of type dtype_ab: the
+ * config's group_size for the static schedule; for the dynamic one the largest size up to it whose
+ * re-read operand panel (AlongN: tile_n * cluster_n rows of B; AlongM: 128 * cluster_m rows of
+ * A; over the K range) takes at most 32 MiB, at least 1.  No counterpart in the reference. */
+int cpg_sched_plan_group_size(const cpg_gemm_config* cfg, int64_t k, int32_t dtype_ab,
+                              int32_t* out);
 /* out[2*i], out[2*i+1] = cluster (m, n) of linear cluster id i, for i < n. */
 int cpg_sched_cluster_map(const cpg_sched_params* p, int32_t* out, int64_t n);
 int cpg_sched_cluster_map_device(const cpg_sched_params* p, int32_t* device_out, int64_t n,

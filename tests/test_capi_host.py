@@ -166,3 +166,40 @@ def test_sched_rs_arrivals_match_the_counting_rule():
             want[owner] += warps * cta_cols
         assert list(out) == want, (m, n, cluster, world, list(out), want)
         assert sum(out) == warps * cta_rows * cta_cols
+
+
+@pytest.mark.parametrize("tile_n,cluster,raster,dynamic,dtype,k,want", [
+    # AlongN, 256 x 512 pair tiles: 512 rows of B per cluster column.
+    (512, (2, 1), 1, 1, "bf16", 8192, 4),      # 8 MiB per column
+    (512, (2, 1), 1, 1, "e4m3", 8192, 8),      # 4 MiB: the reference's 8
+    (512, (2, 1), 1, 1, "bf16", 16384, 2),
+    (512, (2, 1), 1, 1, "bf16", 131072, 1),    # one column is over 32 MiB: at least 1
+    (512, (2, 1), 1, 1, "bf16", 320, 8),
+    (512, (2, 1), 1, 1, "bf16", 0, 8),
+    (512, (2, 1), 1, 0, "bf16", 131072, 8),    # static schedule: the configured size
+    (256, (1, 2), 1, 1, "bf16", 8192, 4),      # cluster_n 2: 512 rows of B per column
+    (256, (1, 1), 1, 1, "bf16", 8192 + 1, 7),  # 256 rows over 129 k-blocks: just over 4 MiB
+    (256, (2, 1), 0, 1, "bf16", 8192, 8),      # AlongM: 256 rows of A per cluster row
+    (256, (1, 1), 0, 1, "bf16", 65536, 2),     # 128 rows of A over 1024 k-blocks: 16 MiB
+])
+def test_plan_group_size_rule(lib, tile_n, cluster, raster, dynamic, dtype, k, want):
+    cfg = _lib.GemmConfigC(128, tile_n, 128, 32, cluster[0], cluster[1], 1, 1, 1, 3, 2, raster,
+                           0, 1, 0, 8, dynamic)
+    code = {"bf16": _lib.CPG_DTYPE_BF16, "e4m3": _lib.CPG_DTYPE_E4M3}[dtype]
+    out = ctypes.c_int32()
+    assert lib.cpg_sched_plan_group_size(ctypes.byref(cfg), k, code, ctypes.byref(out)) == 0
+    assert out.value == want
+
+
+def test_plan_group_size_rejects_bad_arguments(lib):
+    cfg = _lib.GemmConfigC(128, 512, 128, 32, 2, 1, 1, 1, 1, 3, 2, 1, 0, 1, 0, 8, 1)
+    out = ctypes.c_int32()
+    assert lib.cpg_sched_plan_group_size(ctypes.byref(cfg), -1, _lib.CPG_DTYPE_BF16,
+                                         ctypes.byref(out)) == _lib.CPG_ERR_INVALID_SHAPE
+    assert lib.cpg_sched_plan_group_size(ctypes.byref(cfg), 64, _lib.CPG_DTYPE_F32,
+                                         ctypes.byref(out)) == _lib.CPG_ERR_DTYPE
+    assert lib.cpg_sched_plan_group_size(None, 64, _lib.CPG_DTYPE_BF16,
+                                         ctypes.byref(out)) == _lib.CPG_ERR_NULL
+    bad = _lib.GemmConfigC(128, 512, 128, 32, 2, 1, 1, 1, 1, 3, 2, 1, 0, 1, 0, 0, 1)  # group 0
+    assert lib.cpg_sched_plan_group_size(ctypes.byref(bad), 64, _lib.CPG_DTYPE_BF16,
+                                         ctypes.byref(out)) == _lib.CPG_ERR_INVALID_CONFIG
