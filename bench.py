@@ -602,6 +602,8 @@ def run_cpg(args, world, rank, local):
     else:
         plan = compiled.plan_for(a, b, d, 1 if w["fp8"] == "block" else 0, split_k, gated=gated)
     info = plan.launch_info()
+    # The raster group size the plan uses (the reference's 8; lowered under the dynamic schedule).
+    group_size = plan.sched_params().dm_group_size.divisor
     # K ranges and Stream-K into a BF16 D add the cast kernel (the hybrid finishes in the GEMM).
     kernels_per_step = 2 if ws_path else 1
 
@@ -763,7 +765,7 @@ def run_cpg(args, world, rank, local):
                        "bias": bool(w["bias"]), "activation": act, "gated": gated,
                        "split_k": split_k,
                        "scheduler": gemm.dynamic_scheduler and "dynamic" or "static",
-                       "cuda_graph": use_graph},
+                       "group_size": group_size, "cuda_graph": use_graph},
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": min_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
