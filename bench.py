@@ -304,7 +304,7 @@ def run_reference(args, world, rank):
     cpu_step(a)
     t_probe = max(time.perf_counter() - t0, 1e-4)
     per_step_budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = int(max(8, min(w["m"], probe_rows * per_step_budget / t_probe)))
+    rows = int(max(8, min(args.m or w["m"], probe_rows * per_step_budget / t_probe)))
     rows = max(8, rows // 8 * 8)
     a = torch.randn(rows, k, generator=g).to(torch.bfloat16).float()
     for _ in range(args.warmup):
@@ -318,7 +318,7 @@ def run_reference(args, world, rank):
     sample = (f"{rows}x{n}x{k} fp32 row slab of the {args.workload} GEMM per step "
               f"(torch.matmul on {cores} host threads)")
     line = {
-        "impl": "reference", "metric": metric_name(args.workload), "value": value,
+        "impl": "reference", "metric": metric_name(args.workload, args.m), "value": value,
         "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak" if w["m_is_per_gpu"] else "strong", "vs_baseline": None,
@@ -333,7 +333,11 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def metric_name(workload):
+def metric_name(workload, m_override=0):
+    """The metric string of a workload (both arms print the same one); an --m override of the
+    small-M workload names its M."""
+    if workload == "smallm" and m_override:
+        return f"GEMM TFLOPS (BF16 M={m_override}, N=K=8192, HBM-bound)"
     return {"bf16_8192": "GEMM TFLOPS (BF16 8192^3 per GPU, M-sharded, B replicated)",
             "llm": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 + bias, M-sharded)",
             "llm_swiglu": "GEMM TFLOPS (BF16 LLM FFN up 16384x28672x8192 as fused SwiGLU, "
@@ -341,7 +345,7 @@ def metric_name(workload):
             "smallm": "GEMM TFLOPS (BF16 M=128, N=K=8192, HBM-bound)",
             "fp8": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, per-tensor scales)",
             "fp8_block": "GEMM TFLOPS (FP8 E4M3 16384x8192x8192 per GPU, 1x128 / 128x128 block scales)",
-            "tallk": "GEMM TFLOPS (BF16 2048x2048x131072 split-K over GPUs, NCCL reduce-scatter)",
+            "tallk": "GEMM TFLOPS (BF16 2048x2048x131072 split-K over GPUs)",
             "moe": "GEMM TFLOPS (BF16 grouped MoE up-projection, 8 experts x [2x14336, 4096], "
                    "16384 token rows per GPU, fused SwiGLU)",
             }[workload]
@@ -416,7 +420,7 @@ def run_tallk(args, world, rank, local):
     if rank == 0:
         s0, s1 = row_range(m, world, rank)
         line = {
-            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "metric": metric_name(args.workload, args.m), "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
@@ -512,7 +516,7 @@ def run_grouped(args, world, rank, local):
     peaks, peak_src = load_peaks()
     if rank == 0:
         line = {
-            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "metric": metric_name(args.workload, args.m), "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
@@ -751,7 +755,7 @@ def run_cpg(args, world, rank, local):
             peak = NOMINAL_DENSE_FP8_TFLOPS
             peak_note = "nominal dense FP8 (no measured FP8 peak available)"
         line = {
-            "metric": metric_name(args.workload), "value": value, "unit": "TFLOP/s",
+            "metric": metric_name(args.workload, args.m), "value": value, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak" if w["m_is_per_gpu"] else "strong",
             "vs_baseline": None, "dtype": "e4m3" if w["fp8"] else "bf16", "data": "synthetic",
