@@ -726,6 +726,13 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
       return cuda_fail(e, "cudaMalloc(group tile prefix)");
     }
   }
+  // The zeroing above ran on the legacy default stream, which does not order launches on
+  // non-blocking streams: let it finish before the plan is used (once per plan).
+  e = cudaStreamSynchronize(nullptr);
+  if (e != cudaSuccess) {
+    cpg_gemm_destroy(g);
+    return cuda_fail(e, "cudaStreamSynchronize(plan setup)");
+  }
   *out = g;
   return CPG_OK;
 }
@@ -802,6 +809,7 @@ int cpg_gemm_status(cpg_gemm* g, int32_t* status) {
     // A launch that stopped early may have left Stream-K workspace tiles and counts behind.
     if (g->ws_dev != nullptr) cudaMemset(g->ws_dev, 0, g->ws_bytes);
     if (g->cnt_dev != nullptr) cudaMemset(g->cnt_dev, 0, g->cnt_bytes);
+    cudaDeviceSynchronize();  // the clears land before any later launch, on any stream
     if (s == kStatusBadGroups)
       return fail(CPG_ERR_INVALID_SHAPE, "group offsets not non-decreasing within [0, m]");
     return fail(CPG_ERR_DEVICE_TIMEOUT, "kernel wait timed out at site %d", s & 0xFF);
@@ -1243,6 +1251,9 @@ int cpg_peer_alloc(int64_t bytes, void** dev_ptr, cpg_ipc_handle* handle) {
   cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer buffer)");
   e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  // cudaMemset of device memory may return before the zeros land; other processes write into
+  // this buffer as soon as they hold its handle, so the zeros must be in place first.
+  if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
   if (e != cudaSuccess) {
