@@ -191,7 +191,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
  * A plan holds device state that its launches reuse (the status word; for the Stream-K fixup and
  * hybrid splits a workspace and counters; for grouped plans the tile prefix): launches of one
  * plan must be ordered on the device (one stream, or streams joined by events).  Concurrent
- * streams use one plan each; plans are independent of one another. */
+ * streams use one plan each; plans are independent of one another.  A plan also caches the
+ * tensor maps of the last A, B, D pointers, so one host thread at a time may call it. */
 int cpg_gemm_run(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
                  void* stream);
 
