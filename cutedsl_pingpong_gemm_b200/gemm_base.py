@@ -79,7 +79,8 @@ class CompiledGemm:
     prefix, the hybrid split's fixup workspace and counters) is rebuilt by each launch, so
     launches of such a plan must be stream-ordered: concurrent streams use one ``CompiledGemm``
     each.  (Plans are not keyed by stream: creating one allocates device memory, which a CUDA
-    graph capture on a fresh stream would forbid.)  ``release()`` drops the caches.
+    graph capture on a fresh stream would forbid.)  ``release()`` drops the caches.  One host
+    thread at a time may call a compiled GEMM (its plans cache tensor maps).
     """
 
     def __init__(self, gemm: "GemmSM90"):
