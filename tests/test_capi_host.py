@@ -203,3 +203,51 @@ def test_plan_group_size_rejects_bad_arguments(lib):
     bad = _lib.GemmConfigC(128, 512, 128, 32, 2, 1, 1, 1, 1, 3, 2, 1, 0, 1, 0, 0, 1)  # group 0
     assert lib.cpg_sched_plan_group_size(ctypes.byref(bad), 64, _lib.CPG_DTYPE_BF16,
                                          ctypes.byref(out)) == _lib.CPG_ERR_INVALID_CONFIG
+
+
+def test_entry_points_reject_bad_arguments_before_touching_the_gpu(lib):
+    """Every entry point validates its arguments first and returns a CPG_ERR_* code with a
+    message; none of these calls reaches the CUDA runtime."""
+    null = None
+    f32, bf16 = _lib.CPG_DTYPE_F32, _lib.CPG_DTYPE_BF16
+    cases = [
+        # quantiser: extents, dtype, scales, block shapes
+        (lambda: lib.cpg_quantize_e4m3(null, bf16, -1, 8, 8, null, 8, null, 0, 0, null),
+         _lib.CPG_ERR_INVALID_SHAPE, "extents"),
+        (lambda: lib.cpg_quantize_e4m3(null, bf16, 4, 16, 8, null, 16, null, 0, 0, null),
+         _lib.CPG_ERR_INVALID_SHAPE, "extents"),
+        (lambda: lib.cpg_quantize_e4m3(null, _lib.CPG_DTYPE_E4M3, 4, 8, 8, null, 8, null, 0, 0,
+                                       null), _lib.CPG_ERR_DTYPE, "BF16 or FP32"),
+        (lambda: lib.cpg_quantize_e4m3(null, bf16, 4, 8, 8, null, 8, null, 0, 0, null),
+         _lib.CPG_ERR_NULL, "scales"),
+        # cast: extents and NULL buffers
+        (lambda: lib.cpg_cast_f32_bf16(null, 4, 8, 4, null, 8, null, null),
+         _lib.CPG_ERR_INVALID_SHAPE, "extents"),
+        (lambda: lib.cpg_cast_f32_bf16(null, 4, 8, 8, null, 8, null, null),
+         _lib.CPG_ERR_NULL, "non-NULL"),
+        # peer buffers and the peer finish
+        (lambda: lib.cpg_peer_alloc(0, ctypes.byref(ctypes.c_void_p()),
+                                    ctypes.byref(_lib.IpcHandleC())),
+         _lib.CPG_ERR_INVALID_SHAPE, "positive"),
+        (lambda: lib.cpg_peer_open(null, ctypes.byref(ctypes.c_void_p())),
+         _lib.CPG_ERR_NULL, "NULL"),
+        (lambda: lib.cpg_peer_finish(null, 8, null, 0, 4, 6, null, 8, null, null, 100, null),
+         _lib.CPG_ERR_ALIGNMENT, "multiples of 4"),
+        (lambda: lib.cpg_peer_finish(null, 8, null, 0, 4, 8, null, 8, null, null, 100, null),
+         _lib.CPG_ERR_NULL, "count and status"),
+        # plans
+        (lambda: lib.cpg_gemm_run(null, null, null, null, null, null), _lib.CPG_ERR_NULL, "NULL"),
+        (lambda: lib.cpg_gemm_run_grouped(null, null, null, null, null, null, null),
+         _lib.CPG_ERR_NULL, "NULL"),
+        (lambda: lib.cpg_gemm_status(null, ctypes.byref(ctypes.c_int32())), _lib.CPG_ERR_NULL,
+         "non-NULL"),
+        (lambda: lib.cpg_gemm_splitk_static(null, null, null, null, null, null, null),
+         _lib.CPG_ERR_NULL, "non-NULL"),
+        (lambda: lib.cpg_sched_cluster_map(null, null, 4), _lib.CPG_ERR_NULL, "NULL"),
+    ]
+    for i, (call, code, words) in enumerate(cases):
+        assert call() == code, i
+        assert words in lib.cpg_last_error_message().decode(), (i, lib.cpg_last_error_message())
+    # Destroying or closing nothing is not an error.
+    assert lib.cpg_gemm_destroy(null) == _lib.CPG_OK
+    assert lib.cpg_peer_close(null) == _lib.CPG_OK and lib.cpg_peer_free(null) == _lib.CPG_OK
