@@ -16,7 +16,9 @@ GEMM epilogue over NVLink peer memory, or with ``--exchange nccl`` an NCCL reduc
 
 The tile schedule (``--scheduler auto``) is the dynamic one (cluster launch control) for the
 dense workloads and the reference's static persistent schedule for small M (Stream-K), the
-grouped MoE and block-scaled FP8, as measured fastest for each.
+grouped MoE and block-scaled FP8, as measured fastest for each.  Under the dynamic schedule the
+plan sizes the raster group so that a group's B panel stays within 32 MiB of L2 (``config``'s
+``group_size``; the static schedule keeps the reference's 8).
 
 Timing: W untimed warm-up steps, then exactly K steps between a barrier + synchronize on both
 sides, timed with CUDA events on the launching stream, max over ranks.  Inputs are larger than
