@@ -31,7 +31,8 @@ def test_fastdivmod_divmod_match_reference(golden_fdm):
 
 
 def test_known_answer_table():
-    # Values the reference's FastDivmod.create returns on the host (survey table).
+    # Values the reference's FastDivmod.create returned when it was executed on the host
+    # (fast_math.py:56-76), written out as a known-answer table.
     table = {1: (0x80000000, 0xFFFFFFFF), 2: (0x80000000, 0), 7: (2454267027, 2),
              8: (0x80000000, 2), 12: (2863311531, 3), 64: (0x80000000, 5), 1000: (2199023256, 9)}
     for d, (mult, shift) in table.items():
