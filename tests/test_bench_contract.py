@@ -1,6 +1,6 @@
 """bench.py's reference arm runs on host cores alone, so its JSON line is checked here on CPU:
 the keys the driver reads, a positive throughput and the e2e / cpu_baseline objects that the
-reference arm must carry."""
+reference arm must carry.  The bench's host-side helpers are checked as well."""
 import json
 import os
 import subprocess
@@ -31,3 +31,25 @@ def test_reference_arm_prints_the_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_bench_helpers():
+    """The bench's data plumbing: recorded ncu traffic per workload and schedule, metric names,
+    and the seeded MoE group sizes."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+        recorded = json.load(f)
+    assert bench.load_traffic("bf16_8192", "dynamic") == recorded["bf16_8192"]["dram_bytes_per_launch"]
+    assert bench.load_traffic("bf16_8192", "static") == \
+        recorded["bf16_8192:static"]["dram_bytes_per_launch"]
+    assert bench.load_traffic("moe", "static") is None
+    # Both arms print the same metric name; an --m override of the small-M workload names its M.
+    for w in bench.WORKLOADS:
+        assert bench.metric_name(w) == bench.metric_name(w, 0)
+    assert "M=16," in bench.metric_name("smallm", 16)
+    sizes = bench.group_sizes(16384, 8, seed=11)
+    assert sum(sizes) == 16384 and len(sizes) == 8 and min(sizes) > 0
+    assert sizes == bench.group_sizes(16384, 8, seed=11)
