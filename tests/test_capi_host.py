@@ -251,3 +251,28 @@ def test_entry_points_reject_bad_arguments_before_touching_the_gpu(lib):
     # Destroying or closing nothing is not an error.
     assert lib.cpg_gemm_destroy(null) == _lib.CPG_OK
     assert lib.cpg_peer_close(null) == _lib.CPG_OK and lib.cpg_peer_free(null) == _lib.CPG_OK
+
+
+def test_product_code_never_imports_the_oracle():
+    """The oracle is the checker only: the package imports nothing from it, and bench.py reaches
+    it only from its CPU-baseline / reference-arm functions."""
+    import ast
+    pkg = os.path.join(ROOT, "cutedsl_pingpong_gemm_b200")
+    for name in sorted(os.listdir(pkg)):
+        if name.endswith(".py"):
+            with open(os.path.join(pkg, name)) as f:
+                tree = ast.parse(f.read())
+            for node in ast.walk(tree):
+                if isinstance(node, ast.ImportFrom):
+                    assert not (node.module or "").startswith("oracle"), name
+                elif isinstance(node, ast.Import):
+                    assert not any(a.name.startswith("oracle") for a in node.names), name
+    with open(os.path.join(ROOT, "bench.py")) as f:
+        tree = ast.parse(f.read())
+    users = set()
+    for fn in ast.walk(tree):
+        if isinstance(fn, ast.FunctionDef):
+            for node in ast.walk(fn):
+                if isinstance(node, ast.ImportFrom) and (node.module or "").startswith("oracle"):
+                    users.add(fn.name)
+    assert users == {"cpu_matmul_rate", "run_reference"}, users
