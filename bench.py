@@ -74,6 +74,11 @@ WORKLOADS = {
     # reduced with one NCCL reduce-scatter, then cast to BF16 (strong scaling).
     "tallk": dict(m=2048, n=2048, k=131072, a_scale=1.0, b_scale=131072 ** -0.5, bias=False,
                   m_is_per_gpu=False, fp8=None, split="k"),
+    # The reference's own benchmark (gemm_base.py:578-609): 65536 x 4096 x 8192 BF16, A and B
+    # ~ N(0,1), with its constructor arguments: tile (128, 256), epi (128, 32), cluster (2, 1, 1),
+    # atom (2, 1), ab_stage=3, reuse_ab=False, is_persistent=True (the static schedule).
+    "ref_harness": dict(m=65536, n=4096, k=8192, a_scale=1.0, b_scale=1.0, bias=False,
+                        m_is_per_gpu=True, fp8=None, ref_ctor=True),
 }
 
 
@@ -258,6 +263,152 @@ def reduce_sum(x, world):
     return float(t.item())
 
 
+def gather_floats(values, world):
+    """Every rank's list of floats (same length on every rank), in rank order."""
+    if world == 1:
+        return [list(values)]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float("nan") if v is None else v for v in values], dtype=torch.float64,
+                     device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [[None if math.isnan(x) else x for x in o.tolist()] for o in out]
+
+
+def per_rank_summary(ms_local, clocks, world):
+    """Each rank's CUDA-event time per step and median SM clock, so that a multi-GPU line names
+    the rank (and clock) that set its max-over-ranks time."""
+    rows = gather_floats([ms_local, clocks.get("sm_mhz")], world)
+    return [{"rank": r, "ms_per_step": v[0], "sm_mhz": v[1]} for r, v in enumerate(rows)]
+
+
+# ------------------------------------------------------------------ post-run parity check
+# After the timed region every rank checks the D its last timed step wrote, on its own GPU in
+# fp64, against the product of the same device inputs: sampled rows element-wise and, for the
+# linear epilogues, the column and row sums of the whole of D (O(MK + NK) work: (1^T A) B^T and
+# A (B^T 1)).  Tolerance (the project spec, as in the tests): relative Frobenius <= 1e-2 (BF16) /
+# 3e-2 (FP8) and element-wise |D - R| <= 2^-8 |R| + K 2^-23 (|A| |B|^T) (+ the activation terms).
+# The reference harness checked its timed output the same way, right after the launch
+# (gemm_base.py:609-619: allclose and a count of wrong elements).
+BF16_REL = 2.0 ** -8
+ACC_SLACK_PER_K = 2.0 ** -23
+ACT_SLOPE = 1.13      # max |act'(y)| of relu, silu, gelu, gelu_tanh
+ACT_REL = 2.0 ** -18  # the device's expf / erff / tanhf against fp64
+PARITY_ROWS = 64
+
+
+def _act64(name, y):
+    import torch
+    if name is None:
+        return y
+    if name == "relu":
+        return y.clamp_min(0.0)
+    if name == "silu":
+        return y * torch.sigmoid(y)
+    if name == "gelu":
+        return 0.5 * y * (1.0 + torch.erf(y * 0.7071067811865476))
+    if name == "gelu_tanh":
+        return 0.5 * y * (1.0 + torch.tanh(0.7978845608028654 * (y + 0.044715 * y * y * y)))
+    raise ValueError(name)
+
+
+def expected_rows(pre, s, k, n, bias=None, act=None, gated=False):
+    """Expected D rows and their element-wise tolerance from the fp64 products of those rows,
+    ``pre`` = A_rows B^T and ``s`` = |A_rows| |B|^T (gated: B = [W_gate; W_up], 2n columns)."""
+    slack = k * ACC_SLACK_PER_K
+    if gated:
+        g, u = pre[:, :n], pre[:, n:]
+        tg, tu = slack * s[:, :n], slack * s[:, n:]
+        ag = _act64(act, g)
+        r = ag * u
+        tol = (BF16_REL * r.abs() + ACT_SLOPE * tg * (u.abs() + tu) + ag.abs() * tu
+               + ACT_REL * (g.abs() * u.abs() + r.abs()) + 1e-6)
+        return r, tol
+    tol_pre = slack * s
+    if bias is not None:
+        pre = pre + bias.double()
+        tol_pre = tol_pre + 2.0 ** -24 * bias.double().abs()
+    if act is None:
+        return pre, BF16_REL * pre.abs() + tol_pre
+    r = _act64(act, pre)
+    return r, BF16_REL * r.abs() + ACT_SLOPE * tol_pre + ACT_REL * pre.abs() + 1e-6
+
+
+def rows_verdict(d_rows, r, tol):
+    """(worst |D - R| / tol, relative Frobenius error) of sampled rows."""
+    import torch
+    diff = d_rows.double() - r
+    ratio = float((diff.abs() / tol.clamp_min(1e-300)).max()) if diff.numel() else 0.0
+    den = float(torch.linalg.vector_norm(r))
+    frob = float(torch.linalg.vector_norm(diff)) / den if den > 0 else 0.0
+    return ratio, frob
+
+
+def checksum_ratio(d, a, b64, k, bias=None):
+    """Worst |sum - expected| / bound over the column sums and row sums of the whole of D."""
+    import torch
+    f64 = torch.float64
+    m, n = d.shape
+    ref_col = torch.mv(b64, a.sum(0, dtype=f64))
+    abs_col = torch.mv(b64.abs(), a.abs().sum(0, dtype=f64))
+    ref_row = torch.mv(a.double(), b64.sum(0))
+    abs_row = torch.mv(a.double().abs(), b64.abs().sum(0))
+    if bias is not None:
+        ref_col = ref_col + m * bias.double()
+        ref_row = ref_row + bias.double().sum()
+    da = d.abs()
+    bound_col = BF16_REL * da.sum(0, dtype=f64) + k * ACC_SLACK_PER_K * abs_col + 1e-6 * m
+    bound_row = BF16_REL * da.sum(1, dtype=f64) + k * ACC_SLACK_PER_K * abs_row + 1e-6 * n
+    r_col = float(((d.sum(0, dtype=f64) - ref_col).abs() / bound_col).max())
+    r_row = float(((d.sum(1, dtype=f64) - ref_row).abs() / bound_row).max())
+    return max(r_col, r_row)
+
+
+def parity_dense(d, a, b, k, bias=None, act=None, gated=False, frob_tol=1e-2, seed=0):
+    """Post-run check of one rank's whole D = epilogue(A B^T) (A, B: the kernel's operands, or
+    their dequantised values for FP8).  Returns the rank's verdict dict."""
+    import torch
+    m = d.shape[0]
+    n = d.shape[1]
+    g = torch.Generator().manual_seed(seed)
+    rows = torch.randperm(m, generator=g)[:PARITY_ROWS].sort().values.to(d.device)
+    b64 = b.double()
+    a_s = a[rows].double()
+    pre = a_s @ b64.t()
+    s = a_s.abs() @ b64.abs().t()
+    r, tol = expected_rows(pre, s, k, n, bias, act, gated)
+    ratio, frob = rows_verdict(d[rows], r, tol)
+    checks = f"{rows.numel()} sampled rows element-wise"
+    if act is None and not gated:
+        ratio = max(ratio, checksum_ratio(d, a, b64, k, bias))
+        checks += " + fp64 column and row sums of all of D"
+    nan = bool(torch.isnan(d).any())
+    return {"ok": ratio <= 1.0 and frob <= frob_tol and not nan, "max_ratio": ratio,
+            "frob_sampled": frob, "frob_tol": frob_tol, "checks": checks}
+
+
+def parity_reduce(res, world):
+    """Combine the ranks' verdicts (collective: every rank calls it once)."""
+    if world == 1:
+        return dict(res, ranks=1)
+    vals = gather_floats([1.0 if res["ok"] else 0.0, res["max_ratio"], res["frob_sampled"]],
+                         world)
+    return dict(res, ok=all(v[0] == 1.0 for v in vals), max_ratio=max(v[1] for v in vals),
+                frob_sampled=max(v[2] for v in vals), ranks=world)
+
+
+def dequantized(q, scales, mode, block=None):
+    """FP32 values of E4M3 operands on the device: q * s per tensor or per block."""
+    qf = q.float()
+    if mode == "tensor":
+        return qf * scales
+    rows, cols = qf.shape
+    if block == (1, 128):  # scales [ceil(K/128), rows]
+        return qf * scales.t().repeat_interleave(128, dim=1)[:, :cols]
+    return qf * scales.repeat_interleave(128, dim=0).repeat_interleave(128, dim=1)[:rows, :cols]
+
+
 # ------------------------------------------------------------------ CPU baseline (oracle)
 def cpu_matmul_rate(rows, n, k, seconds, max_reps=50, seed=0):
     """fp32 CPU matmul of a rows x k slab against B^T (the oracle's computation)."""
@@ -276,6 +427,38 @@ def cpu_matmul_rate(rows, n, k, seconds, max_reps=50, seed=0):
         if el >= seconds or reps >= max_reps:
             break
     return 2.0 * rows * n * k * reps / el / 1e12, cores, reps, el
+
+
+def workload_config(args, world):
+    """The workload's ``config``: the same dict in both arms (the kernel's own choices go to the
+    GPU arm's ``kernel_config``)."""
+    w = WORKLOADS[args.workload]
+    n, k = w["n"], w["k"]
+    m_w = args.m or w["m"]
+    if w.get("split") == "k":
+        peer = args.exchange == "p2p" and world > 1
+        if world == 1:
+            par = "1 GPU, K split inside the GPU"
+        elif peer:
+            par = (f"split-K x{world} (GEMM epilogue adds partials into the owners' memory over "
+                   f"NVLink), K split again inside each GPU")
+        else:
+            par = f"split-K x{world} (NCCL reduce-scatter), K split again inside each GPU"
+        return {"workload": args.workload, "m": m_w, "n": n, "k": k, "parallelism": par,
+                "rs_chunks": max(1, args.chunks) if not peer else 1,
+                "l2": "A and B 512 MiB per GPU at 1 GPU; no flush"}
+    if w.get("groups"):
+        return {"workload": args.workload, "rows_per_gpu": m_w, "n": n, "k": k,
+                "groups": w["groups"], "gated": bool(w.get("gated")), "activation": w.get("act"),
+                "parallelism": f"tokens per GPU x{world}, experts replicated",
+                "l2": "B is 1.9 GB; no flush"}
+    m = m_w if w["m_is_per_gpu"] else m_w // world
+    return {"workload": args.workload, "m_per_gpu": m, "n": n, "k": k, "m_total": m * world,
+            "parallelism": f"m-shard x{world}, B replicated", "bias": bool(w["bias"]),
+            "activation": w.get("act") or args.activation, "gated": bool(w.get("gated")),
+            "fp8_scales": w["fp8"],
+            "l2": ("inputs larger than L2 (B 128 MiB, A 2 MiB, read once per step); no flush"
+                   if w.get("small_m") else "inputs larger than L2 (126 MB); no flush")}
 
 
 def run_reference(args, world, rank):
@@ -325,9 +508,9 @@ def run_reference(args, world, rank):
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak" if w["m_is_per_gpu"] else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "m": w["m"], "n": n, "k": k, "rows_per_step": rows},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "rows_per_step": rows},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference kernel is sm_90a CuTe-DSL (wgmma) and cannot run on sm_100; the "
                 "reference arm is the fp32 CPU oracle of D = A @ B.T",
@@ -350,7 +533,54 @@ def metric_name(workload, m_override=0):
             "tallk": "GEMM TFLOPS (BF16 2048x2048x131072 split-K over GPUs)",
             "moe": "GEMM TFLOPS (BF16 grouped MoE up-projection, 8 experts x [2x14336, 4096], "
                    "16384 token rows per GPU, fused SwiGLU)",
+            "ref_harness": "GEMM TFLOPS (BF16 65536x4096x8192 per GPU, the reference harness "
+                           "shape and constructor arguments)",
             }[workload]
+
+
+def parity_splitk(out, a_k, b_k, m, n, k, world, rank):
+    """Post-run check of this rank's rows of a split-K D = sum_q A_q B_q^T, where rank q holds
+    the K range q of A and B.  Every rank computes its fp64 contributions to the sampled rows
+    (PARITY_ROWS // world rows of every rank's range) and to every rank's column and row sums;
+    summed over the ranks (all-reduce, the same collectives on every rank) they give the
+    expected values of this rank's rows."""
+    import torch
+    import torch.distributed as dist
+    from cutedsl_pingpong_gemm_b200.sharding import row_range
+    f64 = torch.float64
+    dev = a_k.device
+    a64, b64 = a_k.double(), b_k.double()
+    per = max(1, PARITY_ROWS // world)
+    g = torch.Generator().manual_seed(5)
+    samples, ranges = [], []
+    for q in range(world):
+        s0, s1 = row_range(m, world, q)
+        ranges.append((s0, s1))
+        samples.append((torch.randperm(s1 - s0, generator=g)[:per] + s0).sort().values)
+    rows = torch.cat(samples).to(dev)
+    pre = a64[rows] @ b64.t()
+    sab = a64[rows].abs() @ b64.abs().t()
+    col = torch.stack([torch.mv(b64, a64[s0:s1].sum(0)) for s0, s1 in ranges])
+    col_abs = torch.stack([torch.mv(b64.abs(), a64[s0:s1].abs().sum(0)) for s0, s1 in ranges])
+    row = torch.mv(a64, b64.sum(0))
+    row_abs = torch.mv(a64.abs(), b64.abs().sum(0))
+    if world > 1:
+        for t in (pre, sab, col, col_abs, row, row_abs):
+            dist.all_reduce(t)
+    s0, s1 = ranges[rank]
+    mine = slice(rank * per, rank * per + samples[rank].numel())
+    r, tol = expected_rows(pre[mine], sab[mine], k, n)
+    ratio, frob = rows_verdict(out[(samples[rank] - s0).to(dev)], r, tol)
+    da = out.abs()
+    bound_col = BF16_REL * da.sum(0, dtype=f64) + k * ACC_SLACK_PER_K * col_abs[rank] + 1e-6 * (s1 - s0)
+    bound_row = BF16_REL * da.sum(1, dtype=f64) + k * ACC_SLACK_PER_K * row_abs[s0:s1] + 1e-6 * n
+    ratio = max(ratio, float(((out.sum(0, dtype=f64) - col[rank]).abs() / bound_col).max()),
+                float(((out.sum(1, dtype=f64) - row[s0:s1]).abs() / bound_row).max()))
+    nan = bool(torch.isnan(out).any())
+    return {"ok": ratio <= 1.0 and frob <= 1e-2 and not nan, "max_ratio": ratio,
+            "frob_sampled": frob, "frob_tol": 1e-2,
+            "checks": (f"{per} sampled rows per rank element-wise + fp64 column and row sums of "
+                       f"each rank's rows (contributions of every K range summed over ranks)")}
 
 
 # ------------------------------------------------------------------ GPU arm: tall-K split-K
@@ -416,6 +646,11 @@ def run_tallk(args, world, rank, local):
     barrier(world)
     ms_local = e0.elapsed_time(e1) / args.steps
     ms = reduce_max(ms_local, world)
+    clocks = sampler.summary()
+    per_rank = per_rank_summary(ms_local, clocks, world)
+    if peer:
+        sk.check_status()
+    parity = parity_reduce(parity_splitk(out, a_k, b_k, m, n, k, world, rank), world)
     total_flops = 2.0 * m * n * k
     value = total_flops / (ms * 1e-3) / 1e12
     peaks, peak_src = load_peaks()
@@ -426,27 +661,25 @@ def run_tallk(args, world, rank, local):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": args.workload, "m": m, "n": n, "k": k,
-                       "parallelism": (f"split-K x{world} (GEMM epilogue adds partials into the "
-                                       f"owners' memory over NVLink), auto in-GPU split" if peer
-                                       else f"split-K x{world} (NCCL reduce-scatter), auto "
-                                       f"in-GPU split"),
-                       "rs_chunks": chunks, "scheduler": args.scheduler,
-                       "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
-                       "rows_per_rank": s1 - s0, "l2": "inputs 512 MiB per rank at 1 GPU; no flush"},
+            "config": workload_config(args, world),
+            "kernel_config": {"scheduler": args.scheduler, "tile": [128, tile_n],
+                              "cluster": [cm, 1, 1], "ab_stage": stages,
+                              "exchange": "p2p" if peer else ("nccl" if world > 1 else None),
+                              "rows_per_rank": s1 - s0},
             "roofline": {"bound": "tensor", "achieved": total_flops / world / (ms_local * 1e-3) / 1e12,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": total_flops / world / (ms_local * 1e-3) / 1e12 / peaks["bf16_tflops"],
                          "peak_source": f"{peak_src} bf16_tflops", "traffic": None,
                          "note": "achieved covers GEMM + reduce-scatter + cast per step"},
-            "clocks": sampler.summary(), "gpu_launches": launches[0] * world, "e2e": None,
-            "cpu_baseline": None,
+            "clocks": clocks, "per_rank": per_rank, "parity": parity,
+            "gpu_launches": launches[0] * world, "e2e": None, "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
     del out
     if peer:
-        sk.check_status()
         sk.close()
+    if not parity["ok"]:
+        raise SystemExit(f"parity check failed: {parity}")
 
 
 # ------------------------------------------------------------------ GPU arm: grouped (MoE)
@@ -512,6 +745,27 @@ def run_grouped(args, world, rank, local):
     barrier(world)
     ms_local = e0.elapsed_time(e1) / args.steps
     ms = reduce_max(ms_local, world)
+    clocks = sampler.summary()
+    per_rank = per_rank_summary(ms_local, clocks, world)
+    # Post-run check: sampled rows of every non-empty group against that group's weights.
+    worst, frob, bad_nan = 0.0, 0.0, bool(torch.isnan(d).any())
+    g = torch.Generator().manual_seed(9)
+    for gi in range(groups):
+        r0, r1 = off[gi], off[gi + 1]
+        if r1 <= r0:
+            continue
+        rows = (torch.randperm(r1 - r0, generator=g)[:max(1, PARITY_ROWS // groups)] + r0).sort().values
+        rows = rows.to(dev)
+        b64 = b[gi].double()
+        pre = a[rows].double() @ b64.t()
+        sab = a[rows].double().abs() @ b64.abs().t()
+        r, tol = expected_rows(pre, sab, k, n, None, act, gated)
+        ratio_g, frob_g = rows_verdict(d[rows], r, tol)
+        worst, frob = max(worst, ratio_g), max(frob, frob_g)
+    parity = parity_reduce({"ok": worst <= 1.0 and frob <= 1e-2 and not bad_nan,
+                            "max_ratio": worst, "frob_sampled": frob, "frob_tol": 1e-2,
+                            "checks": f"{max(1, PARITY_ROWS // groups)} sampled rows per group "
+                                      f"element-wise (fused SwiGLU: no linear checksums)"}, world)
     flops_per_gpu = 2.0 * t * b_rows * k
     value = flops_per_gpu * world / (ms * 1e-3) / 1e12
     achieved = flops_per_gpu / (ms_local * 1e-3) / 1e12
@@ -522,12 +776,10 @@ def run_grouped(args, world, rank, local):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": args.workload, "rows_per_gpu": t, "n": n, "k": k,
-                       "groups": groups, "group_rows": sizes, "tile": [128, tile_n],
-                       "cluster": [cm, 1, 1], "ab_stage": stages, "activation": act,
-                       "gated": gated, "scheduler": args.scheduler,
-                       "parallelism": f"tokens per GPU x{world}, experts replicated",
-                       "l2": "B is 1.9 GB; no flush"},
+            "config": workload_config(args, world),
+            "kernel_config": {"group_rows": sizes, "tile": [128, tile_n], "cluster": [cm, 1, 1],
+                              "ab_stage": stages, "scheduler": args.scheduler},
+            "per_rank": per_rank, "parity": parity,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                          "peak_source": f"{peak_src} bf16_tflops (cuBLAS burst)",
@@ -535,10 +787,12 @@ def run_grouped(args, world, rank, local):
                                                                 peaks["bf16_tflops"]),
                          "traffic": None, "algorithmic_flops_per_launch": flops_per_gpu,
                          "kernel": "group_tile_prefix_kernel + cpg::gemm_sm100_kernel (grouped)"},
-            "clocks": sampler.summary(), "gpu_launches": 2 * args.steps * world, "e2e": None,
+            "clocks": clocks, "gpu_launches": 2 * args.steps * world, "e2e": None,
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
+    if not parity["ok"]:
+        raise SystemExit(f"parity check failed: {parity}")
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -567,7 +821,8 @@ def run_cpg(args, world, rank, local):
     scale_a = scale_b = None
     if w.get("small_m"):
         args.cluster_m = 1  # one 128-row tile: the pair's second CTA would have no rows
-    tile_n = args.tile_n or (128 if w.get("small_m") else
+    ref_ctor = bool(w.get("ref_ctor"))  # the reference harness's own constructor arguments
+    tile_n = args.tile_n or (128 if w.get("small_m") else 256 if ref_ctor else
                              (512 if args.cluster_m == 2 or gated else 256))
     if w["fp8"] is not None:
         from cutedsl_pingpong_gemm_b200.quant import quantize_e4m3
@@ -581,8 +836,9 @@ def run_cpg(args, world, rank, local):
         torch.cuda.synchronize()
 
     cm = args.cluster_m
-    stages = args.stages or {(512, 2): 3, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get((tile_n, cm),
-                                                                                   8 if cm == 2 else 6)
+    stages = args.stages or (3 if ref_ctor else
+                             {(512, 2): 3, (512, 1): 2, (256, 2): 6, (256, 1): 4}.get(
+                                 (tile_n, cm), 8 if cm == 2 else 6))
     epi_stage = args.epi_stages or 2
     if w["fp8"] == "block" and not args.stages:
         # Deepest ring that fits 227 KiB next to 8 promotion warps' epilogue staging (4 KiB per
@@ -590,9 +846,9 @@ def run_cpg(args, world, rank, local):
         stages, epi_stage = {(128, 1): (5, 2), (128, 2): (8, 1), (256, 1): (4, 1),
                              (256, 2): (6, 1)}[(tile_n, cm)]
     gemm = GemmSM90(tile_shape_mn=(128, tile_n), epi_tile_mn=(128, 32),
-                    cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(1, 1), ab_stage=stages,
-                    epi_stage=epi_stage, raster_order=RasterOrder.AlongN, reuse_ab=False,
-                    is_persistent=True,
+                    cluster_shape_mnk=(cm, 1, 1), atom_layout_mn=(2, 1) if ref_ctor else (1, 1),
+                    ab_stage=stages, epi_stage=epi_stage, raster_order=RasterOrder.AlongN,
+                    reuse_ab=False, is_persistent=True,
                     dynamic_scheduler=args.scheduler == "dynamic")
     compiled = cpg_compile(gemm, a, b, d, stream, scale_a=scale_a, scale_b=scale_b, gated=gated)
     # The split is picked from the tile count (small M: K ranges or Stream-K; a partial last
@@ -665,6 +921,20 @@ def run_cpg(args, world, rank, local):
     status = plan.status()
     if status != 0:
         raise SystemExit(f"kernel status {status:#x}")
+    clocks = sampler.summary()
+    per_rank = per_rank_summary(ms_local, clocks, world)
+
+    # ---------------- post-run parity of the D the last timed step wrote (every rank)
+    if w["fp8"] is None:
+        a_ref, b_ref = a, b
+    elif w["fp8"] == "tensor":
+        a_ref, b_ref = dequantized(a, scale_a, "tensor"), dequantized(b, scale_b, "tensor")
+    else:
+        a_ref = dequantized(a, scale_a, "block", (1, 128))
+        b_ref = dequantized(b, scale_b, "block", (128, 128))
+    parity = parity_reduce(parity_dense(d, a_ref, b_ref, k, bias=bias, act=act, gated=gated,
+                                        frob_tol=3e-2 if w["fp8"] else 1e-2, seed=rank), world)
+    del a_ref, b_ref
 
     flops_per_gpu = 2.0 * m * b_rows * k  # a gated step computes gate and up: 2 N columns
     total_flops = flops_per_gpu * world
@@ -729,7 +999,12 @@ def run_cpg(args, world, rank, local):
         torch.cuda.synchronize()
         barrier(world)
         e2e_ms = reduce_max(f0.elapsed_time(f1) / args.e2e_steps, world)
+        # The downloaded D of the last step is the timed run's D, byte for byte (same inputs,
+        # and the kernel's summation order does not depend on the schedule).
+        last = sets[(args.e2e_steps - 1) % 2][3]
+        same = reduce_max(0.0 if torch.equal(last, d.cpu()) else 1.0, world) == 0.0
         e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "output_matches_timed_run": same,
                "h2d_bytes_per_step": int((a.numel() + b.numel()) * a.element_size() * world),
                "d2h_bytes_per_step": int(d.numel() * d.element_size() * world),
                "steps": args.e2e_steps, "ms_per_step": e2e_ms,
@@ -738,7 +1013,6 @@ def run_cpg(args, world, rank, local):
                        "pinned host memory and downloads D; uploads of step i + 1 and the "
                        "download of step i - 1 overlap the GEMM of step i (two buffer sets)"}
 
-    clocks = sampler.summary()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = 512
@@ -762,16 +1036,15 @@ def run_cpg(args, world, rank, local):
             "higher_is_better": True, "scaling": "weak" if w["m_is_per_gpu"] else "strong",
             "vs_baseline": None, "dtype": "e4m3" if w["fp8"] else "bf16", "data": "synthetic",
             "pct_nominal_dense_peak": 100.0 * value / (nominal * world),
-            "config": {"workload": args.workload, "m_per_gpu": m, "n": n, "k": k,
-                       "m_total": m * world, "parallelism": f"m-shard x{world}, B replicated",
-                       "tile": [128, tile_n], "cluster": [cm, 1, 1], "ab_stage": stages,
-                       "epi_stage": epi_stage, "fp8_scales": w["fp8"],
-                       "grid": list(info["grid"]), "smem_bytes": info["smem_bytes"],
-                       "l2": "inputs larger than L2 (A, B, D >= 128 MiB each for bf16_8192); no flush",
-                       "bias": bool(w["bias"]), "activation": act, "gated": gated,
-                       "split_k": split_k,
-                       "scheduler": gemm.dynamic_scheduler and "dynamic" or "static",
-                       "group_size": group_size, "cuda_graph": use_graph},
+            "config": workload_config(args, world),
+            "kernel_config": {"tile": [128, tile_n], "cluster": [cm, 1, 1],
+                              "atom": list(gemm.atom_layout_mnk[:2]), "ab_stage": stages,
+                              "epi_stage": epi_stage, "grid": list(info["grid"]),
+                              "smem_bytes": info["smem_bytes"], "split_k": split_k,
+                              "scheduler": gemm.dynamic_scheduler and "dynamic" or "static",
+                              "group_size": group_size, "cuda_graph": use_graph,
+                              "reference_constructor": ref_ctor},
+            "per_rank": per_rank, "parity": parity,
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": min_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
@@ -794,13 +1067,16 @@ def run_cpg(args, world, rank, local):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if not parity["ok"] or (e2e is not None and not e2e["output_matches_timed_run"]):
+        raise SystemExit(f"parity check failed: {parity}")
 
 
 def main():
     args = parse_args()
     if args.scheduler == "auto":
         w = WORKLOADS[args.workload]
-        dense = not (w.get("small_m") or w.get("groups") or w["fp8"] == "block")
+        dense = not (w.get("small_m") or w.get("groups") or w["fp8"] == "block"
+                     or w.get("ref_ctor"))
         args.scheduler = "dynamic" if dense else "static"
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -1500,14 +1500,17 @@ extern "C" int cpg_gemm_splitk_static(const cpg_gemm_config* cfg, const cpg_gemm
   if ((prob->lda * eab) % 16 != 0 || (prob->ldb * eab) % 16 != 0 || (prob->ldd * 2) % 16 != 0)
     return fail(CPG_ERR_ALIGNMENT, "row strides must be multiples of 16 bytes");
   const int64_t ldw = (prob->n + 3) / 4 * 4;  // FP32 [M, N] rows padded to 16 bytes
-  const int64_t need = prob->m * ldw * static_cast<int64_t>(sizeof(float));
-  if (need > static_cast<int64_t>(kStaticScratchBytes))
+  // Compare by division first: M and N may each be up to 2^31 - 1, so M * ldw * 4 could pass
+  // 2^63 and wrap before a multiplied comparison saw it.
+  const int64_t cap_floats = static_cast<int64_t>(kStaticScratchBytes / sizeof(float));
+  if (prob->m > 0 && ldw > cap_floats / prob->m)
     return fail(CPG_ERR_INVALID_SHAPE,
-                "M x N = %lld x %lld needs %lld bytes of FP32 scratch; the static scratch holds "
+                "M x N = %lld x %lld needs %.0f bytes of FP32 scratch; the static scratch holds "
                 "%lld bytes (M * round_up(N, 4) <= %lld)",
                 static_cast<long long>(prob->m), static_cast<long long>(prob->n),
-                static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes),
-                static_cast<long long>(kStaticScratchBytes / sizeof(float)));
+                static_cast<double>(prob->m) * static_cast<double>(ldw) * sizeof(float),
+                static_cast<long long>(kStaticScratchBytes), static_cast<long long>(cap_floats));
+  const int64_t need = prob->m * ldw * static_cast<int64_t>(sizeof(float));  // <= 16 MiB now
   if (prob->m == 0 || prob->n == 0) return CPG_OK;
   if (d == nullptr) return fail(CPG_ERR_NULL, "D is NULL");
   if ((reinterpret_cast<uintptr_t>(d) & 15u) != 0) return fail(CPG_ERR_ALIGNMENT, "D alignment");

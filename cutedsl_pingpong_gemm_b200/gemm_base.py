@@ -19,7 +19,8 @@ TMEM, TMA loads/stores, persistent grouped tile scheduler); there is no other ex
 
 Argument meaning on sm_100a:
 
-* ``tile_shape_mn``: the CTA tile, (128, N) with N in {64, 128, 256}.
+* ``tile_shape_mn``: the CTA tile, (128, N) with N in {64, 128, 256, 512} (512: CTA pairs only,
+  the benchmarks' default: a 256 x 512 pair tile fills the 512 TMEM columns).
 * ``cluster_shape_mnk``: (1,1,1) runs one CTA per tile; (2,1,1) runs CTA pairs that issue
   ``tcgen05.mma.cta_group::2`` on a 256-row tile (each CTA loads its own A rows and half of B);
   (1,2,1) and (2,2,1) group independent CTAs/pairs along N.  Clusters only change the tile order
@@ -468,7 +469,9 @@ class GemmSM90:
         self.raster_order = raster_order
         self.scheduler_group_size = 8
         self.cluster_shape_mnk = tuple(cluster_shape_mnk)
-        self.cta_tile_shape_mnk = (*tile_shape_mn, 64)  # K tile: one 128-byte swizzled BF16 row
+        # K tile: one 128-byte swizzled row of the operands (64 BF16; compile() sets 128 for
+        # FP8 E4M3 operands, see cta_tile_k).
+        self.cta_tile_shape_mnk = (*tile_shape_mn, 64)
         tile_M, tile_N = self.cta_tile_shape_mnk[0], self.cta_tile_shape_mnk[1]
 
         # Atom layout (gemm_base.py:72-75)
@@ -509,6 +512,13 @@ class GemmSM90:
             "Dynamic scheduler runs several tiles per CTA and can't reuse AB for epilogue"
         self._compiled: Optional[CompiledGemm] = None
 
+    @staticmethod
+    def cta_tile_k(dtype) -> int:
+        """K extent of one pipeline stage: a 128-byte swizzled row of the operand type (64 BF16
+        elements, 128 FP8 E4M3)."""
+        import torch
+        return 128 if dtype == torch.float8_e4m3fn else 64
+
     @property
     def max_active_clusters(self) -> int:
         """gemm_base.py:117, queried lazily (it needs the GPU)."""
@@ -539,6 +549,7 @@ class GemmSM90:
         one element, as in ``__call__``) plan the block-scaled FP8 kernel instead of the plain one;
         ``gated`` plans the gated FFN form (B = [W_gate; W_up])."""
         compiled = CompiledGemm(self)
+        self.cta_tile_shape_mnk = (*self.cta_tile_shape_mnk[:2], self.cta_tile_k(a.dtype))
         block = scale_a is not None and scale_a.numel() > 1
         compiled.plan_for(a, b, c, _lib.CPG_SCALE_BLOCK if block else _lib.CPG_SCALE_TENSOR,
                           gated=gated)

@@ -105,9 +105,17 @@ class SimpleTileScheduler:
 
     @staticmethod
     def _map_cta_coords(params: "SimpleTileScheduler.Params", cluster_id_in_problem: int) -> Tuple[int, int]:
-        """tile_scheduler.py:125-146 for a single linear cluster id."""
-        m = SimpleTileScheduler.cluster_map(params, cluster_id_in_problem + 1)
-        return int(m[cluster_id_in_problem, 0]), int(m[cluster_id_in_problem, 1])
+        """tile_scheduler.py:125-146 for one linear cluster id, in O(1): the group and the
+        position in it come from the params' FastDivmods (the kernels' host/device arithmetic),
+        every second group runs its slow coordinate backwards."""
+        group_id, id_in_group = params.dm_num_clusters_in_group.divmod(int(cluster_id_in_problem))
+        dm = params.dm_group_size if group_id < params.num_groups_regular else params.dm_group_size_tail
+        slow, fast_in_group = dm.divmod(id_in_group)
+        if group_id % 2 == 1:
+            nslow = params.ncluster_mnl[1] if params.raster_order == RasterOrder.AlongM else params.ncluster_mnl[0]
+            slow = nslow - 1 - slow
+        fast = group_id * params.dm_group_size.divisor + fast_in_group
+        return (slow, fast) if params.raster_order == RasterOrder.AlongN else (fast, slow)
 
     @staticmethod
     def cluster_map(params: "SimpleTileScheduler.Params", n: int = None) -> np.ndarray:
@@ -134,19 +142,30 @@ class SimpleTileScheduler:
         return out
 
     @staticmethod
-    def schedule(params: "SimpleTileScheduler.Params", grid: Tuple[int, int, int]) -> Dict[Tuple[int, int, int], List[Tuple[int, int]]]:
-        """Per-CTA (pid_m, pid_n) sequence for a launch of ``grid`` (tile_scheduler.py:94-183)."""
+    def schedule(params: "SimpleTileScheduler.Params", grid: Tuple[int, int, int]) -> Dict[Tuple[int, int, int], List[Tuple[int, ...]]]:
+        """Per-CTA tile sequence for a launch of ``grid`` (tile_scheduler.py:94-183).
+
+        With one batch (L = 1) the entries are ``(pid_m, pid_n)``, exactly the reference's
+        schedule.  With L > 1 they are ``(pid_m, pid_n, l)``: a persistent CTA's linear cluster
+        id is first split into (batch l, id within the problem) with ``dm_clusters_per_problem``,
+        as the sm_100a kernels do (the reference fixes the batch at 0, tile_scheduler.py:96, and
+        so never runs past one problem); a non-persistent CTA's batch is ``blockIdx.z``."""
         cmap = SimpleTileScheduler.cluster_map(params)
         cm, cn = params.cluster_shape_mn
-        total = params.ncluster_mnl[0] * params.ncluster_mnl[1] * params.ncluster_mnl[2]
+        per_problem = params.ncluster_mnl[0] * params.ncluster_mnl[1]
+        nl = params.ncluster_mnl[2]
+        total = per_problem * nl
         out = {}
         for bz in range(grid[2]):
             for by in range(grid[1]):
                 for bx in range(grid[0]):
                     if params.is_persistent:
-                        cids = list(range(bz, total, grid[2]))
+                        work = [divmod(c, per_problem) for c in range(bz, total, grid[2])]
                     else:
-                        cids = [(bx // cm) + (by // cn) * (grid[0] // cm)]
-                    out[(bx, by, bz)] = [(int(cmap[c, 0]) * cm + bx % cm, int(cmap[c, 1]) * cn + by % cn)
-                                         for c in cids]
+                        work = [(bz, (bx // cm) + (by // cn) * (grid[0] // cm))]
+                    tiles = []
+                    for l, c in work:
+                        t = (int(cmap[c, 0]) * cm + bx % cm, int(cmap[c, 1]) * cn + by % cn)
+                        tiles.append(t if nl == 1 else t + (l,))
+                    out[(bx, by, bz)] = tiles
         return out

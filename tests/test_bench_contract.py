@@ -53,3 +53,77 @@ def test_bench_helpers():
     sizes = bench.group_sizes(16384, 8, seed=11)
     assert sum(sizes) == 16384 and len(sizes) == 8 and min(sizes) > 0
     assert sizes == bench.group_sizes(16384, 8, seed=11)
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    return bench
+
+
+def test_both_arms_share_the_workload_config():
+    """The reference arm and the GPU arm print the same ``config`` (both from workload_config),
+    so the two lines describe the same workload key for key."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+         "ref_harness", "--steps", "3", "--warmup", "3"],
+        cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][0])
+    bench = _bench_module()
+
+    class Args:
+        workload, m, exchange, chunks, activation = "ref_harness", 0, "p2p", 1, None
+
+    assert d["config"] == bench.workload_config(Args, 1)
+    assert d["config"]["m_per_gpu"] == 65536 and d["config"]["n"] == 4096
+    for w in bench.WORKLOADS:
+        Args.workload = w
+        cfg = bench.workload_config(Args, 4)
+        assert cfg["workload"] == w and cfg["k"] == bench.WORKLOADS[w]["k"]
+
+
+def test_post_run_parity_check_accepts_the_product_and_rejects_planted_mistakes():
+    """bench.py's post-run check on CPU tensors: a correctly rounded D passes, D with one wrong
+    element, a missing bias, or a wrong activation fails; the split-K form at one rank too."""
+    import torch
+    bench = _bench_module()
+    g = torch.Generator().manual_seed(3)
+    m, n, k = 192, 160, 512
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=g) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(n, generator=g).to(torch.bfloat16)
+    r = a.double() @ b.double().t() + bias.double()
+    d = r.to(torch.bfloat16)
+    assert bench.parity_dense(d, a, b, k, bias=bias)["ok"]
+    bad = d.clone()
+    bad[7, 11] += 0.5
+    res = bench.parity_dense(bad, a, b, k, bias=bias)
+    assert not res["ok"] and res["max_ratio"] > 1  # caught by the checksums if not sampled
+    assert not bench.parity_dense(d, a, b, k)["ok"]  # bias left out of the expectation
+    act = bench._act64("silu", r).to(torch.bfloat16)
+    assert bench.parity_dense(act, a, b, k, bias=bias, act="silu")["ok"]
+    assert not bench.parity_dense(act, a, b, k, bias=bias, act="gelu")["ok"]
+    # gated: B = [W_gate; W_up]
+    bg = torch.cat([b, b.flip(0)])
+    pre = a.double() @ bg.double().t()
+    dg = (bench._act64("silu", pre[:, :n]) * pre[:, n:]).to(torch.bfloat16)
+    assert bench.parity_dense(dg, a, bg, k, act="silu", gated=True)["ok"]
+    assert not bench.parity_dense(dg * 1.05, a, bg, k, act="silu", gated=True)["ok"]
+    # split-K at one rank: the rank's rows are all of D
+    d0 = (a.double() @ b.double().t()).to(torch.bfloat16)
+    assert bench.parity_splitk(d0, a, b, m, n, k, 1, 0)["ok"]
+    d1 = d0.clone()
+    d1[100] = 0
+    assert not bench.parity_splitk(d1, a, b, m, n, k, 1, 0)["ok"]
+    # FP8 operands are checked through their dequantised values
+    q = torch.randn(256, 300, generator=g).to(torch.float8_e4m3fn)
+    s_rows = torch.rand(3, 256, generator=g) + 0.5
+    deq = bench.dequantized(q, s_rows, "block", (1, 128))
+    assert torch.equal(deq[:, 130], q[:, 130].float() * s_rows[1])
+    s_blk = torch.rand(2, 3, generator=g) + 0.5
+    deq = bench.dequantized(q, s_blk, "block", (128, 128))
+    assert torch.equal(deq[200, 290], q[200, 290].float() * s_blk[1, 2])

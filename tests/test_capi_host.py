@@ -89,6 +89,35 @@ def test_host_schedule_matches_oracle_schedule(lib):
             assert ours == ts.schedule(po, ts.get_grid_shape(po, 5))
 
 
+def test_map_cta_coords_single_id_matches_reference(lib, golden_maps):
+    """The O(1) single-id map equals the reference-executed map at every id of every config."""
+    index, maps = golden_maps
+    for cfg in index["configs"][:12]:
+        p = _params(cfg)
+        want = maps[cfg["key"]]
+        for cid in range(want.shape[0]):
+            assert SimpleTileScheduler._map_cta_coords(p, cid) == tuple(want[cid]), (cfg["key"], cid)
+
+
+@pytest.mark.parametrize("persistent", [True, False])
+@pytest.mark.parametrize("cluster", [(1, 1, 1), (2, 1, 1), (1, 2, 1)])
+def test_schedule_with_batches_covers_every_tile_once(lib, persistent, cluster):
+    """L = 3 batches: every (pid_m, pid_n, l) of the problem appears exactly once, and batch 0
+    holds the single-batch schedule's tiles."""
+    ntm, ntn, nl = 6, 10, 3
+    args = SimpleTileSchedulerArguments((ntm, ntn, nl), RasterOrder.AlongN, 8, cluster, persistent)
+    p = SimpleTileScheduler.to_underlying_arguments(args)
+    grid = SimpleTileScheduler.get_grid_shape(p, 7)
+    tiles = [t for seq in SimpleTileScheduler.schedule(p, grid).values() for t in seq]
+    assert sorted(tiles) == sorted((m, n, l) for m in range(ntm) for n in range(ntn)
+                                   for l in range(nl))
+    one = SimpleTileScheduler.to_underlying_arguments(
+        SimpleTileSchedulerArguments((ntm, ntn, 1), RasterOrder.AlongN, 8, cluster, persistent))
+    single = {t for seq in SimpleTileScheduler.schedule(
+        one, SimpleTileScheduler.get_grid_shape(one, 7)).values() for t in seq}
+    assert {t[:2] for t in tiles if t[2] == 0} == single
+
+
 def test_sched_params_reject_cluster_k(lib):
     args = SimpleTileSchedulerArguments((4, 4, 1), RasterOrder.AlongN, 8, (1, 1, 2), True)
     with pytest.raises(_lib.CpgError) as e:
@@ -251,6 +280,22 @@ def test_entry_points_reject_bad_arguments_before_touching_the_gpu(lib):
     # Destroying or closing nothing is not an error.
     assert lib.cpg_gemm_destroy(null) == _lib.CPG_OK
     assert lib.cpg_peer_close(null) == _lib.CPG_OK and lib.cpg_peer_free(null) == _lib.CPG_OK
+
+
+def test_static_splitk_rejects_huge_extents_without_overflow(lib):
+    """M = N = 2^31 - 1 would need about 2^64 bytes of FP32 scratch: a size check that multiplies
+    first wraps past 2^63 and lets the call through.  The entry point must reject it with
+    CPG_ERR_INVALID_SHAPE before any CUDA call (none is possible here: no GPU)."""
+    big = (1 << 31) - 1
+    cfg = _lib.GemmConfigC(128, 256, 128, 32, 1, 1, 1, 1, 1, 4, 2, 1, 0, 1, 0, 8)
+    for m, n in ((big, big), (big, 4), (2, big), (4097, 1024)):
+        ldd = (n + 7) // 8 * 8
+        prob = _lib.GemmProblemC(m, n, 64, 64, 64, ldd, _lib.CPG_DTYPE_BF16, _lib.CPG_DTYPE_BF16,
+                                 _lib.CPG_SCALE_TENSOR, 2)
+        rc = lib.cpg_gemm_splitk_static(ctypes.byref(cfg), ctypes.byref(prob), None, None, None,
+                                        None, None)
+        assert rc == _lib.CPG_ERR_INVALID_SHAPE, (m, n, rc)
+        assert "static scratch" in lib.cpg_last_error_message().decode(), (m, n)
 
 
 def test_product_code_never_imports_the_oracle():
