@@ -32,6 +32,7 @@ CPG_SCALE_BLOCK = 1
 CPG_INJECT_SKIP_LOADS = 1
 CPG_SPLIT_K_STREAM = -1
 CPG_SPLIT_K_HYBRID = -2
+CPG_SPLIT_K_DECODE = -3
 
 CPG_ACT_NONE = 0
 CPG_ACT_RELU = 1
@@ -41,7 +42,7 @@ CPG_ACT_GELU_TANH = 4
 ACTIVATIONS = {None: CPG_ACT_NONE, "none": CPG_ACT_NONE, "relu": CPG_ACT_RELU,
                "silu": CPG_ACT_SILU, "gelu": CPG_ACT_GELU, "gelu_tanh": CPG_ACT_GELU_TANH}
 
-ABI_VERSION = 12
+ABI_VERSION = 13
 
 
 class CpgError(RuntimeError):

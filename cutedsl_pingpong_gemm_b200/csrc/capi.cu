@@ -13,6 +13,7 @@
 #include <string>
 
 #include "cpgemm.h"
+#include "gemm_decode.cuh"
 #include "gemm_fp8_block.cuh"
 #include "gemm_kernel.cuh"
 #include "peer_kernels.cuh"
@@ -359,11 +360,14 @@ struct cpg_gemm {
   const void* map_b_ptr;
   const void* map_d_ptr;
   CUtensorMap tm_a, tm_b, tm_d;
+  // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
+  int32_t decode;
+  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages;
 };
 
 extern "C" {
 
-int cpg_abi_version(void) { return 12; }
+int cpg_abi_version(void) { return 13; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -449,6 +453,185 @@ static int alloc_fixup_workspace(cpg_gemm* g, int64_t tiles) {
   return rc;
 }
 
+using DecodeFn = void (*)(const CUtensorMap, const CUtensorMap, const cpg::DecodeParams);
+
+static const void* decode_kernel(int dtype_ab, int dtype_d) {
+  DecodeFn fn;
+  if (dtype_ab == CPG_DTYPE_E4M3)
+    fn = dtype_d == CPG_DTYPE_F32 ? &cpg::gemm_decode_kernel<cpg::e4m3_t, float>
+                                  : &cpg::gemm_decode_kernel<cpg::e4m3_t, __nv_bfloat16>;
+  else
+    fn = dtype_d == CPG_DTYPE_F32 ? &cpg::gemm_decode_kernel<__nv_bfloat16, float>
+                                  : &cpg::gemm_decode_kernel<__nv_bfloat16, __nv_bfloat16>;
+  return reinterpret_cast<const void*>(fn);
+}
+
+// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 128 rows of B each; the K range of a
+// tile is split over a cluster of S CTAs, S the largest of 4, 2, 1 that keeps every CTA of the
+// grid resident at once (tiles * S <= SMs) and gives every CTA a k-block.  Stages: the deepest
+// ring that fits (at most the CTA's k-blocks).
+static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
+                              const cudaDeviceProp& prop, cpg_gemm** out) {
+  if (prob->m < 1 || prob->m > cpg::kDecodeMaxM)
+    return fail(CPG_ERR_INVALID_SHAPE, "the small-M kernel takes 1 <= M <= %d, got %lld",
+                cpg::kDecodeMaxM, static_cast<long long>(prob->m));
+  if (prob->scale_mode != CPG_SCALE_TENSOR || prob->gated || prob->grouped || prob->l > 1)
+    return fail(CPG_ERR_UNSUPPORTED,
+                "the small-M kernel has no block scales, gating, batches or groups");
+  const int64_t tiles = (prob->n + cpg::kDecodeTileN - 1) / cpg::kDecodeTileN;
+  if (tiles > 65535)
+    return fail(CPG_ERR_INVALID_SHAPE, "the small-M kernel takes N <= %d",
+                65535 * cpg::kDecodeTileN);
+  const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
+  const int64_t k_iters = (prob->k + bk - 1) / bk;
+  const int64_t sms = prop.multiProcessorCount;
+  int splits = 1;
+  for (int s = cpg::kDecodeMaxSplits; s > 1; s /= 2) {
+    if (tiles * s <= sms && k_iters >= s) {
+      splits = s;
+      break;
+    }
+  }
+  const int mma_n = static_cast<int>((prob->m + 15) / 16 * 16);
+  int tmem_cols = 32;
+  while (tmem_cols < mma_n) tmem_cols *= 2;
+  const int64_t kps = k_iters > 0 ? (k_iters + splits - 1) / splits : 0;
+  int stages = 0;
+  for (int st = cpg::kDecodeMaxStages; st >= 2; --st) {
+    if (static_cast<int64_t>(cpg::decode_layout(st, mma_n, splits).bytes) <=
+        static_cast<int64_t>(prop.sharedMemPerBlockOptin)) {
+      stages = st;
+      break;
+    }
+  }
+  if (stages == 0) return fail(CPG_ERR_SMEM, "the small-M kernel does not fit in shared memory");
+  if (kps >= 2 && stages > kps) stages = static_cast<int>(kps);
+  if (stages < 2) stages = 2;
+  const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits).bytes);
+  const void* fn = decode_kernel(prob->dtype_ab, prob->dtype_d);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(small-M kernel smem)");
+  int mac = 0;
+  {
+    cudaLaunchConfig_t lc = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.gridDim = dim3(splits, 1, 1);
+    lc.blockDim = dim3(cpg::kDecodeThreads, 1, 1);
+    lc.dynamicSmemBytes = smem;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&mac, fn, &lc);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters(small-M kernel)");
+    if (mac <= 0) return fail(CPG_ERR_NO_DEVICE, "the small-M kernel cannot be resident");
+  }
+
+  cpg_gemm* g = new cpg_gemm();
+  std::memset(static_cast<void*>(g), 0, sizeof(*g));
+  g->cfg = *cfg;
+  g->prob = *prob;
+  g->device = device;
+  g->v = Variant{cpg::kDecodeTileN, 1, prob->dtype_ab, prob->dtype_d, CPG_SCALE_TENSOR, fn,
+                 nullptr, cpg::kDecodeThreads, cpg::kEpiWarps};
+  g->smem_bytes = smem;
+  g->max_active_clusters = mac;
+  g->timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
+  const char* env = std::getenv("CPG_WAIT_TIMEOUT_MS");
+  if (env != nullptr && std::atoi(env) > 0) g->timeout_ns = uint64_t(std::atoi(env)) * 1000000ull;
+  // B streams through once; every cluster re-reads A (a few rows): keep A in L2.
+  g->l2_policy_a = 2;
+  g->l2_policy_b = 1;
+  g->k_iters = static_cast<int32_t>(k_iters);
+  g->k_iters_per_split = static_cast<int32_t>(kps);
+  g->splits = 1;  // no split-K ranges in the scheduler's sense: the cluster reduces in place
+  g->batches = 1;
+  g->sched = cpg::sched_params_create(1, static_cast<int32_t>(tiles > 0 ? tiles : 1), 1,
+                                      CPG_RASTER_ALONG_N, 1, 1, 1, 0);
+  g->grid[0] = splits;
+  g->grid[1] = static_cast<int32_t>(tiles > 0 ? tiles : 1);
+  g->grid[2] = 1;
+  g->cluster[0] = splits;
+  g->cluster[1] = 1;
+  g->cluster[2] = 1;
+  g->decode = 1;
+  g->dec_mma_n = mma_n;
+  g->dec_tmem_cols = tmem_cols;
+  g->dec_kps = static_cast<int32_t>(kps);
+  g->dec_splits = splits;
+  g->dec_stages = stages;
+  e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
+  if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+  if (e != cudaSuccess) {
+    cpg_gemm_destroy(g);
+    return cuda_fail(e, "small-M plan status word");
+  }
+  *out = g;
+  return CPG_OK;
+}
+
+static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const cpg_epilogue* epi,
+                      cudaStream_t st) {
+  const cpg_gemm_problem& pr = g->prob;
+  if (epi != nullptr && (epi->activation != CPG_ACT_NONE || epi->source != nullptr))
+    return fail(CPG_ERR_UNSUPPORTED, "the small-M kernel has no activation and no C source");
+  const int eab = elem_bytes(pr.dtype_ab);
+  const int bk = cpg::kRowBytes / eab;
+  if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b) {
+    int rc = encode_tiled(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda,
+                          g->dec_mma_n, bk);
+    if (rc != CPG_OK) return rc;
+    rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
+                      cpg::kDecodeTileN, bk);
+    if (rc != CPG_OK) return rc;
+    g->map_a_ptr = a;
+    g->map_b_ptr = b;
+    g->map_d_ptr = nullptr;
+    g->maps_valid = true;
+  }
+  cpg::DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = static_cast<int32_t>(pr.m);
+  p.n = static_cast<int32_t>(pr.n);
+  p.k = static_cast<int32_t>(pr.k);
+  p.mma_n = g->dec_mma_n;
+  p.tmem_cols = g->dec_tmem_cols;
+  p.k_iters = g->k_iters;
+  p.kps = g->dec_kps;
+  p.splits = g->dec_splits;
+  p.stages = g->dec_stages;
+  p.alpha = epi != nullptr ? epi->alpha : 1.0f;
+  p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
+  p.scale_b = epi != nullptr ? epi->scale_b : nullptr;
+  p.bias = epi != nullptr ? static_cast<const __nv_bfloat16*>(epi->bias) : nullptr;
+  p.d = d;
+  p.ldd = pr.ldd;
+  p.status = g->status_dev;
+  p.timeout_ns = g->timeout_ns;
+  p.l2_policy_a = g->l2_policy_a;
+  p.l2_policy_b = g->l2_policy_b;
+  cudaLaunchConfig_t lc = {};
+  cudaLaunchAttribute attr[1];
+  lc.gridDim = dim3(g->grid[0], g->grid[1], 1);
+  lc.blockDim = dim3(cpg::kDecodeThreads, 1, 1);
+  lc.dynamicSmemBytes = g->smem_bytes;
+  lc.stream = st;
+  if (g->dec_splits > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = g->dec_splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  void* args[] = {&g->tm_a, &g->tm_b, &p};
+  cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, args);
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "small-M kernel launch");
+}
+
 int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
                     cpg_gemm** out) {
   if (cfg == nullptr || prob == nullptr || out == nullptr)
@@ -499,6 +682,7 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   if (prop.major != 10)
     return fail(CPG_ERR_NO_DEVICE, "device %d is sm_%d%d; this build targets sm_100a", device,
                 prop.major, prop.minor);
+  if (prob->split_k == CPG_SPLIT_K_DECODE) return create_decode_plan(cfg, prob, device, prop, out);
 
   Variant v;
   const int cta_group = cfg->cluster_m == 2 ? 2 : 1;
@@ -516,7 +700,8 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
     return fail(CPG_ERR_UNSUPPORTED, "reuse_ab is not implemented for block-scaled FP8");
   if (prob->split_k < CPG_SPLIT_K_HYBRID)
     return fail(CPG_ERR_INVALID_SHAPE,
-                "split_k must be >= 0, CPG_SPLIT_K_STREAM or CPG_SPLIT_K_HYBRID");
+                "split_k must be >= 0, CPG_SPLIT_K_STREAM, CPG_SPLIT_K_HYBRID or "
+                "CPG_SPLIT_K_DECODE");
   const bool sk_any = prob->split_k == CPG_SPLIT_K_STREAM || prob->split_k == CPG_SPLIT_K_HYBRID;
   if (prob->split_k > 1 &&
       (prob->dtype_d != CPG_DTYPE_F32 || v.scale_mode != CPG_SCALE_TENSOR))
@@ -905,6 +1090,10 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
   if (a == nullptr || b == nullptr) return fail(CPG_ERR_NULL, "A and B must be non-NULL");
   if ((reinterpret_cast<uintptr_t>(a) & 15u) != 0 || (reinterpret_cast<uintptr_t>(b) & 15u) != 0)
     return fail(CPG_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+  if (g->decode) {
+    if (rs != nullptr) return fail(CPG_ERR_UNSUPPORTED, "a small-M plan has no peer exchange");
+    return run_decode(g, a, b, d, epi, st);
+  }
 
   const int eab = elem_bytes(pr.dtype_ab), ed = elem_bytes(pr.dtype_d);
   const int bk = cpg::kRowBytes / eab;         // k-block: one 128-byte row of A / B
@@ -1292,7 +1481,7 @@ static int check_reduce_scatter(const cpg_gemm* g, const cpg_reduce_scatter* rs)
   if (g == nullptr || rs == nullptr) return fail(CPG_ERR_NULL, "plan and rs must be non-NULL");
   const cpg_gemm_problem& pr = g->prob;
   if (pr.dtype_d != CPG_DTYPE_F32 || g->stream_k || g->groups > 0 || g->batches > 1 ||
-      pr.gated || g->v.scale_mode != CPG_SCALE_TENSOR)
+      pr.gated || g->v.scale_mode != CPG_SCALE_TENSOR || g->decode)
     return fail(CPG_ERR_UNSUPPORTED,
                 "the peer reduce-scatter needs an FP32-output plan without Stream-K, batches, "
                 "groups, gating or block scales");

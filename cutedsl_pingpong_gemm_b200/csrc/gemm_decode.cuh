@@ -1,0 +1,319 @@
+// Small-M ("decode") GEMM for sm_100a: D[M, N] = alpha * s_a * s_b * A[M, K] . B[N, K]^T + bias
+// for M <= 128, the decode-like shapes where B (the weight, N x K) is read from HBM once and A
+// holds a few token rows.
+//
+// The tile is transposed with respect to the plain kernel: each CTA computes D^T for 128 rows of
+// B, so B's rows fill the MMA's M side (128 TMEM lanes) and the M token rows of A are the MMA's N
+// (rounded up to 16; rows past M are zero-filled by TMA).  No 128-row A tile is padded out of a
+// handful of rows, and every loaded byte of B feeds the tensor core once.
+//
+// A 128-row tile of B alone leaves most SMs idle (N = 8192 gives 64 tiles), so the K range of a
+// tile is split over the S CTAs of a cluster (S = 1, 2 or 4; cluster dims (S, 1, 1), grid
+// (S, ceil(N / 128))).  Each CTA accumulates its K range in TMEM; the partial sums are then
+// reduced through distributed shared memory, in one launch and without any global workspace:
+// the 128 rows of the tile are dealt to the CTAs by TMEM lane quadrant (CTA r owns rows
+// [r * 128 / S, (r + 1) * 128 / S)), the warps holding another CTA's rows store them into that
+// CTA's receive buffer (st.shared::cluster, 16-byte vectors, rows padded by 16 bytes so a warp's
+// stores hit distinct banks) and arrive on its receive barrier with cluster-scope release; the
+// owner adds the S - 1 received rows to its own, applies alpha, the FP8 scales and the bias and
+// writes its rows of D^T as columns of D (for each token row m, a warp writes 32 consecutive
+// elements).
+//
+// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and MMA issuer
+// (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4).  Every wait is
+// bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA loads and MMAs
+// are drained before TMEM is freed, and the final cluster barrier keeps every CTA resident until
+// no peer can still write into its shared memory.
+#pragma once
+#include "gemm_kernel.cuh"
+
+namespace cpg {
+
+constexpr int kDecodeThreads = 192;
+constexpr int kDecodeMaxM = 128;      // MMA N: the token rows of one launch
+constexpr int kDecodeTileN = 128;     // rows of B per CTA (the MMA's M, one TMEM lane each)
+constexpr int kDecodeMaxSplits = 4;   // CTAs per cluster: one TMEM lane quadrant each at most
+constexpr int kDecodeMaxStages = 12;
+constexpr int32_t kSiteDecodeRecv = 11;  // the owner waiting for its peers' partial sums
+
+struct DecodeParams {
+  int32_t m, n, k;
+  int32_t mma_n;       // round_up(M, 16)
+  int32_t tmem_cols;   // power of two >= max(32, mma_n)
+  int32_t k_iters;     // ceil(K / BK)
+  int32_t kps;         // k-blocks per CTA of a cluster
+  int32_t splits;      // CTAs per cluster: 1, 2 or 4
+  int32_t stages;
+  float alpha;
+  const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
+  const float* scale_b;
+  const __nv_bfloat16* bias;  // optional, length N
+  void* d;
+  int64_t ldd;
+  int32_t* status;
+  uint64_t timeout_ns;
+  int32_t l2_policy_a;  // 0 normal, 1 evict first, 2 evict last
+  int32_t l2_policy_b;
+};
+
+// Shared-memory layout (offsets from the 1024-byte aligned base), the same on host and device.
+struct DecodeLayout {
+  uint32_t b_bytes;          // 128 rows of B x 128 bytes
+  uint32_t stage_bytes;      // B rows + mma_n rows of A
+  uint32_t recv_off;         // receive buffer: (S - 1) * 128 / S rows of mma_n + 4 floats
+  uint32_t recv_row_floats;
+  uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
+  uint32_t slot_off;         // TMEM base address, abort flag
+  uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
+};
+
+__host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int splits) {
+  DecodeLayout l;
+  l.b_bytes = kDecodeTileN * kRowBytes;
+  l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n) * kRowBytes;
+  l.recv_off = static_cast<uint32_t>(stages) * l.stage_bytes;
+  l.recv_row_floats = static_cast<uint32_t>(mma_n) + 4u;
+  const uint32_t recv_rows = splits > 1 ? (splits - 1) * (kDecodeTileN / splits) : 0u;
+  l.bar_off = l.recv_off + recv_rows * l.recv_row_floats * 4u;
+  l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
+  l.bytes = l.slot_off + 16u + 1024u;
+  return l;
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT to_out(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <>
+__device__ __forceinline__ float to_out<float>(float x) {
+  return x;
+}
+
+template <typename AB, typename OutT>
+__global__ void __launch_bounds__(kDecodeThreads, 1)
+    gemm_decode_kernel(const __grid_constant__ CUtensorMap tm_a,
+                       const __grid_constant__ CUtensorMap tm_b, const DecodeParams p) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using OT = OperandTraits<AB>;
+  constexpr int kBK = OT::kBK;
+  constexpr int kUmmaK = OT::kUmmaK;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+
+  const int stages = p.stages;
+  const int S = p.splits;
+  const DecodeLayout lay = decode_layout(stages, p.mma_n, S);
+  const uint32_t full_bar = base + lay.bar_off;
+  const uint32_t empty_bar = full_bar + 8u * stages;
+  const uint32_t tfull_bar = empty_bar + 8u * stages;
+  const uint32_t recv_bar = tfull_bar + 8u;
+  const uint32_t drain_bar = recv_bar + 8u;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + lay.slot_off);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(base_ptr + lay.slot_off + 4);
+
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = ptx::lane_id();
+  const uint32_t rank = S > 1 ? ptx::cluster_ctarank() : 0u;
+  const uint32_t rows_per_owner = static_cast<uint32_t>(kDecodeTileN / S);
+  const int32_t n0 = static_cast<int32_t>(blockIdx.y) * kDecodeTileN;
+  const int32_t kb0 = static_cast<int32_t>(rank) * p.kps;
+  const int32_t kb1 = min(p.k_iters, kb0 + p.kps);
+  const bool has_k = kb1 > kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      ptx::mbar_init(full_bar + 8u * s, 1);
+      ptx::mbar_init(empty_bar + 8u * s, 1);
+    }
+    ptx::mbar_init(tfull_bar, 1);
+    ptx::mbar_init(recv_bar, S > 1 ? (S - 1) * rows_per_owner : 1u);
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbarrier_init_cluster();
+    ptx::fence_proxy_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_a);
+    ptx::prefetch_tensormap(&tm_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)),
+                       static_cast<uint32_t>(p.tmem_cols));
+    ptx::tmem_relinquish<1>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (S > 1) ptx::cluster_sync();  // every CTA's receive barrier initialised before any arrive
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  ptx::WaitCtx ctx{abort_flag, p.status, p.timeout_ns};
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy(p.l2_policy_a);
+      const uint64_t pol_b = l2_policy(p.l2_policy_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int32_t kb = kb0; kb < kb1; ++kb) {
+        if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) break;
+        const uint32_t fb = full_bar + 8u * stage;
+        const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
+        ptx::mbar_arrive_expect_tx(fb, lay.stage_bytes);
+        ptx::tma_load_3d(&tm_b, sb, fb, kb * kBK, n0, 0, pol_b);
+        ptx::tma_load_3d(&tm_a, sb + lay.b_bytes, fb, kb * kBK, 0, 0, pol_a);
+        ++issued;
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // Drain: the last fill of every stage has landed before the CTA may exit (bounded, and
+      // independent of an abort: a TMA write must not reach freed shared memory).
+      ptx::WaitCtx dctx = ctx;
+      volatile int32_t no_abort = 0;
+      dctx.abort_flag = &no_abort;
+      for (int i = issued > stages ? issued - stages : 0; i < issued; ++i)
+        ptx::mbar_wait(full_bar + 8u * (i % stages), static_cast<uint32_t>((i / stages) & 1),
+                       dctx, kSiteDrainLoads);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kDecodeTileN, p.mma_n)
+                                      : ptx::make_idesc_bf16_f32(kDecodeTileN, p.mma_n);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int32_t kb = kb0; kb < kb1; ++kb) {
+        if (!ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) break;
+        ptx::tc_fence_after();
+        const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
+        const uint64_t da = ptx::make_sw128_kmajor_desc(sb);                // 128 rows of B
+        const uint64_t db = ptx::make_sw128_kmajor_desc(sb + lay.b_bytes);  // mma_n rows of A
+#pragma unroll
+        for (int k = 0; k < kBK / kUmmaK; ++k) {
+          const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+          if constexpr (OT::kFp8) {
+            ptx::umma_f8_ss<1>(tmem_base, da + static_cast<uint64_t>(2 * k),
+                               db + static_cast<uint64_t>(2 * k), idesc, acc);
+          } else {
+            ptx::umma_f16_ss<1>(tmem_base, da + static_cast<uint64_t>(2 * k),
+                                db + static_cast<uint64_t>(2 * k), idesc, acc);
+          }
+        }
+        ptx::umma_commit<1>(empty_bar + 8u * stage);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      ptx::umma_commit<1>(tfull_bar);
+      // No MMA may still write TMEM when it is freed.
+      ptx::umma_commit<1>(drain_bar);
+      ptx::WaitCtx dctx = ctx;
+      volatile int32_t no_abort = 0;
+      dctx.abort_flag = &no_abort;
+      ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- reduction + epilogue
+    const uint32_t quad = warp & 3u;
+    const uint32_t row = quad * 32u + lane;  // TMEM lane = row of the B tile
+    const int32_t n = n0 + static_cast<int32_t>(row);
+    const uint32_t owner = quad / static_cast<uint32_t>(4 / S);
+    bool ok = ptx::mbar_wait(tfull_bar, 0u, ctx, kSiteEpiTmemFull);
+    ok = __all_sync(0xffffffffu, ok) && *abort_flag == 0;
+    ptx::tc_fence_after();
+    const uint32_t t_row = tmem_base + ((quad * 32u) << 16);
+    const int chunks = p.mma_n / 16;
+    const bool read_tmem = ok && has_k;
+    if (owner != rank) {
+      // Send this row's partial sums to the CTA that owns it.
+      const uint32_t slot = rank < owner ? rank : rank - 1u;
+      const uint32_t local = row - owner * rows_per_owner;
+      const uint32_t dst = ptx::mapa_shared(
+          base + lay.recv_off + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, owner);
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t v[16];
+        if (read_tmem) {
+          ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
+          ptx::tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          ptx::st_shared_cluster_v4(dst + static_cast<uint32_t>(64 * c + 16 * j), v[4 * j],
+                                    v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+      ptx::mbar_arrive_release_cluster(ptx::mapa_shared(recv_bar, owner));
+    } else {
+      bool got = S == 1 || ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
+      got = __all_sync(0xffffffffu, got) && ok;
+      if (got) {
+        float scale = p.alpha;
+        if (p.scale_a != nullptr) scale *= *p.scale_a;
+        if (p.scale_b != nullptr) scale *= *p.scale_b;
+        const bool n_ok = n < p.n;
+        const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
+        const uint32_t local = row - rank * rows_per_owner;
+        OutT* d = static_cast<OutT*>(p.d);
+        for (int c = 0; c < chunks; ++c) {
+          uint32_t v[16];
+          if (has_k) {
+            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
+            ptx::tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0u;
+          }
+          float acc[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
+          for (int src = 0; src < S - 1; ++src) {
+            const uint32_t r_addr = base + lay.recv_off +
+                                    ((static_cast<uint32_t>(src) * rows_per_owner + local) *
+                                         lay.recv_row_floats +
+                                     static_cast<uint32_t>(16 * c)) *
+                                        4u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
+              acc[4 * j] += __uint_as_float(w.x);
+              acc[4 * j + 1] += __uint_as_float(w.y);
+              acc[4 * j + 2] += __uint_as_float(w.z);
+              acc[4 * j + 3] += __uint_as_float(w.w);
+            }
+          }
+          if (n_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int32_t m = 16 * c + j;
+              if (m < p.m)
+                d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (S > 1) ptx::cluster_sync();  // no CTA leaves while a peer may still store into it
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<1>(tmem_base, static_cast<uint32_t>(p.tmem_cols));
+  }
+#endif
+}
+
+}  // namespace cpg

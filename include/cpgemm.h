@@ -122,7 +122,8 @@ typedef struct cpg_gemm_problem {
                             share of all (tile, k-block) pairs; with FP32 D the shares add into
                             D, with BF16 D the last contributor of each tile finishes it from
                             an FP32 workspace the plan owns (no memset, no cast);
-                            CPG_SPLIT_K_HYBRID: see below.  Activations, C and gated need 0/1 */
+                            CPG_SPLIT_K_HYBRID, CPG_SPLIT_K_DECODE (M <= 128): see below.
+                            Activations, C and gated need 0/1 */
   int32_t gated;         /* 0, or 1: gated FFN (e.g. SwiGLU).  B holds [W_gate; W_up] as 2N rows
                             of K (ldb its row stride), D is M x N and
                             D[:, n] = act(alpha s_a s_b A . W_gate[n]) * alpha s_a s_b A . W_up[n];
@@ -148,6 +149,13 @@ typedef struct cpg_gemm_problem {
  * the last contributor of a split tile finishes it (bias, rounding, store) from an FP32
  * workspace the plan owns.  For problems whose tiles leave the last wave partly idle. */
 #define CPG_SPLIT_K_HYBRID (-2)
+/* Small-M (decode-like) kernel, for 1 <= M <= 128: each CTA computes D^T for 128 rows of B (B's
+ * rows on the MMA's M side, the M rows of A on its N side, rounded up to 16), the K range of a
+ * tile is split over a cluster of 1, 2 or 4 CTAs and the partial sums are added in distributed
+ * shared memory, in one launch with no workspace.  BF16 or E4M3 operands (per-tensor scales),
+ * BF16 or FP32 D, alpha and bias; no activation, C, gating, batches or groups.  The tile, cluster
+ * and stage settings of the config do not apply (the kernel picks its own). */
+#define CPG_SPLIT_K_DECODE (-3)
 
 /* Per-call epilogue options:
  *   D = act(alpha * s_a * s_b * (A . B^T) + bias + beta * C), rounded to D's type.
