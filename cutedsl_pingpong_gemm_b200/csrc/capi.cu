@@ -338,6 +338,7 @@ struct cpg_gemm {
   int32_t trace_stride;
   uint64_t timeout_ns;
   int32_t fault_inject;
+  int32_t pdl;  // launch with programmatic stream serialization (CPG_PDL=1)
   int32_t l2_policy_a, l2_policy_b, l2_policy_d;
   int32_t k_iters;
   int32_t k_iters_per_split;
@@ -794,6 +795,10 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   }
   // D tiles are written once and never read back by the kernel.
   g->l2_policy_d = 1;
+  // Programmatic dependent launch between consecutive GEMMs of a stream (the next one's set-up
+  // overlaps this one's last wave); off unless CPG_PDL=1.
+  const char* pdl = std::getenv("CPG_PDL");
+  g->pdl = (pdl != nullptr && std::atoi(pdl) == 1) ? 1 : 0;
   const char* pa = std::getenv("CPG_L2_POLICY_A");
   const char* pb = std::getenv("CPG_L2_POLICY_B");
   const char* pd = std::getenv("CPG_L2_POLICY_D");
@@ -1202,19 +1207,26 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     }
   }
   cudaLaunchConfig_t lc = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   lc.gridDim = dim3(g->grid[0], g->grid[1], g->grid[2]);
   lc.blockDim = dim3(g->v.threads, 1, 1);
   lc.dynamicSmemBytes = g->smem_bytes;
   lc.stream = st;
   lc.numAttrs = 0;
+  lc.attrs = attr;
   if (g->cluster[0] * g->cluster[1] > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = g->cluster[0];
-    attr[0].val.clusterDim.y = g->cluster[1];
-    attr[0].val.clusterDim.z = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
+    attr[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[lc.numAttrs].val.clusterDim.x = g->cluster[0];
+    attr[lc.numAttrs].val.clusterDim.y = g->cluster[1];
+    attr[lc.numAttrs].val.clusterDim.z = 1;
+    ++lc.numAttrs;
+  }
+  // Only right after another kernel: not after the split-K memset or the group prefix kernel.
+  const bool memset_before = (g->splits > 1 || (g->stream_k && !g->fixup)) && rs == nullptr;
+  if (g->pdl && !memset_before && g->groups == 0 && !block) {
+    attr[lc.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[lc.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++lc.numAttrs;
   }
   void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &g->tm_ws, &p};
   void* block_args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p, &bs};

@@ -287,8 +287,14 @@ class CompiledGemm:
         the tiles fill the GPU.
 
         Measured on one B200, 2048 x 2048 output tiles of 256 x 256 (32 clusters) with K = 65536:
-        Stream-K 981 TFLOP/s, 5 ranges (2.2 waves) 1272, 2 ranges (one 86 % wave) 1319; on
-        M = 128, N = K = 8192 (64 tiles, 128 k-blocks) Stream-K is the fastest."""
+        Stream-K 981 TFLOP/s, 5 ranges (2.2 waves) 1272, 2 ranges (one 86 % wave) 1319.
+
+        One batch of M <= 128 rows takes the small-M kernel instead (CPG_SPLIT_K_DECODE, -3: B's
+        rows on the MMA's M side, K split over a cluster and reduced in shared memory, one
+        launch): on N = K = 8192 it measured 28.2 / 31.1 / 34.5 us for M = 16 / 64 / 128 against
+        32.8 / 34.6 / 34.8 us for Stream-K + cast."""
+        if m <= 128 and batches == 1:
+            return _lib.CPG_SPLIT_K_DECODE
         gemm = self.gemm
         cm, cn, _ = gemm.cluster_shape_mnk
         tiles = -(-max(m, 1) // (128 * cm)) * -(-max(n, 1) // gemm.cta_tile_shape_mnk[1])

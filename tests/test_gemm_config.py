@@ -130,7 +130,8 @@ def test_capi_validate_dynamic_scheduler(lib):
 
 def test_auto_split_k_avoids_stream_k_when_dynamic(monkeypatch):
     """Stream-K partitions the k-blocks statically, so the automatic split of a dynamic-schedule
-    GEMM picks K ranges instead (decode-like M = 128, N = K = 8192 would take Stream-K)."""
+    GEMM picks K ranges instead (M = 256, N = K = 8192 would take Stream-K); one batch of at
+    most 128 rows takes the small-M kernel under either schedule."""
     from cutedsl_pingpong_gemm_b200.gemm_base import CompiledGemm
     for dyn, want_stream in ((False, True), (True, False)):
         g = GemmSM90(tile_shape_mn=(128, 128), epi_tile_mn=(128, 32), cluster_shape_mnk=(1, 1, 1),
@@ -139,9 +140,11 @@ def test_auto_split_k_avoids_stream_k_when_dynamic(monkeypatch):
         g._max_active_clusters = 148  # B200: one CTA per SM (no GPU here)
         c = CompiledGemm.__new__(CompiledGemm)
         c.gemm = g
-        s = c.auto_split_k(128, 8192, 8192)
+        s = c.auto_split_k(256, 8192, 8192)
         assert (s == _lib.CPG_SPLIT_K_STREAM) == want_stream, (dyn, s)
         assert s != 0
+        assert c.auto_split_k(128, 8192, 8192) == _lib.CPG_SPLIT_K_DECODE
+        assert c.auto_split_k(128, 8192, 8192, batches=2) != _lib.CPG_SPLIT_K_DECODE
 
 
 def test_release_drops_cached_plans_and_workspaces():

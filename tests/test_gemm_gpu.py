@@ -432,14 +432,15 @@ def test_tile_order_512_matches_reference():
 
 @pytest.mark.parametrize("m", [16, 64, 128])
 def test_small_m_auto_split_bf16(m):
-    """BASELINE config 5 (decode-like M at N = K = 8192): split-K picked automatically, partial
-    sums in the FP32 workspace, then rounded into the BF16 output with the bias."""
+    """BASELINE config 5 (decode-like M at N = K = 8192): the automatic choice (the small-M
+    kernel), then the same through explicit K ranges (FP32 workspace, rounded into the BF16
+    output with the bias)."""
     n, k = 8192, 8192
     a, b, bias = gemm_ref.make_inputs(m, n, k, seed=m, b_scale=k ** -0.5, with_bias=True)
     gemm = make_gemm(256, (1, 1, 1))
     d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
     compiled = cpg_compile(gemm, a.cuda(), b.cuda(), d)
-    assert compiled.auto_split_k(m, n, k) != 1  # Stream-K (-1) for this persistent kernel
+    assert compiled.auto_split_k(m, n, k) == _lib.CPG_SPLIT_K_DECODE  # the small-M kernel
     compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=0)
     torch.cuda.synchronize()
     assert gemm_ref.check(d.cpu(), a, b, bias=bias)["ok"]
@@ -474,8 +475,7 @@ def test_stream_k_bf16_through_api():
     a, b, bias = gemm_ref.make_inputs(m, n, k, seed=1, b_scale=k ** -0.5, with_bias=True)
     d = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     compiled = cpg_compile(make_gemm(256, (1, 1, 1)), a.cuda(), b.cuda(), d)
-    assert compiled.auto_split_k(m, n, k) == -1
     for _ in range(2):  # the workspace is reused: the second call must clear it again
-        compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=0)
+        compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=-1)
     torch.cuda.synchronize()
     assert gemm_ref.check(d.cpu(), a, b, bias=bias)["ok"]
