@@ -338,7 +338,6 @@ struct cpg_gemm {
   int32_t trace_stride;
   uint64_t timeout_ns;
   int32_t fault_inject;
-  int32_t pdl;  // launch with programmatic stream serialization (CPG_PDL=1)
   int32_t l2_policy_a, l2_policy_b, l2_policy_d;
   int32_t k_iters;
   int32_t k_iters_per_split;
@@ -363,7 +362,7 @@ struct cpg_gemm {
   CUtensorMap tm_a, tm_b, tm_d;
   // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
   int32_t decode;
-  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages;
+  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_rblocks;
 };
 
 extern "C" {
@@ -467,10 +466,12 @@ static const void* decode_kernel(int dtype_ab, int dtype_d) {
   return reinterpret_cast<const void*>(fn);
 }
 
-// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 128 rows of B each; the K range of a
-// tile is split over a cluster of S CTAs, S the largest of 4, 2, 1 that keeps every CTA of the
-// grid resident at once (tiles * S <= SMs) and gives every CTA a k-block.  Stages: the deepest
-// ring that fits (at most the CTA's k-blocks).
+// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 128 R rows of B, R = 2 row blocks when
+// A has 64 or more rows (every tile re-reads all of A from L2; two blocks halve that) and the
+// tiles still fill the SMs with 4 CTAs each, else R = 1.  The K range of a tile is split over a
+// cluster of S CTAs, S the largest of 4, 2, 1 that keeps every CTA of the grid resident at once
+// (tiles * S <= SMs) and gives every CTA a k-block.  Stages: the deepest ring that fits (at most
+// the CTA's k-blocks), and at least enough to hold the reduction's receive buffer.
 static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
                               const cudaDeviceProp& prop, cpg_gemm** out) {
   if (prob->m < 1 || prob->m > cpg::kDecodeMaxM)
@@ -479,13 +480,23 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   if (prob->scale_mode != CPG_SCALE_TENSOR || prob->gated || prob->grouped || prob->l > 1)
     return fail(CPG_ERR_UNSUPPORTED,
                 "the small-M kernel has no block scales, gating, batches or groups");
-  const int64_t tiles = (prob->n + cpg::kDecodeTileN - 1) / cpg::kDecodeTileN;
-  if (tiles > 65535)
-    return fail(CPG_ERR_INVALID_SHAPE, "the small-M kernel takes N <= %d",
-                65535 * cpg::kDecodeTileN);
   const int64_t bk = cpg::kRowBytes / elem_bytes(prob->dtype_ab);
   const int64_t k_iters = (prob->k + bk - 1) / bk;
   const int64_t sms = prop.multiProcessorCount;
+  const int mma_n = static_cast<int>((prob->m + 15) / 16 * 16);
+  const int64_t wide_tiles = (prob->n + 2 * cpg::kDecodeTileN - 1) / (2 * cpg::kDecodeTileN);
+  int rblocks = (mma_n >= 64 && wide_tiles * 4 <= sms && k_iters >= 4) ? 2 : 1;
+  // Tuning overrides (measurement only): CPG_DECODE_RBLOCKS (1, 2), CPG_DECODE_SPLITS (1, 2, 4),
+  // CPG_DECODE_STAGES (>= 2).
+  const char* env_r = std::getenv("CPG_DECODE_RBLOCKS");
+  const char* env_s = std::getenv("CPG_DECODE_SPLITS");
+  const char* env_st = std::getenv("CPG_DECODE_STAGES");
+  if (env_r != nullptr && (std::atoi(env_r) == 1 || std::atoi(env_r) == 2)) rblocks = std::atoi(env_r);
+  const int64_t tile_rows = int64_t(rblocks) * cpg::kDecodeTileN;
+  const int64_t tiles = (prob->n + tile_rows - 1) / tile_rows;
+  if (tiles > 65535)
+    return fail(CPG_ERR_INVALID_SHAPE, "the small-M kernel takes N <= %lld",
+                static_cast<long long>(65535 * tile_rows));
   int splits = 1;
   for (int s = cpg::kDecodeMaxSplits; s > 1; s /= 2) {
     if (tiles * s <= sms && k_iters >= s) {
@@ -493,13 +504,16 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
       break;
     }
   }
-  const int mma_n = static_cast<int>((prob->m + 15) / 16 * 16);
+  if (env_s != nullptr) {
+    const int v = std::atoi(env_s);
+    if ((v == 1 || v == 2 || v == 4) && v <= k_iters) splits = v;
+  }
   int tmem_cols = 32;
-  while (tmem_cols < mma_n) tmem_cols *= 2;
+  while (tmem_cols < rblocks * mma_n) tmem_cols *= 2;
   const int64_t kps = k_iters > 0 ? (k_iters + splits - 1) / splits : 0;
   int stages = 0;
   for (int st = cpg::kDecodeMaxStages; st >= 2; --st) {
-    if (static_cast<int64_t>(cpg::decode_layout(st, mma_n, splits).bytes) <=
+    if (static_cast<int64_t>(cpg::decode_layout(st, mma_n, splits, rblocks).bytes) <=
         static_cast<int64_t>(prop.sharedMemPerBlockOptin)) {
       stages = st;
       break;
@@ -507,8 +521,16 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   }
   if (stages == 0) return fail(CPG_ERR_SMEM, "the small-M kernel does not fit in shared memory");
   if (kps >= 2 && stages > kps) stages = static_cast<int>(kps);
+  if (env_st != nullptr && std::atoi(env_st) >= 2 && std::atoi(env_st) < stages)
+    stages = std::atoi(env_st);
   if (stages < 2) stages = 2;
-  const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits).bytes);
+  // The receive buffer of the in-cluster reduction lives in the stages.
+  while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, rblocks).stage_bytes <
+         cpg::decode_layout(stages, mma_n, splits, rblocks).recv_bytes)
+    ++stages;
+  const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits, rblocks).bytes);
+  if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
+    return fail(CPG_ERR_SMEM, "the small-M kernel does not fit in shared memory");
   const void* fn = decode_kernel(prob->dtype_ab, prob->dtype_d);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(small-M kernel smem)");
@@ -563,6 +585,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_kps = static_cast<int32_t>(kps);
   g->dec_splits = splits;
   g->dec_stages = stages;
+  g->dec_rblocks = rblocks;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
@@ -586,7 +609,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
                           g->dec_mma_n, bk);
     if (rc != CPG_OK) return rc;
     rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
-                      cpg::kDecodeTileN, bk);
+                      g->dec_rblocks * cpg::kDecodeTileN, bk);
     if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
@@ -603,6 +626,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.k_iters = g->k_iters;
   p.kps = g->dec_kps;
   p.splits = g->dec_splits;
+  p.rblocks = g->dec_rblocks;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
   p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
@@ -795,10 +819,6 @@ int cpg_gemm_create(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, in
   }
   // D tiles are written once and never read back by the kernel.
   g->l2_policy_d = 1;
-  // Programmatic dependent launch between consecutive GEMMs of a stream (the next one's set-up
-  // overlaps this one's last wave); off unless CPG_PDL=1.
-  const char* pdl = std::getenv("CPG_PDL");
-  g->pdl = (pdl != nullptr && std::atoi(pdl) == 1) ? 1 : 0;
   const char* pa = std::getenv("CPG_L2_POLICY_A");
   const char* pb = std::getenv("CPG_L2_POLICY_B");
   const char* pd = std::getenv("CPG_L2_POLICY_D");
@@ -1207,7 +1227,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     }
   }
   cudaLaunchConfig_t lc = {};
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   lc.gridDim = dim3(g->grid[0], g->grid[1], g->grid[2]);
   lc.blockDim = dim3(g->v.threads, 1, 1);
   lc.dynamicSmemBytes = g->smem_bytes;
@@ -1221,13 +1241,7 @@ static int run_impl(cpg_gemm* g, const void* a, const void* b, void* d, const cp
     attr[lc.numAttrs].val.clusterDim.z = 1;
     ++lc.numAttrs;
   }
-  // Only right after another kernel: not after the split-K memset or the group prefix kernel.
-  const bool memset_before = (g->splits > 1 || (g->stream_k && !g->fixup)) && rs == nullptr;
-  if (g->pdl && !memset_before && g->groups == 0 && !block) {
-    attr[lc.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[lc.numAttrs].val.programmaticStreamSerializationAllowed = 1;
-    ++lc.numAttrs;
-  }
+
   void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &g->tm_ws, &p};
   void* block_args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p, &bs};
   cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, block ? block_args : args);

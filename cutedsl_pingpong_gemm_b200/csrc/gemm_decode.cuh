@@ -2,28 +2,31 @@
 // for M <= 128, the decode-like shapes where B (the weight, N x K) is read from HBM once and A
 // holds a few token rows.
 //
-// The tile is transposed with respect to the plain kernel: each CTA computes D^T for 128 rows of
-// B, so B's rows fill the MMA's M side (128 TMEM lanes) and the M token rows of A are the MMA's N
-// (rounded up to 16; rows past M are zero-filled by TMA).  No 128-row A tile is padded out of a
-// handful of rows, and every loaded byte of B feeds the tensor core once.
+// The tile is transposed with respect to the plain kernel: each CTA computes D^T for 128 R rows
+// of B (R = 1 or 2 row blocks, one M = 128 MMA and one TMEM accumulator each), so B's rows fill
+// the MMA's M side (128 TMEM lanes per block) and the M token rows of A are the MMA's N (rounded
+// up to 16; rows past M are zero-filled by TMA).  No 128-row A tile is padded out of a handful of
+// rows, and every loaded byte of B feeds the tensor core once.  Two row blocks per CTA halve the
+// re-reads of A from L2 (every tile reads all of A), which matter once A has 64 rows or more.
 //
-// A 128-row tile of B alone leaves most SMs idle (N = 8192 gives 64 tiles), so the K range of a
+// A tile of B alone leaves most SMs idle (N = 8192 gives 64 or 32 tiles), so the K range of a
 // tile is split over the S CTAs of a cluster (S = 1, 2 or 4; cluster dims (S, 1, 1), grid
-// (S, ceil(N / 128))).  Each CTA accumulates its K range in TMEM; the partial sums are then
+// (S, ceil(N / (128 R)))).  Each CTA accumulates its K range in TMEM; the partial sums are then
 // reduced through distributed shared memory, in one launch and without any global workspace:
-// the 128 rows of the tile are dealt to the CTAs by TMEM lane quadrant (CTA r owns rows
-// [r * 128 / S, (r + 1) * 128 / S)), the warps holding another CTA's rows store them into that
-// CTA's receive buffer (st.shared::cluster, 16-byte vectors, rows padded by 16 bytes so a warp's
-// stores hit distinct banks) and arrive on its receive barrier with cluster-scope release; the
-// owner adds the S - 1 received rows to its own, applies alpha, the FP8 scales and the bias and
-// writes its rows of D^T as columns of D (for each token row m, a warp writes 32 consecutive
-// elements).
+// the 128 R rows of the tile are dealt to the CTAs in blocks of 128 R / S rows (CTA r owns rows
+// [r 128 R / S, (r + 1) 128 R / S)).  Once every CTA of the cluster has finished its MMAs and its
+// loads (a cluster barrier), the A/B stages are free and serve as receive buffers: the warps
+// holding another CTA's rows store them there (st.shared::cluster, 16-byte vectors, rows padded
+// by 16 bytes so a warp's stores hit distinct banks) and arrive on that CTA's receive barrier
+// with cluster-scope release; the owner adds the S - 1 received rows to its own, applies alpha,
+// the FP8 scales and the bias and writes its rows of D^T as columns of D (for each token row m, a
+// warp writes 32 consecutive elements).
 //
 // Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and MMA issuer
-// (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4).  Every wait is
-// bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA loads and MMAs
-// are drained before TMEM is freed, and the final cluster barrier keeps every CTA resident until
-// no peer can still write into its shared memory.
+// (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4 of every block).
+// Every wait is bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA
+// loads and MMAs are drained before the stages are reused or TMEM is freed, and the final
+// cluster barrier keeps every CTA resident until no peer can still write into its shared memory.
 #pragma once
 #include "gemm_kernel.cuh"
 
@@ -31,8 +34,9 @@ namespace cpg {
 
 constexpr int kDecodeThreads = 192;
 constexpr int kDecodeMaxM = 128;      // MMA N: the token rows of one launch
-constexpr int kDecodeTileN = 128;     // rows of B per CTA (the MMA's M, one TMEM lane each)
-constexpr int kDecodeMaxSplits = 4;   // CTAs per cluster: one TMEM lane quadrant each at most
+constexpr int kDecodeTileN = 128;     // rows of B per row block (the MMA's M, one TMEM lane each)
+constexpr int kDecodeMaxBlocks = 2;   // row blocks per CTA
+constexpr int kDecodeMaxSplits = 4;   // CTAs per cluster (owners of at least 32 rows each)
 constexpr int kDecodeMaxStages = 12;
 constexpr int32_t kSiteDecodeRecv = 11;  // the owner waiting for its peers' partial sums
 
@@ -43,6 +47,7 @@ struct DecodeParams {
   int32_t k_iters;     // ceil(K / BK)
   int32_t kps;         // k-blocks per CTA of a cluster
   int32_t splits;      // CTAs per cluster: 1, 2 or 4
+  int32_t rblocks;     // 128-row blocks of B per CTA: 1 or 2
   int32_t stages;
   float alpha;
   const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
@@ -57,24 +62,28 @@ struct DecodeParams {
 };
 
 // Shared-memory layout (offsets from the 1024-byte aligned base), the same on host and device.
+// The receive buffer of the reduction aliases the A/B stages (used only after every CTA of the
+// cluster has finished with them).
 struct DecodeLayout {
-  uint32_t b_bytes;          // 128 rows of B x 128 bytes
+  uint32_t b_bytes;          // 128 R rows of B x 128 bytes
   uint32_t stage_bytes;      // B rows + mma_n rows of A
-  uint32_t recv_off;         // receive buffer: (S - 1) * 128 / S rows of mma_n + 4 floats
-  uint32_t recv_row_floats;
+  uint32_t recv_row_floats;  // mma_n + 4 (16 bytes of padding per row)
+  uint32_t recv_bytes;       // (S - 1) * 128 R / S rows
   uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
   uint32_t slot_off;         // TMEM base address, abort flag
   uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
 };
 
-__host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int splits) {
+__host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int splits,
+                                                      int rblocks) {
   DecodeLayout l;
-  l.b_bytes = kDecodeTileN * kRowBytes;
+  l.b_bytes = static_cast<uint32_t>(rblocks) * kDecodeTileN * kRowBytes;
   l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n) * kRowBytes;
-  l.recv_off = static_cast<uint32_t>(stages) * l.stage_bytes;
   l.recv_row_floats = static_cast<uint32_t>(mma_n) + 4u;
-  const uint32_t recv_rows = splits > 1 ? (splits - 1) * (kDecodeTileN / splits) : 0u;
-  l.bar_off = l.recv_off + recv_rows * l.recv_row_floats * 4u;
+  const uint32_t recv_rows =
+      splits > 1 ? (splits - 1) * (static_cast<uint32_t>(rblocks) * kDecodeTileN / splits) : 0u;
+  l.recv_bytes = recv_rows * l.recv_row_floats * 4u;
+  l.bar_off = static_cast<uint32_t>(stages) * l.stage_bytes;
   l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
   l.bytes = l.slot_off + 16u + 1024u;
   return l;
@@ -106,7 +115,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   const int stages = p.stages;
   const int S = p.splits;
-  const DecodeLayout lay = decode_layout(stages, p.mma_n, S);
+  const int R = p.rblocks;
+  const DecodeLayout lay = decode_layout(stages, p.mma_n, S, R);
   const uint32_t full_bar = base + lay.bar_off;
   const uint32_t empty_bar = full_bar + 8u * stages;
   const uint32_t tfull_bar = empty_bar + 8u * stages;
@@ -118,8 +128,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = ptx::lane_id();
   const uint32_t rank = S > 1 ? ptx::cluster_ctarank() : 0u;
-  const uint32_t rows_per_owner = static_cast<uint32_t>(kDecodeTileN / S);
-  const int32_t n0 = static_cast<int32_t>(blockIdx.y) * kDecodeTileN;
+  const uint32_t rows_per_owner = static_cast<uint32_t>(R * kDecodeTileN / S);
+  const int32_t n0 = static_cast<int32_t>(blockIdx.y) * R * kDecodeTileN;
   const int32_t kb0 = static_cast<int32_t>(rank) * p.kps;
   const int32_t kb1 = min(p.k_iters, kb0 + p.kps);
   const bool has_k = kb1 > kb0;
@@ -194,17 +204,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         if (!ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) break;
         ptx::tc_fence_after();
         const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
-        const uint64_t da = ptx::make_sw128_kmajor_desc(sb);                // 128 rows of B
         const uint64_t db = ptx::make_sw128_kmajor_desc(sb + lay.b_bytes);  // mma_n rows of A
 #pragma unroll
         for (int k = 0; k < kBK / kUmmaK; ++k) {
           const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-          if constexpr (OT::kFp8) {
-            ptx::umma_f8_ss<1>(tmem_base, da + static_cast<uint64_t>(2 * k),
-                               db + static_cast<uint64_t>(2 * k), idesc, acc);
-          } else {
-            ptx::umma_f16_ss<1>(tmem_base, da + static_cast<uint64_t>(2 * k),
-                                db + static_cast<uint64_t>(2 * k), idesc, acc);
+          for (int r = 0; r < R; ++r) {
+            // Row block r: B rows 128 r .. (1024-byte aligned, 16 KiB apart), accumulator r.
+            const uint64_t dar = ptx::make_sw128_kmajor_desc(sb + r * kDecodeTileN * kRowBytes);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(r * p.mma_n);
+            if constexpr (OT::kFp8) {
+              ptx::umma_f8_ss<1>(d_tmem, dar + static_cast<uint64_t>(2 * k),
+                                 db + static_cast<uint64_t>(2 * k), idesc, acc);
+            } else {
+              ptx::umma_f16_ss<1>(d_tmem, dar + static_cast<uint64_t>(2 * k),
+                                  db + static_cast<uint64_t>(2 * k), idesc, acc);
+            }
           }
         }
         ptx::umma_commit<1>(empty_bar + 8u * stage);
@@ -222,24 +236,33 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       ptx::mbar_wait(drain_bar, 0u, dctx, kSiteDrainMma);
     }
     __syncwarp();
-  } else {
-    // ---------------------------------------------------------------- reduction + epilogue
-    const uint32_t quad = warp & 3u;
-    const uint32_t row = quad * 32u + lane;  // TMEM lane = row of the B tile
-    const int32_t n = n0 + static_cast<int32_t>(row);
-    const uint32_t owner = quad / static_cast<uint32_t>(4 / S);
-    bool ok = ptx::mbar_wait(tfull_bar, 0u, ctx, kSiteEpiTmemFull);
+  }
+  // Every CTA of the cluster has drained its loads and MMAs (warps 0 and 1 above) and its
+  // epilogue warps have seen the accumulators complete: the stages of all of them are free to
+  // receive partial sums.
+  bool ok = true;
+  if (warp >= 2) {
+    ok = ptx::mbar_wait(tfull_bar, 0u, ctx, kSiteEpiTmemFull);
     ok = __all_sync(0xffffffffu, ok) && *abort_flag == 0;
     ptx::tc_fence_after();
-    const uint32_t t_row = tmem_base + ((quad * 32u) << 16);
+  }
+  ptx::fence_proxy_async_shared();  // the stages' async-proxy use ends before generic stores
+  if (S > 1) ptx::cluster_sync();
+  if (warp >= 2) {
+    // ---------------------------------------------------------------- reduction + epilogue
+    const uint32_t quad = warp & 3u;
     const int chunks = p.mma_n / 16;
     const bool read_tmem = ok && has_k;
-    if (owner != rank) {
-      // Send this row's partial sums to the CTA that owns it.
+    // Sends first (they never wait), then the owned rows (which wait for the peers' sends).
+    for (int r = 0; r < R; ++r) {
+      const uint32_t row = static_cast<uint32_t>(r * kDecodeTileN) + quad * 32u + lane;
+      const uint32_t owner = (row - lane) / rows_per_owner;  // uniform over the warp
+      if (owner == rank) continue;
+      const uint32_t t_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(r * p.mma_n);
       const uint32_t slot = rank < owner ? rank : rank - 1u;
       const uint32_t local = row - owner * rows_per_owner;
       const uint32_t dst = ptx::mapa_shared(
-          base + lay.recv_off + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, owner);
+          base + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, owner);
       for (int c = 0; c < chunks; ++c) {
         uint32_t v[16];
         if (read_tmem) {
@@ -255,51 +278,59 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
                                     v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       }
       ptx::mbar_arrive_release_cluster(ptx::mapa_shared(recv_bar, owner));
-    } else {
-      bool got = S == 1 || ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
-      got = __all_sync(0xffffffffu, got) && ok;
-      if (got) {
-        float scale = p.alpha;
-        if (p.scale_a != nullptr) scale *= *p.scale_a;
-        if (p.scale_b != nullptr) scale *= *p.scale_b;
-        const bool n_ok = n < p.n;
-        const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
-        const uint32_t local = row - rank * rows_per_owner;
-        OutT* d = static_cast<OutT*>(p.d);
-        for (int c = 0; c < chunks; ++c) {
-          uint32_t v[16];
-          if (has_k) {
-            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
-            ptx::tmem_ld_wait();
-          } else {
+    }
+    bool waited = false, got = ok;
+    for (int r = 0; r < R; ++r) {
+      const uint32_t row = static_cast<uint32_t>(r * kDecodeTileN) + quad * 32u + lane;
+      const uint32_t owner = (row - lane) / rows_per_owner;
+      if (owner != rank) continue;
+      if (!waited && S > 1) {
+        bool g = ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
+        got = __all_sync(0xffffffffu, g) && ok;
+        waited = true;
+      }
+      if (!got) break;
+      const uint32_t t_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(r * p.mma_n);
+      const int32_t n = n0 + static_cast<int32_t>(row);
+      float scale = p.alpha;
+      if (p.scale_a != nullptr) scale *= *p.scale_a;
+      if (p.scale_b != nullptr) scale *= *p.scale_b;
+      const bool n_ok = n < p.n;
+      const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
+      const uint32_t local = row - rank * rows_per_owner;
+      OutT* d = static_cast<OutT*>(p.d);
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t v[16];
+        if (has_k) {
+          ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
+          ptx::tmem_ld_wait();
+        } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0u;
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+        }
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
+        for (int src = 0; src < S - 1; ++src) {
+          const uint32_t r_addr = base + ((static_cast<uint32_t>(src) * rows_per_owner + local) *
+                                              lay.recv_row_floats +
+                                          static_cast<uint32_t>(16 * c)) *
+                                             4u;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
+            acc[4 * j] += __uint_as_float(w.x);
+            acc[4 * j + 1] += __uint_as_float(w.y);
+            acc[4 * j + 2] += __uint_as_float(w.z);
+            acc[4 * j + 3] += __uint_as_float(w.w);
           }
-          float acc[16];
+        }
+        if (n_ok) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
-          for (int src = 0; src < S - 1; ++src) {
-            const uint32_t r_addr = base + lay.recv_off +
-                                    ((static_cast<uint32_t>(src) * rows_per_owner + local) *
-                                         lay.recv_row_floats +
-                                     static_cast<uint32_t>(16 * c)) *
-                                        4u;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
-              acc[4 * j] += __uint_as_float(w.x);
-              acc[4 * j + 1] += __uint_as_float(w.y);
-              acc[4 * j + 2] += __uint_as_float(w.z);
-              acc[4 * j + 3] += __uint_as_float(w.w);
-            }
-          }
-          if (n_ok) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int32_t m = 16 * c + j;
-              if (m < p.m)
-                d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
-            }
+          for (int j = 0; j < 16; ++j) {
+            const int32_t m = 16 * c + j;
+            if (m < p.m)
+              d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
           }
         }
       }

@@ -969,11 +969,6 @@ __global__ void __launch_bounds__(EpiShape<BN>::kThreads, 1)
   if (cluster_barriers) ptx::cluster_sync();  // peer barriers initialised before use
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Programmatic dependent launch: the set-up above (barriers, TMEM, descriptor prefetch) may
-  // overlap the previous kernel of the stream; global memory is touched only after it completed.
-  // The next launch may then be scheduled as this grid's CTAs exit.
-  ptx::griddep_wait();
-  ptx::griddep_launch_dependents();
 
   ptx::WaitCtx ctx{abort_flag, p.status, p.timeout_ns};
   const SchedParams& sp = p.sched;

@@ -508,20 +508,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-// ---------------------------------------------------------------- programmatic dependent launch
-// Wait until the grids this one depends on (the previous kernel in the stream, when this launch
-// allowed programmatic serialization) have completed and their memory is visible; a no-op
-// otherwise.
-__device__ __forceinline__ void griddep_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-// Let the next kernel in the stream (if launched with programmatic serialization) be scheduled
-// once every CTA of this grid has issued this or exited; it still waits in griddep_wait for this
-// grid to complete before it touches memory.
-__device__ __forceinline__ void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // ---------------------------------------------------------------- cluster launch control
 // Ask to cancel the launch of a cluster of this grid that has not started yet.  The 16-byte
 // response is written (async proxy) to this CTA's shared memory at `resp` and completes 16 bytes
