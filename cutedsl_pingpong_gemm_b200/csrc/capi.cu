@@ -362,7 +362,7 @@ struct cpg_gemm {
   CUtensorMap tm_a, tm_b, tm_d;
   // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
   int32_t decode;
-  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_rblocks;
+  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_rblocks, dec_spin;
 };
 
 extern "C" {
@@ -586,6 +586,8 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_splits = splits;
   g->dec_stages = stages;
   g->dec_rblocks = rblocks;
+  const char* env_spin = std::getenv("CPG_DECODE_SPIN");
+  g->dec_spin = env_spin != nullptr ? (std::atoi(env_spin) != 0) : 1;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
@@ -627,6 +629,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.kps = g->dec_kps;
   p.splits = g->dec_splits;
   p.rblocks = g->dec_rblocks;
+  p.spin = g->dec_spin;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
   p.scale_a = epi != nullptr ? epi->scale_a : nullptr;

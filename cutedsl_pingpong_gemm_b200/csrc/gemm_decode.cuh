@@ -49,6 +49,7 @@ struct DecodeParams {
   int32_t splits;      // CTAs per cluster: 1, 2 or 4
   int32_t rblocks;     // 128-row blocks of B per CTA: 1 or 2
   int32_t stages;
+  int32_t spin;        // producer / MMA lanes poll their barriers instead of sleeping
   float alpha;
   const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
   const float* scale_b;
@@ -171,7 +172,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int32_t kb = kb0; kb < kb1; ++kb) {
-        if (!ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx, kSiteProducerEmpty)) break;
+        const bool slot_free = p.spin ? ptx::mbar_wait_spin(empty_bar + 8u * stage, phase ^ 1u, ctx,
+                                                       kSiteProducerEmpty)
+                                 : ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx,
+                                                  kSiteProducerEmpty);
+        if (!slot_free) break;
         const uint32_t fb = full_bar + 8u * stage;
         const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
         ptx::mbar_arrive_expect_tx(fb, lay.stage_bytes);
@@ -201,7 +206,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int32_t kb = kb0; kb < kb1; ++kb) {
-        if (!ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)) break;
+        const bool full = p.spin ? ptx::mbar_wait_spin(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)
+                                 : ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull);
+        if (!full) break;
         ptx::tc_fence_after();
         const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
         const uint64_t db = ptx::make_sw128_kmajor_desc(sb + lay.b_bytes);  // mma_n rows of A

@@ -165,6 +165,38 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
   }
 }
 
+// Non-blocking test of the phase with parity `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// As mbar_wait, but polling with the non-blocking test_wait instead of sleeping in try_wait: for
+// loops whose work per phase is short next to a suspended thread's wake-up (the small-M
+// kernel's producer and MMA lanes).  Bounded the same way (deadline and abort flag, checked
+// every 256 polls).
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, const WaitCtx& ctx,
+                                               int32_t site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 256; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (*ctx.abort_flag) return false;
+    if (globaltimer() - t0 > ctx.timeout_ns) {
+      record_timeout(ctx, site);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -126,3 +126,33 @@ def test_multi_gpu_mshard_and_splitk(tmp_path):
         outs.append((p.returncode, out))
     assert all(rc == 0 for rc, _ in outs), outs
     assert "RESULT 1" in outs[0][1], outs[0][1]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("workload,exchange", [("tallk", "p2p"), ("tallk", "nccl"), ("llm", "p2p")])
+def test_bench_full_size_parity_on_every_gpu(workload, exchange):
+    """The benchmarked multi-GPU configurations at full size, through the bench itself under
+    torchrun on every GPU of the box: tall K (2048 x 2048 x 131072 split over the ranks, partial
+    sums exchanged by the GEMM epilogue over NVLink or by an NCCL reduce-scatter) and the LLM
+    up-projection (16384 x 28672 x 8192 + bias, M split over the ranks).  Each rank checks the
+    rows it owns after the timed steps (sampled rows element-wise and fp64 column / row sums,
+    the contributions of every K range summed over the ranks for split-K) and the line reports
+    the combined verdict."""
+    import json
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("needs at least two GPUs")
+    world = min(ngpu, 8)
+    cmd = ["timeout", "-k", "60", "600", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
+           f"--master-port={_free_port()}", os.path.join(ROOT, "bench.py"), "--gpus", str(world),
+           "--workload", workload, "--exchange", exchange, "--steps", "2", "--warmup", "1",
+           "--no-e2e"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    out = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
+    assert out.returncode == 0, (out.stdout[-2000:], out.stderr[-3000:])
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d["n_gpus"] == world and d["parity"]["ok"] and d["parity"]["ranks"] == world, d["parity"]
+    assert len(d["per_rank"]) == world
