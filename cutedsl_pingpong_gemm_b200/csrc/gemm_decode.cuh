@@ -203,35 +203,39 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kDecodeTileN, p.mma_n)
                                       : ptx::make_idesc_bf16_f32(kDecodeTileN, p.mma_n);
+      // Descriptors as 32-bit low halves: stage s's B block r starts at
+      // b_lo0 + s * stage_step + r * block_step, its A rows a_lo0 + s * stage_step.
+      const uint32_t hi = ptx::sw128_desc_hi();
+      const uint32_t stage_step = lay.stage_bytes >> 4;
+      const uint32_t block_step = (kDecodeTileN * kRowBytes) >> 4;
+      const uint32_t b_lo0 = ptx::sw128_desc_lo(base);
+      const uint32_t a_lo0 = ptx::sw128_desc_lo(base + lay.b_bytes);
+      uint32_t b_lo = b_lo0, a_lo = a_lo0;
       int stage = 0;
       uint32_t phase = 0;
       for (int32_t kb = kb0; kb < kb1; ++kb) {
         const bool full = p.spin ? ptx::mbar_wait_spin(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)
                                  : ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull);
         if (!full) break;
-        ptx::tc_fence_after();
-        const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
-        const uint64_t db = ptx::make_sw128_kmajor_desc(sb + lay.b_bytes);  // mma_n rows of A
+        // The stage's bytes arrived through the async proxy (TMA) and are read through it (the
+        // MMA): the completed barrier phase orders them; no tcgen05 fence is needed here.
 #pragma unroll
         for (int k = 0; k < kBK / kUmmaK; ++k) {
           const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-          for (int r = 0; r < R; ++r) {
-            // Row block r: B rows 128 r .. (1024-byte aligned, 16 KiB apart), accumulator r.
-            const uint64_t dar = ptx::make_sw128_kmajor_desc(sb + r * kDecodeTileN * kRowBytes);
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(r * p.mma_n);
-            if constexpr (OT::kFp8) {
-              ptx::umma_f8_ss<1>(d_tmem, dar + static_cast<uint64_t>(2 * k),
-                                 db + static_cast<uint64_t>(2 * k), idesc, acc);
-            } else {
-              ptx::umma_f16_ss<1>(d_tmem, dar + static_cast<uint64_t>(2 * k),
-                                  db + static_cast<uint64_t>(2 * k), idesc, acc);
-            }
-          }
+          for (int r = 0; r < R; ++r)
+            ptx::umma_ss_lohi<1, OT::kFp8>(tmem_base + static_cast<uint32_t>(r * p.mma_n),
+                                           b_lo + r * block_step + 2u * k, a_lo + 2u * k, hi,
+                                           idesc, acc);
         }
         ptx::umma_commit<1>(empty_bar + 8u * stage);
         if (++stage == stages) {
           stage = 0;
           phase ^= 1u;
+          b_lo = b_lo0;
+          a_lo = a_lo0;
+        } else {
+          b_lo += stage_step;
+          a_lo += stage_step;
         }
       }
       ptx::umma_commit<1>(tfull_bar);
