@@ -362,7 +362,7 @@ struct cpg_gemm {
   CUtensorMap tm_a, tm_b, tm_d;
   // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
   int32_t decode;
-  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_rblocks, dec_spin;
+  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_cg, dec_spin;
 };
 
 extern "C" {
@@ -455,23 +455,29 @@ static int alloc_fixup_workspace(cpg_gemm* g, int64_t tiles) {
 
 using DecodeFn = void (*)(const CUtensorMap, const CUtensorMap, const cpg::DecodeParams);
 
-static const void* decode_kernel(int dtype_ab, int dtype_d) {
+static const void* decode_kernel(int dtype_ab, int dtype_d, int cta_group) {
+  const bool fp8 = dtype_ab == CPG_DTYPE_E4M3, f32 = dtype_d == CPG_DTYPE_F32;
   DecodeFn fn;
-  if (dtype_ab == CPG_DTYPE_E4M3)
-    fn = dtype_d == CPG_DTYPE_F32 ? &cpg::gemm_decode_kernel<cpg::e4m3_t, float>
-                                  : &cpg::gemm_decode_kernel<cpg::e4m3_t, __nv_bfloat16>;
-  else
-    fn = dtype_d == CPG_DTYPE_F32 ? &cpg::gemm_decode_kernel<__nv_bfloat16, float>
-                                  : &cpg::gemm_decode_kernel<__nv_bfloat16, __nv_bfloat16>;
+  if (cta_group == 2) {
+    fn = fp8 ? (f32 ? &cpg::gemm_decode_kernel<cpg::e4m3_t, float, 2>
+                    : &cpg::gemm_decode_kernel<cpg::e4m3_t, __nv_bfloat16, 2>)
+             : (f32 ? &cpg::gemm_decode_kernel<__nv_bfloat16, float, 2>
+                    : &cpg::gemm_decode_kernel<__nv_bfloat16, __nv_bfloat16, 2>);
+  } else {
+    fn = fp8 ? (f32 ? &cpg::gemm_decode_kernel<cpg::e4m3_t, float, 1>
+                    : &cpg::gemm_decode_kernel<cpg::e4m3_t, __nv_bfloat16, 1>)
+             : (f32 ? &cpg::gemm_decode_kernel<__nv_bfloat16, float, 1>
+                    : &cpg::gemm_decode_kernel<__nv_bfloat16, __nv_bfloat16, 1>);
+  }
   return reinterpret_cast<const void*>(fn);
 }
 
-// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 128 R rows of B, R = 2 row blocks when
-// A has 64 or more rows (every tile re-reads all of A from L2; two blocks halve that) and the
-// tiles still fill the SMs with 4 CTAs each, else R = 1.  The K range of a tile is split over a
-// cluster of S CTAs, S the largest of 4, 2, 1 that keeps every CTA of the grid resident at once
-// (tiles * S <= SMs) and gives every CTA a k-block.  Stages: the deepest ring that fits (at most
-// the CTA's k-blocks), and at least enough to hold the reduction's receive buffer.
+// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 256 rows of B on a CTA pair (one
+// cta_group::2 MMA per k-step covers both CTAs' 128 rows, half the MMA instructions per loaded
+// byte of single CTAs).  The K range of a tile is split over a cluster of S pairs, S the largest
+// of 4, 2, 1 that keeps every CTA of the grid resident at once (tiles * 2 S <= SMs) and gives
+// every pair a k-block.  Stages: the deepest ring that fits (at most the pair's k-blocks), and
+// at least enough to hold the reduction's receive buffer.
 static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
                               const cudaDeviceProp& prop, cpg_gemm** out) {
   if (prob->m < 1 || prob->m > cpg::kDecodeMaxM)
@@ -484,22 +490,20 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   const int64_t k_iters = (prob->k + bk - 1) / bk;
   const int64_t sms = prop.multiProcessorCount;
   const int mma_n = static_cast<int>((prob->m + 15) / 16 * 16);
-  const int64_t wide_tiles = (prob->n + 2 * cpg::kDecodeTileN - 1) / (2 * cpg::kDecodeTileN);
-  int rblocks = (mma_n >= 64 && wide_tiles * 4 <= sms && k_iters >= 4) ? 2 : 1;
-  // Tuning overrides (measurement only): CPG_DECODE_RBLOCKS (1, 2), CPG_DECODE_SPLITS (1, 2, 4),
-  // CPG_DECODE_STAGES (>= 2).
-  const char* env_r = std::getenv("CPG_DECODE_RBLOCKS");
+  // Tuning overrides (measurement only): CPG_DECODE_PAIR (0: single CTAs), CPG_DECODE_SPLITS
+  // (1, 2, 4), CPG_DECODE_STAGES (>= 2), CPG_DECODE_SPIN (0: sleeping waits).
+  const char* env_pair = std::getenv("CPG_DECODE_PAIR");
   const char* env_s = std::getenv("CPG_DECODE_SPLITS");
   const char* env_st = std::getenv("CPG_DECODE_STAGES");
-  if (env_r != nullptr && (std::atoi(env_r) == 1 || std::atoi(env_r) == 2)) rblocks = std::atoi(env_r);
-  const int64_t tile_rows = int64_t(rblocks) * cpg::kDecodeTileN;
+  const int cg = (env_pair != nullptr && std::atoi(env_pair) == 0) ? 1 : 2;
+  const int64_t tile_rows = int64_t(cg) * cpg::kDecodeTileN;
   const int64_t tiles = (prob->n + tile_rows - 1) / tile_rows;
   if (tiles > 65535)
     return fail(CPG_ERR_INVALID_SHAPE, "the small-M kernel takes N <= %lld",
                 static_cast<long long>(65535 * tile_rows));
   int splits = 1;
   for (int s = cpg::kDecodeMaxSplits; s > 1; s /= 2) {
-    if (tiles * s <= sms && k_iters >= s) {
+    if (tiles * cg * s <= sms && k_iters >= s) {
       splits = s;
       break;
     }
@@ -509,11 +513,11 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
     if ((v == 1 || v == 2 || v == 4) && v <= k_iters) splits = v;
   }
   int tmem_cols = 32;
-  while (tmem_cols < rblocks * mma_n) tmem_cols *= 2;
+  while (tmem_cols < mma_n) tmem_cols *= 2;
   const int64_t kps = k_iters > 0 ? (k_iters + splits - 1) / splits : 0;
   int stages = 0;
   for (int st = cpg::kDecodeMaxStages; st >= 2; --st) {
-    if (static_cast<int64_t>(cpg::decode_layout(st, mma_n, splits, rblocks).bytes) <=
+    if (static_cast<int64_t>(cpg::decode_layout(st, mma_n, splits, cg).bytes) <=
         static_cast<int64_t>(prop.sharedMemPerBlockOptin)) {
       stages = st;
       break;
@@ -525,13 +529,13 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
     stages = std::atoi(env_st);
   if (stages < 2) stages = 2;
   // The receive buffer of the in-cluster reduction lives in the stages.
-  while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, rblocks).stage_bytes <
-         cpg::decode_layout(stages, mma_n, splits, rblocks).recv_bytes)
+  while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, cg).stage_bytes <
+         cpg::decode_layout(stages, mma_n, splits, cg).recv_bytes)
     ++stages;
-  const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits, rblocks).bytes);
+  const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits, cg).bytes);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "the small-M kernel does not fit in shared memory");
-  const void* fn = decode_kernel(prob->dtype_ab, prob->dtype_d);
+  const void* fn = decode_kernel(prob->dtype_ab, prob->dtype_d, cg);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(small-M kernel smem)");
   int mac = 0;
@@ -539,10 +543,10 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
     cudaLaunchConfig_t lc = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.x = cg * splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    lc.gridDim = dim3(splits, 1, 1);
+    lc.gridDim = dim3(cg * splits, 1, 1);
     lc.blockDim = dim3(cpg::kDecodeThreads, 1, 1);
     lc.dynamicSmemBytes = smem;
     lc.attrs = attr;
@@ -557,7 +561,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->cfg = *cfg;
   g->prob = *prob;
   g->device = device;
-  g->v = Variant{cpg::kDecodeTileN, 1, prob->dtype_ab, prob->dtype_d, CPG_SCALE_TENSOR, fn,
+  g->v = Variant{cpg::kDecodeTileN * cg, cg, prob->dtype_ab, prob->dtype_d, CPG_SCALE_TENSOR, fn,
                  nullptr, cpg::kDecodeThreads, cpg::kEpiWarps};
   g->smem_bytes = smem;
   g->max_active_clusters = mac;
@@ -573,10 +577,10 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->batches = 1;
   g->sched = cpg::sched_params_create(1, static_cast<int32_t>(tiles > 0 ? tiles : 1), 1,
                                       CPG_RASTER_ALONG_N, 1, 1, 1, 0);
-  g->grid[0] = splits;
+  g->grid[0] = cg * splits;
   g->grid[1] = static_cast<int32_t>(tiles > 0 ? tiles : 1);
   g->grid[2] = 1;
-  g->cluster[0] = splits;
+  g->cluster[0] = cg * splits;
   g->cluster[1] = 1;
   g->cluster[2] = 1;
   g->decode = 1;
@@ -585,7 +589,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_kps = static_cast<int32_t>(kps);
   g->dec_splits = splits;
   g->dec_stages = stages;
-  g->dec_rblocks = rblocks;
+  g->dec_cg = cg;
   const char* env_spin = std::getenv("CPG_DECODE_SPIN");
   g->dec_spin = env_spin != nullptr ? (std::atoi(env_spin) != 0) : 1;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
@@ -607,11 +611,12 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   const int eab = elem_bytes(pr.dtype_ab);
   const int bk = cpg::kRowBytes / eab;
   if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b) {
+    // Each CTA loads its 128 rows of B and (pairs) half of the token rows of A.
     int rc = encode_tiled(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda,
-                          g->dec_mma_n, bk);
+                          g->dec_mma_n / g->dec_cg, bk);
     if (rc != CPG_OK) return rc;
     rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
-                      g->dec_rblocks * cpg::kDecodeTileN, bk);
+                      cpg::kDecodeTileN, bk);
     if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
@@ -628,7 +633,6 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.k_iters = g->k_iters;
   p.kps = g->dec_kps;
   p.splits = g->dec_splits;
-  p.rblocks = g->dec_rblocks;
   p.spin = g->dec_spin;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
@@ -647,9 +651,9 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   lc.blockDim = dim3(cpg::kDecodeThreads, 1, 1);
   lc.dynamicSmemBytes = g->smem_bytes;
   lc.stream = st;
-  if (g->dec_splits > 1) {
+  if (g->dec_splits * g->dec_cg > 1) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = g->dec_splits;
+    attr[0].val.clusterDim.x = g->dec_splits * g->dec_cg;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;

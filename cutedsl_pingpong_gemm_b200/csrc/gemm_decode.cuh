@@ -2,31 +2,37 @@
 // for M <= 128, the decode-like shapes where B (the weight, N x K) is read from HBM once and A
 // holds a few token rows.
 //
-// The tile is transposed with respect to the plain kernel: each CTA computes D^T for 128 R rows
-// of B (R = 1 or 2 row blocks, one M = 128 MMA and one TMEM accumulator each), so B's rows fill
-// the MMA's M side (128 TMEM lanes per block) and the M token rows of A are the MMA's N (rounded
-// up to 16; rows past M are zero-filled by TMA).  No 128-row A tile is padded out of a handful of
-// rows, and every loaded byte of B feeds the tensor core once.  Two row blocks per CTA halve the
-// re-reads of A from L2 (every tile reads all of A), which matter once A has 64 rows or more.
+// The tile is transposed with respect to the plain kernel: the MMA computes D^T, B's rows on its
+// M side (one TMEM lane each) and the M token rows of A on its N side (rounded up to 16; rows
+// past M are zero-filled by TMA).  No 128-row A tile is padded out of a handful of rows, and every
+// loaded byte of B feeds the tensor core once.  With so little math per byte, what bounds a CTA
+// is the MMA issue rate of its one issuing thread (about 100 cycles per tcgen05.mma whatever its
+// N, plus about 200 per k-block for the barrier wait and commit, measured with a clock64 trace),
+// so the kernel runs on CTA pairs (CG = 2): one tcgen05.mma.cta_group::2 with M = 256 covers 128
+// rows of B in each CTA of the pair, which halves the MMA instructions per loaded byte.  Each CTA
+// of a pair loads its own 128 rows of B and half of the token rows of A; the loads complete on
+// the leader's barrier and the leader's commits release the stages of both CTAs.  CG = 1 runs
+// single CTAs on 128-row tiles.
 //
-// A tile of B alone leaves most SMs idle (N = 8192 gives 64 or 32 tiles), so the K range of a
-// tile is split over the S CTAs of a cluster (S = 1, 2 or 4; cluster dims (S, 1, 1), grid
-// (S, ceil(N / (128 R)))).  Each CTA accumulates its K range in TMEM; the partial sums are then
-// reduced through distributed shared memory, in one launch and without any global workspace:
-// the 128 R rows of the tile are dealt to the CTAs in blocks of 128 R / S rows (CTA r owns rows
-// [r 128 R / S, (r + 1) 128 R / S)).  Once every CTA of the cluster has finished its MMAs and its
-// loads (a cluster barrier), the A/B stages are free and serve as receive buffers: the warps
-// holding another CTA's rows store them there (st.shared::cluster, 16-byte vectors, rows padded
-// by 16 bytes so a warp's stores hit distinct banks) and arrive on that CTA's receive barrier
-// with cluster-scope release; the owner adds the S - 1 received rows to its own, applies alpha,
-// the FP8 scales and the bias and writes its rows of D^T as columns of D (for each token row m, a
-// warp writes 32 consecutive elements).
+// A tile of B (128 CG rows) alone leaves most SMs idle (N = 8192 gives 32 pair tiles), so the K
+// range of a tile is split over S pairs (or CTAs) of one cluster (S = 1, 2 or 4; cluster dims
+// (CG S, 1, 1), CTA rank CG kr + q for K range kr and position q in the pair; grid
+// (CG S, ceil(N / (128 CG)))).  Each pair accumulates its K range in TMEM; the partial sums are
+// then reduced through distributed shared memory, in one launch and without any global
+// workspace: the 128 rows a CTA holds are dealt to the S CTAs holding the same rows in blocks
+// of 128 / S rows.  Once every CTA of the cluster has finished its MMAs and its loads (a cluster
+// barrier), the A/B stages are free and serve as receive buffers: the warps holding another
+// CTA's rows store them there (st.shared::cluster, 16-byte vectors, rows padded by 16 bytes so a
+// warp's stores hit distinct banks) and arrive on that CTA's receive barrier with cluster-scope
+// release; the owner adds the S - 1 received rows to its own, applies alpha, the FP8 scales and
+// the bias and writes its rows of D^T as columns of D (for each token row m, a warp writes 32
+// consecutive elements).
 //
-// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and MMA issuer
-// (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4 of every block).
-// Every wait is bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA
-// loads and MMAs are drained before the stages are reused or TMEM is freed, and the final
-// cluster barrier keeps every CTA resident until no peer can still write into its shared memory.
+// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
+// MMA issuer (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4).  Every
+// wait is bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA loads
+// and MMAs are drained before the stages are reused or TMEM is freed, and the final cluster
+// barrier keeps every CTA resident until no peer can still write into its shared memory.
 #pragma once
 #include "gemm_kernel.cuh"
 
@@ -34,9 +40,8 @@ namespace cpg {
 
 constexpr int kDecodeThreads = 192;
 constexpr int kDecodeMaxM = 128;      // MMA N: the token rows of one launch
-constexpr int kDecodeTileN = 128;     // rows of B per row block (the MMA's M, one TMEM lane each)
-constexpr int kDecodeMaxBlocks = 2;   // row blocks per CTA
-constexpr int kDecodeMaxSplits = 4;   // CTAs per cluster (owners of at least 32 rows each)
+constexpr int kDecodeTileN = 128;     // rows of B per CTA (the MMA's M per CTA, one TMEM lane each)
+constexpr int kDecodeMaxSplits = 4;   // K ranges per cluster (owners of at least 32 rows each)
 constexpr int kDecodeMaxStages = 12;
 constexpr int32_t kSiteDecodeRecv = 11;  // the owner waiting for its peers' partial sums
 
@@ -45,9 +50,8 @@ struct DecodeParams {
   int32_t mma_n;       // round_up(M, 16)
   int32_t tmem_cols;   // power of two >= max(32, mma_n)
   int32_t k_iters;     // ceil(K / BK)
-  int32_t kps;         // k-blocks per CTA of a cluster
-  int32_t splits;      // CTAs per cluster: 1, 2 or 4
-  int32_t rblocks;     // 128-row blocks of B per CTA: 1 or 2
+  int32_t kps;         // k-blocks per K range
+  int32_t splits;      // K ranges per cluster: 1, 2 or 4
   int32_t stages;
   int32_t spin;        // producer / MMA lanes poll their barriers instead of sleeping
   float alpha;
@@ -62,27 +66,26 @@ struct DecodeParams {
   int32_t l2_policy_b;
 };
 
-// Shared-memory layout (offsets from the 1024-byte aligned base), the same on host and device.
-// The receive buffer of the reduction aliases the A/B stages (used only after every CTA of the
-// cluster has finished with them).
+// Shared-memory layout of one CTA (offsets from the 1024-byte aligned base), the same on host and
+// device.  The receive buffer of the reduction aliases the A/B stages (used only after every CTA
+// of the cluster has finished with them).
 struct DecodeLayout {
-  uint32_t b_bytes;          // 128 R rows of B x 128 bytes
-  uint32_t stage_bytes;      // B rows + mma_n rows of A
+  uint32_t b_bytes;          // 128 rows of B x 128 bytes
+  uint32_t stage_bytes;      // B rows + this CTA's mma_n / CG rows of A
   uint32_t recv_row_floats;  // mma_n + 4 (16 bytes of padding per row)
-  uint32_t recv_bytes;       // (S - 1) * 128 R / S rows
+  uint32_t recv_bytes;       // (S - 1) * 128 / S rows
   uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
   uint32_t slot_off;         // TMEM base address, abort flag
   uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
 };
 
 __host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int splits,
-                                                      int rblocks) {
+                                                      int cta_group) {
   DecodeLayout l;
-  l.b_bytes = static_cast<uint32_t>(rblocks) * kDecodeTileN * kRowBytes;
-  l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n) * kRowBytes;
+  l.b_bytes = kDecodeTileN * kRowBytes;
+  l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n / cta_group) * kRowBytes;
   l.recv_row_floats = static_cast<uint32_t>(mma_n) + 4u;
-  const uint32_t recv_rows =
-      splits > 1 ? (splits - 1) * (static_cast<uint32_t>(rblocks) * kDecodeTileN / splits) : 0u;
+  const uint32_t recv_rows = splits > 1 ? (splits - 1) * (kDecodeTileN / splits) : 0u;
   l.recv_bytes = recv_rows * l.recv_row_floats * 4u;
   l.bar_off = static_cast<uint32_t>(stages) * l.stage_bytes;
   l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
@@ -101,7 +104,7 @@ __device__ __forceinline__ float to_out<float>(float x) {
   return x;
 }
 
-template <typename AB, typename OutT>
+template <typename AB, typename OutT, int CG>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, const DecodeParams p) {
@@ -116,8 +119,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   const int stages = p.stages;
   const int S = p.splits;
-  const int R = p.rblocks;
-  const DecodeLayout lay = decode_layout(stages, p.mma_n, S, R);
+  const DecodeLayout lay = decode_layout(stages, p.mma_n, S, CG);
   const uint32_t full_bar = base + lay.bar_off;
   const uint32_t empty_bar = full_bar + 8u * stages;
   const uint32_t tfull_bar = empty_bar + 8u * stages;
@@ -128,10 +130,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = ptx::lane_id();
-  const uint32_t rank = S > 1 ? ptx::cluster_ctarank() : 0u;
-  const uint32_t rows_per_owner = static_cast<uint32_t>(R * kDecodeTileN / S);
-  const int32_t n0 = static_cast<int32_t>(blockIdx.y) * R * kDecodeTileN;
-  const int32_t kb0 = static_cast<int32_t>(rank) * p.kps;
+  const bool clustered = S * CG > 1;
+  const uint32_t crank = clustered ? ptx::cluster_ctarank() : 0u;
+  const uint32_t q = CG == 2 ? (crank & 1u) : 0u;              // position in the pair
+  const uint32_t kr = CG == 2 ? (crank >> 1) : crank;          // K range of this CTA
+  const bool leader = q == 0u;
+  const uint32_t leader_rank = crank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader_rank);
+  const uint32_t rows_per_owner = static_cast<uint32_t>(kDecodeTileN / S);
+  const int32_t n0 = static_cast<int32_t>(blockIdx.y) * (CG * kDecodeTileN) +
+                     static_cast<int32_t>(q) * kDecodeTileN;  // this CTA's first row of B
+  const int32_t a_row0 = static_cast<int32_t>(q) * (p.mma_n / CG);  // its first row of A
+  const int32_t kb0 = static_cast<int32_t>(kr) * p.kps;
   const int32_t kb1 = min(p.k_iters, kb0 + p.kps);
   const bool has_k = kb1 > kb0;
 
@@ -152,13 +162,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::prefetch_tensormap(&tm_b);
   }
   if (warp == 1) {
-    ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)),
-                       static_cast<uint32_t>(p.tmem_cols));
-    ptx::tmem_relinquish<1>();
+    ptx::tmem_alloc<CG>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)),
+                        static_cast<uint32_t>(p.tmem_cols));
+    ptx::tmem_relinquish<CG>();
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (S > 1) ptx::cluster_sync();  // every CTA's receive barrier initialised before any arrive
+  if (clustered) ptx::cluster_sync();  // every CTA's barriers initialised before any remote use
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   ptx::WaitCtx ctx{abort_flag, p.status, p.timeout_ns};
@@ -172,62 +182,74 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int32_t kb = kb0; kb < kb1; ++kb) {
-        const bool slot_free = p.spin ? ptx::mbar_wait_spin(empty_bar + 8u * stage, phase ^ 1u, ctx,
-                                                       kSiteProducerEmpty)
-                                 : ptx::mbar_wait(empty_bar + 8u * stage, phase ^ 1u, ctx,
-                                                  kSiteProducerEmpty);
+        const uint32_t eb = empty_bar + 8u * stage;
+        const bool slot_free = p.spin ? ptx::mbar_wait_spin(eb, phase ^ 1u, ctx, kSiteProducerEmpty)
+                                      : ptx::mbar_wait(eb, phase ^ 1u, ctx, kSiteProducerEmpty);
         if (!slot_free) break;
         const uint32_t fb = full_bar + 8u * stage;
         const uint32_t sb = base + static_cast<uint32_t>(stage) * lay.stage_bytes;
-        ptx::mbar_arrive_expect_tx(fb, lay.stage_bytes);
-        ptx::tma_load_3d(&tm_b, sb, fb, kb * kBK, n0, 0, pol_b);
-        ptx::tma_load_3d(&tm_a, sb + lay.b_bytes, fb, kb * kBK, 0, 0, pol_a);
+        if constexpr (CG == 1) {
+          ptx::mbar_arrive_expect_tx(fb, lay.stage_bytes);
+          ptx::tma_load_3d(&tm_b, sb, fb, kb * kBK, n0, 0, pol_b);
+          ptx::tma_load_3d(&tm_a, sb + lay.b_bytes, fb, kb * kBK, a_row0, 0, pol_a);
+        } else {
+          // Both CTAs' bytes complete on the leader's barrier.
+          if (leader) ptx::mbar_arrive_expect_tx(fb, 2u * lay.stage_bytes);
+          const uint32_t fb_leader = ptx::mapa_shared(fb, leader_rank);
+          ptx::tma_load_3d_pair(&tm_b, sb, fb_leader, kb * kBK, n0, 0, pol_b);
+          ptx::tma_load_3d_pair(&tm_a, sb + lay.b_bytes, fb_leader, kb * kBK, a_row0, 0, pol_a);
+        }
         ++issued;
         if (++stage == stages) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      // Drain: the last fill of every stage has landed before the CTA may exit (bounded, and
-      // independent of an abort: a TMA write must not reach freed shared memory).
+      // Drain: the last fill of every stage has landed before the stages are reused or the CTA
+      // exits (bounded, and independent of an abort on the leader, whose full barriers count
+      // both CTAs' bytes; the other CTA of a pair waits for its fills to be consumed).
       ptx::WaitCtx dctx = ctx;
       volatile int32_t no_abort = 0;
       dctx.abort_flag = &no_abort;
-      for (int i = issued > stages ? issued - stages : 0; i < issued; ++i)
-        ptx::mbar_wait(full_bar + 8u * (i % stages), static_cast<uint32_t>((i / stages) & 1),
-                       dctx, kSiteDrainLoads);
+      for (int i = issued > stages ? issued - stages : 0; i < issued; ++i) {
+        const uint32_t par = static_cast<uint32_t>((i / stages) & 1);
+        if (leader)
+          ptx::mbar_wait(full_bar + 8u * (i % stages), par, dctx, kSiteDrainLoads);
+        else if (*abort_flag == 0)
+          ptx::mbar_wait(empty_bar + 8u * (i % stages), par, dctx, kSiteDrainLoads);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(kDecodeTileN, p.mma_n)
-                                      : ptx::make_idesc_bf16_f32(kDecodeTileN, p.mma_n);
-      // Descriptors as 32-bit low halves: stage s's B block r starts at
-      // b_lo0 + s * stage_step + r * block_step, its A rows a_lo0 + s * stage_step.
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && leader) {
+      const uint32_t idesc = OT::kFp8 ? ptx::make_idesc_e4m3_f32(CG * kDecodeTileN, p.mma_n)
+                                      : ptx::make_idesc_bf16_f32(CG * kDecodeTileN, p.mma_n);
+      // Descriptors as 32-bit low halves: stage s's B rows start at b_lo0 + s * stage_step,
+      // its A rows at a_lo0 + s * stage_step.
       const uint32_t hi = ptx::sw128_desc_hi();
       const uint32_t stage_step = lay.stage_bytes >> 4;
-      const uint32_t block_step = (kDecodeTileN * kRowBytes) >> 4;
       const uint32_t b_lo0 = ptx::sw128_desc_lo(base);
       const uint32_t a_lo0 = ptx::sw128_desc_lo(base + lay.b_bytes);
       uint32_t b_lo = b_lo0, a_lo = a_lo0;
       int stage = 0;
       uint32_t phase = 0;
       for (int32_t kb = kb0; kb < kb1; ++kb) {
-        const bool full = p.spin ? ptx::mbar_wait_spin(full_bar + 8u * stage, phase, ctx, kSiteMmaFull)
-                                 : ptx::mbar_wait(full_bar + 8u * stage, phase, ctx, kSiteMmaFull);
+        const uint32_t fb = full_bar + 8u * stage;
+        const bool full = p.spin ? ptx::mbar_wait_spin(fb, phase, ctx, kSiteMmaFull)
+                                 : ptx::mbar_wait(fb, phase, ctx, kSiteMmaFull);
         if (!full) break;
         // The stage's bytes arrived through the async proxy (TMA) and are read through it (the
         // MMA): the completed barrier phase orders them; no tcgen05 fence is needed here.
 #pragma unroll
-        for (int k = 0; k < kBK / kUmmaK; ++k) {
-          const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
-          for (int r = 0; r < R; ++r)
-            ptx::umma_ss_lohi<1, OT::kFp8>(tmem_base + static_cast<uint32_t>(r * p.mma_n),
-                                           b_lo + r * block_step + 2u * k, a_lo + 2u * k, hi,
-                                           idesc, acc);
+        for (int k = 0; k < kBK / kUmmaK; ++k)
+          ptx::umma_ss_lohi<CG, OT::kFp8>(tmem_base, b_lo + 2u * k, a_lo + 2u * k, hi, idesc,
+                                          (kb > kb0 || k > 0) ? 1u : 0u);
+        if constexpr (CG == 1) {
+          ptx::umma_commit<1>(empty_bar + 8u * stage);
+        } else {
+          ptx::umma_commit_pair(empty_bar + 8u * stage, pair_mask);
         }
-        ptx::umma_commit<1>(empty_bar + 8u * stage);
         if (++stage == stages) {
           stage = 0;
           phase ^= 1u;
@@ -238,9 +260,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           a_lo += stage_step;
         }
       }
-      ptx::umma_commit<1>(tfull_bar);
-      // No MMA may still write TMEM when it is freed.
-      ptx::umma_commit<1>(drain_bar);
+      if constexpr (CG == 1) {
+        ptx::umma_commit<1>(tfull_bar);
+      } else {
+        ptx::umma_commit_pair(tfull_bar, pair_mask);
+      }
+      // No MMA may still read the stages or write TMEM when they are reused or freed.
+      ptx::umma_commit<CG>(drain_bar);
       ptx::WaitCtx dctx = ctx;
       volatile int32_t no_abort = 0;
       dctx.abort_flag = &no_abort;
@@ -258,22 +284,22 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::tc_fence_after();
   }
   ptx::fence_proxy_async_shared();  // the stages' async-proxy use ends before generic stores
-  if (S > 1) ptx::cluster_sync();
+  if (clustered) ptx::cluster_sync();
   if (warp >= 2) {
     // ---------------------------------------------------------------- reduction + epilogue
     const uint32_t quad = warp & 3u;
     const int chunks = p.mma_n / 16;
-    const bool read_tmem = ok && has_k;
-    // Sends first (they never wait), then the owned rows (which wait for the peers' sends).
-    for (int r = 0; r < R; ++r) {
-      const uint32_t row = static_cast<uint32_t>(r * kDecodeTileN) + quad * 32u + lane;
-      const uint32_t owner = (row - lane) / rows_per_owner;  // uniform over the warp
-      if (owner == rank) continue;
-      const uint32_t t_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(r * p.mma_n);
-      const uint32_t slot = rank < owner ? rank : rank - 1u;
+    const uint32_t row = quad * 32u + lane;                  // TMEM lane = row of this CTA's block
+    const uint32_t owner = (row - lane) / rows_per_owner;    // K range owning it (warp-uniform)
+    const uint32_t t_row = tmem_base + ((quad * 32u) << 16);
+    if (owner != kr) {
+      // Send this row's partial sums to the CTA of the owning K range holding the same rows.
+      const uint32_t dst_rank = owner * CG + q;
+      const uint32_t slot = kr < owner ? kr : kr - 1u;
       const uint32_t local = row - owner * rows_per_owner;
       const uint32_t dst = ptx::mapa_shared(
-          base + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, owner);
+          base + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, dst_rank);
+      const bool read_tmem = ok && has_k;
       for (int c = 0; c < chunks; ++c) {
         uint32_t v[16];
         if (read_tmem) {
@@ -288,60 +314,52 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           ptx::st_shared_cluster_v4(dst + static_cast<uint32_t>(64 * c + 16 * j), v[4 * j],
                                     v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       }
-      ptx::mbar_arrive_release_cluster(ptx::mapa_shared(recv_bar, owner));
-    }
-    bool waited = false, got = ok;
-    for (int r = 0; r < R; ++r) {
-      const uint32_t row = static_cast<uint32_t>(r * kDecodeTileN) + quad * 32u + lane;
-      const uint32_t owner = (row - lane) / rows_per_owner;
-      if (owner != rank) continue;
-      if (!waited && S > 1) {
-        bool g = ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
-        got = __all_sync(0xffffffffu, g) && ok;
-        waited = true;
-      }
-      if (!got) break;
-      const uint32_t t_row = tmem_base + ((quad * 32u) << 16) + static_cast<uint32_t>(r * p.mma_n);
-      const int32_t n = n0 + static_cast<int32_t>(row);
-      float scale = p.alpha;
-      if (p.scale_a != nullptr) scale *= *p.scale_a;
-      if (p.scale_b != nullptr) scale *= *p.scale_b;
-      const bool n_ok = n < p.n;
-      const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
-      const uint32_t local = row - rank * rows_per_owner;
-      OutT* d = static_cast<OutT*>(p.d);
-      for (int c = 0; c < chunks; ++c) {
-        uint32_t v[16];
-        if (has_k) {
-          ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
-          ptx::tmem_ld_wait();
-        } else {
+      ptx::mbar_arrive_release_cluster(ptx::mapa_shared(recv_bar, dst_rank));
+    } else {
+      bool got = S == 1 || ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
+      got = __all_sync(0xffffffffu, got) && ok;
+      if (got) {
+        const int32_t n = n0 + static_cast<int32_t>(row);
+        float scale = p.alpha;
+        if (p.scale_a != nullptr) scale *= *p.scale_a;
+        if (p.scale_b != nullptr) scale *= *p.scale_b;
+        const bool n_ok = n < p.n;
+        const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
+        const uint32_t local = row - kr * rows_per_owner;
+        OutT* d = static_cast<OutT*>(p.d);
+        for (int c = 0; c < chunks; ++c) {
+          uint32_t v[16];
+          if (has_k) {
+            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
+            ptx::tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0u;
-        }
-        float acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
-        for (int src = 0; src < S - 1; ++src) {
-          const uint32_t r_addr = base + ((static_cast<uint32_t>(src) * rows_per_owner + local) *
-                                              lay.recv_row_floats +
-                                          static_cast<uint32_t>(16 * c)) *
-                                             4u;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
-            acc[4 * j] += __uint_as_float(w.x);
-            acc[4 * j + 1] += __uint_as_float(w.y);
-            acc[4 * j + 2] += __uint_as_float(w.z);
-            acc[4 * j + 3] += __uint_as_float(w.w);
+            for (int j = 0; j < 16; ++j) v[j] = 0u;
           }
-        }
-        if (n_ok) {
+          float acc[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int32_t m = 16 * c + j;
-            if (m < p.m)
-              d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
+          for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
+          for (int src = 0; src < S - 1; ++src) {
+            const uint32_t r_addr = base + ((static_cast<uint32_t>(src) * rows_per_owner + local) *
+                                                lay.recv_row_floats +
+                                            static_cast<uint32_t>(16 * c)) *
+                                               4u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
+              acc[4 * j] += __uint_as_float(w.x);
+              acc[4 * j + 1] += __uint_as_float(w.y);
+              acc[4 * j + 2] += __uint_as_float(w.z);
+              acc[4 * j + 3] += __uint_as_float(w.w);
+            }
+          }
+          if (n_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int32_t m = 16 * c + j;
+              if (m < p.m)
+                d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
+            }
           }
         }
       }
@@ -350,10 +368,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (S > 1) ptx::cluster_sync();  // no CTA leaves while a peer may still store into it
+  if (clustered) ptx::cluster_sync();  // no CTA leaves while a peer may still store into it
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc<1>(tmem_base, static_cast<uint32_t>(p.tmem_cols));
+    ptx::tmem_dealloc<CG>(tmem_base, static_cast<uint32_t>(p.tmem_cols));
   }
 #endif
 }
