@@ -685,14 +685,17 @@ def run_tallk(args, world, rank, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
+    # Host-side set-up (NVML handles and counter reads take milliseconds) before the barrier:
+    # the ranks exchange partial sums every step, so a rank that starts late makes the others
+    # wait inside their timed region.
     sampler = ClockSampler(local)
     nvl = NvlinkCounter(local)
+    nvl.start()
     launches[0] = 0
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    nvl.start()
+    barrier(world)
+    torch.cuda.synchronize()
     e0.record(stream)
     for i in range(args.steps):
         out = step()

@@ -362,7 +362,7 @@ struct cpg_gemm {
   CUtensorMap tm_a, tm_b, tm_d;
   // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
   int32_t decode;
-  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_cg, dec_spin;
+  int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_cg, dec_spin, dec_rotate;
 };
 
 extern "C" {
@@ -472,12 +472,13 @@ static const void* decode_kernel(int dtype_ab, int dtype_d, int cta_group) {
   return reinterpret_cast<const void*>(fn);
 }
 
-// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 256 rows of B on a CTA pair (one
-// cta_group::2 MMA per k-step covers both CTAs' 128 rows, half the MMA instructions per loaded
-// byte of single CTAs).  The K range of a tile is split over a cluster of S pairs, S the largest
-// of 4, 2, 1 that keeps every CTA of the grid resident at once (tiles * 2 S <= SMs) and gives
-// every pair a k-block.  Stages: the deepest ring that fits (at most the pair's k-blocks), and
-// at least enough to hold the reduction's receive buffer.
+// Plan of the small-M kernel (CPG_SPLIT_K_DECODE).  Tiles: 128 rows of B per CTA.  The K range of
+// a tile is split over a cluster of S CTAs, S the largest of 4, 2, 1 that keeps every CTA of the
+// grid resident at once (tiles * S <= SMs) and gives every CTA a k-block.  Stages: the deepest
+// ring that fits (at most the CTA's k-blocks), and at least enough to hold the reduction's
+// receive buffer.  Measured on N = K = 8192 against the CTA-pair form (CPG_DECODE_PAIR=1: 256-row
+// tiles, one cta_group::2 MMA per k-step for both CTAs): M = 16 / 64 / 128 28.7 / 32.8 / 36.6 us
+// single against 30.7 / 34.8 / 38.2 us paired, on one box in one call.
 static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem* prob, int device,
                               const cudaDeviceProp& prop, cpg_gemm** out) {
   if (prob->m < 1 || prob->m > cpg::kDecodeMaxM)
@@ -490,12 +491,13 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   const int64_t k_iters = (prob->k + bk - 1) / bk;
   const int64_t sms = prop.multiProcessorCount;
   const int mma_n = static_cast<int>((prob->m + 15) / 16 * 16);
-  // Tuning overrides (measurement only): CPG_DECODE_PAIR (0: single CTAs), CPG_DECODE_SPLITS
-  // (1, 2, 4), CPG_DECODE_STAGES (>= 2), CPG_DECODE_SPIN (0: sleeping waits).
+  // Tuning overrides (measurement only): CPG_DECODE_PAIR (1: CTA pairs), CPG_DECODE_SPLITS
+  // (1, 2, 4), CPG_DECODE_STAGES (>= 2), CPG_DECODE_SPIN (0: sleeping waits),
+  // CPG_DECODE_ROTATE (0: every tile walks its K range from the start).
   const char* env_pair = std::getenv("CPG_DECODE_PAIR");
   const char* env_s = std::getenv("CPG_DECODE_SPLITS");
   const char* env_st = std::getenv("CPG_DECODE_STAGES");
-  const int cg = (env_pair != nullptr && std::atoi(env_pair) == 0) ? 1 : 2;
+  const int cg = (env_pair != nullptr && std::atoi(env_pair) == 1) ? 2 : 1;
   const int64_t tile_rows = int64_t(cg) * cpg::kDecodeTileN;
   const int64_t tiles = (prob->n + tile_rows - 1) / tile_rows;
   if (tiles > 65535)
@@ -592,6 +594,8 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_cg = cg;
   const char* env_spin = std::getenv("CPG_DECODE_SPIN");
   g->dec_spin = env_spin != nullptr ? (std::atoi(env_spin) != 0) : 1;
+  const char* env_rot = std::getenv("CPG_DECODE_ROTATE");
+  g->dec_rotate = env_rot != nullptr ? (std::atoi(env_rot) != 0) : 1;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
@@ -634,6 +638,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.kps = g->dec_kps;
   p.splits = g->dec_splits;
   p.spin = g->dec_spin;
+  p.rotate = g->dec_rotate;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
   p.scale_a = epi != nullptr ? epi->scale_a : nullptr;

@@ -5,14 +5,14 @@
 // The tile is transposed with respect to the plain kernel: the MMA computes D^T, B's rows on its
 // M side (one TMEM lane each) and the M token rows of A on its N side (rounded up to 16; rows
 // past M are zero-filled by TMA).  No 128-row A tile is padded out of a handful of rows, and every
-// loaded byte of B feeds the tensor core once.  With so little math per byte, what bounds a CTA
-// is the MMA issue rate of its one issuing thread (about 100 cycles per tcgen05.mma whatever its
-// N, plus about 200 per k-block for the barrier wait and commit, measured with a clock64 trace),
-// so the kernel runs on CTA pairs (CG = 2): one tcgen05.mma.cta_group::2 with M = 256 covers 128
-// rows of B in each CTA of the pair, which halves the MMA instructions per loaded byte.  Each CTA
-// of a pair loads its own 128 rows of B and half of the token rows of A; the loads complete on
-// the leader's barrier and the leader's commits release the stages of both CTAs.  CG = 1 runs
-// single CTAs on 128-row tiles.
+// loaded byte of B feeds the tensor core once.  With so little math per byte, the MMA issue rate
+// of a CTA's one issuing thread is one of its limits (about 100 cycles per tcgen05.mma whatever
+// its N, plus about 200 per k-block for the barrier wait and the commit, measured with a clock64
+// trace); the CTA-pair form (CG = 2) halves the MMA instructions per loaded byte: one
+// tcgen05.mma.cta_group::2 with M = 256 covers 128 rows of B in each CTA of the pair, each CTA
+// loading its own 128 rows of B and half of the token rows of A, the loads completing on the
+// leader's barrier and the leader's commits releasing the stages of both CTAs.  Measured on
+// B200 it ran level with or slower than single CTAs (CG = 1, 128-row tiles), the default.
 //
 // A tile of B (128 CG rows) alone leaves most SMs idle (N = 8192 gives 32 pair tiles), so the K
 // range of a tile is split over S pairs (or CTAs) of one cluster (S = 1, 2 or 4; cluster dims
@@ -54,6 +54,7 @@ struct DecodeParams {
   int32_t splits;      // K ranges per cluster: 1, 2 or 4
   int32_t stages;
   int32_t spin;        // producer / MMA lanes poll their barriers instead of sleeping
+  int32_t rotate;      // start each tile's K range at a tile-dependent k-block (see below)
   float alpha;
   const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
   const float* scale_b;
@@ -144,6 +145,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   const int32_t kb0 = static_cast<int32_t>(kr) * p.kps;
   const int32_t kb1 = min(p.k_iters, kb0 + p.kps);
   const bool has_k = kb1 > kb0;
+  // All tiles stream the same k-block column of B at about the same time, and B's rows are K
+  // elements apart, so the bytes in flight would share their offset modulo the row length and
+  // crowd a few DRAM channels; starting each tile's walk over its K range at a different
+  // k-block (rotate: tile * 5 modulo the range) spreads them.  Producer and MMA walk the same
+  // order; the first k-block walked starts the accumulator.
+  const int32_t nkb = kb1 > kb0 ? kb1 - kb0 : 1;
+  const int32_t rot = p.rotate ? static_cast<int32_t>((blockIdx.y * 5u) % static_cast<uint32_t>(nkb)) : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -181,7 +189,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int32_t kb = kb0; kb < kb1; ++kb) {
+      for (int32_t i = 0; i < kb1 - kb0; ++i) {
+        const int32_t kb = kb0 + (i + rot) % nkb;
         const uint32_t eb = empty_bar + 8u * stage;
         const bool slot_free = p.spin ? ptx::mbar_wait_spin(eb, phase ^ 1u, ctx, kSiteProducerEmpty)
                                       : ptx::mbar_wait(eb, phase ^ 1u, ctx, kSiteProducerEmpty);
@@ -234,7 +243,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       uint32_t b_lo = b_lo0, a_lo = a_lo0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int32_t kb = kb0; kb < kb1; ++kb) {
+      for (int32_t i = 0; i < kb1 - kb0; ++i) {
         const uint32_t fb = full_bar + 8u * stage;
         const bool full = p.spin ? ptx::mbar_wait_spin(fb, phase, ctx, kSiteMmaFull)
                                  : ptx::mbar_wait(fb, phase, ctx, kSiteMmaFull);
@@ -244,7 +253,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 #pragma unroll
         for (int k = 0; k < kBK / kUmmaK; ++k)
           ptx::umma_ss_lohi<CG, OT::kFp8>(tmem_base, b_lo + 2u * k, a_lo + 2u * k, hi, idesc,
-                                          (kb > kb0 || k > 0) ? 1u : 0u);
+                                          (i > 0 || k > 0) ? 1u : 0u);
         if constexpr (CG == 1) {
           ptx::umma_commit<1>(empty_bar + 8u * stage);
         } else {

@@ -1,9 +1,9 @@
 """The small-M kernel (split_k = CPG_SPLIT_K_DECODE) on the GPU, through the public API / C ABI.
 
 BASELINE config 5 (decode-like M in {16, 64, 128} at N = K = 8192) and ragged shapes around it:
-a CTA pair computes D^T for 256 rows of B (one cta_group::2 MMA per k-step), the K range of a
-tile is split over a cluster of 1, 2 or 4 pairs and the partial sums are added in distributed
-shared memory.  Checked against the fp32 CPU
+a CTA computes D^T for 128 rows of B, the K range of a tile is split over a cluster of 1, 2 or 4
+CTAs (or CTA pairs, one cta_group::2 MMA per k-step for 256 rows) and the partial sums are added
+in distributed shared memory.  Checked against the fp32 CPU
 oracle with the tolerance of the other GPU tests (relative Frobenius <= 1e-2 for BF16 output,
 3e-2 for FP8 E4M3 operands, and the element-wise bound |D - R| <= 2^-8 |R| + K 2^-23 (|A| |B|^T)),
 for every cluster size the plan can pick, M not a multiple of 16, ragged N and K, FP32 output,
@@ -42,23 +42,23 @@ def run(m, n, k, seed, bias=True, alpha=1.0, out_dtype=torch.bfloat16):
 @pytest.mark.parametrize("m", [16, 64, 128])
 def test_baseline_small_m_configs(m):
     """BASELINE config 5 exactly: M x 8192 x 8192, N(0,1)/sqrt(K) entries, BF16 out with bias.
-    32 tiles of 256 rows of B, each on 2 CTA pairs (K split in two): a cluster of 4 CTAs."""
+    64 tiles of 128 rows of B, each on 2 CTAs (K split in two): a cluster of 2."""
     d, a, b, bb, plan = run(m, 8192, 8192, seed=m)
     res = gemm_ref.check(d, a, b, bias=bb)
     assert res["ok"], res
     info = plan.launch_info()
-    assert info["grid"][:2] == (4, 32) and info["cluster"][0] == 4
+    assert info["grid"][:2] == (2, 64) and info["cluster"][0] == 2
 
 
 @pytest.mark.parametrize("m,n,k,cluster,tiles", [
-    (1, 520, 4096 + 64, 8, 3),       # 3 tiles of 256 rows: 4 pairs per cluster
-    (17, 520, 128, 4, 3),            # 2 k-blocks: at most 2 pairs
-    (33, 128 * 3 + 8, 64, 2, 2),     # one k-block: one pair
-    (100, 16384, 1000 + 8, 2, 64),   # 64 tiles: no room for a second pair per tile
-    (128, 9472, 3000 + 40, 4, 37),   # 37 tiles x 2 pairs fill the 148 SMs
-    (5, 4096, 130 * 64, 8, 16),      # 16 tiles x 4 pairs
-    (64, 1000, 1000 + 8, 8, 4),      # ragged N: the last tile has 232 rows, its second CTA 104
-    (80, 2056, 640, 8, 9),           # 10 k-blocks over 4 pairs: 3, 3, 3, 1; last tile 8 rows
+    (1, 520, 4096 + 64, 4, 5),       # 5 tiles of 128 rows: 4 CTAs per cluster
+    (17, 520, 128, 2, 5),            # 2 k-blocks: at most 2 CTAs
+    (33, 128 * 3 + 8, 64, 1, 4),     # one k-block: no split
+    (100, 16384, 1000 + 8, 1, 128),  # 128 tiles: no room for a second CTA per tile
+    (128, 9472, 3000 + 40, 2, 74),   # 74 tiles x 2 CTAs fill the 148 SMs
+    (5, 4096, 130 * 64, 4, 32),      # 32 tiles x 4
+    (64, 1000, 1000 + 8, 4, 8),      # ragged N: the last tile has 104 rows
+    (80, 2056, 640, 4, 17),          # 10 k-blocks over 4 CTAs: 3, 3, 3, 1; last tile 8 rows
 ])
 def test_ragged_shapes_and_cluster_sizes(m, n, k, cluster, tiles):
     d, a, b, bb, plan = run(m, n, k, seed=m + n + k)
@@ -68,14 +68,20 @@ def test_ragged_shapes_and_cluster_sizes(m, n, k, cluster, tiles):
     assert info["cluster"][0] == cluster and info["grid"][1] == tiles
 
 
-@pytest.mark.parametrize("m,n,k,cluster", [(16, 8192, 8192, 2), (100, 1000, 2048, 4),
-                                           (128, 4096, 4096 + 64, 4)])
-def test_single_cta_variant(monkeypatch, m, n, k, cluster):
-    """The single-CTA variant (CPG_DECODE_PAIR=0: 128-row tiles, no CTA pairs) on the same checks."""
-    monkeypatch.setenv("CPG_DECODE_PAIR", "0")
+@pytest.mark.parametrize("m,n,k,env,cluster", [
+    (16, 8192, 8192, {"CPG_DECODE_PAIR": "1"}, 4),      # 32 pair tiles x 2 pairs
+    (100, 1000, 2048, {"CPG_DECODE_PAIR": "1"}, 8),     # 4 pair tiles x 4 pairs, ragged N
+    (128, 4096, 4096 + 64, {"CPG_DECODE_PAIR": "1", "CPG_DECODE_ROTATE": "0"}, 8),
+    (64, 2056, 640, {"CPG_DECODE_ROTATE": "0", "CPG_DECODE_SPIN": "0"}, 4),
+])
+def test_other_variants(monkeypatch, m, n, k, env, cluster):
+    """The CTA-pair form (256-row tiles, one cta_group::2 MMA per k-step for both CTAs of a pair),
+    every tile walking its K range from the start, and sleeping pipeline waits: the same checks."""
+    for key, value in env.items():
+        monkeypatch.setenv(key, value)
     d, a, b, bb, plan = run(m, n, k, seed=m + k)
     res = gemm_ref.check(d, a, b, bias=bb)
-    assert res["ok"], (m, n, k, res)
+    assert res["ok"], (m, n, k, env, res)
     assert plan.launch_info()["cluster"][0] == cluster
 
 

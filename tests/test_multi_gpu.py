@@ -71,6 +71,8 @@ WORKER = textwrap.dedent(r'''
         torch.cuda.synchronize()
         res4 = gemm_ref.check(rows_p.cpu(), a2[r0:r1], b2)
         ok &= res4["ok"] and rows_p.shape == (r1 - r0, n2)
+        if not res4["ok"]:
+            print(f"RANK {rank} peer call {it} failed: {res4}", flush=True)
     pk.check_status()
     m3, n3, k3 = 128 * (2 * world + 1) - 40, 1000, 6144
     a3, b3, bias3 = gemm_ref.make_inputs(m3, n3, k3, seed=7, b_scale=k3 ** -0.5, with_bias=True)
@@ -84,9 +86,14 @@ WORKER = textwrap.dedent(r'''
         q0, q1 = row_range(m3, world, rank)
         res5 = gemm_ref.check(rows3.cpu(), a3[q0:q1], b3, bias=bias3)
         ok &= res5["ok"] and rows3.shape == (q1 - q0, n3)
+        if not res5["ok"]:
+            print(f"RANK {rank} peer dynamic call {it} failed: {res5}", flush=True)
     pk3.check_status()
     pk.close()
     pk3.close()
+    checks = {"mshard": res["ok"], "splitk_nccl": res2["ok"], "splitk_chunked": res3["ok"],
+              "peer": res4["ok"], "peer_dynamic_bias": res5["ok"]}
+    print(f"RANK {rank} rows {r0}:{r1} ok={ok} {checks}", flush=True)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
@@ -124,7 +131,8 @@ def test_multi_gpu_mshard_and_splitk(tmp_path):
             p.kill()
             out, _ = p.communicate()
         outs.append((p.returncode, out))
-    assert all(rc == 0 for rc, _ in outs), outs
+    summary = [ln for _, out in outs for ln in out.splitlines() if ln.startswith("RANK")]
+    assert all(rc == 0 for rc, _ in outs), ([rc for rc, _ in outs], summary, outs[0][1][-3000:])
     assert "RESULT 1" in outs[0][1], outs[0][1]
 
 
