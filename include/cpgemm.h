@@ -302,7 +302,9 @@ int cpg_cast_f32_bf16(const float* x, int64_t rows, int64_t cols, int64_t ldx, v
  *     rejected with CPG_ERR_INVALID_SHAPE and a message naming the sizes.
  *   - It calls no cudaMalloc / cudaFree.  The first call on a device looks up the array's
  *     device address (cudaGetSymbolAddress, which also loads the module there); make that first
- *     call before any stream capture.
+ *     call before any stream capture.  The address is kept for the life of the process: a
+ *     cudaDeviceReset unloads the module on that device and would leave it stale, so do not call
+ *     this entry point on a device after resetting it.
  *   - Every call uses the same array and it keeps the last call's contents; the call clears the
  *     part it accumulates into.  Calls that overlap on the GPU (different streams, or different
  *     host threads) race on the array and must be serialised by the caller.
