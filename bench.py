@@ -309,16 +309,6 @@ def reduce_max(x, world):
     return float(t.item())
 
 
-def reduce_sum(x, world):
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
-
-
 def gather_floats(values, world):
     """Every rank's list of floats (same length on every rank), in rank order."""
     if world == 1:
