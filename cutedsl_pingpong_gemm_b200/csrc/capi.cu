@@ -530,9 +530,10 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   if (env_st != nullptr && std::atoi(env_st) >= 2 && std::atoi(env_st) < stages)
     stages = std::atoi(env_st);
   if (stages < 2) stages = 2;
-  // The receive buffer of the in-cluster reduction lives in the stages.
+  // The send and receive buffers of the in-cluster reduction live in the stages.
   while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, cg).stage_bytes <
-         cpg::decode_layout(stages, mma_n, splits, cg).recv_bytes)
+         cpg::decode_layout(stages, mma_n, splits, cg).send_off +
+             cpg::decode_layout(stages, mma_n, splits, cg).recv_bytes)
     ++stages;
   const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits, cg).bytes);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))

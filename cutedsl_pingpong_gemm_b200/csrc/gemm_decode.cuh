@@ -21,11 +21,13 @@
 // then reduced through distributed shared memory, in one launch and without any global
 // workspace: the 128 rows a CTA holds are dealt to the S CTAs holding the same rows in blocks
 // of 128 / S rows.  Once every CTA of the cluster has finished its MMAs and its loads (a cluster
-// barrier), the A/B stages are free and serve as receive buffers: the warps holding another
-// CTA's rows store them there (st.shared::cluster, 16-byte vectors, rows padded by 16 bytes so a
-// warp's stores hit distinct banks) and arrive on that CTA's receive barrier with cluster-scope
-// release; the owner adds the S - 1 received rows to its own, applies alpha, the FP8 scales and
-// the bias and writes its rows of D^T as columns of D (for each token row m, a warp writes 32
+// barrier), the A/B stages are free and serve as send and receive buffers: the warps holding
+// another CTA's rows stage them in a local send block laid out as the owner's receive slot (rows
+// padded by 16 bytes so a warp's 16-byte stores hit distinct banks), and one thread copies each
+// block to its owner with one bulk transfer (cp.async.bulk.shared::cluster) completing on the
+// owner's receive barrier (per-thread remote stores of the same bytes measured ~10 us at M = 128);
+// the owner adds the S - 1 received blocks to its own rows, applies alpha, the FP8 scales and the
+// bias and writes its rows of D^T as columns of D (for each token row m, a warp writes 32
 // consecutive elements).
 //
 // Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
@@ -68,13 +70,15 @@ struct DecodeParams {
 };
 
 // Shared-memory layout of one CTA (offsets from the 1024-byte aligned base), the same on host and
-// device.  The receive buffer of the reduction aliases the A/B stages (used only after every CTA
-// of the cluster has finished with them).
+// device.  The receive and send buffers of the reduction alias the A/B stages (used only after
+// every CTA of the cluster has finished with them); the stages must hold send_off + recv_bytes.
 struct DecodeLayout {
   uint32_t b_bytes;          // 128 rows of B x 128 bytes
   uint32_t stage_bytes;      // B rows + this CTA's mma_n / CG rows of A
   uint32_t recv_row_floats;  // mma_n + 4 (16 bytes of padding per row)
-  uint32_t recv_bytes;       // (S - 1) * 128 / S rows
+  uint32_t block_bytes;      // one owner's rows of one sender: 128 / S rows
+  uint32_t recv_bytes;       // (S - 1) blocks received, at offset 0 of the stages
+  uint32_t send_off;         // (S - 1) blocks staged for sending, after the received ones
   uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
   uint32_t slot_off;         // TMEM base address, abort flag
   uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
@@ -86,8 +90,9 @@ __host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int
   l.b_bytes = kDecodeTileN * kRowBytes;
   l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n / cta_group) * kRowBytes;
   l.recv_row_floats = static_cast<uint32_t>(mma_n) + 4u;
-  const uint32_t recv_rows = splits > 1 ? (splits - 1) * (kDecodeTileN / splits) : 0u;
-  l.recv_bytes = recv_rows * l.recv_row_floats * 4u;
+  l.block_bytes = static_cast<uint32_t>(kDecodeTileN / splits) * l.recv_row_floats * 4u;
+  l.recv_bytes = splits > 1 ? static_cast<uint32_t>(splits - 1) * l.block_bytes : 0u;
+  l.send_off = (l.recv_bytes + 127u) & ~127u;
   l.bar_off = static_cast<uint32_t>(stages) * l.stage_bytes;
   l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
   l.bytes = l.slot_off + 16u + 1024u;
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       ptx::mbar_init(empty_bar + 8u * s, 1);
     }
     ptx::mbar_init(tfull_bar, 1);
-    ptx::mbar_init(recv_bar, S > 1 ? (S - 1) * rows_per_owner : 1u);
+    ptx::mbar_init(recv_bar, 1);
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbarrier_init_cluster();
@@ -293,6 +298,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::tc_fence_after();
   }
   ptx::fence_proxy_async_shared();  // the stages' async-proxy use ends before generic stores
+  // The S - 1 blocks this CTA receives complete their bytes on recv_bar; arm it before any peer
+  // can send (the cluster barrier below orders this before every copy).
+  if (threadIdx.x == 0 && S > 1) ptx::mbar_arrive_expect_tx(recv_bar, lay.recv_bytes);
   if (clustered) ptx::cluster_sync();
   if (warp >= 2) {
     // ---------------------------------------------------------------- reduction + epilogue
@@ -302,12 +310,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     const uint32_t owner = (row - lane) / rows_per_owner;    // K range owning it (warp-uniform)
     const uint32_t t_row = tmem_base + ((quad * 32u) << 16);
     if (owner != kr) {
-      // Send this row's partial sums to the CTA of the owning K range holding the same rows.
-      const uint32_t dst_rank = owner * CG + q;
-      const uint32_t slot = kr < owner ? kr : kr - 1u;
+      // Stage this row's partial sums in this CTA's send block for its owner (the block's
+      // layout is the owner's receive slot: 128 / S rows of mma_n + 4 floats).
+      const uint32_t block = owner < kr ? owner : owner - 1u;
       const uint32_t local = row - owner * rows_per_owner;
-      const uint32_t dst = ptx::mapa_shared(
-          base + (slot * rows_per_owner + local) * lay.recv_row_floats * 4u, dst_rank);
+      const uint32_t dst = base + lay.send_off + block * lay.block_bytes +
+                           local * lay.recv_row_floats * 4u;
       const bool read_tmem = ok && has_k;
       for (int c = 0; c < chunks; ++c) {
         uint32_t v[16];
@@ -320,12 +328,29 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          ptx::st_shared_cluster_v4(dst + static_cast<uint32_t>(64 * c + 16 * j), v[4 * j],
-                                    v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          ptx::st_shared_v4(dst + static_cast<uint32_t>(64 * c + 16 * j), v[4 * j], v[4 * j + 1],
+                            v[4 * j + 2], v[4 * j + 3]);
       }
-      ptx::mbar_arrive_release_cluster(ptx::mapa_shared(recv_bar, dst_rank));
-    } else {
-      bool got = S == 1 || ptx::mbar_wait_acquire_cluster(recv_bar, 0u, ctx, kSiteDecodeRecv);
+      ptx::fence_proxy_async_shared();  // generic stores before the bulk copies read them
+    }
+    // All send blocks are staged: one thread copies each to its owner's receive slot in one
+    // bulk transfer, completing the bytes on the owner's receive barrier.
+    if (S > 1) {
+      ptx::named_barrier_sync(1, 4 * 32);
+      if (warp == 2 && lane == 0) {
+        for (uint32_t o = 0; o < static_cast<uint32_t>(S); ++o) {
+          if (o == kr) continue;
+          const uint32_t block = o < kr ? o : o - 1u;
+          const uint32_t slot = kr < o ? kr : kr - 1u;  // this CTA's slot at owner o
+          const uint32_t dst_rank = o * CG + q;
+          ptx::bulk_copy_to_cluster(ptx::mapa_shared(base + slot * lay.block_bytes, dst_rank),
+                                    base + lay.send_off + block * lay.block_bytes,
+                                    lay.block_bytes, ptx::mapa_shared(recv_bar, dst_rank));
+        }
+      }
+    }
+    if (owner == kr) {
+      bool got = S == 1 || ptx::mbar_wait(recv_bar, 0u, ctx, kSiteDecodeRecv);
       got = __all_sync(0xffffffffu, got) && ok;
       if (got) {
         const int32_t n = n0 + static_cast<int32_t>(row);

@@ -633,6 +633,21 @@ __device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint
                "r"(b), "r"(c), "r"(d)
                : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory into another CTA's of the cluster (addresses from mapa_shared), completing the bytes
+// on that CTA's barrier `cluster_bar`.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src,
+                                                     uint32_t bytes, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(src), "r"(bytes), "r"(cluster_bar)
+      : "memory");
+}
+// Named barrier `id` over `threads` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
