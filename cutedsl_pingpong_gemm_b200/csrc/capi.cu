@@ -68,13 +68,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D row-major matrix [rows, cols] with row stride `ld` elements, tiled into
-// box_rows x box_cols boxes with 128-byte swizzle.
-// 3-D tiled tensor map (columns, rows, batches) with a 128-byte swizzled box of box_rows x
-// box_cols x 1.  An unbatched operand has one batch; its batch stride is then any legal value.
+// 3-D tiled tensor map (columns, rows, batches) with a box of box_rows x box_cols x 1, 128-byte
+// swizzled unless told otherwise.  An unbatched operand has one batch; its batch stride is then
+// any legal value.
 int encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* ptr,
                  int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols,
-                 int64_t batches = 1, int64_t batch_stride = 0) {
+                 int64_t batches = 1, int64_t batch_stride = 0,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(CPG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   if (batches < 1) batches = 1;
@@ -90,7 +90,7 @@ int encode_tiled(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const v
   cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return fail(CPG_ERR_CUDA,
@@ -453,7 +453,8 @@ static int alloc_fixup_workspace(cpg_gemm* g, int64_t tiles) {
   return rc;
 }
 
-using DecodeFn = void (*)(const CUtensorMap, const CUtensorMap, const cpg::DecodeParams);
+using DecodeFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const cpg::DecodeParams);
 
 static const void* decode_kernel(int dtype_ab, int dtype_d, int cta_group) {
   const bool fp8 = dtype_ab == CPG_DTYPE_E4M3, f32 = dtype_d == CPG_DTYPE_F32;
@@ -530,10 +531,10 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   if (env_st != nullptr && std::atoi(env_st) >= 2 && std::atoi(env_st) < stages)
     stages = std::atoi(env_st);
   if (stages < 2) stages = 2;
-  // The send and receive buffers of the in-cluster reduction live in the stages.
+  // The send, receive and output staging buffers of the epilogue live in the stages.
+  const int out_bytes = elem_bytes(prob->dtype_d);
   while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, cg).stage_bytes <
-         cpg::decode_layout(stages, mma_n, splits, cg).send_off +
-             cpg::decode_layout(stages, mma_n, splits, cg).recv_bytes)
+         cpg::decode_layout(stages, mma_n, splits, cg).epi_bytes(out_bytes))
     ++stages;
   const int smem = static_cast<int>(cpg::decode_layout(stages, mma_n, splits, cg).bytes);
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
@@ -615,7 +616,8 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
     return fail(CPG_ERR_UNSUPPORTED, "the small-M kernel has no activation and no C source");
   const int eab = elem_bytes(pr.dtype_ab);
   const int bk = cpg::kRowBytes / eab;
-  if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b) {
+  const int ed = elem_bytes(pr.dtype_d);
+  if (!g->maps_valid || g->map_a_ptr != a || g->map_b_ptr != b || g->map_d_ptr != d) {
     // Each CTA loads its 128 rows of B and (pairs) half of the token rows of A.
     int rc = encode_tiled(&g->tm_a, tma_dtype(pr.dtype_ab), eab, a, pr.m, pr.k, pr.lda,
                           g->dec_mma_n / g->dec_cg, bk);
@@ -623,9 +625,14 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
     rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
                       cpg::kDecodeTileN, bk);
     if (rc != CPG_OK) return rc;
+    // D is written by each owning warp as one box of its 32 columns (rows of D^T) x mma_n rows,
+    // staged unswizzled in shared memory; rows past M and columns past N are clipped.
+    rc = encode_tiled(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, g->dec_mma_n,
+                      32, 1, 0, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
-    g->map_d_ptr = nullptr;
+    g->map_d_ptr = d;
     g->maps_valid = true;
   }
   cpg::DecodeParams p;
@@ -665,7 +672,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  void* args[] = {&g->tm_a, &g->tm_b, &p};
+  void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p};
   cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, args);
   return e == cudaSuccess ? CPG_OK : cuda_fail(e, "small-M kernel launch");
 }

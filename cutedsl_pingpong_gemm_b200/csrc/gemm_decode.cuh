@@ -27,8 +27,9 @@
 // block to its owner with one bulk transfer (cp.async.bulk.shared::cluster) completing on the
 // owner's receive barrier (per-thread remote stores of the same bytes measured ~10 us at M = 128);
 // the owner adds the S - 1 received blocks to its own rows, applies alpha, the FP8 scales and the
-// bias and writes its rows of D^T as columns of D (for each token row m, a warp writes 32
-// consecutive elements).
+// bias, stages its rows of D^T as a box of D (token rows x 32 columns per warp) in the freed
+// stages and writes it with one TMA store (128 two-byte global stores per thread measured ~6 us
+// at M = 128).
 //
 // Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
 // MMA issuer (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4).  Every
@@ -70,8 +71,9 @@ struct DecodeParams {
 };
 
 // Shared-memory layout of one CTA (offsets from the 1024-byte aligned base), the same on host and
-// device.  The receive and send buffers of the reduction alias the A/B stages (used only after
-// every CTA of the cluster has finished with them); the stages must hold send_off + recv_bytes.
+// device.  The receive and send buffers of the reduction and the staging of D alias the A/B
+// stages (used only after every CTA of the cluster has finished with them); the stages must hold
+// epi_bytes().
 struct DecodeLayout {
   uint32_t b_bytes;          // 128 rows of B x 128 bytes
   uint32_t stage_bytes;      // B rows + this CTA's mma_n / CG rows of A
@@ -79,9 +81,18 @@ struct DecodeLayout {
   uint32_t block_bytes;      // one owner's rows of one sender: 128 / S rows
   uint32_t recv_bytes;       // (S - 1) blocks received, at offset 0 of the stages
   uint32_t send_off;         // (S - 1) blocks staged for sending, after the received ones
+  uint32_t out_off;          // D staging of the 4 epilogue warps, after the send blocks
   uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
   uint32_t slot_off;         // TMEM base address, abort flag
   uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
+  // One warp's box of D: mma_n token rows x 32 columns, unswizzled.
+  __host__ __device__ uint32_t out_box_bytes(int out_elem_bytes) const {
+    return (recv_row_floats - 4u) * 32u * static_cast<uint32_t>(out_elem_bytes);
+  }
+  // Bytes of the stages the epilogue uses (received, send and D staging buffers).
+  __host__ __device__ uint32_t epi_bytes(int out_elem_bytes) const {
+    return out_off + 4u * out_box_bytes(out_elem_bytes);
+  }
 };
 
 __host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int splits,
@@ -93,6 +104,7 @@ __host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int
   l.block_bytes = static_cast<uint32_t>(kDecodeTileN / splits) * l.recv_row_floats * 4u;
   l.recv_bytes = splits > 1 ? static_cast<uint32_t>(splits - 1) * l.block_bytes : 0u;
   l.send_off = (l.recv_bytes + 127u) & ~127u;
+  l.out_off = (l.send_off + l.recv_bytes + 127u) & ~127u;
   l.bar_off = static_cast<uint32_t>(stages) * l.stage_bytes;
   l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
   l.bytes = l.slot_off + 16u + 1024u;
@@ -113,7 +125,8 @@ __device__ __forceinline__ float to_out<float>(float x) {
 template <typename AB, typename OutT, int CG>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tm_a,
-                       const __grid_constant__ CUtensorMap tm_b, const DecodeParams p) {
+                       const __grid_constant__ CUtensorMap tm_b,
+                       const __grid_constant__ CUtensorMap tm_d, const DecodeParams p) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using OT = OperandTraits<AB>;
   constexpr int kBK = OT::kBK;
@@ -173,6 +186,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&tm_a);
     ptx::prefetch_tensormap(&tm_b);
+    ptx::prefetch_tensormap(&tm_d);
   }
   if (warp == 1) {
     ptx::tmem_alloc<CG>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)),
@@ -357,22 +371,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         float scale = p.alpha;
         if (p.scale_a != nullptr) scale *= *p.scale_a;
         if (p.scale_b != nullptr) scale *= *p.scale_b;
-        const bool n_ok = n < p.n;
-        const float bias = (p.bias != nullptr && n_ok) ? __bfloat162float(p.bias[n]) : 0.f;
+        const float bias = (p.bias != nullptr && n < p.n) ? __bfloat162float(p.bias[n]) : 0.f;
         const uint32_t local = row - kr * rows_per_owner;
-        OutT* d = static_cast<OutT*>(p.d);
-        for (int c = 0; c < chunks; ++c) {
-          uint32_t v[16];
-          if (has_k) {
-            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
-            ptx::tmem_ld_wait();
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0u;
-          }
+        // This warp's box of D (mma_n token rows x its 32 columns, unswizzled): lane l holds
+        // column l of every row, so each row of the box is one conflict-free warp store; one
+        // TMA store writes the box (rows past M and columns past N clipped).
+        const uint32_t box_off = lay.out_off + quad * lay.out_box_bytes(sizeof(OutT));
+        OutT* box = reinterpret_cast<OutT*>(base_ptr + box_off);
+        auto finish_chunk = [&](int c, const uint32_t (&v)[16]) {
           float acc[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(v[j]);
+          for (int j = 0; j < 16; ++j) acc[j] = has_k ? __uint_as_float(v[j]) : 0.f;
           for (int src = 0; src < S - 1; ++src) {
             const uint32_t r_addr = base + ((static_cast<uint32_t>(src) * rows_per_owner + local) *
                                                 lay.recv_row_floats +
@@ -387,15 +396,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
               acc[4 * j + 3] += __uint_as_float(w.w);
             }
           }
-          if (n_ok) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int32_t m = 16 * c + j;
-              if (m < p.m)
-                d[static_cast<int64_t>(m) * p.ldd + n] = to_out<OutT>(acc[j] * scale + bias);
-            }
+          for (int j = 0; j < 16; ++j)
+            box[(16 * c + j) * 32 + static_cast<int>(lane)] = to_out<OutT>(acc[j] * scale + bias);
+        };
+        // Two TMEM loads in flight per wait.
+        for (int c = 0; c < chunks; c += 2) {
+          uint32_t v0[16], v1[16];
+          const bool two = c + 1 < chunks;
+          if (has_k) {
+            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v0);
+            if (two) ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * (c + 1)), v1);
+            ptx::tmem_ld_wait();
           }
+          finish_chunk(c, v0);
+          if (two) finish_chunk(c + 1, v1);
         }
+        ptx::fence_proxy_async_shared();  // the box's generic stores before the TMA store
+        __syncwarp();
+        const int32_t col0 = n0 + static_cast<int32_t>(quad * 32u);
+        if (lane == 0 && col0 < p.n) {
+          ptx::tma_store_3d(&tm_d, base + box_off, col0, 0, 0);
+          ptx::bulk_commit_group();
+          ptx::bulk_wait_group<0>();  // the box is read and written before the CTA exits
+        }
+        __syncwarp();
       }
     }
   }
