@@ -363,6 +363,7 @@ struct cpg_gemm {
   // Small-M plan (CPG_SPLIT_K_DECODE): gemm_decode_kernel with these launch constants.
   int32_t decode;
   int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_cg, dec_spin, dec_rotate;
+  int32_t dec_pdl;  // launched as a programmatic dependent of the stream's previous kernel
 };
 
 extern "C" {
@@ -531,7 +532,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   if (env_st != nullptr && std::atoi(env_st) >= 2 && std::atoi(env_st) < stages)
     stages = std::atoi(env_st);
   if (stages < 2) stages = 2;
-  // The send, receive and output staging buffers of the epilogue live in the stages.
+  // The send blocks and the D boxes of the epilogue live in the stages.
   const int out_bytes = elem_bytes(prob->dtype_d);
   while (static_cast<int64_t>(stages) * cpg::decode_layout(stages, mma_n, splits, cg).stage_bytes <
          cpg::decode_layout(stages, mma_n, splits, cg).epi_bytes(out_bytes))
@@ -566,7 +567,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->prob = *prob;
   g->device = device;
   g->v = Variant{cpg::kDecodeTileN * cg, cg, prob->dtype_ab, prob->dtype_d, CPG_SCALE_TENSOR, fn,
-                 nullptr, cpg::kDecodeThreads, cpg::kEpiWarps};
+                 nullptr, cpg::kDecodeThreads, cpg::kDecodeEpiWarps};
   g->smem_bytes = smem;
   g->max_active_clusters = mac;
   g->timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;
@@ -598,6 +599,8 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_spin = env_spin != nullptr ? (std::atoi(env_spin) != 0) : 1;
   const char* env_rot = std::getenv("CPG_DECODE_ROTATE");
   g->dec_rotate = env_rot != nullptr ? (std::atoi(env_rot) != 0) : 1;
+  const char* env_pdl = std::getenv("CPG_DECODE_PDL");
+  g->dec_pdl = env_pdl != nullptr ? (std::atoi(env_pdl) != 0) : 1;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
@@ -625,10 +628,10 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
     rc = encode_tiled(&g->tm_b, tma_dtype(pr.dtype_ab), eab, b, pr.n, pr.k, pr.ldb,
                       cpg::kDecodeTileN, bk);
     if (rc != CPG_OK) return rc;
-    // D is written by each owning warp as one box of its 32 columns (rows of D^T) x mma_n rows,
-    // staged unswizzled in shared memory; rows past M and columns past N are clipped.
-    rc = encode_tiled(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, g->dec_mma_n,
-                      32, 1, 0, CU_TENSOR_MAP_SWIZZLE_NONE);
+    // D is written in boxes of 16 token rows x 32 columns (rows of D^T of one TMEM lane
+    // quadrant), staged unswizzled in shared memory; rows past M and columns past N are clipped.
+    rc = encode_tiled(&g->tm_d, tma_dtype(pr.dtype_d), ed, d, pr.m, pr.n, pr.ldd, 16, 32, 1, 0,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc != CPG_OK) return rc;
     g->map_a_ptr = a;
     g->map_b_ptr = b;
@@ -647,6 +650,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.splits = g->dec_splits;
   p.spin = g->dec_spin;
   p.rotate = g->dec_rotate;
+  p.pdl = g->dec_pdl;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
   p.scale_a = epi != nullptr ? epi->scale_a : nullptr;
@@ -659,18 +663,27 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.l2_policy_a = g->l2_policy_a;
   p.l2_policy_b = g->l2_policy_b;
   cudaLaunchConfig_t lc = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   lc.gridDim = dim3(g->grid[0], g->grid[1], 1);
   lc.blockDim = dim3(cpg::kDecodeThreads, 1, 1);
   lc.dynamicSmemBytes = g->smem_bytes;
   lc.stream = st;
+  lc.attrs = attr;
+  lc.numAttrs = 0;
   if (g->dec_splits * g->dec_cg > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = g->dec_splits * g->dec_cg;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
+    attr[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[lc.numAttrs].val.clusterDim.x = g->dec_splits * g->dec_cg;
+    attr[lc.numAttrs].val.clusterDim.y = 1;
+    attr[lc.numAttrs].val.clusterDim.z = 1;
+    ++lc.numAttrs;
+  }
+  if (g->dec_pdl) {
+    // The kernel may start while the stream's previous kernel finishes: it sets up (barriers,
+    // TMEM, an L2 prefetch of its first tiles of B) and then waits for that kernel to complete
+    // before it touches any other global memory.
+    attr[lc.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[lc.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++lc.numAttrs;
   }
   void* args[] = {&g->tm_a, &g->tm_b, &g->tm_d, &p};
   cudaError_t e = cudaLaunchKernelExC(&lc, g->v.fn, args);

@@ -20,28 +20,30 @@
 // (CG S, ceil(N / (128 CG)))).  Each pair accumulates its K range in TMEM; the partial sums are
 // then reduced through distributed shared memory, in one launch and without any global
 // workspace: the 128 rows a CTA holds are dealt to the S CTAs holding the same rows in blocks
-// of 128 / S rows.  Once every CTA of the cluster has finished its MMAs and its loads (a cluster
-// barrier), the A/B stages are free and serve as send and receive buffers: the warps holding
-// another CTA's rows stage them in a local send block laid out as the owner's receive slot (rows
-// padded by 16 bytes so a warp's 16-byte stores hit distinct banks), and one thread copies each
-// block to its owner with one bulk transfer (cp.async.bulk.shared::cluster) completing on the
-// owner's receive barrier (per-thread remote stores of the same bytes measured ~10 us at M = 128);
-// the owner adds the S - 1 received blocks to its own rows, applies alpha, the FP8 scales and the
-// bias, stages its rows of D^T as a box of D (token rows x 32 columns per warp) in the freed
-// stages and writes it with one TMA store (128 two-byte global stores per thread measured ~6 us
-// at M = 128).
+// of 128 / S rows.  Each CTA's receive slots have shared memory of their own, armed at start-up,
+// so a CTA sends as soon as its own accumulators are complete: its warps holding another CTA's
+// rows stage them in a send block (in its now free A/B stages) laid out as the owner's receive
+// slot (rows padded by 16 bytes so a warp's 16-byte stores hit distinct banks), and one lane per
+// 32 rows copies them to the owner with one bulk transfer (cp.async.bulk.shared::cluster)
+// completing on the owner's receive barrier (per-thread remote stores of the same bytes measured
+// ~10 us at M = 128).  The owner adds the S - 1 received blocks to its own rows, applies alpha,
+// the FP8 scales and the bias, stages its rows of D^T as boxes of D (16 token rows x 32 columns)
+// in its stages and writes each with one TMA store (128 two-byte global stores per thread
+// measured ~6 us at M = 128).
 //
-// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
-// MMA issuer (one lane), warps 2-5 the epilogue (warp w reads TMEM lane quadrant w mod 4).  Every
-// wait is bounded (WaitCtx): on a timeout the status word records the site; in-flight TMA loads
-// and MMAs are drained before the stages are reused or TMEM is freed, and the final cluster
-// barrier keeps every CTA resident until no peer can still write into its shared memory.
+// Roles (320 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
+// MMA issuer (one lane), warps 2-9 the epilogue (warp w reads TMEM lane quadrant w mod 4, warps
+// w and w + 4 splitting its columns).  Every wait is bounded (WaitCtx): on a timeout the status
+// word records the site; in-flight TMA loads and MMAs are drained before the stages are reused
+// or TMEM is freed, and the final cluster barrier keeps every CTA resident until every bulk copy
+// into or out of its shared memory has completed.
 #pragma once
 #include "gemm_kernel.cuh"
 
 namespace cpg {
 
-constexpr int kDecodeThreads = 192;
+constexpr int kDecodeThreads = 320;
+constexpr int kDecodeEpiWarps = 8;   // two per TMEM lane quadrant, each with half the columns
 constexpr int kDecodeMaxM = 128;      // MMA N: the token rows of one launch
 constexpr int kDecodeTileN = 128;     // rows of B per CTA (the MMA's M per CTA, one TMEM lane each)
 constexpr int kDecodeMaxSplits = 4;   // K ranges per cluster (owners of at least 32 rows each)
@@ -58,6 +60,7 @@ struct DecodeParams {
   int32_t stages;
   int32_t spin;        // producer / MMA lanes poll their barriers instead of sleeping
   int32_t rotate;      // start each tile's K range at a tile-dependent k-block (see below)
+  int32_t pdl;         // launched as a programmatic dependent: set up, then wait (see below)
   float alpha;
   const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
   const float* scale_b;
@@ -71,25 +74,26 @@ struct DecodeParams {
 };
 
 // Shared-memory layout of one CTA (offsets from the 1024-byte aligned base), the same on host and
-// device.  The receive and send buffers of the reduction and the staging of D alias the A/B
-// stages (used only after every CTA of the cluster has finished with them); the stages must hold
-// epi_bytes().
+// device.  The send blocks of the reduction and the staging of D alias the A/B stages (used once
+// this CTA's own loads and MMAs are done); the stages must hold epi_bytes().  The receive slots
+// have memory of their own after the stages, so a peer may send while this CTA still computes.
 struct DecodeLayout {
   uint32_t b_bytes;          // 128 rows of B x 128 bytes
   uint32_t stage_bytes;      // B rows + this CTA's mma_n / CG rows of A
-  uint32_t recv_row_floats;  // mma_n + 4 (16 bytes of padding per row)
+  uint32_t row_floats;       // mma_n + 4 (16 bytes of padding per row)
   uint32_t block_bytes;      // one owner's rows of one sender: 128 / S rows
-  uint32_t recv_bytes;       // (S - 1) blocks received, at offset 0 of the stages
-  uint32_t send_off;         // (S - 1) blocks staged for sending, after the received ones
-  uint32_t out_off;          // D staging of the 4 epilogue warps, after the send blocks
+  uint32_t recv_bytes;       // (S - 1) blocks sent, and as many received
+  uint32_t send_off;         // send blocks, at offset 0 of the stages
+  uint32_t out_off;          // D boxes of the 4 TMEM lane quadrants, after the send blocks
+  uint32_t recv_off;         // receive slots, after the stages
   uint32_t bar_off;          // full[stages], empty[stages], tmem_full, recv, drain
   uint32_t slot_off;         // TMEM base address, abort flag
   uint32_t bytes;            // dynamic shared memory to request (with the alignment slack)
-  // One warp's box of D: mma_n token rows x 32 columns, unswizzled.
+  // One lane quadrant's box of D: mma_n token rows x 32 columns, unswizzled.
   __host__ __device__ uint32_t out_box_bytes(int out_elem_bytes) const {
-    return (recv_row_floats - 4u) * 32u * static_cast<uint32_t>(out_elem_bytes);
+    return (row_floats - 4u) * 32u * static_cast<uint32_t>(out_elem_bytes);
   }
-  // Bytes of the stages the epilogue uses (received, send and D staging buffers).
+  // Bytes of the stages the epilogue uses (send blocks and D boxes).
   __host__ __device__ uint32_t epi_bytes(int out_elem_bytes) const {
     return out_off + 4u * out_box_bytes(out_elem_bytes);
   }
@@ -100,12 +104,13 @@ __host__ __device__ inline DecodeLayout decode_layout(int stages, int mma_n, int
   DecodeLayout l;
   l.b_bytes = kDecodeTileN * kRowBytes;
   l.stage_bytes = l.b_bytes + static_cast<uint32_t>(mma_n / cta_group) * kRowBytes;
-  l.recv_row_floats = static_cast<uint32_t>(mma_n) + 4u;
-  l.block_bytes = static_cast<uint32_t>(kDecodeTileN / splits) * l.recv_row_floats * 4u;
+  l.row_floats = static_cast<uint32_t>(mma_n) + 4u;
+  l.block_bytes = static_cast<uint32_t>(kDecodeTileN / splits) * l.row_floats * 4u;
   l.recv_bytes = splits > 1 ? static_cast<uint32_t>(splits - 1) * l.block_bytes : 0u;
-  l.send_off = (l.recv_bytes + 127u) & ~127u;
-  l.out_off = (l.send_off + l.recv_bytes + 127u) & ~127u;
-  l.bar_off = static_cast<uint32_t>(stages) * l.stage_bytes;
+  l.send_off = 0u;
+  l.out_off = (l.recv_bytes + 127u) & ~127u;
+  l.recv_off = static_cast<uint32_t>(stages) * l.stage_bytes;
+  l.bar_off = l.recv_off + ((l.recv_bytes + 127u) & ~127u);
   l.slot_off = l.bar_off + (2u * stages + 3u) * 8u;
   l.bytes = l.slot_off + 16u + 1024u;
   return l;
@@ -179,19 +184,57 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::mbar_init(tfull_bar, 1);
     ptx::mbar_init(recv_bar, 1);
     ptx::mbar_init(drain_bar, 1);
+    // The S - 1 blocks this CTA receives complete their bytes on recv_bar (armed before the
+    // start-up cluster barrier, which every peer passes before it can send).
+    if (S > 1) ptx::mbar_arrive_expect_tx(recv_bar, lay.recv_bytes);
     *abort_flag = 0;
     ptx::fence_mbarrier_init_cluster();
     ptx::fence_proxy_async_shared();
   }
+  // Programmatic dependent launch (pdl): the next kernel on the stream may be scheduled as soon as
+  // every CTA of this one has started; this kernel in turn sets up (barriers, TMEM, the tensor
+  // maps and an L2 prefetch of its first tiles of B, the weight) while the previous kernel
+  // finishes, and waits for it to complete before any other global access (A, bias, scales, D,
+  // the status word).  Without a programmatic dependency the wait returns at once.
+  if (p.pdl) ptx::griddep_launch_dependents();
+  const int32_t n_early = min(stages, kb1 - kb0);
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&tm_a);
     ptx::prefetch_tensormap(&tm_b);
     ptx::prefetch_tensormap(&tm_d);
+    if (p.pdl)
+      for (int32_t i = 0; i < n_early; ++i)
+        ptx::tma_prefetch_l2_3d(&tm_b, (kb0 + (i + rot) % nkb) * kBK, n0, 0);
   }
   if (warp == 1) {
     ptx::tmem_alloc<CG>(ptx::smem_u32(const_cast<uint32_t*>(tmem_slot)),
                         static_cast<uint32_t>(p.tmem_cols));
     ptx::tmem_relinquish<CG>();
+  }
+  ptx::griddep_wait();
+  // Producer state (thread 0 = warp 0, lane 0).  A single CTA's loads complete on its own
+  // barriers, which thread 0 has initialised: it fills the first `stages` stages (free by
+  // construction) before the start-up barriers, whose latency then overlaps the first loads'
+  // DRAM latency.  A pair's loads complete on the leader's barrier and wait for the cluster
+  // barrier below.
+  int p_stage = 0;
+  uint32_t p_phase = 0;
+  int32_t issued = 0;
+  const uint64_t pol_a = l2_policy(p.l2_policy_a);
+  const uint64_t pol_b = l2_policy(p.l2_policy_b);
+  if constexpr (CG == 1) {
+    if (threadIdx.x == 0) {
+      for (; issued < n_early; ++issued) {
+        const int32_t kb = kb0 + (issued + rot) % nkb;
+        const uint32_t fb = full_bar + 8u * issued;
+        const uint32_t sb = base + static_cast<uint32_t>(issued) * lay.stage_bytes;
+        ptx::mbar_arrive_expect_tx(fb, lay.stage_bytes);
+        ptx::tma_load_3d(&tm_b, sb, fb, kb * kBK, n0, 0, pol_b);
+        ptx::tma_load_3d(&tm_a, sb + lay.b_bytes, fb, kb * kBK, a_row0, 0, pol_a);
+      }
+      p_stage = issued == stages ? 0 : issued;
+      p_phase = issued == stages ? 1u : 0u;
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -203,12 +246,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = l2_policy(p.l2_policy_a);
-      const uint64_t pol_b = l2_policy(p.l2_policy_b);
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      for (int32_t i = 0; i < kb1 - kb0; ++i) {
+      int stage = p_stage;
+      uint32_t phase = p_phase;
+      for (int32_t i = issued; i < kb1 - kb0; ++i) {
         const int32_t kb = kb0 + (i + rot) % nkb;
         const uint32_t eb = empty_bar + 8u * stage;
         const bool slot_free = p.spin ? ptx::mbar_wait_spin(eb, phase ^ 1u, ctx, kSiteProducerEmpty)
@@ -302,9 +342,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     }
     __syncwarp();
   }
-  // Every CTA of the cluster has drained its loads and MMAs (warps 0 and 1 above) and its
-  // epilogue warps have seen the accumulators complete: the stages of all of them are free to
-  // receive partial sums.
+  // ---------------------------------------------------------------- reduction + epilogue
+  // The epilogue warps wait for the accumulators; warps 0 and 1 reach the barrier below after
+  // draining their loads and MMAs, so past it this CTA's stages are free for the send blocks and
+  // the D boxes.  The receive slots have memory of their own, armed at start-up: a peer sends as
+  // soon as its own accumulators are complete, with no cluster-wide barrier in between.
   bool ok = true;
   if (warp >= 2) {
     ok = ptx::mbar_wait(tfull_bar, 0u, ctx, kSiteEpiTmemFull);
@@ -312,58 +354,61 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::tc_fence_after();
   }
   ptx::fence_proxy_async_shared();  // the stages' async-proxy use ends before generic stores
-  // The S - 1 blocks this CTA receives complete their bytes on recv_bar; arm it before any peer
-  // can send (the cluster barrier below orders this before every copy).
-  if (threadIdx.x == 0 && S > 1) ptx::mbar_arrive_expect_tx(recv_bar, lay.recv_bytes);
-  if (clustered) ptx::cluster_sync();
+  __syncthreads();
   if (warp >= 2) {
-    // ---------------------------------------------------------------- reduction + epilogue
+    // Warp w reads TMEM lane quadrant w mod 4 (rows 32 quad .. 32 quad + 31 of this CTA's tile)
+    // and the 16-column chunks c = half + 2 j of the accumulator (token rows 16 c .. 16 c + 15).
     const uint32_t quad = warp & 3u;
+    const uint32_t half = (warp - 2u) >> 2;
     const int chunks = p.mma_n / 16;
-    const uint32_t row = quad * 32u + lane;                  // TMEM lane = row of this CTA's block
-    const uint32_t owner = (row - lane) / rows_per_owner;    // K range owning it (warp-uniform)
+    const uint32_t row = quad * 32u + lane;
+    const uint32_t owner = (quad * 32u) / rows_per_owner;  // K range owning these rows
+    const uint32_t local = row - owner * rows_per_owner;  // row within the owner's block
     const uint32_t t_row = tmem_base + ((quad * 32u) << 16);
+    const bool read_tmem = ok && has_k;
+    uint32_t v[4][16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = static_cast<int>(half) + 2 * j;
+      if (read_tmem && c < chunks) ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v[j]);
+    }
+    if (read_tmem) {
+      ptx::tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[j][i] = 0u;
+    }
     if (owner != kr) {
-      // Stage this row's partial sums in this CTA's send block for its owner (the block's
-      // layout is the owner's receive slot: 128 / S rows of mma_n + 4 floats).
+      // Stage these rows' partial sums in the send block for their owner (laid out as the
+      // owner's receive slot: 128 / S rows of mma_n + 4 floats); once both warps of the quadrant
+      // are done, one lane copies its 32 rows to the owner in one bulk transfer, completing the
+      // bytes on the owner's receive barrier.
       const uint32_t block = owner < kr ? owner : owner - 1u;
-      const uint32_t local = row - owner * rows_per_owner;
-      const uint32_t dst = base + lay.send_off + block * lay.block_bytes +
-                           local * lay.recv_row_floats * 4u;
-      const bool read_tmem = ok && has_k;
-      for (int c = 0; c < chunks; ++c) {
-        uint32_t v[16];
-        if (read_tmem) {
-          ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v);
-          ptx::tmem_ld_wait();
-        } else {
+      const uint32_t q_off = (quad * 32u - owner * rows_per_owner) * lay.row_floats * 4u;
+      const uint32_t src = base + lay.send_off + block * lay.block_bytes + q_off;
+      const uint32_t dst = src + lane * lay.row_floats * 4u;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0u;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const int c = static_cast<int>(half) + 2 * j;
+        if (c < chunks) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          ptx::st_shared_v4(dst + static_cast<uint32_t>(64 * c + 16 * j), v[4 * j], v[4 * j + 1],
-                            v[4 * j + 2], v[4 * j + 3]);
-      }
-      ptx::fence_proxy_async_shared();  // generic stores before the bulk copies read them
-    }
-    // All send blocks are staged: one thread copies each to its owner's receive slot in one
-    // bulk transfer, completing the bytes on the owner's receive barrier.
-    if (S > 1) {
-      ptx::named_barrier_sync(1, 4 * 32);
-      if (warp == 2 && lane == 0) {
-        for (uint32_t o = 0; o < static_cast<uint32_t>(S); ++o) {
-          if (o == kr) continue;
-          const uint32_t block = o < kr ? o : o - 1u;
-          const uint32_t slot = kr < o ? kr : kr - 1u;  // this CTA's slot at owner o
-          const uint32_t dst_rank = o * CG + q;
-          ptx::bulk_copy_to_cluster(ptx::mapa_shared(base + slot * lay.block_bytes, dst_rank),
-                                    base + lay.send_off + block * lay.block_bytes,
-                                    lay.block_bytes, ptx::mapa_shared(recv_bar, dst_rank));
+          for (int i = 0; i < 4; ++i)
+            ptx::st_shared_v4(dst + static_cast<uint32_t>(64 * c + 16 * i), v[j][4 * i],
+                              v[j][4 * i + 1], v[j][4 * i + 2], v[j][4 * i + 3]);
         }
       }
-    }
-    if (owner == kr) {
+      ptx::fence_proxy_async_shared();  // generic stores before the bulk copy reads them
+      ptx::named_barrier_sync(1u + quad, 64u);
+      if (half == 0u && lane == 0u) {
+        const uint32_t slot = kr < owner ? kr : kr - 1u;  // this CTA's slot at the owner
+        const uint32_t dst_rank = owner * CG + q;
+        ptx::bulk_copy_to_cluster(
+            ptx::mapa_shared(base + lay.recv_off + slot * lay.block_bytes + q_off, dst_rank), src,
+            32u * lay.row_floats * 4u, ptx::mapa_shared(recv_bar, dst_rank));
+      }
+    } else {
       bool got = S == 1 || ptx::mbar_wait(recv_bar, 0u, ctx, kSiteDecodeRecv);
       got = __all_sync(0xffffffffu, got) && ok;
       if (got) {
@@ -372,53 +417,51 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         if (p.scale_a != nullptr) scale *= *p.scale_a;
         if (p.scale_b != nullptr) scale *= *p.scale_b;
         const float bias = (p.bias != nullptr && n < p.n) ? __bfloat162float(p.bias[n]) : 0.f;
-        const uint32_t local = row - kr * rows_per_owner;
-        // This warp's box of D (mma_n token rows x its 32 columns, unswizzled): lane l holds
-        // column l of every row, so each row of the box is one conflict-free warp store; one
-        // TMA store writes the box (rows past M and columns past N clipped).
+        // The quadrant's box of D (mma_n token rows x its 32 columns, unswizzled): lane l holds
+        // column l of every row, so each row of the box is one conflict-free warp store; each
+        // chunk of 16 rows is written by one TMA store (rows past M, columns past N clipped).
         const uint32_t box_off = lay.out_off + quad * lay.out_box_bytes(sizeof(OutT));
         OutT* box = reinterpret_cast<OutT*>(base_ptr + box_off);
-        auto finish_chunk = [&](int c, const uint32_t (&v)[16]) {
-          float acc[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = has_k ? __uint_as_float(v[j]) : 0.f;
-          for (int src = 0; src < S - 1; ++src) {
-            const uint32_t r_addr = base + ((static_cast<uint32_t>(src) * rows_per_owner + local) *
-                                                lay.recv_row_floats +
-                                            static_cast<uint32_t>(16 * c)) *
-                                               4u;
+        for (int j = 0; j < 4; ++j) {
+          const int c = static_cast<int>(half) + 2 * j;
+          if (c < chunks) {
+            float acc[16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = ptx::ld_shared_v4(r_addr + 16u * j);
-              acc[4 * j] += __uint_as_float(w.x);
-              acc[4 * j + 1] += __uint_as_float(w.y);
-              acc[4 * j + 2] += __uint_as_float(w.z);
-              acc[4 * j + 3] += __uint_as_float(w.w);
+            for (int i = 0; i < 16; ++i) acc[i] = __uint_as_float(v[j][i]);
+            for (int sidx = 0; sidx < S - 1; ++sidx) {
+              const uint32_t r_addr =
+                  base + lay.recv_off +
+                  ((static_cast<uint32_t>(sidx) * rows_per_owner + local) * lay.row_floats +
+                   static_cast<uint32_t>(16 * c)) * 4u;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 w = ptx::ld_shared_v4(r_addr + 16u * i);
+                acc[4 * i] += __uint_as_float(w.x);
+                acc[4 * i + 1] += __uint_as_float(w.y);
+                acc[4 * i + 2] += __uint_as_float(w.z);
+                acc[4 * i + 3] += __uint_as_float(w.w);
+              }
             }
-          }
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            box[(16 * c + j) * 32 + static_cast<int>(lane)] = to_out<OutT>(acc[j] * scale + bias);
-        };
-        // Two TMEM loads in flight per wait.
-        for (int c = 0; c < chunks; c += 2) {
-          uint32_t v0[16], v1[16];
-          const bool two = c + 1 < chunks;
-          if (has_k) {
-            ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * c), v0);
-            if (two) ptx::tmem_ld_32x32b_x16(t_row + static_cast<uint32_t>(16 * (c + 1)), v1);
-            ptx::tmem_ld_wait();
+            for (int i = 0; i < 16; ++i)
+              box[(16 * c + i) * 32 + static_cast<int>(lane)] = to_out<OutT>(acc[i] * scale + bias);
           }
-          finish_chunk(c, v0);
-          if (two) finish_chunk(c + 1, v1);
         }
-        ptx::fence_proxy_async_shared();  // the box's generic stores before the TMA store
+        ptx::fence_proxy_async_shared();  // the box's generic stores before the TMA stores
         __syncwarp();
         const int32_t col0 = n0 + static_cast<int32_t>(quad * 32u);
         if (lane == 0 && col0 < p.n) {
-          ptx::tma_store_3d(&tm_d, base + box_off, col0, 0, 0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = static_cast<int>(half) + 2 * j;
+            if (c < chunks)
+              ptx::tma_store_3d(&tm_d, base + box_off + static_cast<uint32_t>(c * 16 * 32) *
+                                                            static_cast<uint32_t>(sizeof(OutT)),
+                                col0, 16 * c, 0);
+          }
           ptx::bulk_commit_group();
-          ptx::bulk_wait_group<0>();  // the box is read and written before the CTA exits
+          ptx::bulk_wait_group_read<0>();  // the box is read before its memory is released
         }
         __syncwarp();
       }

@@ -205,6 +205,27 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* m) {
 // Tensor maps are 3-D: (columns, rows, batch); an unbatched operand has one batch (z = 0).
 
 // Tiled load into this CTA's shared memory, completing its bytes on barrier `bar` (this CTA).
+// Prefetch a tile of a tensor into L2 (no shared memory, no barrier).  Only a hint: L2 is the
+// coherence point, so a prefetch never makes a later load see stale data.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* m, int32_t x, int32_t y,
+                                                   int32_t z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// Programmatic dependent launch: let the grid launched after this one on the stream be scheduled
+// once every CTA of this grid has executed this (or exited) ...
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// ... and, in that later grid, wait until the grids it depends on have completed and their memory
+// operations are visible (returns at once without such a dependency).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* m, uint32_t dst, uint32_t bar,
                                             int32_t x, int32_t y, int32_t z, uint64_t policy) {
   asm volatile(
