@@ -355,6 +355,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   }
   ptx::fence_proxy_async_shared();  // the stages' async-proxy use ends before generic stores
   __syncthreads();
+  // The closing cluster barrier is split: each warp arrives once it has no more business with a
+  // peer's shared memory (warps 0 and 1 now, a sender once its copy is issued, an owner once its
+  // partial sums have arrived), and all wait at the very end, so no CTA leaves while a bulk copy
+  // may still read or write its shared memory, and the wait is mostly over by then.
+  if (clustered && warp < 2) ptx::cluster_arrive();
   if (warp >= 2) {
     // Warp w reads TMEM lane quadrant w mod 4 (rows 32 quad .. 32 quad + 31 of this CTA's tile)
     // and the 16-column chunks c = half + 2 j of the accumulator (token rows 16 c .. 16 c + 15).
@@ -408,9 +413,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             ptx::mapa_shared(base + lay.recv_off + slot * lay.block_bytes + q_off, dst_rank), src,
             32u * lay.row_floats * 4u, ptx::mapa_shared(recv_bar, dst_rank));
       }
+      __syncwarp();
+      if (clustered) ptx::cluster_arrive();
     } else {
       bool got = S == 1 || ptx::mbar_wait(recv_bar, 0u, ctx, kSiteDecodeRecv);
       got = __all_sync(0xffffffffu, got) && ok;
+      if (clustered) ptx::cluster_arrive();
       if (got) {
         const int32_t n = n0 + static_cast<int32_t>(row);
         float scale = p.alpha;
@@ -468,9 +476,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     }
   }
 
+  if (clustered) ptx::cluster_wait();  // no CTA leaves while a peer may still copy into or out of it
   ptx::tc_fence_before();
   __syncthreads();
-  if (clustered) ptx::cluster_sync();  // no CTA leaves while a peer may still store into it
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc<CG>(tmem_base, static_cast<uint32_t>(p.tmem_cols));
