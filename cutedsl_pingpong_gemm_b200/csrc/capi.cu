@@ -368,7 +368,7 @@ struct cpg_gemm {
 
 extern "C" {
 
-int cpg_abi_version(void) { return 13; }
+int cpg_abi_version(void) { return 14; }
 
 const char* cpg_strerror(int code) {
   switch (code) {
@@ -1566,6 +1566,32 @@ static int check_reduce_scatter(const cpg_gemm* g, const cpg_reduce_scatter* rs)
   return CPG_OK;
 }
 
+// One arrival of a reduce-scatter call on every rank's counter, after the call's GEMM (and so
+// after this rank's previous cpg_peer_finish, in stream order).  A rank that owns no rows gets no
+// tile arrivals: without this its finish would return at once and its next-but-one call could add
+// into an owner's buffer before the owner had read and cleared it.  With it, every finish waits
+// until every rank has completed its previous finish.
+struct EpochCounters {
+  uint32_t* count[CPG_MAX_PEERS];
+  int32_t ranks;
+};
+__global__ void rs_epoch_kernel(const EpochCounters c) {
+  if (static_cast<int32_t>(threadIdx.x) < c.ranks) {
+    cpg::ptx::fence_sc_sys();
+    cpg::ptx::red_release_sys_add_u32(c.count[threadIdx.x], 1u);
+  }
+}
+
+static int rs_epoch(const cpg_reduce_scatter* rs, cudaStream_t st) {
+  EpochCounters c;
+  std::memset(&c, 0, sizeof(c));
+  c.ranks = rs->ranks;
+  for (int q = 0; q < rs->ranks; ++q) c.count[q] = static_cast<uint32_t*>(rs->count[q]);
+  rs_epoch_kernel<<<1, 32, 0, st>>>(c);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CPG_OK : cuda_fail(e, "reduce-scatter epoch kernel launch");
+}
+
 int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
                                 const cpg_reduce_scatter* rs, const cpg_epilogue* epi,
                                 void* stream) {
@@ -1575,7 +1601,8 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
   if (epi != nullptr &&
       (epi->bias != nullptr || epi->activation != CPG_ACT_NONE || epi->source != nullptr))
     return fail(CPG_ERR_UNSUPPORTED, "bias, activations and C belong to cpg_peer_finish");
-  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;  // no arrivals (cpg_gemm_rs_arrivals)
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return rs_epoch(rs, st);  // no tile arrivals
   if (g->splits > 1 && g->ws_dev == nullptr) {
     // The K ranges of a tile are summed in this GPU's L2 first (the Stream-K fixup workspace,
     // one tile per cluster tile of the problem), so each tile crosses to its owner once.
@@ -1589,7 +1616,9 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* g, const void* a, const void* b,
     if (rc2 != CPG_OK) return rc2;
   }
   // The output tensor map is built on this rank's buffer and never used for stores.
-  return run_impl(g, a, b, rs->dst[rs->rank], epi, stream, nullptr, rs);
+  rc = run_impl(g, a, b, rs->dst[rs->rank], epi, stream, nullptr, rs);
+  if (rc != CPG_OK) return rc;
+  return rs_epoch(rs, st);
 }
 
 // Every CTA tile of the schedule (row tiles of all clusters, including a pair's tile past M)
@@ -1636,8 +1665,8 @@ int cpg_gemm_rs_arrivals(const cpg_gemm* g, const cpg_reduce_scatter* rs, uint32
   if (per_rank == nullptr) return fail(CPG_ERR_NULL, "per_rank is NULL");
   for (int q = 0; q < rs->ranks; ++q) per_rank[q] = 0;
   const cpg_gemm_problem& pr = g->prob;
-  if (pr.m == 0 || pr.n == 0 || pr.k == 0) return CPG_OK;
-  rs_arrivals(g->sched, g->v.epi_warps, rs, per_rank);
+  if (pr.m != 0 && pr.n != 0 && pr.k != 0) rs_arrivals(g->sched, g->v.epi_warps, rs, per_rank);
+  for (int q = 0; q < rs->ranks; ++q) ++per_rank[q];  // the call's epoch arrival (rs_epoch)
   return CPG_OK;
 }
 

@@ -356,9 +356,13 @@ int cpg_gemm_run_reduce_scatter(cpg_gemm* plan, const void* a, const void* b,
                                 void* stream);
 /* How much one cpg_gemm_run_reduce_scatter of this plan raises each rank's counter:
  * per_rank[q] for q < rs->ranks (one per epilogue warp -- 4, or 8 for tile_n 512 -- of every
- * CTA tile whose rows rank q owns). */
+ * CTA tile whose rows rank q owns), plus one: every call also arrives once on every rank's
+ * counter after its GEMM, so that each finish also waits for every rank's previous finish (a
+ * rank owning no rows would otherwise not wait at all and could run two calls ahead into a
+ * buffer its owner has not read yet). */
 int cpg_gemm_rs_arrivals(const cpg_gemm* plan, const cpg_reduce_scatter* rs, uint32_t* per_rank);
-/* The same count from scheduler parameters and the tile width alone (no device needed). */
+/* The tiles' share of that count (without the call's own arrival) from scheduler parameters and
+ * the tile width alone (no device needed). */
 int cpg_sched_rs_arrivals(const cpg_sched_params* sched, int32_t tile_n,
                           const cpg_reduce_scatter* rs, uint32_t* per_rank);
 /* Owner side: wait (bounded by timeout_ms; on a timeout *status gets a nonzero code and nothing

@@ -91,13 +91,38 @@ WORKER = textwrap.dedent(r'''
     pk3.check_status()
     pk.close()
     pk3.close()
+    # One 128-row tile: rank 0 owns every row and the other ranks none, so their finishes wait
+    # only for the per-call arrivals.  Rank 0 lags (a spin kernel before each call) while the
+    # others issue calls back to back; a rank running ahead into a buffer rank 0 has not read yet
+    # would add its partial sums twice.  Every call's rows are checked at the end.
+    m4, n4, k4 = 128, 512, 1024 * world
+    a4, b4, _ = gemm_ref.make_inputs(m4, n4, k4, seed=9, b_scale=k4 ** -0.5)
+    ks4, ke4 = k_ranges(k4, world)[rank]
+    a4k, b4k = a4[:, ks4:ke4].cuda().contiguous(), b4[:, ks4:ke4].cuda().contiguous()
+    pk4 = PeerSplitK(gemm, world, rank, local_split_k=1)
+    outs4 = []
+    for it in range(6):
+        if rank == 0:
+            torch.cuda._sleep(2_000_000)
+        outs4.append(pk4(a4k, b4k, m4, n4))
+    torch.cuda.synchronize()
+    res6 = {"ok": True}
+    if rank == 0:
+        for it, o in enumerate(outs4):
+            r6 = gemm_ref.check(o.cpu(), a4, b4)
+            if not r6["ok"]:
+                res6 = r6
+                print(f"RANK 0 rows owned alone, call {it} failed: {r6}", flush=True)
+    ok &= res6["ok"]
+    pk4.check_status()
+    pk4.close()
     checks = {"mshard": res["ok"], "splitk_nccl": res2["ok"], "splitk_chunked": res3["ok"],
-              "peer": res4["ok"], "peer_dynamic_bias": res5["ok"]}
+              "peer": res4["ok"], "peer_dynamic_bias": res5["ok"], "peer_rowless": res6["ok"]}
     print(f"RANK {rank} rows {r0}:{r1} ok={ok} {checks}", flush=True)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
-        print("RESULT", int(flag.item()), res, res2, res3, res4, res5, flush=True)
+        print("RESULT", int(flag.item()), res, res2, res3, res4, res5, res6, flush=True)
     dist.destroy_process_group()
     sys.exit(0 if ok else 1)
 ''')

@@ -105,6 +105,45 @@ def test_reduce_scatter_rounds(tile_n, cluster, dynamic, world, split):
             assert int(torch.count_nonzero(em.bufs[q]).item()) == 0
 
 
+@pytest.mark.parametrize("m,n,k,dynamic,split,rounds", [
+    (512, 768, 8192, False, 2, 3),              # 4 row tiles over 8 ranks: ranks 4-7 own no rows
+    (128 * 17 - 40, 1000, 6144, True, 0, 2)])   # ragged M, bias, the automatic in-GPU split
+def test_reduce_scatter_eight_ranks(m, n, k, dynamic, split, rounds):
+    """The peer reduce-scatter shapes of the 8-process test in test_multi_gpu.py (its GEMM
+    arguments, K split over 8 ranks, each rank's K range split again inside the GPU), with the 8
+    ranks emulated on one GPU: the arrival counts of every owner, ranks without rows, the
+    running count over repeated calls and the cleared buffers."""
+    from types import SimpleNamespace
+    from cutedsl_pingpong_gemm_b200.gemm_base import CompiledGemm
+    from cutedsl_pingpong_gemm_b200.sharding import PeerSplitK
+    world = 8
+    gemm = GemmSM90((128, 256), (128, 32), (2, 1, 1), (1, 1), ab_stage=6, reuse_ab=False,
+                    is_persistent=True, dynamic_scheduler=dynamic)
+    if split == 0:
+        ks, ke = k_ranges(k, world)[0]
+        split = PeerSplitK._split(SimpleNamespace(gemm=gemm, local_split_k=0), CompiledGemm(gemm),
+                                  m, n, ke - ks)
+    a, b, bias = gemm_ref.make_inputs(m, n, k, seed=7, b_scale=k ** -0.5, with_bias=dynamic)
+    em = Emulated(gemm, m, n, k, world, split, a, b)
+    dbias = bias.cuda() if bias is not None else None
+    for _ in range(rounds):
+        em.gemms()
+        outs = []
+        for q in range(world):
+            rows = em.starts[q + 1] - em.starts[q]
+            out = torch.full((max(rows, 1), n), float("nan"), dtype=torch.bfloat16, device="cuda")
+            em.finish(q, out, dbias)
+            outs.append(out)
+        torch.cuda.synchronize()
+        assert int(em.status.item()) == 0
+        for q in range(world):
+            s, e = em.starts[q], em.starts[q + 1]
+            if e > s:
+                res = gemm_ref.check(outs[q][: e - s].cpu(), a[s:e], b, bias=bias)
+                assert res["ok"], (q, split, res)
+            assert int(torch.count_nonzero(em.bufs[q]).item()) == 0
+
+
 def test_finish_times_out_when_arrivals_are_missing():
     """A finish whose target is never reached gives up after its limit with a status code and
     writes nothing; the context stays usable."""
