@@ -91,15 +91,18 @@ WORKER = textwrap.dedent(r'''
     pk3.check_status()
     pk.close()
     pk3.close()
-    # One 128-row tile: rank 0 owns every row and the other ranks none, so their finishes wait
+    # One 128-row tile on single-CTA clusters (no pair tile past M, whose arrivals would count
+    # for the last rank): rank 0 owns every row and the other ranks none, so their finishes wait
     # only for the per-call arrivals.  Rank 0 lags (a spin kernel before each call) while the
     # others issue calls back to back; a rank running ahead into a buffer rank 0 has not read yet
     # would add its partial sums twice.  Every call's rows are checked at the end.
+    gemm1 = GemmSM90((128, 256), (128, 32), (1, 1, 1), (1, 1), ab_stage=3, reuse_ab=False,
+                     is_persistent=True)
     m4, n4, k4 = 128, 512, 1024 * world
     a4, b4, _ = gemm_ref.make_inputs(m4, n4, k4, seed=9, b_scale=k4 ** -0.5)
     ks4, ke4 = k_ranges(k4, world)[rank]
     a4k, b4k = a4[:, ks4:ke4].cuda().contiguous(), b4[:, ks4:ke4].cuda().contiguous()
-    pk4 = PeerSplitK(gemm, world, rank, local_split_k=1)
+    pk4 = PeerSplitK(gemm1, world, rank, local_split_k=1)
     outs4 = []
     for it in range(6):
         if rank == 0:
