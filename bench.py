@@ -299,6 +299,16 @@ def barrier(world):
         dist.barrier()
 
 
+def align_start(world, dev):
+    """Start the ranks' timed steps together on the device: a one-element all-reduce on the
+    current stream, after which every rank's next kernel starts at (nearly) the same time,
+    however late each host left the barrier."""
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        dist.all_reduce(torch.ones(1, device=dev))
+
+
 def reduce_max(x, world):
     if world == 1:
         return x
@@ -667,7 +677,7 @@ def run_tallk(args, world, rank, local):
     def step():
         out = sk(a_k, b_k, m, n)
         if peer:
-            launches[0] += 2  # GEMM (exchange in its epilogue) + finish
+            launches[0] += 3  # GEMM (exchange in its epilogue), per-call arrival, finish
         else:
             launches[0] += 2 * len(sk.column_chunks(n)) if chunks > 1 else 2  # GEMM + cast each
         return out
@@ -686,6 +696,10 @@ def run_tallk(args, world, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
+    # The ranks exchange partial sums every step, so their steps are coupled: a rank whose host
+    # leaves the barrier late would hold up the others inside their timed regions (measured:
+    # 267 us per step at 8 GPUs against 150 us of GEMM and finish per rank).
+    align_start(world, dev)
     e0.record(stream)
     for i in range(args.steps):
         out = step()
