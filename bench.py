@@ -48,6 +48,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 NOMINAL_DENSE_FP8_TFLOPS = 4500.0
 
+GRAPH_STEPS = 20  # calls per captured graph of the small-M workload
+
 WORKLOADS = {
     # m is per GPU when m_is_per_gpu (weak scaling), else the total split over the GPUs.
     "bf16_8192": dict(m=8192, n=8192, k=8192, a_scale=1.0, b_scale=8192 ** -0.5, bias=False,
@@ -109,8 +111,9 @@ def parse_args():
                     help="tallk: column chunks whose reduce-scatter overlaps the next chunk's "
                          "GEMM (measured slower than 1 on two GPUs)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
-                    help="replay each timed step from a CUDA graph captured through the public "
-                         "API (auto: for the launch-bound small-M workload)")
+                    help="replay the timed steps from CUDA graphs of up to 20 consecutive calls "
+                         "captured through the public API (auto: for the launch-bound small-M "
+                         "workload)")
     ap.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                     help="tallk at N > 1: p2p: the GEMM epilogue adds the FP32 partials into the "
                          "owning rank's memory over NVLink (measured 6-8%% faster than NCCL on "
@@ -954,24 +957,41 @@ def run_cpg(args, world, rank, local):
         step()
     torch.cuda.synchronize()
     use_graph = args.graph == "on" or (args.graph == "auto" and bool(w.get("small_m")))
-    graph = None
+    # The timed region runs `units`: (callable, steps it makes) in order, exactly args.steps.
+    units = [(step, 1)] * args.steps
     if use_graph:
         # A step of tens of microseconds is bound by the host's launch path (measured: 40.5 us
-        # eager vs 32.9 us replayed for M = 128); a serving loop replays a captured graph.
-        cap = torch.cuda.Stream(dev)
-        cap.wait_stream(stream)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=cap):
-            compiled(a, b, d, cap, bias=bias, scale_a=scale_a, scale_b=scale_b, split_k=split_k,
-                     activation=act, gated=gated)
-        stream.wait_stream(cap)
+        # eager vs 32.9 us replayed one call per graph for M = 128); a serving loop replays a
+        # graph of consecutive calls, in which each GEMM (a programmatic dependent of the one
+        # before) sets up while the previous one finishes.  Graphs of up to GRAPH_STEPS calls.
+        def capture(count):
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(stream)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for _ in range(count):
+                    compiled(a, b, d, cap, bias=bias, scale_a=scale_a, scale_b=scale_b,
+                             split_k=split_k, activation=act, gated=gated)
+            stream.wait_stream(cap)
+            return g
 
-        def step():  # noqa: F811 - the timed step replays the captured call
-            graph.replay()
-            launches[0] += kernels_per_step
+        group = max(1, min(args.steps, GRAPH_STEPS))
+        graphs = {group: capture(group)}
+        rem = args.steps % group
+        if rem:
+            graphs[rem] = capture(rem)
 
+        def replayer(count):
+            def run():
+                graphs[count].replay()
+                launches[0] += kernels_per_step * count
+            return run
+
+        units = [(replayer(group), group)] * (args.steps // group)
+        if rem:
+            units.append((replayer(rem), rem))
         for _ in range(3):
-            step()
+            replayer(group)()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -981,10 +1001,11 @@ def run_cpg(args, world, rank, local):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        step()
+    for i, (run_unit, _) in enumerate(units):
+        run_unit()
         if i == 0:
             sampler.start()  # the GPU is busy from here on: no idle-clock samples
+    assert sum(c for _, c in units) == args.steps
     e1.record(stream)
     torch.cuda.synchronize()
     sampler.stop()
@@ -1119,7 +1140,9 @@ def run_cpg(args, world, rank, local):
                               "epi_stage": epi_stage, "grid": list(info["grid"]),
                               "smem_bytes": info["smem_bytes"], "split_k": split_k,
                               "scheduler": gemm.dynamic_scheduler and "dynamic" or "static",
-                              "group_size": group_size, "cuda_graph": use_graph,
+                              "group_size": group_size,
+                              "cuda_graph": (f"graphs of {min(args.steps, GRAPH_STEPS)} calls"
+                                             if use_graph else False),
                               "reference_constructor": ref_ctor},
             "per_rank": per_rank, "parity": parity,
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
