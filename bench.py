@@ -223,6 +223,67 @@ class ClockSampler:
                 "reasons": names, "samples": len(self.samples)}
 
 
+class ExternalClockSampler:
+    """The same summary as ClockSampler from a separate ``nvidia-smi`` process polling every
+    10 ms (started before the barrier, stopped after the timed region), for steps coupled across
+    ranks: there an in-process polling thread stalled a rank's launches and with them every other
+    rank (tall K on 8 GPUs: 268-270 us per step against 216-218 us without the thread)."""
+
+    def __init__(self, cuda_index, period_ms=10):
+        import subprocess
+        import torch
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self.window = (None, None)
+        self.proc = None
+        p = torch.cuda.get_device_properties(cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", bus, "--query-gpu=timestamp,clocks.sm,clocks.max.sm,"
+                 "clocks_event_reasons.active", "--format=csv,noheader,nounits",
+                 f"--loop-ms={period_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except OSError:
+            self.proc = None
+
+    def start(self):
+        self.window = (time.time(), None)
+
+    def stop(self):
+        import datetime as _dt
+        self.window = (self.window[0], time.time() + 0.02)
+        if self.proc is None:
+            return
+        time.sleep(0.03)  # at least one sample after the timed region
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        t0, t1 = self.window
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != 4:
+                continue
+            try:
+                ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                mhz, max_mhz, reasons = int(parts[1]), int(parts[2]), int(parts[3], 16)
+            except ValueError:
+                continue
+            self.max_mhz = max_mhz
+            if t0 is not None and t0 <= ts <= t1:
+                self.samples.append(mhz)
+                self.reasons |= reasons
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        names = [n for bit, n in ClockSampler.REASONS if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
 class NvlinkCounter:
     """NVLink data bytes this GPU sent and received (NVML throughput counters, summed over its
     links), read before and after the timed region; None where the driver does not expose them."""
@@ -691,7 +752,10 @@ def run_tallk(args, world, rank, local):
     # Host-side set-up (NVML handles and counter reads take milliseconds) before the barrier:
     # the ranks exchange partial sums every step, so a rank that starts late makes the others
     # wait inside their timed region.
-    sampler = ClockSampler(local)
+    # The ranks exchange partial sums every step, so their steps are coupled: anything that
+    # stalls one rank's host stalls every rank.  Clocks then come from a separate process, and
+    # the ranks start together on the device, however late each host leaves the barrier.
+    sampler = ExternalClockSampler(local) if world > 1 else ClockSampler(local)
     nvl = NvlinkCounter(local)
     nvl.start()
     launches[0] = 0
@@ -699,9 +763,6 @@ def run_tallk(args, world, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    # The ranks exchange partial sums every step, so their steps are coupled: a rank whose host
-    # leaves the barrier late would hold up the others inside their timed regions (measured:
-    # 267 us per step at 8 GPUs against 150 us of GEMM and finish per rank).
     align_start(world, dev)
     e0.record(stream)
     for i in range(args.steps):
