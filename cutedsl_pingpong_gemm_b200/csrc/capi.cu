@@ -289,8 +289,19 @@ dim3 cast_grid(int64_t rows, int64_t cols) {
   return dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by), 1);
 }
 
+// Raise (never lower) a kernel's dynamic shared-memory limit on the current device.  Plans of
+// different shapes share a kernel function: a plan created later with a smaller need must not
+// make an earlier plan's launch fail.
+cudaError_t raise_smem_limit(const void* fn, int smem) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+  if (e != cudaSuccess) return e;
+  if (fa.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 int query_max_active_clusters(const Variant& v, int smem, int cm, int cn, int* out) {
-  cudaError_t e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = raise_smem_limit(v.fn, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   int dev = 0;
   cudaGetDevice(&dev);
@@ -541,7 +552,7 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   if (smem > static_cast<int>(prop.sharedMemPerBlockOptin))
     return fail(CPG_ERR_SMEM, "the small-M kernel does not fit in shared memory");
   const void* fn = decode_kernel(prob->dtype_ab, prob->dtype_d, cg);
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = raise_smem_limit(fn, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(small-M kernel smem)");
   int mac = 0;
   {

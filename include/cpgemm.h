@@ -154,7 +154,12 @@ typedef struct cpg_gemm_problem {
  * tile is split over a cluster of 1, 2 or 4 CTAs and the partial sums are added in distributed
  * shared memory, in one launch with no workspace.  BF16 or E4M3 operands (per-tensor scales),
  * BF16 or FP32 D, alpha and bias; no activation, C, gating, batches or groups.  The tile, cluster
- * and stage settings of the config do not apply (the kernel picks its own). */
+ * and stage settings of the config do not apply (the kernel picks its own).  It is launched as a
+ * programmatic dependent of the stream's previous kernel (environment CPG_DECODE_PDL=0 at plan
+ * creation: not): it may start while that kernel runs, but before that kernel has completed it
+ * only sets itself up and prefetches its first tiles of B into L2 (a hint, never stale data);
+ * it reads A, B, the bias and the scales and writes D only after.  It lets the next kernel on
+ * the stream start early in the same way. */
 #define CPG_SPLIT_K_DECODE (-3)
 
 /* Per-call epilogue options:

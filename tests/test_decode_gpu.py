@@ -7,7 +7,8 @@ in distributed shared memory.  Checked against the fp32 CPU
 oracle with the tolerance of the other GPU tests (relative Frobenius <= 1e-2 for BF16 output,
 3e-2 for FP8 E4M3 operands, and the element-wise bound |D - R| <= 2^-8 |R| + K 2^-23 (|A| |B|^T)),
 for every cluster size the plan can pick, M not a multiple of 16, ragged N and K, FP32 output,
-bias, alpha, K = 0, CUDA-graph replay, and the rejection of what the kernel does not do.
+bias, alpha, K = 0, CUDA-graph replay, chains of calls each reading the previous one's output
+(programmatic dependent launch), and the rejection of what the kernel does not do.
 """
 import pytest
 import torch
@@ -73,6 +74,7 @@ def test_ragged_shapes_and_cluster_sizes(m, n, k, cluster, tiles):
     (100, 1000, 2048, {"CPG_DECODE_PAIR": "1"}, 8),     # 4 pair tiles x 4 pairs, ragged N
     (128, 4096, 4096 + 64, {"CPG_DECODE_PAIR": "1", "CPG_DECODE_ROTATE": "0"}, 8),
     (64, 2056, 640, {"CPG_DECODE_ROTATE": "0", "CPG_DECODE_SPIN": "0"}, 4),
+    (48, 4096, 4096, {"CPG_DECODE_PDL": "0"}, 4),         # launched without the dependency
 ])
 def test_other_variants(monkeypatch, m, n, k, env, cluster):
     """The CTA-pair form (256-row tiles, one cta_group::2 MMA per k-step for both CTAs of a pair),
@@ -145,6 +147,51 @@ def test_repeated_calls_and_graph_replay_are_bitwise_stable():
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(d, ref)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_chained_calls_wait_for_their_producer(graph):
+    """Each call is a programmatic dependent of the previous kernel on the stream: it may start
+    (barriers, TMEM, an L2 prefetch of B) while that kernel runs, but must read A only after it
+    has completed.  A chain D1 = A B1^T, D2 = D1 B2^T, D3 = D2 B3^T on one stream, D1 and D2
+    poisoned with NaN just before, checked link by link against the oracle on the GPU's own
+    inputs; eagerly and replayed from one CUDA graph."""
+    m = 16
+    dims = [4096, 4096, 2048, 1024]  # K of the first link, then each link's N
+    g = torch.Generator().manual_seed(21)
+    a = torch.randn(m, dims[0], generator=g).to(torch.bfloat16)
+    bs = [(torch.randn(dims[i + 1], dims[i], generator=g) * dims[i] ** -0.5).to(torch.bfloat16)
+          for i in range(3)]
+    da, dbs = a.cuda(), [b.cuda() for b in bs]
+    ds = [torch.empty(m, dims[i + 1], dtype=torch.bfloat16, device="cuda") for i in range(3)]
+    compiled = [cpg_compile(make_gemm(), da if i == 0 else ds[i - 1], dbs[i], ds[i])
+                for i in range(3)]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+
+    def chain():
+        with torch.cuda.stream(s):
+            for d in ds:
+                d.fill_(float("nan"))
+            for i in range(3):
+                compiled[i](da if i == 0 else ds[i - 1], dbs[i], ds[i], s, split_k=DECODE)
+
+    if graph:
+        chain()  # plans and tensor maps before capture
+        torch.cuda.synchronize()
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg, stream=s):
+            chain()
+        for _ in range(3):
+            cg.replay()
+    else:
+        for _ in range(3):
+            chain()
+    torch.cuda.synchronize()
+    inputs = [a] + [d.cpu() for d in ds[:2]]
+    for i in range(3):
+        res = gemm_ref.check(ds[i].cpu(), inputs[i], bs[i])
+        assert res["ok"], (i, res)
 
 
 def test_rejects_what_the_kernel_does_not_do():

@@ -479,3 +479,15 @@ def test_stream_k_bf16_through_api():
         compiled(a.cuda(), b.cuda(), d, None, bias=bias.cuda(), split_k=-1)
     torch.cuda.synchronize()
     assert gemm_ref.check(d.cpu(), a, b, bias=bias)["ok"]
+
+
+def test_plans_of_one_kernel_keep_their_shared_memory():
+    """Plans of different shapes share one kernel function.  A plan with fewer stages created
+    after one with more must not lower the function's shared-memory limit below the first plan's
+    need (its launches would fail with an invalid argument)."""
+    m, n, k = 512, 1024, 1024
+    big = make_gemm(tile_n=256, cluster=(1, 1, 1), stages=4)
+    small = make_gemm(tile_n=256, cluster=(1, 1, 1), stages=2)
+    run_and_check(m, n, k, big, seed=31)
+    run_and_check(m, n, k, small, seed=32)
+    run_and_check(m, n, k, big, seed=33)
