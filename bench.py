@@ -139,15 +139,18 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def load_traffic(workload, scheduler):
-    """ncu DRAM bytes of one launch of the workload's kernel under this tile schedule, or None
-    when no capture of that combination is recorded."""
+def load_traffic(workload, scheduler, m_override=0):
+    """ncu DRAM bytes of one launch of the workload's kernel under this tile schedule (and, for
+    an --m override, that M), or None when no capture of that combination is recorded."""
     path = os.path.join(HERE, "profiles", "traffic.json")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         d = json.load(f)
-    for key in (f"{workload}:{scheduler}", workload):
+    keys = [f"{workload}:{scheduler}", workload]
+    if m_override and m_override != WORKLOADS[workload]["m"]:
+        keys = [f"{workload}:m{m_override}"]
+    for key in keys:
         e = d.get(key)
         if e is not None and e.get("scheduler", scheduler) == scheduler:
             return e.get("dram_bytes_per_launch")
@@ -1209,7 +1212,9 @@ def run_cpg(args, world, rank, local):
             "roofline": ({"bound": "hbm", "achieved": min_bytes / (ms_local * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": min_bytes / (ms_local * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                          "peak_source": f"{peak_src} hbm_gbs", "traffic": load_traffic(args.workload, args.scheduler),
+                          "peak_source": f"{peak_src} hbm_gbs",
+                          "traffic": (load_traffic(args.workload, args.scheduler, args.m)
+                                      if split_k == -3 else None),
                           "algorithmic_bytes_per_step": min_bytes, "split_k": split_k,
                           "kernel": ("cpg::gemm_decode_kernel" if split_k == -3 else
                                      ("cpg::gemm_sm100_kernel (Stream-K)" if split_k == -1 else
@@ -1220,7 +1225,7 @@ def run_cpg(args, world, rank, local):
                          "frac": achieved / peak, "peak_source": peak_note,
                          "frac_sustained": (achieved / peaks.get("bf16_tflops_sustained", peak)
                                             if w["fp8"] is None else None),
-                         "traffic": load_traffic(args.workload, args.scheduler),
+                         "traffic": load_traffic(args.workload, args.scheduler, args.m),
                          "algorithmic_flops_per_launch": flops_per_gpu,
                          "kernel": ("cpg::gemm_fp8_block_kernel" if w["fp8"] == "block"
                                     else "cpg::gemm_sm100_kernel")}),
