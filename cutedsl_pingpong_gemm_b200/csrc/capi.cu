@@ -375,6 +375,7 @@ struct cpg_gemm {
   int32_t decode;
   int32_t dec_mma_n, dec_tmem_cols, dec_kps, dec_splits, dec_stages, dec_cg, dec_spin, dec_rotate;
   int32_t dec_pdl;  // launched as a programmatic dependent of the stream's previous kernel
+  int32_t dec_st_async;  // partial sums by per-thread st.async (else staged bulk copies)
 };
 
 extern "C" {
@@ -612,6 +613,8 @@ static int create_decode_plan(const cpg_gemm_config* cfg, const cpg_gemm_problem
   g->dec_rotate = env_rot != nullptr ? (std::atoi(env_rot) != 0) : 1;
   const char* env_pdl = std::getenv("CPG_DECODE_PDL");
   g->dec_pdl = env_pdl != nullptr ? (std::atoi(env_pdl) != 0) : 1;
+  const char* env_sta = std::getenv("CPG_DECODE_STASYNC");
+  g->dec_st_async = env_sta != nullptr ? (std::atoi(env_sta) != 0) : 0;
   e = cudaMalloc(&g->status_dev, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaMemset(g->status_dev, 0, sizeof(int32_t) * 4);
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
@@ -662,6 +665,7 @@ static int run_decode(cpg_gemm* g, const void* a, const void* b, void* d, const 
   p.spin = g->dec_spin;
   p.rotate = g->dec_rotate;
   p.pdl = g->dec_pdl;
+  p.st_async = g->dec_st_async;
   p.stages = g->dec_stages;
   p.alpha = epi != nullptr ? epi->alpha : 1.0f;
   p.scale_a = epi != nullptr ? epi->scale_a : nullptr;

@@ -61,6 +61,7 @@ struct DecodeParams {
   int32_t spin;        // producer / MMA lanes poll their barriers instead of sleeping
   int32_t rotate;      // start each tile's K range at a tile-dependent k-block (see below)
   int32_t pdl;         // launched as a programmatic dependent: set up, then wait (see below)
+  int32_t st_async;    // partial sums sent by per-thread st.async instead of staged bulk copies
   float alpha;
   const float* scale_a;  // optional per-tensor FP8 scales (device scalars)
   const float* scale_b;
@@ -186,7 +187,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::mbar_init(drain_bar, 1);
     // The S - 1 blocks this CTA receives complete their bytes on recv_bar (armed before the
     // start-up cluster barrier, which every peer passes before it can send).
-    if (S > 1) ptx::mbar_arrive_expect_tx(recv_bar, lay.recv_bytes);
+    if (S > 1)
+      ptx::mbar_arrive_expect_tx(
+          recv_bar, p.st_async ? static_cast<uint32_t>((S - 1) * rows_per_owner * p.mma_n * 4)
+                               : lay.recv_bytes);
     *abort_flag = 0;
     ptx::fence_mbarrier_init_cluster();
     ptx::fence_proxy_async_shared();
@@ -391,27 +395,45 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       // are done, one lane copies its 32 rows to the owner in one bulk transfer, completing the
       // bytes on the owner's receive barrier.
       const uint32_t block = owner < kr ? owner : owner - 1u;
+      const uint32_t slot = kr < owner ? kr : kr - 1u;  // this CTA's slot at the owner
+      const uint32_t dst_rank = owner * CG + q;
       const uint32_t q_off = (quad * 32u - owner * rows_per_owner) * lay.row_floats * 4u;
-      const uint32_t src = base + lay.send_off + block * lay.block_bytes + q_off;
-      const uint32_t dst = src + lane * lay.row_floats * 4u;
+      if (p.st_async) {
+        // Each lane stores its row's partial sums straight into the owner's receive slot, 16
+        // bytes per st.async, each completing on the owner's receive barrier.
+        const uint32_t rdst = ptx::mapa_shared(
+            base + lay.recv_off + slot * lay.block_bytes + q_off + lane * lay.row_floats * 4u,
+            dst_rank);
+        const uint32_t rbar = ptx::mapa_shared(recv_bar, dst_rank);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = static_cast<int>(half) + 2 * j;
-        if (c < chunks) {
+        for (int j = 0; j < 4; ++j) {
+          const int c = static_cast<int>(half) + 2 * j;
+          if (c < chunks) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            ptx::st_shared_v4(dst + static_cast<uint32_t>(64 * c + 16 * i), v[j][4 * i],
-                              v[j][4 * i + 1], v[j][4 * i + 2], v[j][4 * i + 3]);
+            for (int i = 0; i < 4; ++i)
+              ptx::st_async_v4(rdst + static_cast<uint32_t>(64 * c + 16 * i), v[j][4 * i],
+                               v[j][4 * i + 1], v[j][4 * i + 2], v[j][4 * i + 3], rbar);
+          }
         }
-      }
-      ptx::fence_proxy_async_shared();  // generic stores before the bulk copy reads them
-      ptx::named_barrier_sync(1u + quad, 64u);
-      if (half == 0u && lane == 0u) {
-        const uint32_t slot = kr < owner ? kr : kr - 1u;  // this CTA's slot at the owner
-        const uint32_t dst_rank = owner * CG + q;
-        ptx::bulk_copy_to_cluster(
-            ptx::mapa_shared(base + lay.recv_off + slot * lay.block_bytes + q_off, dst_rank), src,
-            32u * lay.row_floats * 4u, ptx::mapa_shared(recv_bar, dst_rank));
+      } else {
+        const uint32_t src = base + lay.send_off + block * lay.block_bytes + q_off;
+        const uint32_t dst = src + lane * lay.row_floats * 4u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = static_cast<int>(half) + 2 * j;
+          if (c < chunks) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              ptx::st_shared_v4(dst + static_cast<uint32_t>(64 * c + 16 * i), v[j][4 * i],
+                                v[j][4 * i + 1], v[j][4 * i + 2], v[j][4 * i + 3]);
+          }
+        }
+        ptx::fence_proxy_async_shared();  // generic stores before the bulk copy reads them
+        ptx::named_barrier_sync(1u + quad, 64u);
+        if (half == 0u && lane == 0u)
+          ptx::bulk_copy_to_cluster(
+              ptx::mapa_shared(base + lay.recv_off + slot * lay.block_bytes + q_off, dst_rank),
+              src, 32u * lay.row_floats * 4u, ptx::mapa_shared(recv_bar, dst_rank));
       }
       __syncwarp();
       if (clustered) ptx::cluster_arrive();

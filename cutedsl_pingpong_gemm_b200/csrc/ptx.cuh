@@ -666,6 +666,16 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint3
       : "memory");
 }
 // Named barrier `id` over `threads` threads (a multiple of 32) of this CTA.
+// Asynchronous 16-byte store into a cluster peer's shared memory, completing its bytes on the
+// peer's mbarrier (both addresses from mapa_shared).
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

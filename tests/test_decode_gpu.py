@@ -75,10 +75,14 @@ def test_ragged_shapes_and_cluster_sizes(m, n, k, cluster, tiles):
     (128, 4096, 4096 + 64, {"CPG_DECODE_PAIR": "1", "CPG_DECODE_ROTATE": "0"}, 8),
     (64, 2056, 640, {"CPG_DECODE_ROTATE": "0", "CPG_DECODE_SPIN": "0"}, 4),
     (48, 4096, 4096, {"CPG_DECODE_PDL": "0"}, 4),         # launched without the dependency
+    (128, 8192, 8192, {"CPG_DECODE_STASYNC": "1"}, 2),    # partial sums by per-thread st.async
+    (5, 4096, 8320, {"CPG_DECODE_STASYNC": "1"}, 4),      # the same into 3 peers
 ])
 def test_other_variants(monkeypatch, m, n, k, env, cluster):
     """The CTA-pair form (256-row tiles, one cta_group::2 MMA per k-step for both CTAs of a pair),
-    every tile walking its K range from the start, and sleeping pipeline waits: the same checks."""
+    every tile walking its K range from the start, sleeping pipeline waits, the launch without
+    the programmatic dependency and the partial sums sent by per-thread st.async: the same
+    checks."""
     for key, value in env.items():
         monkeypatch.setenv(key, value)
     d, a, b, bb, plan = run(m, n, k, seed=m + k)
