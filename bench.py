@@ -238,8 +238,11 @@ class ExternalClockSampler:
         self.samples, self.reasons, self.max_mhz = [], 0, None
         self.window = (None, None)
         self.proc = None
-        p = torch.cuda.get_device_properties(cuda_index)
-        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        except Exception:
+            bus = str(cuda_index)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", bus, "--query-gpu=timestamp,clocks.sm,clocks.max.sm,"
