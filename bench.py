@@ -228,16 +228,21 @@ class ClockSampler:
 
 class ExternalClockSampler:
     """The same summary as ClockSampler from a separate ``nvidia-smi`` process polling every
-    10 ms (started before the barrier, stopped after the timed region), for steps coupled across
+    10 ms (started before the barrier, its output in a temporary file), for steps coupled across
     ranks: there an in-process polling thread stalled a rank's launches and with them every other
-    rank (tall K on 8 GPUs: 268-270 us per step against 216-218 us without the thread)."""
+    rank (tall K on 8 GPUs: 268-270 us per step against 216-218 us without the thread).  The
+    constructor waits (at most 10 s) for the first sample, so the sampler is running before the
+    timed region; when no sample falls inside a short timed region, the first one after its start
+    is taken."""
 
     def __init__(self, cuda_index, period_ms=10):
         import subprocess
+        import tempfile
         import torch
         self.samples, self.reasons, self.max_mhz = [], 0, None
         self.window = (None, None)
         self.proc = None
+        self.out = tempfile.NamedTemporaryFile(mode="w+", prefix="clocks_", suffix=".csv")
         try:
             p = torch.cuda.get_device_properties(cuda_index)
             bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
@@ -247,40 +252,59 @@ class ExternalClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", bus, "--query-gpu=timestamp,clocks.sm,clocks.max.sm,"
                  "clocks_event_reasons.active", "--format=csv,noheader,nounits",
-                 f"--loop-ms={period_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                text=True)
+                 f"--loop-ms={period_ms}"], stdout=self.out, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        deadline = time.time() + 10.0
+        while time.time() < deadline and self.proc.poll() is None:
+            if os.path.getsize(self.out.name) > 0:
+                break
+            time.sleep(0.01)
 
     def start(self):
         self.window = (time.time(), None)
 
-    def stop(self):
+    def _parse(self):
         import datetime as _dt
+        rows = []
+        with open(self.out.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) != 4:
+                    continue
+                try:
+                    ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    rows.append((ts, int(parts[1]), int(parts[2]), int(parts[3], 16)))
+                except ValueError:
+                    continue
+        return rows
+
+    def stop(self):
         self.window = (self.window[0], time.time() + 0.02)
         if self.proc is None:
             return
         time.sleep(0.03)  # at least one sample after the timed region
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
         except Exception:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        rows = self._parse()
+        self.out.close()
         t0, t1 = self.window
-        for line in out.splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) != 4:
-                continue
-            try:
-                ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                mhz, max_mhz, reasons = int(parts[1]), int(parts[2]), int(parts[3], 16)
-            except ValueError:
-                continue
+        if t0 is None:
+            return
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        if not inside:
+            inside = [r for r in rows if r[0] >= t0][:1]
+        for _, mhz, max_mhz, reasons in inside:
+            self.samples.append(mhz)
+            self.reasons |= reasons
             self.max_mhz = max_mhz
-            if t0 is not None and t0 <= ts <= t1:
-                self.samples.append(mhz)
-                self.reasons |= reasons
+        if self.max_mhz is None and rows:
+            self.max_mhz = rows[-1][2]
 
     def summary(self):
         if not self.samples:
