@@ -127,3 +127,37 @@ def test_post_run_parity_check_accepts_the_product_and_rejects_planted_mistakes(
     s_blk = torch.rand(2, 3, generator=g) + 0.5
     deq = bench.dequantized(q, s_blk, "block", (128, 128))
     assert torch.equal(deq[200, 290], q[200, 290].float() * s_blk[1, 2])
+
+
+def test_external_clock_sampler_reads_a_separate_process(tmp_path, monkeypatch):
+    """Coupled multi-GPU runs take their clocks from a separate nvidia-smi process: started and
+    producing samples before the timed region, summarised over the region (or the first sample
+    after its start when the region is shorter than the polling period), and harmless when the
+    tool is missing.  A stand-in nvidia-smi prints the same CSV columns every 10 ms."""
+    import time
+    sys.path.insert(0, ROOT)
+    import bench
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/bash\n"
+                    "while true; do\n"
+                    "  echo \"$(date +'%Y/%m/%d %H:%M:%S.%3N'), 1875, 1965, 0x0000000000000004\"\n"
+                    "  sleep 0.01\n"
+                    "done\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ.get('PATH', '')}")
+    s = bench.ExternalClockSampler(0)
+    s.start()
+    time.sleep(0.2)
+    s.stop()
+    c = s.summary()
+    assert c["samples"] >= 3 and c["sm_mhz"] == 1875 and c["sm_max_mhz"] == 1965
+    assert c["reasons"] == ["sw_power_cap"]
+    short = bench.ExternalClockSampler(0)
+    short.start()
+    short.stop()
+    assert short.summary()["samples"] >= 1
+    monkeypatch.setenv("PATH", str(tmp_path / "nothing_here"))
+    none = bench.ExternalClockSampler(0)
+    none.start()
+    none.stop()
+    assert none.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
