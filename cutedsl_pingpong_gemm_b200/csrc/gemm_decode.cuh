@@ -25,11 +25,13 @@
 // rows stage them in a send block (in its now free A/B stages) laid out as the owner's receive
 // slot (rows padded by 16 bytes so a warp's 16-byte stores hit distinct banks), and one lane per
 // 32 rows copies them to the owner with one bulk transfer (cp.async.bulk.shared::cluster)
-// completing on the owner's receive barrier (per-thread remote stores of the same bytes measured
-// ~10 us at M = 128).  The owner adds the S - 1 received blocks to its own rows, applies alpha,
+// completing on the owner's receive barrier (plain per-thread remote stores of the same bytes
+// measured ~10 us at M = 128; per-thread st.async into the owner's slot, the st_async option,
+// level or slower).  The owner adds the S - 1 received blocks to its own rows, applies alpha,
 // the FP8 scales and the bias, stages its rows of D^T as boxes of D (16 token rows x 32 columns)
 // in its stages and writes each with one TMA store (128 two-byte global stores per thread
-// measured ~6 us at M = 128).
+// measured ~6 us at M = 128).  Each launch is a programmatic dependent of the stream's previous
+// kernel (the pdl option, see the prologue).
 //
 // Roles (320 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocation and (leader CTA)
 // MMA issuer (one lane), warps 2-9 the epilogue (warp w reads TMEM lane quadrant w mod 4, warps
